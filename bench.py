@@ -1,0 +1,446 @@
+#!/usr/bin/env python
+"""Throughput benchmark: aligned frames/s of the B200-native CTC aligner.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
+                    [--mode optimized|conventional]
+                    [--impl ours|reference|reference-cuda]
+
+One step = one ``align`` call over one synthetic batch of BASELINE.json's
+configs[C] (default cfg1, the config the 1-GPU metric is quoted on).  Under
+torchrun each rank aligns its own independent batch of that shape on its own
+GPU (records are independent: no collective on the data path; weak scaling).
+
+impl=ours            this package: device-resident timing (``value``), an
+                     end-to-end host->device->host timing (``e2e``), the live
+                     roofline of the DP forward kernel and a CPU baseline.
+impl=reference       the reference's own CPU implementation of the path (its
+                     corrected C++ comparator, compiled in place into
+                     oracle/_ref) on all host threads; rank 0 only.
+impl=reference-cuda  the reference's own CUDA extension (oracle/_ref) on the
+                     same device-resident batch, timed like ``value``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_FLUSH_BYTES = 256 << 20   # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", type=int, default=1)
+    p.add_argument("--mode", default="optimized", choices=["optimized", "conventional"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="CPU work in the cpu_baseline sample")
+    args = p.parse_args()
+    if args.warmup < 3:
+        p.error("--warmup must be >= 3")
+    return args
+
+
+# ---------------------------------------------------------------- utilities
+
+def rank_info():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def algorithmic_bytes(wl):
+    """Per SURVEY 8(d): 32 B for every sector of a row holding a label column
+    of the record (sectors counted from a 32 B-aligned record base), plus 12 B
+    of output per frame and the 8 B int64 targets.  Returns (emission+target
+    bytes read by the DP, full B_alg)."""
+    read = 0
+    out = 0
+    for i in range(wl.batch):
+        e, t = wl.record(i)
+        T, V = e.shape
+        cols = np.unique(np.r_[t, wl.blank])
+        per_residue = np.array([np.unique((r + cols) // 8).size for r in range(8)])
+        residues = (np.arange(T, dtype=np.int64) * V) % 8
+        read += 32 * int(per_residue[residues].sum()) + 8 * t.size
+        out += 12 * T
+    return read, read + out
+
+
+def traffic_from_profile(config_name):
+    """dram bytes per forward launch from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / f"ffa_viterbi_forward_{config_name}.md"
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+              "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+              "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.device = device_index
+
+    def __enter__(self):
+        import torch
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            target = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            target = str(self.device)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", target, f"--query-gpu={','.join(self.FIELDS)}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.samples = []
+        if self.proc is None:
+            return False
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == len(self.FIELDS):
+                self.samples.append(parts)
+        return False
+
+    def summary(self):
+        if not getattr(self, "samples", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for s in self.samples for k in range(4) if s[3 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------ CPU baselines
+
+def cpu_reference_runner(wl):
+    """The reference's corrected C++ comparator (oracle/_ref) over all host
+    threads, one record per task with the GIL released, as in its benchmark
+    adapter; falls back to our C oracle ("port") if the build is absent."""
+    from oracle import oracle
+    threads = oracle.default_threads()
+    module = oracle.corrected_module()
+    es, ts = wl.records()
+    if module is not None:
+        pool = ThreadPoolExecutor(max_workers=threads)
+        inputs = [(e[None], t[None]) for e, t in zip(es, ts)]
+
+        def run():
+            return list(pool.map(lambda a: module.forced_align(a[0], a[1], wl.blank), inputs))
+        return run, "reference", threads, pool
+
+    def run_port():
+        return oracle.align(es, ts, wl.blank, threads=threads)
+    return run_port, "port", threads, None
+
+
+def time_cpu(run, frames, seconds):
+    run()  # warm the pool / caches
+    done, start = 0, time.perf_counter()
+    while True:
+        run()
+        done += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            return frames * done / elapsed, done, elapsed
+
+
+# ------------------------------------------------------------------ our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import fast_forced_aligner_b200 as ffa
+    from fast_forced_aligner_b200 import workloads
+    from fast_forced_aligner_b200.build import LIB
+
+    rank, world, local = rank_info()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    ffa.load_extension()
+    wl = workloads.config(args.config, shard=rank)
+    frames = int(wl.lengths.sum())
+    frame_list, token_list = wl.lengths.tolist(), wl.target_lengths.tolist()
+    e_host = torch.from_numpy(wl.emissions).pin_memory()
+    t_host = torch.from_numpy(wl.targets).pin_memory()
+    e_dev = e_host.to(device)
+    t_dev = t_host.to(device)
+    ffa.validate_inputs(list(e_dev.split(frame_list)), list(t_dev.split(token_list)), blank_id=wl.blank)
+
+    def step(e, t):
+        return ffa.align_packed(e, frame_list, t, token_list, blank_id=wl.blank, mode=args.mode)
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    import ctypes
+    lib = ctypes.CDLL(str(LIB))
+    ev_fwd0 = torch.cuda.Event(enable_timing=True)
+    ev_fwd1 = torch.cuda.Event(enable_timing=True)
+    ev_fwd0.record(); ev_fwd1.record()
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(e_dev, t_dev)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing: inputs in HBM, L2 flushed before each step
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    fwd_ms = []
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            barrier()
+            lib.ffa_profile_forward_events(ctypes.c_void_p(ev_fwd0.cuda_event),
+                                           ctypes.c_void_p(ev_fwd1.cuda_event))
+            ev0[k].record()
+            result = step(e_dev, t_dev)
+            ev1[k].record()
+            lib.ffa_profile_forward_events(None, None)
+            torch.cuda.synchronize()
+            fwd_ms.append(ev_fwd0.elapsed_time(ev_fwd1))
+            barrier()
+        step_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+        total_ms = max_over_ranks(sum(step_ms))
+
+        # ---- end to end: pinned host -> device -> align -> host, every step
+        lab_host = torch.empty(frames, dtype=torch.int64, pin_memory=True)
+        sc_host = torch.empty(frames, dtype=torch.float32, pin_memory=True)
+        st_host = torch.empty(wl.batch, dtype=torch.int32, pin_memory=True)
+        e_in = torch.empty_like(e_dev)
+        t_in = torch.empty_like(t_dev)
+        for _ in range(args.warmup):
+            e_in.copy_(e_host, non_blocking=True); t_in.copy_(t_host, non_blocking=True)
+            r = step(e_in, t_in)
+            lab_host.copy_(r.labels, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e2e0, e2e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e0.record()
+        for _ in range(args.steps):
+            e_in.copy_(e_host, non_blocking=True)
+            t_in.copy_(t_host, non_blocking=True)
+            r = step(e_in, t_in)
+            lab_host.copy_(r.labels, non_blocking=True)
+            sc_host.copy_(r.scores, non_blocking=True)
+            st_host.copy_(r.status, non_blocking=True)
+        e2e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e2e0.elapsed_time(e2e1))
+        barrier()
+    status_ok = bool((result.status == 0).all().item()) and bool((st_host == 0).all().item())
+
+    all_frames = sum_over_ranks(frames)
+    value = all_frames * args.steps / (total_ms / 1e3)
+    e2e_value = all_frames * args.steps / (e2e_ms / 1e3)
+    fwd_avg_ms = max_over_ranks(statistics.fmean(fwd_ms))
+    read_bytes, alg_bytes = algorithmic_bytes(wl)
+    peak, peak_kind = peaks()
+    achieved = read_bytes / (fwd_avg_ms / 1e3) / 1e9
+    traffic = traffic_from_profile(wl.name)
+    cells = wl.cells()
+    line = {
+        "metric": "aligned frames/sec", "value": value, "unit": "frames/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "records_per_gpu": wl.batch, "frames_per_gpu": frames,
+                   "vocab": wl.vocab, "mode": args.mode, "check_inputs": True,
+                   "inputs": "packed device-resident fp32 [sum T, V] + int64 targets",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": f"records sharded, {world} independent GPU(s), no collective"},
+        "e2e": {"value": e2e_value, "unit": "frames/s",
+                "h2d_bytes_per_step": int(e_host.numel() * 4 + t_host.numel() * 8),
+                "d2h_bytes_per_step": int(frames * 12 + wl.batch * 4),
+                "api": "fast_forced_aligner_b200.align_packed (torch op over the C ABI)"},
+        "roofline": {"kernel": "ffa_viterbi_forward", "bound": "hbm", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
+                     "algorithmic_bytes_per_launch": read_bytes,
+                     "kernel_ms": fwd_avg_ms,
+                     "note": "serial frame dependency: latency-bound DP, see dp_latency"},
+        "dp_latency": {"longest_record_frames": int(wl.lengths.max()),
+                       "ns_per_frame_longest": fwd_avg_ms * 1e6 / float(wl.lengths.max()),
+                       "cells_per_s": cells / (fwd_avg_ms / 1e3), "cells": cells},
+        "b_alg_bytes": alg_bytes,
+        "gpu_launches": 4 * args.steps,
+        "gpu_launches_note": "ffa_viterbi_forward + ffa_trace_fill per align call, "
+                             "in the device-resident and the end-to-end timed loops",
+        "status_ok": status_ok,
+    }
+    clock = clocks.summary()
+    line["clocks"] = clock
+    if rank == 0 and world == 1:
+        run, kind, threads, pool = cpu_reference_runner(wl)
+        cpu_value, passes, seconds = time_cpu(run, frames, args.cpu_seconds)
+        if pool is not None:
+            pool.shutdown()
+        line["cpu_baseline"] = {"value": cpu_value, "unit": "frames/s", "cores": threads, "kind": kind,
+                                "sample": f"{passes} passes over the {wl.name} batch "
+                                          f"({wl.batch} records, {frames} frames) in {seconds:.1f} s"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ reference arms
+
+def run_reference_cpu(args):
+    rank, world, _ = rank_info()
+    if rank != 0:
+        return
+    from fast_forced_aligner_b200 import workloads
+    wl = workloads.config(args.config)
+    frames = int(wl.lengths.sum())
+    run, kind, threads, pool = cpu_reference_runner(wl)
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    if pool is not None:
+        pool.shutdown()
+    value = frames * args.steps / sum(times)
+    line = {
+        "impl": "reference", "metric": "aligned frames/sec", "value": value, "unit": "frames/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "records_per_gpu": wl.batch, "frames_per_gpu": frames,
+                   "vocab": wl.vocab, "mode": "conventional (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} timed passes over the {wl.name} batch "
+                                   f"({wl.batch} records, {frames} frames)"},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_cuda(args):
+    rank, world, local = rank_info()
+    if rank != 0:
+        return
+    import torch
+    from fast_forced_aligner_b200 import workloads
+    from oracle import oracle
+    if not oracle.load_reference_cuda():
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/fast_forced_aligner_cuda.so not built"}))
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    wl = workloads.config(args.config)
+    frames = int(wl.lengths.sum())
+    e_dev = torch.from_numpy(wl.emissions).to(device)
+    t_dev = torch.from_numpy(wl.targets).to(device)
+    es = list(e_dev.split(wl.lengths.tolist()))
+    ts = list(t_dev.split(wl.target_lengths.tolist()))
+    blanks = [wl.blank] * wl.batch
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    results = {}
+    for mode in ("optimized", "conventional"):
+        for _ in range(args.warmup):
+            oracle.reference_cuda_align(es, ts, blanks, mode=mode, check_inputs=True)
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            oracle.reference_cuda_align(es, ts, blanks, mode=mode, check_inputs=True)
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        results[mode] = {"value": frames * args.steps / (total / 1e3), "ms_per_step": total / args.steps}
+    line = {"impl": "reference-cuda", "metric": "aligned frames/sec",
+            "value": results[args.mode]["value"], "unit": "frames/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": results[args.mode]["ms_per_step"],
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "records": wl.batch, "frames": frames, "mode": args.mode,
+                       "l2": "flushed before every timed step",
+                       "api": "reference align op with its public-API arguments (alignment.py:496-501)"},
+            "modes": results}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference_cpu(args)
+    elif args.impl == "reference-cuda":
+        run_reference_cuda(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

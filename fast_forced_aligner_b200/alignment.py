@@ -1,0 +1,299 @@
+"""Public API of the B200-native CTC forced aligner.
+
+A drop-in for the reference's Python surface (brthor/fast-forced-aligner,
+src/fast_forced_aligner/alignment.py): the same names, keyword arguments,
+result fields, status codes, error classes and messages.  The work happens in
+the native library: torch.ops.ffa_b200.* (csrc/ffa_torch.cpp) over the C ABI of
+libffa_b200.so (include/ffa_b200.h), whose sm_100a kernels run the DP.  There
+is no CPU fallback: without the native library every entry point raises.
+"""
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+from functools import lru_cache
+from pathlib import Path
+from typing import Literal
+
+import torch
+from torch import Tensor
+
+Mode = Literal["optimized", "conventional"]
+_PACKAGE = Path(__file__).resolve().parent
+_MODES = {"conventional": 0, "optimized": 1}
+
+
+@lru_cache(maxsize=1)
+def load_extension() -> None:
+    """Load the native library and register the ``torch.ops.ffa_b200`` ops.
+
+    Mirrors the reference's ``load_extension`` (alignment.py:15-63): the same
+    prerequisites and RuntimeError messages.  The native library is built
+    in-tree (``python -m fast_forced_aligner_b200.build``); when it is absent
+    and a CUDA toolkit is available, the first call builds it, like the
+    reference's compile-on-first-use.  Successful calls are memoized.
+
+    Raises:
+        RuntimeError: PyTorch lacks CUDA support, no GPU is accessible, or the
+            native library is missing and cannot be built (no ``nvcc``), or it
+            fails to load.
+    """
+    from torch.utils import cpp_extension
+
+    if torch.version.cuda is None:
+        raise RuntimeError("fast_forced_aligner_b200 requires a CUDA-enabled PyTorch installation")
+    if not torch.cuda.is_available():
+        raise RuntimeError("fast_forced_aligner_b200 requires an accessible NVIDIA GPU and compatible driver")
+    shim = _PACKAGE / "_ffa_torch.so"
+    library = _PACKAGE / "libffa_b200.so"
+    if not (shim.is_file() and library.is_file()):
+        cuda_home = cpp_extension.CUDA_HOME
+        if cuda_home is None or not (Path(cuda_home) / "bin" / "nvcc").is_file():
+            raise RuntimeError(
+                "fast_forced_aligner_b200's native library is not built and cannot be compiled here. "
+                "Install the matching CUDA development toolkit (including nvcc) and a C++ compiler; "
+                "set CUDA_HOME if the toolkit is installed outside its usual location. "
+                "PyTorch's CUDA runtime libraries alone are insufficient."
+            )
+        from . import build as _build
+        _build.build()
+    try:
+        torch.ops.load_library(str(shim))
+    except OSError as error:  # pragma: no cover - depends on the box
+        raise RuntimeError(f"fast_forced_aligner_b200 failed to load its native library: {error}") from error
+
+
+@dataclass(frozen=True)
+class AlignmentBatch:
+    """Packed frame alignments and per-record diagnostics returned by ``align``.
+
+    Same fields, shapes, dtypes and meanings as the reference's
+    ``AlignmentBatch`` (alignment.py:66-148).  Let ``B`` be the batch size and
+    ``N = sum(T_i)``; every tensor lives on the input CUDA device.
+
+    Attributes:
+        lengths: host-known frame counts ``(T_0, ..., T_{B-1})``.
+        labels: int64 ``(N,)`` vocabulary IDs, blanks and repeats retained;
+            ``-1`` at every frame of a failed record.
+        scores: float32 ``(N,)``: ``emissions[i][t, paths[i][t]]``; ``-inf``
+            for failed records.
+        status: int32 ``(B,)``: 0 success, 1 no finite complete path, 2 rejected
+            by the emission-validity mask, 3 invalid target IDs, 4 insufficient
+            CTC frames.  Target errors take precedence over the mask.
+        objective: float32 ``(B,)`` native accumulated path score (the
+            sequential fp32 sum along the returned path).
+        stitched: int32 ``(B,)``: 1 when the optimized route's chunk paths were
+            joined, 0 when conventional DP produced the path.
+        repair_passes: int32 ``(B,)`` repair rounds of the optimized route.
+        repaired_frames: int64 ``(B,)`` frames re-solved by repair rounds.
+        shortcut_stats: int64 ``(B, 3)``: accepted greedy chunks, frames in
+            them, chunks rejected for ambiguous placement.
+        routing_stats: int32 ``(B, 3)``: early-fallback state, budget-rejected
+            repair rounds, largest rejected region.
+        reuse_stats: int64 ``(B, 4)`` in optimized mode when a record has 2048
+            or more frames, else ``(0, 4)``.
+
+    Tensor operations follow PyTorch's CUDA stream semantics; returning this
+    object does not imply the GPU work has completed.
+    """
+
+    lengths: tuple[int, ...]
+    labels: Tensor
+    scores: Tensor
+    status: Tensor
+    objective: Tensor
+    stitched: Tensor
+    repair_passes: Tensor
+    repaired_frames: Tensor
+    shortcut_stats: Tensor
+    routing_stats: Tensor
+    reuse_stats: Tensor
+
+    @property
+    def paths(self) -> tuple[Tensor, ...]:
+        """Per-record views of ``labels`` (no copy, no synchronisation)."""
+        return self.labels.split(self.lengths)
+
+    def raise_for_status(self) -> None:
+        """Read ``status`` on the host (synchronises) and raise for failures.
+
+        Raises ValueError listing the batch indices of statuses 1-4 with the
+        reference's messages (alignment.py:163-230), RuntimeError for an
+        unknown status.
+        """
+        statuses = self.status.cpu().tolist()
+        if not any(statuses):
+            return
+        unknown = [i for i, value in enumerate(statuses) if value not in (0, 1, 2, 3, 4)]
+        if unknown:
+            raise RuntimeError(f"unknown alignment status at batch indices {unknown}")
+        invalid = [i for i, value in enumerate(statuses) if value == 2]
+        failed = [i for i, value in enumerate(statuses) if value == 1]
+        messages = []
+        if invalid:
+            messages.append(f"invalid emissions at batch indices {invalid}")
+        if failed:
+            messages.append(f"no finite complete CTC path for batch indices {failed}")
+        invalid_targets = [i for i, value in enumerate(statuses) if value == 3]
+        insufficient_frames = [i for i, value in enumerate(statuses) if value == 4]
+        if invalid_targets:
+            messages.append(f"invalid target IDs at batch indices {invalid_targets}")
+        if insufficient_frames:
+            messages.append(f"insufficient CTC frames at batch indices {insufficient_frames}")
+        if messages:
+            raise ValueError("; ".join(messages))
+
+
+def _blanks(count: int, blank_id) -> list[int]:
+    blanks = [blank_id] * count if type(blank_id) is int else list(blank_id)
+    if len(blanks) != count:
+        raise ValueError("provide one blank ID per record")
+    if not all(type(b) is int for b in blanks):
+        raise ValueError("unsupported frame count, vocabulary, target length, or blank ID")
+    return blanks
+
+
+def _metadata(emissions: Sequence[Tensor], targets: Sequence[Tensor], blank_id) -> list[int]:
+    """Host-side checks that must precede the op (alignment.py:233-252); the
+    per-tensor checks run in C++ with the same messages."""
+    count = len(emissions)
+    if not 0 < count <= 65535 or len(targets) != count:
+        raise ValueError("provide 1..65535 matching emissions and targets")
+    blanks = _blanks(count, blank_id)
+    first = emissions[0]
+    if not isinstance(first, Tensor) or first.device.type != "cuda":
+        raise ValueError("inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device")
+    return blanks
+
+
+def _check_mask(emission_validity, device, count) -> None:
+    if emission_validity is not None:
+        if (not isinstance(emission_validity, Tensor)
+                or emission_validity.device != device
+                or emission_validity.dtype != torch.bool or emission_validity.ndim != 1
+                or emission_validity.numel() != count
+                or not emission_validity.is_contiguous()):
+            raise ValueError("emission_validity must be contiguous CUDA bool [batch] on the input device")
+
+
+@torch.inference_mode()
+def validate_inputs(
+    emissions: Sequence[Tensor], targets: Sequence[Tensor], *,
+    blank_id: int | Sequence[int] = 0,
+) -> None:
+    """Validate metadata, target IDs and CTC frame feasibility (synchronous).
+
+    Same contract as the reference (alignment.py:255-309): the checks run on
+    the GPU (one warp per record, ``torch.ops.ffa_b200.check_targets``) and one
+    status per record is copied to the host.  Emission values are not scanned.
+
+    Raises:
+        ValueError: metadata violates the input contract, or target IDs /
+            minimum frame counts fail; the message lists failing batch indices.
+    """
+    blanks = _metadata(emissions, targets, blank_id)
+    with torch.cuda.device(emissions[0].device):
+        load_extension()
+        status = torch.ops.ffa_b200.check_targets(list(emissions), list(targets), blanks)
+    failures = [i for i, value in enumerate(status.cpu().tolist()) if value]
+    if failures:
+        raise ValueError(f"invalid target IDs or insufficient CTC frames at batch indices {failures}")
+
+
+@torch.inference_mode()
+def emission_validity(emissions: Sequence[Tensor]) -> Tensor:
+    """Return a CUDA bool ``[B]`` mask that rejects NaN/+inf in each record.
+
+    Same contract as the reference (alignment.py:312-343): every element is
+    scanned (-inf is valid), the mask stays on the device, and no GPU value is
+    read by the host.  Pass it to ``align(..., emission_validity=mask)``.
+    """
+    if not 0 < len(emissions) <= 65535:
+        raise ValueError("provide 1..65535 emission tensors")
+    first = emissions[0]
+    if not isinstance(first, Tensor) or first.device.type != "cuda":
+        raise ValueError("emissions must be contiguous CUDA float32 [T,V] with supported dimensions on one device")
+    with torch.cuda.device(first.device):
+        load_extension()
+        return torch.ops.ffa_b200.emission_validity(list(emissions))
+
+
+def _mode(mode, check_inputs) -> int:
+    if mode not in _MODES:
+        raise ValueError("mode must be 'optimized' or 'conventional'")
+    if type(check_inputs) is not bool:
+        raise TypeError("check_inputs must be bool")
+    return _MODES[mode]
+
+
+@torch.inference_mode()
+def align(
+    emissions: Sequence[Tensor], targets: Sequence[Tensor], *,
+    blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
+    check_inputs: bool = True, emission_validity: Tensor | None = None,
+) -> AlignmentBatch:
+    """Align known CTC targets to resident emissions; return CUDA frame paths.
+
+    Same arguments, result and error behaviour as the reference's ``align``
+    (alignment.py:346-502):
+
+    Args:
+        emissions: ``B`` contiguous CUDA float32 ``(T_i, V_i)`` tensors,
+            ``1 <= B <= 65535``, ``1 <= T_i <= 2**31 - 1``, ``1 <= V_i <= 8192``.
+        targets: ``B`` contiguous CUDA int64 ``(U_i,)`` tensors on the same
+            device, IDs in ``[0, V_i)`` and different from the blank,
+            ``0 <= U_i <= 2047``.
+        blank_id: one Python int or ``B`` Python ints (bools rejected).
+        mode: ``"optimized"`` (default) or ``"conventional"``.  Both return the
+            exact conventional-DP path (stay > step > skip tie rule).
+        check_inputs: validate target IDs (status 3) and frame feasibility
+            (status 4) on the GPU; must be a Python bool.
+        emission_validity: optional CUDA bool ``[B]`` mask; False gives status
+            2 unless target validation fails.
+
+    Returns:
+        AlignmentBatch with packed CUDA outputs.  Failures are recorded in
+        ``status`` and do not raise; call ``raise_for_status``.
+
+    Raises:
+        ValueError: invalid mode, metadata, blank IDs or mask metadata.
+        TypeError: ``check_inputs`` is not a bool.
+        RuntimeError: the native library is unavailable or CUDA fails.
+    """
+    code = _mode(mode, check_inputs)
+    blanks = _metadata(emissions, targets, blank_id)
+    _check_mask(emission_validity, emissions[0].device, len(emissions))
+    with torch.cuda.device(emissions[0].device):
+        load_extension()
+        tensors, lengths = torch.ops.ffa_b200.align(
+            list(emissions), list(targets), blanks, code, emission_validity, check_inputs)
+    return AlignmentBatch(tuple(lengths), *tensors)
+
+
+@torch.inference_mode()
+def align_packed(
+    emissions: Tensor, frames: Sequence[int], targets: Tensor, tokens: Sequence[int], *,
+    blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
+    check_inputs: bool = True, emission_validity: Tensor | None = None,
+) -> AlignmentBatch:
+    """Packed variable-length form of ``align`` (no per-record tensors).
+
+    Record ``i`` is rows ``[sum(frames[:i]), sum(frames[:i+1]))`` of one
+    contiguous CUDA float32 ``(N, V)`` matrix and tokens
+    ``[sum(tokens[:i]), sum(tokens[:i+1]))`` of one contiguous CUDA int64
+    vector.  Results and errors are those of ``align`` on the same records.
+    """
+    code = _mode(mode, check_inputs)
+    frames = [int(f) for f in frames]
+    tokens = [int(u) for u in tokens]
+    if not 0 < len(frames) <= 65535 or len(tokens) != len(frames):
+        raise ValueError("provide 1..65535 matching frame counts, token counts and blanks")
+    blanks = _blanks(len(frames), blank_id)
+    if not isinstance(emissions, Tensor) or emissions.device.type != "cuda":
+        raise ValueError("inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device")
+    _check_mask(emission_validity, emissions.device, len(frames))
+    with torch.cuda.device(emissions.device):
+        load_extension()
+        tensors, lengths = torch.ops.ffa_b200.align_packed(
+            emissions, frames, targets, tokens, blanks, code, emission_validity, check_inputs)
+    return AlignmentBatch(tuple(lengths), *tensors)

@@ -1,0 +1,174 @@
+/*
+ * ffa_b200.h -- C ABI of the B200-native CTC forced aligner (libffa_b200.so).
+ *
+ * The library aligns known CTC transcripts to fp32 emission matrices that are
+ * already resident on one CUDA device.  It is the native boundary under the
+ * Python package fast_forced_aligner_b200, whose align()/emission_validity()
+ * mirror the reference's public API (brthor/fast-forced-aligner,
+ * src/fast_forced_aligner/alignment.py:312-502).
+ *
+ * The reference binds its path through two TORCH_LIBRARY ops
+ * (src/fast_forced_aligner/csrc/alignment.cu:1064-1070):
+ *   align(Tensor[] emissions, Tensor[] targets, int[] blanks, ...)
+ *       -> (Tensor[] outputs, int[] lengths)                 alignment.cu:919
+ *   emission_validity(Tensor[] emissions) -> Tensor           alignment.cu:893
+ * Each entry point below replaces one of them with plain pointers and sizes:
+ * no torch types cross this boundary.  The caller owns every buffer: inputs
+ * are borrowed, outputs and scratch are caller-allocated, and all work is
+ * enqueued on the caller's stream without any host synchronisation.
+ *
+ * Conventions
+ *   - Functions return FFA_OK (0) or a negative ffa_status.  The message of
+ *     the most recent failure on the calling thread is ffa_last_error().
+ *   - Per-record alignment outcomes are NOT return codes: they are written to
+ *     the device `status` array (0 ok, 1 no finite path, 2 masked by the
+ *     emission-validity mask, 3 invalid target IDs, 4 too few frames),
+ *     exactly as the reference's status contract (alignment.py:88-94).
+ *   - Thread safety: every function is reentrant; concurrent calls on
+ *     different streams or devices share no mutable state.
+ */
+#ifndef FFA_B200_H
+#define FFA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FFA_API __attribute__((visibility("default")))
+#else
+#define FFA_API
+#endif
+
+typedef struct CUstream_st* ffa_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+typedef enum ffa_status {
+  FFA_OK = 0,
+  FFA_ERR_INVALID_ARGUMENT = -1, /* malformed batch metadata (ValueError upstream) */
+  FFA_ERR_UNSUPPORTED = -2,      /* sizes outside the supported limits (ValueError) */
+  FFA_ERR_BUFFER_TOO_SMALL = -3, /* workspace/staging smaller than the plan needs */
+  FFA_ERR_CUDA = -4,             /* a CUDA runtime call failed (RuntimeError) */
+  FFA_ERR_INTERNAL = -5
+} ffa_status;
+
+typedef enum ffa_mode {
+  FFA_MODE_CONVENTIONAL = 0, /* full-record max-plus Viterbi DP */
+  FFA_MODE_OPTIMIZED = 1     /* greedy/chunked route with exact DP fallback */
+} ffa_mode;
+
+enum {
+  FFA_FLAG_CHECK_INPUTS = 1 /* validate target IDs and frame feasibility on the device */
+};
+
+/* Limits (alignment.py:237, 249-250; the state limit is this build's). */
+#define FFA_MAX_RECORDS 65535
+#define FFA_MAX_VOCAB 8192
+#define FFA_MAX_FRAMES 2147483647LL
+
+/* One record: a device-resident fp32 [frames, vocab] row-major emission
+ * matrix and an int64 [tokens] transcript (reference: one entry of the
+ * `emissions` / `targets` tensor lists, alignment.cu:961-988). */
+typedef struct ffa_record {
+  const float* emissions;  /* device pointer, 4-byte aligned */
+  const int64_t* targets;  /* device pointer; may be NULL when tokens == 0 */
+  int64_t frames;          /* T, 1 .. FFA_MAX_FRAMES */
+  int32_t vocab;           /* V, 1 .. FFA_MAX_VOCAB */
+  int32_t tokens;          /* U >= 0; states S = 2U + 1 */
+  int32_t blank;           /* 0 .. V-1 */
+  int32_t reserved;        /* must be 0 */
+} ffa_record;
+
+/* Caller-allocated device outputs, packed in record order without padding
+ * (reference AlignmentBatch fields, alignment.py:138-148). */
+typedef struct ffa_outputs {
+  int64_t* labels;          /* [sum T] vocabulary id per frame; -1 for failed records */
+  float* scores;            /* [sum T] selected emission per frame; -inf for failed */
+  int32_t* status;          /* [B] */
+  float* objective;         /* [B] native accumulated path score */
+  int32_t* stitched;        /* [B] 1 = optimized route joined chunk paths */
+  int32_t* repair_passes;   /* [B] */
+  int64_t* repaired_frames; /* [B] */
+  int64_t* shortcut_stats;  /* [B, 3] */
+  int32_t* routing_stats;   /* [B, 3] */
+  int64_t* reuse_stats;     /* [B, 4] or NULL */
+} ffa_outputs;
+
+/* Sizes a call needs, computed on the host from the batch metadata alone. */
+typedef struct ffa_sizes {
+  size_t staging_bytes;   /* host staging (pinned for a truly async upload) */
+  size_t workspace_bytes; /* device scratch, 256-byte aligned */
+  int64_t total_frames;   /* sum of T: length of labels/scores */
+} ffa_sizes;
+
+FFA_API int ffa_abi_version(void);
+FFA_API const char* ffa_last_error(void);
+
+/* ---- align (replaces torch.ops.fast_forced_aligner_cuda.align,
+ *      alignment.cu:919-1061 and alignment.py:346-502) ---------------------- */
+
+/* Host only.  Validates the batch (the reference's metadata checks,
+ * alignment.py:233-252 and alignment.cu:961-971) and reports the buffer
+ * sizes ffa_align needs.  Touches no device memory. */
+FFA_API int ffa_align_query(const ffa_record* records, int64_t count, int mode, int flags,
+                    ffa_sizes* sizes);
+
+/* Enqueue one alignment on `stream`.
+ *   emission_validity: optional device bool[count] mask (NULL = none); a
+ *       false entry gives status 2 unless target validation fails
+ *       (alignment.cu:836, 870-874).
+ *   staging: host memory of sizes.staging_bytes.  The call writes the device
+ *       descriptor table into it and enqueues one cudaMemcpyAsync from it;
+ *       pinned memory keeps the call asynchronous.  Keep it unchanged until
+ *       the stream has passed this call.
+ *   workspace: device scratch of sizes.workspace_bytes, 256-byte aligned,
+ *       not shared with concurrent work on another stream.
+ * No host synchronisation, no allocation, no device-to-host transfer. */
+FFA_API int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
+              const uint8_t* emission_validity, const ffa_outputs* outputs,
+              void* staging, size_t staging_bytes,
+              void* workspace, size_t workspace_bytes, ffa_stream_t stream);
+
+/* ---- emission_validity (replaces torch.ops.fast_forced_aligner_cuda.
+ *      emission_validity, alignment.cu:879-917 and alignment.py:312-343) ---- */
+
+/* Host only: sizes for ffa_emission_validity (targets/tokens/blank ignored). */
+FFA_API int ffa_emission_validity_query(const ffa_record* records, int64_t count, ffa_sizes* sizes);
+
+/* valid[i] = 1 unless record i holds a NaN or +inf (-inf is allowed).
+ * Same staging/workspace contract as ffa_align. */
+FFA_API int ffa_emission_validity(const ffa_record* records, int64_t count, uint8_t* valid,
+                          void* staging, size_t staging_bytes,
+                          void* workspace, size_t workspace_bytes, ffa_stream_t stream);
+
+/* ---- profiling hook (no reference counterpart: the reference exposes no
+ *      per-kernel timing) --------------------------------------------------- */
+
+/* While set, ffa_align calls made on the calling thread record `before` and
+ * `after` (two cudaEvent_t created by the caller) on their stream immediately
+ * around the DP forward kernel, so the caller can read that kernel's device
+ * time with cudaEventElapsedTime.  Pass NULL, NULL to clear. */
+FFA_API int ffa_profile_forward_events(void* before, void* after);
+
+/* ---- target validation (replaces the per-record checks of the reference's
+ *      validate_inputs, alignment.py:255-309) ------------------------------- */
+
+/* Host only: sizes for ffa_check_targets. */
+FFA_API int ffa_check_targets_query(const ffa_record* records, int64_t count, ffa_sizes* sizes);
+
+/* status[i] (device int32[count]) = 3 if a target ID is outside [0, V) or
+ * equals the blank, else 4 if U + adjacent repeats > T, else 0 -- the same
+ * codes and precedence ffa_align writes with FFA_FLAG_CHECK_INPUTS
+ * (alignment.cu:852-874).  Same staging/workspace contract as ffa_align. */
+FFA_API int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
+                              void* staging, size_t staging_bytes,
+                              void* workspace, size_t workspace_bytes, ffa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FFA_B200_H */

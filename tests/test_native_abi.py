@@ -1,0 +1,176 @@
+"""The native boundary without a GPU: library loading, exported symbols,
+host-side planning and the Python surface's argument contract."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+from torch.utils import cpp_extension
+
+import fast_forced_aligner_b200 as ffa
+from fast_forced_aligner_b200 import alignment
+
+ROOT = Path(__file__).resolve().parents[1]
+LIB = ROOT / "fast_forced_aligner_b200" / "libffa_b200.so"
+SHIM = ROOT / "fast_forced_aligner_b200" / "_ffa_torch.so"
+
+
+class Record(ctypes.Structure):
+    _fields_ = [("emissions", ctypes.c_void_p), ("targets", ctypes.c_void_p),
+                ("frames", ctypes.c_int64), ("vocab", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("blank", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class Sizes(ctypes.Structure):
+    _fields_ = [("staging_bytes", ctypes.c_size_t), ("workspace_bytes", ctypes.c_size_t),
+                ("total_frames", ctypes.c_int64)]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not LIB.exists():
+        from fast_forced_aligner_b200 import build
+        build.build()
+    handle = ctypes.CDLL(str(LIB))
+    handle.ffa_last_error.restype = ctypes.c_char_p
+    return handle
+
+
+def declared_symbols():
+    names = []
+    for header in (ROOT / "include").glob("*.h"):
+        names += re.findall(r"FFA_API\s+[\w\s\*]+?\b(ffa_\w+)\s*\(", header.read_text())
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_symbols()
+    assert {"ffa_align", "ffa_align_query", "ffa_emission_validity"} <= set(names)
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.ffa_abi_version() == 1
+
+
+def records(*specs):
+    arr = (Record * len(specs))()
+    for i, (T, V, U, blank) in enumerate(specs):
+        # Planning never dereferences device pointers: fake aligned addresses.
+        arr[i] = Record(0x10000 * (i + 1), 0x900000 * (i + 1) if U else None, T, V, U, blank, 0)
+    return arr
+
+
+def test_align_query_sizes(lib):
+    recs = records((600, 32, 100, 0), (7, 6, 0, 5), (2305, 1025, 2047, 1024))
+    sizes = Sizes()
+    assert lib.ffa_align_query(recs, 3, 0, 1, ctypes.byref(sizes)) == 0
+    assert sizes.total_frames == 600 + 7 + 2305
+    assert sizes.staging_bytes > 0 and sizes.staging_bytes % 256 == 0
+    # Workspace holds at least 2 bits per DP cell (T*S/4 bytes).
+    assert sizes.workspace_bytes >= (600 * 201 + 7 + 2305 * 4095) // 4
+
+
+@pytest.mark.parametrize("spec, code", [
+    ((0, 32, 1, 0), -2), ((10, 0, 1, 0), -2), ((10, 8193, 1, 0), -2),
+    ((10, 32, 2048, 0), -2), ((10, 32, 1, 32), -2), ((10, 32, 1, -1), -2),
+])
+def test_align_query_rejects_unsupported_metadata(lib, spec, code):
+    sizes = Sizes()
+    assert lib.ffa_align_query(records(spec), 1, 0, 1, ctypes.byref(sizes)) == code
+    assert lib.ffa_last_error()
+
+
+def test_align_query_rejects_malformed_calls(lib):
+    sizes = Sizes()
+    assert lib.ffa_align_query(records((10, 32, 1, 0)), 0, 0, 1, ctypes.byref(sizes)) == -1
+    assert lib.ffa_align_query(records((10, 32, 1, 0)), 1, 7, 1, ctypes.byref(sizes)) == -1
+    assert lib.ffa_align_query(records((10, 32, 1, 0)), 1, 0, 8, ctypes.byref(sizes)) == -1
+    missing = records((10, 32, 3, 0))
+    missing[0].targets = None
+    assert lib.ffa_align_query(missing, 1, 0, 1, ctypes.byref(sizes)) == -1
+    unaligned = records((10, 32, 1, 0))
+    unaligned[0].emissions = 0x10002
+    assert lib.ffa_align_query(unaligned, 1, 0, 1, ctypes.byref(sizes)) == -1
+
+
+def test_align_reports_small_buffers_before_any_device_work(lib):
+    recs = records((100, 32, 10, 0))
+    sizes = Sizes()
+    assert lib.ffa_align_query(recs, 1, 0, 1, ctypes.byref(sizes)) == 0
+    outs = (ctypes.c_void_p * 10)(*([0x1000] * 10))
+    staging = ctypes.create_string_buffer(8)
+    rc = lib.ffa_align(recs, ctypes.c_int64(1), 0, 1, None, outs, staging, ctypes.c_size_t(8),
+                       ctypes.c_void_p(0x100000), ctypes.c_size_t(sizes.workspace_bytes), None)
+    assert rc == -3
+    assert b"staging" in lib.ffa_last_error()
+
+
+def test_validity_and_target_queries(lib):
+    sizes = Sizes()
+    assert lib.ffa_emission_validity_query(records((100, 32, 0, 0), (5, 3, 0, 0)), 2,
+                                           ctypes.byref(sizes)) == 0
+    assert sizes.total_frames == 105 and sizes.workspace_bytes >= sizes.staging_bytes
+    assert lib.ffa_check_targets_query(records((100, 32, 5, 0)), 1, ctypes.byref(sizes)) == 0
+
+
+def test_torch_ops_register_without_a_gpu():
+    torch.ops.load_library(str(SHIM))
+    for name in ("align", "align_packed", "emission_validity", "check_targets"):
+        assert hasattr(torch.ops.ffa_b200, name)
+
+
+# ---- Python surface (reference tests/test_extension.py, test_core.py:85-93) ----
+
+@pytest.fixture()
+def fresh_loader():
+    alignment.load_extension.cache_clear()
+    yield
+    alignment.load_extension.cache_clear()
+
+
+def test_cpu_torch_reports_cuda_requirement(monkeypatch, fresh_loader):
+    monkeypatch.setattr(torch.version, "cuda", None)
+    with pytest.raises(RuntimeError, match="CUDA-enabled PyTorch"):
+        ffa.load_extension()
+
+
+def test_missing_gpu_reports_driver_requirement(monkeypatch, fresh_loader):
+    monkeypatch.setattr(torch.version, "cuda", "12.8")
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(RuntimeError, match="accessible NVIDIA GPU"):
+        ffa.load_extension()
+
+
+@pytest.mark.parametrize("toolkit", [None, "/nonexistent/cuda-toolkit"])
+def test_unbuilt_library_without_toolkit_reports_nvcc(monkeypatch, fresh_loader, toolkit, tmp_path):
+    monkeypatch.setattr(torch.version, "cuda", "12.8")
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(cpp_extension, "CUDA_HOME", toolkit)
+    monkeypatch.setattr(alignment, "_PACKAGE", tmp_path)  # no built library there
+    with pytest.raises(RuntimeError, match="including nvcc"):
+        ffa.load_extension()
+
+
+def test_argument_contract_without_gpu():
+    e = torch.zeros(12, 6)
+    t = torch.tensor([1])
+    with pytest.raises(ValueError, match="mode"):
+        ffa.align([e], [t], mode="unknown")
+    with pytest.raises(TypeError, match="check_inputs"):
+        ffa.align([e], [t], check_inputs=1)
+    with pytest.raises(ValueError):
+        ffa.align([], [])
+    with pytest.raises(ValueError):
+        ffa.align([e], [])
+    with pytest.raises(ValueError, match="blank"):
+        ffa.align([e], [t], blank_id=[0, 1])
+    with pytest.raises(TypeError):  # the reference's list(True) raises TypeError too
+        ffa.align([e], [t], blank_id=True)
+    with pytest.raises(ValueError):
+        ffa.align([e], [t], blank_id=[True])
+    with pytest.raises(ValueError, match="CUDA"):
+        ffa.align([e], [t])  # CPU tensors
+    with pytest.raises(ValueError):
+        ffa.emission_validity([])
+    with pytest.raises(ValueError):
+        ffa.emission_validity([e])
