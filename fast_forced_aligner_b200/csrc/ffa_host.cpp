@@ -42,6 +42,7 @@ int ceil_log2(int64_t x) {
 }
 
 struct Geometry {
+  int K;         // states per thread
   int nw;        // warps for the DP
   int slot_log2; // packing slot: 1 << slot_log2 warps
   int seg_log2;  // traceback segment length
@@ -50,10 +51,21 @@ struct Geometry {
   int64_t map_elems;
 };
 
-Geometry geometry(const ffa_record& r) {
+// States per thread.  A record that has an SM to itself (at most one record
+// per SM in the batch) is latency-bound: its frame time is set by the busiest
+// of the SM's four schedulers, so it takes the K that keeps it at <= 4 warps
+// (one per scheduler).  Packed records share SMs and use K = 8.
+int choose_k(int64_t S, bool latency_bound) {
+  if (!latency_bound || S <= 32 * 8 * 4) return 8;
+  if (S <= 32 * 10 * 4) return 10;
+  return 8;  // longer transcripts: more warps rather than longer per-thread chains
+}
+
+Geometry geometry(const ffa_record& r, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
-  g.nw = static_cast<int>((S + 32 * ffa::kStates - 1) / (32 * ffa::kStates));
+  g.K = choose_k(S, latency_bound);
+  g.nw = static_cast<int>((S + 32 * g.K - 1) / (32 * g.K));
   g.slot_log2 = ceil_log2(g.nw);
   // Segment length ~2*sqrt(T) balances the serial map walk (T/H steps) against
   // the per-segment backpointer walk (H steps).
@@ -63,8 +75,9 @@ Geometry geometry(const ffa_record& r) {
   const int64_t H = int64_t{1} << g.seg_log2;
   g.segments = (r.frames + H - 1) / H;
   const int64_t nt = 32 * static_cast<int64_t>(g.nw);
-  g.bp_words = (r.frames + ffa::kFramesPerWord - 1) / ffa::kFramesPerWord * nt;
-  g.map_elems = (g.segments - 1) * nt * ffa::kStates;
+  const int fpw = ffa::frames_per_word_host(g.K);
+  g.bp_words = (r.frames + fpw - 1) / fpw * nt;
+  g.map_elems = (g.segments - 1) * nt * g.K;
   return g;
 }
 
@@ -108,17 +121,21 @@ struct AlignLayout {
   int64_t total_frames, bp_words, map_elems, segments, fill_items;
 };
 
+// One record per SM or fewer: every record's DP is latency-bound.
+bool latency_bound(int64_t count) { return count <= device_sms(); }
+
 int plan_align(const ffa_record* records, int64_t count, AlignLayout* L) {
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0;
+  const bool lat = latency_bound(count);
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
-    const Geometry g = geometry(records[i]);
+    const Geometry g = geometry(records[i], lat);
     frames += records[i].frames;
     bp_words += g.bp_words;
-    map_elems += align_up(static_cast<size_t>(g.map_elems), 4);
+    map_elems += align_up(static_cast<size_t>(g.map_elems), 8);
     segments += g.segments;
     fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
   }
@@ -239,9 +256,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
 
   // Per-record descriptors and arena offsets.
   int64_t out_off = 0, bp_off = 0, map_off = 0, seg_off = 0, nfill = 0;
+  const bool lat = latency_bound(count);
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
-    const Geometry g = geometry(r);
+    const Geometry g = geometry(r, lat);
     ffa::RecordDev d{};
     d.emissions = r.emissions;
     d.targets = r.targets;
@@ -253,45 +271,79 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     d.U = r.tokens;
     d.blank = r.blank;
     d.seg_off = static_cast<int32_t>(seg_off);
-    d.nw = static_cast<uint16_t>(g.nw);
+    d.nw = static_cast<uint8_t>(g.nw);
+    d.kst = static_cast<uint8_t>(g.K);
     d.seg_log2 = static_cast<uint8_t>(g.seg_log2);
+    // TMA row staging needs 16-byte aligned rows and a small row.
+    d.row_mode = (r.vocab % 4 == 0 && r.vocab <= ffa::kRowModeMaxVocab &&
+                  (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0)
+                     ? 1
+                     : 0;
     recs[i] = d;
     for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
       fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
     out_off += r.frames;
     bp_off += g.bp_words;
-    map_off += static_cast<int64_t>(align_up(static_cast<size_t>(g.map_elems), 4));
+    map_off += static_cast<int64_t>(align_up(static_cast<size_t>(g.map_elems), 8));
     seg_off += g.segments;
     order[i] = static_cast<int32_t>(i);
   }
 
-  // Pack records of equal slot size into CTAs, longest first.  Records per
-  // CTA grow only when the batch would otherwise need more than one wave.
-  auto slot_of = [&](int32_t i) {
-    const int64_t S = 2 * static_cast<int64_t>(records[i].tokens) + 1;
-    return ceil_log2((S + 32 * ffa::kStates - 1) / (32 * ffa::kStates));
-  };
+  // Records are grouped by emission staging (TMA row rings vs per-thread
+  // column gather: one launch each), then by slot size, longest first.
+  unsigned max_row_vocab = 0;
+  int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
+  for (int64_t i = 0; i < count; ++i)
+    if (recs[i].row_mode) {
+      max_row_vocab = std::max<unsigned>(max_row_vocab, records[i].vocab);
+      row_vocab = (row_vocab < 0 || row_vocab == records[i].vocab) ? records[i].vocab : 0;
+    }
+  const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
+  const unsigned row_slot_bytes = static_cast<unsigned>(
+      align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4, 128));
+  const int64_t row_slots =
+      row_slot_bytes ? std::max<int64_t>(1, static_cast<int64_t>((ffa::kSmemBudget - header) / row_slot_bytes))
+                     : ffa::kMaxWarps;
+
+  auto slot_of = [&](int32_t i) { return ceil_log2(recs[i].nw); };
   std::sort(order, order + count, [&](int32_t a, int32_t b) {
+    if (recs[a].row_mode != recs[b].row_mode) return recs[a].row_mode > recs[b].row_mode;
+    if (recs[a].kst != recs[b].kst) return recs[a].kst < recs[b].kst;
     const int sa = slot_of(a), sb = slot_of(b);
     if (sa != sb) return sa < sb;
     if (records[a].frames != records[b].frames) return records[a].frames > records[b].frames;
     return a < b;
   });
+  // Records per CTA grow only when the batch would otherwise need more than
+  // one wave; a row-staged slot also needs its ring to fit in shared memory.
   const int64_t sms = device_sms();
   const int64_t per_cta_target = std::max<int64_t>(1, (count + sms - 1) / sms);
-  int64_t nb = 0;
+  int64_t nb = 0, n_row_bundles = 0, max_row_slots = 1;
   for (int64_t k = 0; k < count;) {
     const int cls = slot_of(order[k]);
-    const int64_t capacity = std::min<int64_t>(ffa::kMaxWarps >> cls, per_cta_target);
+    const bool row = recs[order[k]].row_mode != 0;
+    const int kst = recs[order[k]].kst;
+    int64_t capacity = std::min(static_cast<int64_t>(ffa::kMaxWarps >> cls), per_cta_target);
+    if (row) capacity = std::min(capacity, row_slots);
     int64_t n = 0;
-    while (k + n < count && n < capacity && slot_of(order[k + n]) == cls) ++n;
+    while (k + n < count && n < capacity && slot_of(order[k + n]) == cls &&
+           (recs[order[k + n]].row_mode != 0) == row && recs[order[k + n]].kst == kst)
+      ++n;
     bundles[nb++] = ffa::Bundle{static_cast<int32_t>(k), static_cast<uint8_t>(cls),
-                                static_cast<uint8_t>(n), 0};
+                                static_cast<uint8_t>(n), static_cast<uint8_t>(kst), 0};
+    if (row) { ++n_row_bundles; max_row_slots = std::max(max_row_slots, n); }
     k += n;
   }
-  std::stable_sort(bundles, bundles + nb, [&](const ffa::Bundle& a, const ffa::Bundle& b) {
+  auto longest_first = [&](const ffa::Bundle& a, const ffa::Bundle& b) {
     return records[order[a.first]].frames > records[order[b.first]].frames;
-  });
+  };
+  std::stable_sort(bundles, bundles + n_row_bundles, longest_first);
+  std::stable_sort(bundles + n_row_bundles, bundles + nb, longest_first);
+  const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
+  int max_gather_k = 8;
+  for (int64_t i = 0; i < count; ++i)
+    if (!recs[i].row_mode) max_gather_k = std::max<int>(max_gather_k, recs[i].kst);
+  const unsigned gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(max_gather_k));
 
   auto* dev = static_cast<unsigned char*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -311,10 +363,17 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     err = cudaEventRecord(g_profile_before, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
-  err = ffa::launch_forward(drecs, reinterpret_cast<const ffa::Bundle*>(dev + L.bundles),
-                            reinterpret_cast<const int32_t*>(dev + L.order), static_cast<int>(nb),
-                            emission_validity, (flags & FFA_FLAG_CHECK_INPUTS) ? 1 : 0, bp,
-                            reinterpret_cast<uint16_t*>(dev + L.maps), anchors, out, s);
+  const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + L.bundles);
+  const auto* dorder = reinterpret_cast<const int32_t*>(dev + L.order);
+  auto* maps = reinterpret_cast<uint16_t*>(dev + L.maps);
+  const int check = (flags & FFA_FLAG_CHECK_INPUTS) ? 1 : 0;
+  err = ffa::launch_forward(drecs, dbundles, dorder, static_cast<int>(n_row_bundles), true,
+                            row_vocab > 0 ? row_vocab : 0, emission_validity, check, bp, maps,
+                            anchors, out, row_smem, row_slot_bytes, s);
+  if (err != cudaSuccess) return cuda_fail(err, "forward launch");
+  err = ffa::launch_forward(drecs, dbundles + n_row_bundles, dorder,
+                            static_cast<int>(nb - n_row_bundles), false, 0, emission_validity,
+                            check, bp, maps, anchors, out, gather_smem, 0, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   if (g_profile_after != nullptr) {
     err = cudaEventRecord(g_profile_after, s);

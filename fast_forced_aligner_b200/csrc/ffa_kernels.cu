@@ -1,13 +1,14 @@
 // ffa_kernels.cu -- sm_100a kernels of the B200-native CTC forced aligner.
 //
 //   ffa_viterbi_forward   conventional max-plus Viterbi forward pass, one
-//                         record per warp group, packed into 1024-thread CTAs;
+//                         record per warp group, packed into 512-thread CTAs;
 //                         writes 2-bit backpointers and per-segment ancestor
 //                         maps, then walks the maps from the terminal state
 //                         (semantics: reference alignment.cu:354-523)
 //   ffa_trace_fill        parallel traceback of every segment of every
 //                         record + label/score gather (alignment.cu:597-667)
 //   ffa_validity_scan     NaN/+inf scan of the emissions (alignment.cu:879-891)
+//   ffa_check_targets     target-ID and frame-feasibility checks alone
 //
 // Arithmetic contract: each DP cell is ONE fp32 round-to-nearest addition of
 // the selected predecessor score and the cell's emission, with the selection
@@ -28,15 +29,66 @@ namespace {
 __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
-
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
 __device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
-  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(gmem_src) : "memory");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after kWaitNs nanoseconds and reports the failure
+// instead of hanging.  A caller that saw one failure makes no further waits.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity,
+                                          unsigned long long limit_ns = kWaitNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - start > limit_ns) return false;
+  return true;
+}
+// One TMA bulk copy global -> shared (no tensor map, no multicast), completed
+// on `bar` with a transaction-byte count.
+__device__ __forceinline__ void tma_bulk_load(void* smem_dst, const void* gmem_src, unsigned bytes,
+                                              unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
 __device__ __forceinline__ int clamp_label(int64_t token, int V) {
@@ -46,223 +98,332 @@ __device__ __forceinline__ int clamp_label(int64_t token, int V) {
 }
 
 struct Boundary {
-  float alpha;  // score of the warp's last state
+  float alpha;  // score of a warp's last state
   int delta;    // its ancestor delta
 };
 
-// Dynamic shared memory of one forward CTA.
-struct ForwardSmem {
-  float ring[kRing][3][kCtaThreads];   // per-thread emission prefetch ring
-  Boundary bnd[2][kMaxWarps];          // last-state hand-off between warps
+// Shared-memory header of one forward CTA; emission rings follow it.
+struct ForwardShared {
+  Boundary bnd[2][kMaxWarps];  // last-state hand-off between warps of a slot
+  Boundary edge;               // {-inf, 0}: the "left neighbour" of a record's first warp
   int red_bad[kMaxWarps];
   int red_rep[kMaxWarps];
-  float term_last[kMaxWarps];          // per slot: alpha[S-1], alpha[S-2]
+  float term_last[kMaxWarps];  // per slot: alpha[S-1], alpha[S-2]
   float term_prev[kMaxWarps];
   int slot_status[kMaxWarps];
+  int slot_fault[kMaxWarps];   // a bounded wait ran out (reported as status 5)
+  unsigned long long full[kMaxWarps][kRowRing];  // per slot: row group landed
 };
 
-}  // namespace
+// Emission rings start at this 128-byte aligned offset (TMA destinations
+// must be 16-byte aligned); the host planner uses the same value.
+constexpr size_t kForwardHeader = (sizeof(ForwardShared) + 127) / 128 * 128;
+static_assert(kForwardHeader % 128 == 0, "ring offset alignment");
 
-// One CTA = one Bundle of records of the same slot size.  Warps of a slot run
-// the record's DP in lock step with one named barrier per frame; a one-warp
-// slot needs only __syncwarp.  Thread i of a record owns states 4i..4i+3.
-__global__ void __launch_bounds__(kCtaThreads, 1)
-ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict__ bundles,
-                    const int32_t* __restrict__ order, const uint8_t* __restrict__ mask,
-                    int check_inputs, uint32_t* __restrict__ bp_arena,
-                    uint16_t* __restrict__ map_arena, int32_t* __restrict__ anchors,
-                    OutputsDev out) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  ForwardSmem& sm = *reinterpret_cast<ForwardSmem*>(smem_raw);
+// One DP frame for this thread's K states (s = K*tl + k; odd k are tokens).
+// Selection: stay, then step if strictly greater, then skip if strictly
+// greater and legal (alignment.cu:418-424); one fp32 add per cell.  Also
+// advances the ancestor deltas d (distance back to the state at the end of the
+// previous traceback segment).  Returns the frame's backpointers as two bit
+// planes: bit k = "moved" (jump >= 1) of state k, bit K+q = "skipped"
+// (jump == 2) of token q = k/2, so jump = moved + skipped.
+template <int K>
+__device__ __forceinline__ unsigned dp_frame(float (&a)[K], int (&d)[K], float p1, int pd, float eb,
+                                             const float (&et)[K / 2], unsigned skip) {
+  float na[K];
+  int nd[K];
+  unsigned bits = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float x1 = k >= 1 ? a[k - 1] : p1;
+    const int d1 = k >= 1 ? d[k - 1] : pd;
+    const bool c = x1 > a[k];
+    float b = c ? x1 : a[k];
+    int n = c ? d1 + 1 : d[k];
+    if (k & 1) {
+      const float x2 = k >= 2 ? a[k - 2] : p1;
+      const int d2 = k >= 2 ? d[k - 2] : pd;
+      const bool j2 = ((skip >> (k >> 1)) & 1u) && x2 > b;
+      b = j2 ? x2 : b;
+      n = j2 ? d2 + 2 : n;
+      bits |= (static_cast<unsigned>(c || j2) << k) | (static_cast<unsigned>(j2) << (K + (k >> 1)));
+      na[k] = __fadd_rn(b, et[k >> 1]);
+    } else {
+      bits |= static_cast<unsigned>(c) << k;
+      na[k] = __fadd_rn(b, eb);
+    }
+    nd[k] = n;
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) { a[k] = na[k]; d[k] = nd[k]; }
+  return bits;
+}
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const Bundle bd = bundles[blockIdx.x];
-  const int slot = warp >> bd.slot_log2;
-  if (slot >= bd.count) return;
-  const int r = order[bd.first + slot];
-  const RecordDev rec = recs[r];
-  const int lw = warp & ((1 << bd.slot_log2) - 1);  // warp within the record
-  if (lw >= rec.nw) return;
-  const int NT = rec.nw * 32;
-  const int tl = lw * 32 + lane;  // thread within the record
-  const bool single = rec.nw == 1;
-  auto slot_sync = [&]() {
-    if (single) __syncwarp();
-    else named_barrier(slot, NT);
-  };
+// Backpointer word geometry: 1.5*K bits per frame and thread, packed in
+// 16-bit lanes of 32-bit words when they fit (two frames per word).
+__host__ __device__ constexpr int frames_per_word(int K) { return 3 * K / 2 <= 16 ? 2 : 1; }
 
-  const int T = rec.T, V = rec.V, U = rec.U, blank = rec.blank;
+// Jump of state s (owned by a thread with K states) from one frame's bits.
+__device__ __forceinline__ int jump_of(unsigned bits, int s, int K) {
+  const int k = s % K;
+  const unsigned moved = (bits >> k) & 1u;
+  const unsigned skipped = (k & 1) ? (bits >> (K + (k >> 1))) & 1u : 0u;
+  return static_cast<int>(moved + skipped);
+}
+
+// Per-record geometry shared by the DP body.
+struct SlotCtx {
+  int tid, warp, lane, slot, lw, NT, tl, r;
+  bool single;
+  __device__ __forceinline__ void sync() const {
+    // Unconditional (a one-warp record uses a 32-thread barrier): a branch
+    // here costs more than the barrier.
+    named_barrier(slot, NT);
+  }
+};
+
+// The DP of one record after its status checks: frame loop unrolled by
+// kGroup, terminal state, segment-map walk.  Thread tl owns states
+// K*tl .. K*tl+K-1 (odd offsets are tokens K/2*tl + k/2).
+template <int K, bool kRow, int kV>
+__device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec,
+                                          ForwardShared& sh, unsigned char* smem_raw,
+                                          uint32_t* __restrict__ bp_arena,
+                                          uint16_t* __restrict__ map_arena,
+                                          int32_t* __restrict__ anchors, const OutputsDev& out,
+                                          unsigned row_slot_bytes) {
+  constexpr int KT = K / 2;
+  constexpr int FPW = frames_per_word(K);
+  const int tl = x.tl, lane = x.lane, warp = x.warp, NT = x.NT, slot = x.slot;
+  const int T = rec.T, U = rec.U, blank = rec.blank;
+  const int V = kV > 0 ? kV : rec.V;
   const int S = 2 * U + 1;
   const int64_t* tgt = rec.targets;
 
-  // ---- status: mask, then target validation (alignment.cu:836, 852-874) ----
-  int status = (mask != nullptr && !mask[r]) ? 2 : 0;
-  if (check_inputs) {
-    int bad = 0, rep = 0;
-    for (int k = tl; k < U; k += NT) {
-      const int64_t token = tgt[k];
-      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
-      if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+  int col[KT];
+  unsigned skip = 0;
+  {
+    const int first = KT * tl;
+    int prev = (first >= 1 && first - 1 < U) ? clamp_label(tgt[first - 1], V) : -1;
+#pragma unroll
+    for (int q = 0; q < KT; ++q) {
+      const int u = first + q;
+      col[q] = u < U ? clamp_label(tgt[u], V) : blank;
+      // Skip s-2 -> s is legal for a token that differs from the previous
+      // token and from the blank (alignment.cu:407).
+      if (u < U && u >= 1 && col[q] != blank && col[q] != prev) skip |= 1u << q;
+      prev = col[q];
     }
-    bad = __reduce_or_sync(0xffffffffu, bad);
-    rep = __reduce_add_sync(0xffffffffu, rep);
-    if (lane == 0) { sm.red_bad[warp] = bad; sm.red_rep[warp] = rep; }
-    slot_sync();
-    if (tl == 0) {
-      int b = 0, p = 0;
-      for (int w = 0; w < rec.nw; ++w) { b |= sm.red_bad[warp + w]; p += sm.red_rep[warp + w]; }
-      if (b) status = 3;
-      else if (static_cast<int64_t>(U) + p > T) status = 4;
-      sm.slot_status[slot] = status;
-    }
-    slot_sync();
-    status = sm.slot_status[slot];
   }
-  if (tl == 0) {
-    // Diagnostics of the conventional route are all zero (alignment.py:101-129).
-    out.stitched[r] = 0;
-    out.repair_passes[r] = 0;
-    out.repaired_frames[r] = 0;
-    for (int j = 0; j < 3; ++j) { out.shortcut_stats[3 * r + j] = 0; out.routing_stats[3 * r + j] = 0; }
-    if (out.reuse_stats) for (int j = 0; j < 4; ++j) out.reuse_stats[4 * r + j] = 0;
-    if (status >= 2) { out.status[r] = status; out.objective[r] = -INFINITY; }
-  }
-  if (status >= 2) return;
-
-  // ---- states owned by this thread: s = 4*tl + k; odd k carry tokens ----
-  const int tok1 = 2 * tl, tok3 = 2 * tl + 1;
-  const int col1 = tok1 < U ? clamp_label(tgt[tok1], V) : blank;
-  const int col3 = tok3 < U ? clamp_label(tgt[tok3], V) : blank;
-  const int colm = (tok1 >= 1 && tok1 - 1 < U) ? clamp_label(tgt[tok1 - 1], V) : -1;
-  // Skip s-2 -> s is legal for a token state that differs from the token two
-  // states back (alignment.cu:407).
-  const bool sk1 = tok1 < U && tok1 >= 1 && col1 != blank && col1 != colm;
-  const bool sk3 = tok3 < U && col3 != blank && col3 != col1;
 
   const float* e = rec.emissions;
-  float* ring0 = &sm.ring[0][0][tid];
-  auto issue = [&](int64_t f) {
+  const int ngroups = (T + kGroup - 1) / kGroup;
+  float* ring = reinterpret_cast<float*>(smem_raw + kForwardHeader) +
+                static_cast<size_t>(slot) * (row_slot_bytes / 4);
+  float* gring = reinterpret_cast<float*>(smem_raw + kForwardHeader) + x.tid;
+  unsigned long long* full = sh.full[slot];
+  bool fault = false;
+
+  const int nchunks = (T + kChunkFrames - 1) / kChunkFrames;
+  auto issue_chunk = [&](int c) {  // kRow: by the record's thread 0
+    const int first = c * kChunkFrames;
+    const int rows = min(kChunkFrames, T - first);
+    const unsigned bytes = static_cast<unsigned>(rows) * V * 4u;
+    unsigned long long* bar = &full[c % kRowRing];
+    mbar_expect_tx(bar, bytes);
+    tma_bulk_load(ring + (c % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(first) * V, bytes, bar);
+  };
+  auto gather = [&](int64_t f) {  // !kRow: KT + 1 private 4-byte copies
     if (f < T) {
-      const float* row = e + static_cast<int64_t>(f) * V;
-      float* dst = ring0 + (f % kRing) * 3 * kCtaThreads;
+      const float* row = e + f * V;
+      float* dst = gring + (f % kGroup) * (KT + 1) * kCtaThreads;
       cp_async4(dst, row + blank);
-      cp_async4(dst + kCtaThreads, row + col1);
-      cp_async4(dst + 2 * kCtaThreads, row + col3);
+#pragma unroll
+      for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
     }
     cp_async_commit();
   };
+  if constexpr (kRow) {
+    if (tl == 0) {
+      for (int k = 0; k < kRowRing; ++k) mbar_init(&full[k], 1);
+      fence_mbar_init();
+      for (int c = 0; c < kRowRing && c < nchunks; ++c) issue_chunk(c);
+    }
+  } else {
 #pragma unroll
-  for (int f = 0; f < kRing - 1; ++f) issue(f);
-
-  // ---- frame 0: alpha[s] = e[0, l[s]] for s < 2 (alignment.cu:409) ----
-  issue(kRing - 1);
-  cp_async_wait<kRing - 1>();
-  float a0, a1, a2, a3;
-  {
-    const float* cur = ring0;
-    a0 = (tl == 0) ? cur[0] : -INFINITY;
-    a1 = (tl == 0 && S > 1) ? cur[kCtaThreads] : -INFINITY;
-    a2 = -INFINITY;
-    a3 = -INFINITY;
+    for (int f = 0; f < kGroup - 1; ++f) gather(f);
   }
-  int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
-  if (lane == 31) sm.bnd[1][warp] = Boundary{a3, d3};
-  slot_sync();
+  x.sync();
 
+  float a[K];
+  int d[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) { a[k] = -INFINITY; d[k] = 0; }
   const int hmask = (1 << rec.seg_log2) - 1;
-  const int H = 1 << rec.seg_log2;
   uint32_t* bp = bp_arena + rec.bp_off + tl;
-  uint16_t* maps = map_arena + rec.map_off + 4 * tl;
-  const int64_t map_stride = static_cast<int64_t>(NT) * kStates;
+  uint16_t* maps = map_arena + rec.map_off + K * tl;
+  const int64_t map_stride = static_cast<int64_t>(NT) * K;
+  const Boundary* left = x.lw > 0 ? &sh.bnd[0][warp - 1] : &sh.edge;
+  const int left_stride = x.lw > 0 ? kMaxWarps : 0;
+  // Skip frames in which none of this warp's states lies in the reachable
+  // band [S - 2(T - t), 2t + 1]: states above it are still unreachable (-inf)
+  // and states below it can no longer reach the end, and in-band states read
+  // only in-band states, so skipping is exact.  Active iff
+  // band_lo <= 2t <= band_hi.
+  const int w_lo = x.lw * 32 * K;
+  const int w_hi = w_lo + 32 * K - 1;
+  const unsigned band_lo = static_cast<unsigned>(max(w_lo - 1, 0));
+  const int64_t hi64 = static_cast<int64_t>(w_hi) - S + 2 * static_cast<int64_t>(T);
+  const bool never = hi64 < 0;
+  const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
   uint32_t word = 0;
 
-  for (int t = 1; t < T; ++t) {
-    issue(static_cast<int64_t>(t) + kRing - 1);
-    cp_async_wait<kRing - 1>();
-    const float* cur = ring0 + (t % kRing) * 3 * kCtaThreads;
-    const float eb = cur[0], e1 = cur[kCtaThreads], e3 = cur[2 * kCtaThreads];
+  auto load = [&](int t, int j, const float* rows, float& eb, float (&et)[KT]) {
+    if constexpr (kRow) {
+      const float* row = rows + j * V;
+      eb = row[blank];
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = row[col[q]];
+    } else {
+      gather(static_cast<int64_t>(t) + kGroup - 1);
+      cp_async_wait<kGroup - 1>();
+      const float* cur = gring + (t & (kGroup - 1)) * (KT + 1) * kCtaThreads;
+      eb = cur[0];
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+    }
+  };
+  auto store_map = [&](int t) {
+    // Ancestor map of segment t/H: state at its last frame -> state at the
+    // last frame of the previous segment, as a delta.
+    uint32_t* dst = reinterpret_cast<uint32_t*>(maps + ((t >> rec.seg_log2) - 1) * map_stride);
+#pragma unroll
+    for (int q = 0; q < KT; ++q)
+      dst[q] = static_cast<uint32_t>(d[2 * q]) | (static_cast<uint32_t>(d[2 * q + 1]) << 16);
+  };
+  auto store_word = [&](int t) {
+    bp[static_cast<int64_t>(t / FPW) * NT] = word;
+    word = 0;
+  };
+  auto frame = [&](int t, int j, const float* rows) {
+    float eb, et[KT];
+    load(t, j, rows, eb, et);
+    // Left neighbour's last state at t-1 (s-1 for k=0, s-2 for k=1): from
+    // lane-1, or for lane 0 from the warp on the left (branch-free).
+    float p1 = __shfl_up_sync(0xffffffffu, a[K - 1], 1);
+    int pd = __shfl_up_sync(0xffffffffu, d[K - 1], 1);
+    const Boundary nb = left[(t & 1) * left_stride];
+    if (lane == 0) { p1 = nb.alpha; pd = nb.delta; }
+    if (j == 0 && (t & hmask) == 0) {  // a new traceback segment starts at t
+#pragma unroll
+      for (int k = 0; k < K; ++k) d[k] = 0;
+      pd = 0;
+    }
+    const unsigned bits = dp_frame<K>(a, d, p1, pd, eb, et, skip);
+    if constexpr (FPW == 2) {
+      word |= bits << (16 * (t & 1));
+      if (t & 1) store_word(t);
+    } else {
+      word = bits;
+      store_word(t);
+    }
+    if (j == kGroup - 1 && (t & hmask) == hmask && t > hmask) store_map(t);
+    if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], d[K - 1]};
+    x.sync();
+  };
 
-    // Left neighbour's last state (s-1 for k=0, s-2 for k=1).
-    float p1 = __shfl_up_sync(0xffffffffu, a3, 1);
-    int pd = __shfl_up_sync(0xffffffffu, d3, 1);
-    if (lane == 0) {
-      if (lw > 0) {
-        const Boundary b = sm.bnd[t & 1][warp - 1];
-        p1 = b.alpha;
-        pd = b.delta;
-      } else {
-        p1 = -INFINITY;
-        pd = 0;
+  for (int g = 0; g < ngroups; ++g) {
+    const float* rows = nullptr;
+    if constexpr (kRow) {
+      const int c = g / kChunkGroups;
+      if (g % kChunkGroups == 0 && !fault && !mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1))
+        fault = true;
+      rows = ring + ((c % kRowRing) * kChunkFrames + (g % kChunkGroups) * kGroup) * V;
+    }
+    const int t0 = g * kGroup;
+    // The band test is made once per group: a group with at least one frame
+    // in which this warp has in-band states runs every frame (the plain DP is
+    // exact everywhere); a group with none only keeps the barriers (and the
+    // gather ring) in step.  Its backpointers and maps are never read.
+    const unsigned g2 = 2u * static_cast<unsigned>(t0);
+    const bool group_active = g == 0 || (!never && g2 + 2u * (kGroup - 1) >= band_lo && g2 <= band_hi);
+    if (!group_active) {
+#pragma unroll 1
+      for (int j = 0; j < kGroup && t0 + j < T; ++j) {
+        if constexpr (!kRow) {
+          float eb, et[KT];
+          load(t0 + j, j, rows, eb, et);
+        }
+        x.sync();
+      }
+      if constexpr (FPW == 2) word = 0;
+    } else if (g == 0) {
+      // Frame 0: alpha[s] = e[0, l[s]] for s < 2, else -inf (alignment.cu:409).
+      float eb, et[KT];
+      load(0, 0, rows, eb, et);
+#pragma unroll
+      for (int k = 0; k < K; ++k) { a[k] = -INFINITY; d[k] = 0; }
+      if (tl == 0) {
+        a[0] = eb;
+        if (S > 1) a[1] = et[0];
+      }
+      if (lane == 31) sh.bnd[1][warp] = Boundary{a[K - 1], 0};
+      x.sync();
+#pragma unroll 1
+      for (int j = 1; j < kGroup && j < T; ++j) frame(j, j, rows);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGroup; ++j)
+        if (t0 + j < T) frame(t0 + j, j, rows);
+    }
+    if constexpr (kRow) {
+      // Every thread has read this chunk's rows (the last barrier above), so
+      // its ring slot can take the chunk kRowRing ahead.
+      const int c = g / kChunkGroups;
+      if (tl == 0 && (g % kChunkGroups == kChunkGroups - 1 || g == ngroups - 1) &&
+          c + kRowRing < nchunks) {
+        fence_proxy_async();
+        issue_chunk(c + kRowRing);
       }
     }
-    if ((t & hmask) == 0) { d0 = d1 = d2 = d3 = 0; pd = 0; }  // new traceback segment
-
-    // k = 0 (blank): stay, step.
-    const bool c0 = p1 > a0;
-    const float b0 = c0 ? p1 : a0;
-    const int n0 = c0 ? pd + 1 : d0;
-    // k = 1 (token): stay, step, skip.
-    const bool c1 = a0 > a1;
-    float b1 = c1 ? a0 : a1;
-    unsigned j1 = c1 ? 1u : 0u;
-    int s1 = c1 ? d0 : d1;
-    if (sk1 && p1 > b1) { b1 = p1; j1 = 2u; s1 = pd; }
-    // k = 2 (blank): stay, step.
-    const bool c2 = a1 > a2;
-    const float b2 = c2 ? a1 : a2;
-    const int n2 = c2 ? d1 + 1 : d2;
-    // k = 3 (token): stay, step, skip.
-    const bool c3 = a2 > a3;
-    float b3 = c3 ? a2 : a3;
-    unsigned j3 = c3 ? 1u : 0u;
-    int s3 = c3 ? d2 : d3;
-    if (sk3 && a1 > b3) { b3 = a1; j3 = 2u; s3 = d1; }
-
-    a0 = __fadd_rn(b0, eb);
-    a1 = __fadd_rn(b1, e1);
-    a2 = __fadd_rn(b2, eb);
-    a3 = __fadd_rn(b3, e3);
-    d0 = n0;
-    d1 = s1 + static_cast<int>(j1);
-    d2 = n2;
-    d3 = s3 + static_cast<int>(j3);
-
-    const unsigned bits = (c0 ? 1u : 0u) | (j1 << 2) | ((c2 ? 1u : 0u) << 4) | (j3 << 6);
-    word |= bits << (8 * (t & 3));
-    if ((t & 3) == 3 || t == T - 1) {
-      bp[static_cast<int64_t>(t >> 2) * NT] = word;
-      word = 0;
-    }
-    if (t >= H && ((t & hmask) == hmask || t == T - 1)) {
-      // Ancestor map of segment c = t/H: state at its last frame -> state at
-      // the last frame of segment c-1, stored as a delta.
-      const int64_t c = t >> rec.seg_log2;
-      uint2 packed;
-      packed.x = static_cast<uint32_t>(d0) | (static_cast<uint32_t>(d1) << 16);
-      packed.y = static_cast<uint32_t>(d2) | (static_cast<uint32_t>(d3) << 16);
-      *reinterpret_cast<uint2*>(maps + (c - 1) * map_stride) = packed;
-    }
-    if (lane == 31) sm.bnd[(t + 1) & 1][warp] = Boundary{a3, d3};
-    slot_sync();
   }
-  cp_async_wait<0>();
+  if constexpr (!kRow) cp_async_wait<0>();
+  if constexpr (kRow) {
+    // After a failed wait, give the issuing thread's copies still in flight a
+    // short, bounded chance to land before the CTA's shared memory goes away.
+    if (fault && tl == 0)
+      for (int c = max(0, nchunks - kRowRing); c < nchunks; ++c)
+        mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1, kDrainNs);
+  }
+  {  // a word or a map the last frame left open
+    const int tl_ = T - 1;
+    if (FPW == 2 && tl_ > 0 && (tl_ & 1) == 0) store_word(tl_);
+    if (tl_ > hmask && (tl_ & hmask) != hmask) store_map(tl_);
+  }
+  if (fault) sh.slot_fault[slot] = 1;
 
   // ---- terminal state (alignment.cu:497-510) ----
   const int last = S - 1;  // even
-  if ((last >> 2) == tl) sm.term_last[slot] = (last & 3) == 0 ? a0 : a2;
-  if (S > 1 && ((last - 1) >> 2) == tl) sm.term_prev[slot] = ((last - 1) & 3) == 1 ? a1 : a3;
-  slot_sync();
+  // One predicated store per state keeps a[] in registers (a runtime index
+  // into it would move the array to local memory).
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int s = K * tl + k;
+    if (s == last) sh.term_last[slot] = a[k];
+    if (s == last - 1) sh.term_prev[slot] = a[k];
+  }
+  x.sync();
   if (tl == 0) {
-    const float vlast = sm.term_last[slot];
+    const float vlast = sh.term_last[slot];
     int terminal = last;
     float objective = vlast;
     if (S > 1) {
-      const float vprev = sm.term_prev[slot];
+      const float vprev = sh.term_prev[slot];
       if (vprev >= vlast) { terminal = last - 1; objective = vprev; }
     }
     const bool ok = isfinite(objective);
-    out.objective[r] = objective;
-    out.status[r] = ok ? 0 : 1;
+    out.objective[x.r] = objective;
+    out.status[x.r] = sh.slot_fault[slot] ? kStatusDeviceFault : (ok ? 0 : 1);
     if (ok) {
       // Walk the segment maps back from the terminal: one anchor per segment.
       const int C = static_cast<int>((static_cast<int64_t>(T) + hmask) >> rec.seg_log2);
@@ -275,6 +436,91 @@ ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict
         anc[c - 1] = s;
       }
     }
+  }
+}
+
+}  // namespace
+
+// One CTA = one Bundle of records with the same slot size and the same states
+// per thread.  Warps of a slot run the record's DP in lock step with one named
+// barrier per frame (a one-warp slot needs only __syncwarp).  kRow: emission
+// rows arrive kGroup frames at a time by one TMA bulk copy into a
+// kRowRing-deep ring per record; otherwise each thread gathers its columns
+// with cp.async into a private ring (large vocabularies).
+template <bool kRow, int kV>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict__ bundles,
+                    const int32_t* __restrict__ order, const uint8_t* __restrict__ mask,
+                    int check_inputs, uint32_t* __restrict__ bp_arena,
+                    uint16_t* __restrict__ map_arena, int32_t* __restrict__ anchors,
+                    OutputsDev out, unsigned row_slot_bytes) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
+
+  SlotCtx x;
+  x.tid = threadIdx.x;
+  x.warp = x.tid >> 5;
+  x.lane = x.tid & 31;
+  const Bundle bd = bundles[blockIdx.x];
+  x.slot = x.warp >> bd.slot_log2;
+  if (x.tid == 0) sh.edge = Boundary{-INFINITY, 0};
+  __syncthreads();
+  if (x.slot >= bd.count) return;
+  x.r = order[bd.first + x.slot];
+  const RecordDev rec = recs[x.r];
+  x.lw = x.warp & ((1 << bd.slot_log2) - 1);  // warp within the record
+  if (x.lw >= rec.nw) return;
+  x.NT = rec.nw * 32;
+  x.tl = x.lw * 32 + x.lane;  // thread within the record
+  x.single = rec.nw == 1;
+  const int tl = x.tl, lane = x.lane, warp = x.warp, r = x.r;
+  const int T = rec.T, V = rec.V, U = rec.U, blank = rec.blank;
+  const int64_t* tgt = rec.targets;
+
+  // ---- status: mask, then target validation (alignment.cu:836, 852-874) ----
+  int status = (mask != nullptr && !mask[r]) ? 2 : 0;
+  if (tl == 0) sh.slot_fault[x.slot] = 0;
+  if (check_inputs) {
+    int bad = 0, rep = 0;
+    for (int k = tl; k < U; k += x.NT) {
+      const int64_t token = tgt[k];
+      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
+      if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    rep = __reduce_add_sync(0xffffffffu, rep);
+    if (lane == 0) { sh.red_bad[warp] = bad; sh.red_rep[warp] = rep; }
+    x.sync();
+    if (tl == 0) {
+      int b = 0, p = 0;
+      for (int w = 0; w < rec.nw; ++w) { b |= sh.red_bad[warp + w]; p += sh.red_rep[warp + w]; }
+      if (b) status = 3;
+      else if (static_cast<int64_t>(U) + p > T) status = 4;
+      sh.slot_status[x.slot] = status;
+    }
+    x.sync();
+    status = sh.slot_status[x.slot];
+  }
+  if (tl == 0) {
+    // Diagnostics of the conventional route are all zero (alignment.py:101-129).
+    out.stitched[r] = 0;
+    out.repair_passes[r] = 0;
+    out.repaired_frames[r] = 0;
+    for (int j = 0; j < 3; ++j) { out.shortcut_stats[3 * r + j] = 0; out.routing_stats[3 * r + j] = 0; }
+    if (out.reuse_stats) for (int j = 0; j < 4; ++j) out.reuse_stats[4 * r + j] = 0;
+    if (status >= 2) { out.status[r] = status; out.objective[r] = -INFINITY; }
+  }
+  if (status >= 2) return;
+
+  switch (rec.kst) {
+    default:
+      record_dp<8, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
+      break;
+    case 10:
+      record_dp<10, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
+      break;
+
+
   }
 }
 
@@ -306,15 +552,17 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
   int32_t* p = path[warp];
   if (lane == 0) {
     const int NT = rec.nw * 32;
+    const int K = rec.kst;
+    const int fpw = frames_per_word(K);
     const uint32_t* bp = bp_arena + rec.bp_off;
     int s = anchors[rec.seg_off + c];
     int64_t cached = -1;
     uint32_t word = 0;
     p[b - 1 - a] = s;
     for (int t = b - 1; t > a; --t) {
-      const int64_t key = static_cast<int64_t>(t >> 2) * NT + (s >> 2);
+      const int64_t key = static_cast<int64_t>(t / fpw) * NT + s / K;
       if (key != cached) { word = bp[key]; cached = key; }
-      s -= (word >> (8 * (t & 3) + 2 * (s & 3))) & 3u;
+      s -= jump_of(fpw == 2 ? word >> (16 * (t & 1)) : word, s, K);
       p[t - 1 - a] = s;
     }
   }
@@ -380,22 +628,24 @@ __global__ void ffa_fill_u8(uint8_t* p, int64_t n, uint8_t value) {
     p[i] = value;
 }
 
-size_t forward_smem_bytes() { return sizeof(ForwardSmem); }
+size_t forward_header_bytes() { return kForwardHeader; }
 
 cudaError_t launch_forward(const RecordDev* recs, const Bundle* bundles, const int32_t* order,
-                           int num_bundles, const uint8_t* mask, int check_inputs,
+                           int num_bundles, bool row_mode, int row_vocab, const uint8_t* mask,
+                           int check_inputs,
                            uint32_t* bp, uint16_t* maps, int32_t* anchors,
-                           const OutputsDev& out, cudaStream_t stream) {
+                           const OutputsDev& out, unsigned smem_bytes, unsigned row_slot_bytes,
+                           cudaStream_t stream) {
   if (num_bundles <= 0) return cudaSuccess;
-  const size_t smem = sizeof(ForwardSmem);
+  auto kernel = !row_mode ? ffa_viterbi_forward<false, 0>
+                         : (row_vocab == 32 ? ffa_viterbi_forward<true, 32> : ffa_viterbi_forward<true, 0>);
   // Opting in to >48 KiB of dynamic shared memory is per device; the call is
   // cheap and idempotent, so it is repeated rather than cached.
-  cudaError_t err = cudaFuncSetAttribute(ffa_viterbi_forward,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes));
   if (err != cudaSuccess) return err;
-  ffa_viterbi_forward<<<num_bundles, kCtaThreads, smem, stream>>>(
-      recs, bundles, order, mask, check_inputs, bp, maps, anchors, out);
+  kernel<<<num_bundles, kCtaThreads, smem_bytes, stream>>>(
+      recs, bundles, order, mask, check_inputs, bp, maps, anchors, out, row_slot_bytes);
   return cudaGetLastError();
 }
 
