@@ -198,6 +198,8 @@ int cuda_fail(cudaError_t err, const char* what) {
 
 }  // namespace
 
+void ffa::set_last_error(const char* message) { g_error = message; }
+
 extern "C" {
 
 int ffa_abi_version(void) { return FFA_ABI_VERSION; }

@@ -120,6 +120,9 @@ cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_it
 cudaError_t launch_validity(const ScanRecord* recs, int64_t count, const ScanItem* items,
                             int64_t num_items, uint8_t* valid, cudaStream_t stream);
 
+// Sets the message ffa_last_error() returns on this thread (ffa_host.cpp).
+void set_last_error(const char* message);
+
 cudaError_t launch_check_targets(const RecordDev* recs, int64_t count, int32_t* status,
                                  cudaStream_t stream);
 

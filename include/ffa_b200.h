@@ -145,6 +145,29 @@ FFA_API int ffa_emission_validity(const ffa_record* records, int64_t count, uint
                           void* staging, size_t staging_bytes,
                           void* workspace, size_t workspace_bytes, ffa_stream_t stream);
 
+/* ---- allocation-free align (no counterpart in the reference, whose
+ *      align always allocates its scratch with at::empty) ------------------- */
+
+/* For callers that cannot allocate device memory when they align -- code
+ * running inside a framework that owns every device allocation, pipelines
+ * whose memory is fixed at start-up -- this runs exactly what ffa_align runs,
+ * but its scratch comes from buffers built into the library instead of from
+ * the caller: a 64 MiB device array (held on each GPU that loads it until
+ * the process exits) and a 2 MiB static host staging array.  Inputs and
+ * outputs are the caller's, as for ffa_align.  No cudaMalloc, cudaFree or
+ * other allocating routine is called.
+ *   - A batch whose ffa_align_query sizes exceed those limits is rejected
+ *     with FFA_ERR_UNSUPPORTED and a message in ffa_last_error().
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the two buffers: calls that may overlap on a GPU (other
+ *     streams, other host threads) race and must be serialised by the caller.
+ *     Nothing in them needs clearing between calls. */
+FFA_API int ffa_align_noalloc(const ffa_record* records, int64_t count, int mode, int flags,
+                              const uint8_t* emission_validity, const ffa_outputs* outputs,
+                              ffa_stream_t stream);
+
 /* ---- profiling hook (no reference counterpart: the reference exposes no
  *      per-kernel timing) --------------------------------------------------- */
 
