@@ -52,13 +52,14 @@ struct Geometry {
 };
 
 // States per thread.  A record that has an SM to itself (at most one record
-// per SM in the batch) is latency-bound: its frame time is set by the busiest
-// of the SM's four schedulers, so it takes the K that keeps it at <= 4 warps
-// (one per scheduler).  Packed records share SMs and use K = 8.
+// per SM in the batch) is latency-bound: its frame time is the per-frame
+// dependency chain, shortest with 4 states per thread and up to 16 warps
+// (measured: ~260 cycles per frame at 8 warps against ~280 for K = 8 at 4
+// warps).  Packed records share SMs, where fewer instructions per state win:
+// K = 8.
 int choose_k(int64_t S, bool latency_bound) {
-  if (!latency_bound || S <= 32 * 8 * 4) return 8;
-  if (S <= 32 * 10 * 4) return 10;
-  return 8;  // longer transcripts: more warps rather than longer per-thread chains
+  if (latency_bound && S <= 32 * 4 * 16) return 4;
+  return 8;
 }
 
 Geometry geometry(const ffa_record& r, bool latency_bound) {

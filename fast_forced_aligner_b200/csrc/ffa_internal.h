@@ -10,7 +10,7 @@
 namespace ffa {
 
 // DP geometry.  A record's CTC states s = 0..S-1 are owned in contiguous
-// runs of K per thread (thread i owns K*i..K*i+K-1; K in {8, 10}), 32
+// runs of K per thread (thread i owns K*i..K*i+K-1; K in {4, 8}), 32
 // threads per warp, up to kMaxWarps warps per record.  With an even run length
 // the first state of every run is a blank, so a thread needs only the last
 // state of its left neighbour.  S <= 4096, the reference's own limit

@@ -516,8 +516,8 @@ ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict
     default:
       record_dp<8, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
       break;
-    case 10:
-      record_dp<10, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
+    case 4:
+      record_dp<4, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
       break;
 
 
@@ -550,20 +550,34 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
     return;
   }
   int32_t* p = path[warp];
-  if (lane == 0) {
+  {
+    // The path moves at most 2 states per frame, so over FB frames it stays
+    // within 2*FB/K + 2 threads' words: the warp loads those FB x NTH words
+    // in one round trip, then steps through them with shuffles.  Every lane
+    // tracks the same state.
     const int NT = rec.nw * 32;
     const int K = rec.kst;
     const int fpw = frames_per_word(K);
+    const int FB = K >= 8 ? 8 : 6;
+    const int NTH = 2 * FB / K + 2;
     const uint32_t* bp = bp_arena + rec.bp_off;
     int s = anchors[rec.seg_off + c];
-    int64_t cached = -1;
-    uint32_t word = 0;
-    p[b - 1 - a] = s;
-    for (int t = b - 1; t > a; --t) {
-      const int64_t key = static_cast<int64_t>(t / fpw) * NT + s / K;
-      if (key != cached) { word = bp[key]; cached = key; }
-      s -= jump_of(fpw == 2 ? word >> (16 * (t & 1)) : word, s, K);
-      p[t - 1 - a] = s;
+    if (lane == 0) p[b - 1 - a] = s;
+    for (int t = b - 1; t > a;) {
+      const int f = lane / NTH, dd = lane % NTH;
+      const int tt = t - f;
+      const int th = s / K - dd;
+      uint32_t w = 0;
+      if (f < FB && tt > a && th >= 0) w = bp[static_cast<int64_t>(tt / fpw) * NT + th];
+      const int steps = min(FB, t - a);
+      const int th0 = s / K;
+      for (int i = 0; i < steps; ++i) {
+        const int ct = t - i;
+        const uint32_t word = __shfl_sync(0xffffffffu, w, i * NTH + (th0 - s / K));
+        s -= jump_of(fpw == 2 ? word >> (16 * (ct & 1)) : word, s, K);
+        if (lane == 0) p[ct - 1 - a] = s;
+      }
+      t -= steps;
     }
   }
   __syncwarp();

@@ -76,40 +76,23 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> run_align(
   ffa_sizes sizes{};
   check_status(ffa_align_query(recs.data(), count, cmode, flags, &sizes));
 
-  // One allocation holds every output; the returned tensors are typed views.
+  // One caching-allocator block per output (cheaper than carving typed views
+  // out of one block, which costs several dispatcher calls per view).
   const int64_t N = sizes.total_frames;
   int64_t max_frames = 0;
   for (const auto& r : recs) max_frames = std::max(max_frames, r.frames);
   const bool reuse = cmode == FFA_MODE_OPTIMIZED && max_frames >= 2048;
-  const int64_t reuse_rows = reuse ? count : 0;
-  auto pad8 = [](int64_t x) { return (x + 7) / 8 * 8; };
-  const int64_t o_labels = 0;
-  const int64_t o_scores = o_labels + 8 * N;
-  const int64_t o_status = o_scores + pad8(4 * N);
-  const int64_t o_objective = o_status + pad8(4 * count);
-  const int64_t o_stitched = o_objective + pad8(4 * count);
-  const int64_t o_passes = o_stitched + pad8(4 * count);
-  const int64_t o_frames = o_passes + pad8(4 * count);
-  const int64_t o_shortcut = o_frames + 8 * count;
-  const int64_t o_routing = o_shortcut + 24 * count;
-  const int64_t o_reuse = o_routing + pad8(12 * count);
-  const int64_t total = o_reuse + 32 * reuse_rows;
   const auto opts = at::TensorOptions().device(device);
-  auto block = at::empty({std::max<int64_t>(total, 8)}, opts.dtype(at::kByte));
-  auto view = [&](int64_t off, int64_t bytes, at::ScalarType type) {
-    return block.narrow(0, off, bytes).view(type);
-  };
-  auto labels = view(o_labels, 8 * N, at::kLong);
-  auto scores = view(o_scores, 4 * N, at::kFloat);
-  auto status = view(o_status, 4 * count, at::kInt);
-  auto objective = view(o_objective, 4 * count, at::kFloat);
-  auto stitched = view(o_stitched, 4 * count, at::kInt);
-  auto passes = view(o_passes, 4 * count, at::kInt);
-  auto repaired = view(o_frames, 8 * count, at::kLong);
-  auto shortcut = view(o_shortcut, 24 * count, at::kLong).view({count, 3});
-  auto routing = view(o_routing, 12 * count, at::kInt).view({count, 3});
-  auto reuse_stats = reuse ? view(o_reuse, 32 * count, at::kLong).view({count, 4})
-                           : at::empty({0, 4}, opts.dtype(at::kLong));
+  auto labels = at::empty({N}, opts.dtype(at::kLong));
+  auto scores = at::empty({N}, opts.dtype(at::kFloat));
+  auto status = at::empty({count}, opts.dtype(at::kInt));
+  auto objective = at::empty({count}, opts.dtype(at::kFloat));
+  auto stitched = at::empty({count}, opts.dtype(at::kInt));
+  auto passes = at::empty({count}, opts.dtype(at::kInt));
+  auto repaired = at::empty({count}, opts.dtype(at::kLong));
+  auto shortcut = at::empty({count, 3}, opts.dtype(at::kLong));
+  auto routing = at::empty({count, 3}, opts.dtype(at::kInt));
+  auto reuse_stats = at::empty({reuse ? count : 0, 4}, opts.dtype(at::kLong));
 
   auto staging = pinned_staging(sizes.staging_bytes);
   auto workspace = at::empty({static_cast<int64_t>(std::max<size_t>(sizes.workspace_bytes, 256))},
