@@ -244,8 +244,14 @@ def align(
             device, IDs in ``[0, V_i)`` and different from the blank,
             ``0 <= U_i <= 2047``.
         blank_id: one Python int or ``B`` Python ints (bools rejected).
-        mode: ``"optimized"`` (default) or ``"conventional"``.  Both return the
-            exact conventional-DP path (stay > step > skip tie rule).
+        mode: ``"optimized"`` (default) or ``"conventional"``.  Conventional
+            runs the exact max-plus Viterbi DP (stay > step > skip tie rule).
+            Optimized solves long records in 32-frame pieces joined at legal
+            seams (with repairs, and the conventional DP as fallback); it
+            returns the conventional outputs bit for bit unless the
+            conventional DP meets a tie on its path -- equal scores, or scores
+            closer than the fp32 rounding step of its running sum -- where it
+            returns a path of the same optimal score.
         check_inputs: validate target IDs (status 3) and frame feasibility
             (status 4) on the GPU; must be a Python bool.
         emission_validity: optional CUDA bool ``[B]`` mask; False gives status
@@ -263,10 +269,10 @@ def align(
     code = _mode(mode, check_inputs)
     blanks = _metadata(emissions, targets, blank_id)
     _check_mask(emission_validity, emissions[0].device, len(emissions))
-    with torch.cuda.device(emissions[0].device):
-        load_extension()
-        tensors, lengths = torch.ops.ffa_b200.align(
-            list(emissions), list(targets), blanks, code, emission_validity, check_inputs)
+    load_extension()
+    # The op runs under a device guard for the inputs' device.
+    tensors, lengths = torch.ops.ffa_b200.align(
+        list(emissions), list(targets), blanks, code, emission_validity, check_inputs)
     return AlignmentBatch(tuple(lengths), *tensors)
 
 
@@ -292,8 +298,8 @@ def align_packed(
     if not isinstance(emissions, Tensor) or emissions.device.type != "cuda":
         raise ValueError("inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device")
     _check_mask(emission_validity, emissions.device, len(frames))
-    with torch.cuda.device(emissions.device):
-        load_extension()
-        tensors, lengths = torch.ops.ffa_b200.align_packed(
-            emissions, frames, targets, tokens, blanks, code, emission_validity, check_inputs)
+    load_extension()
+    # The op runs under a device guard for the inputs' device.
+    tensors, lengths = torch.ops.ffa_b200.align_packed(
+        emissions, frames, targets, tokens, blanks, code, emission_validity, check_inputs)
     return AlignmentBatch(tuple(lengths), *tensors)

@@ -6,8 +6,9 @@
 //   - no allocation: outputs, workspace and host staging belong to the caller
 //     (the torch shim hands in caching-allocator memory), so the call is
 //     stream-ordered and never synchronises the host;
-//   - records are planned on the host into packed CTAs ("bundles") of equal
-//     slot size, longest first, so one launch covers a ragged batch;
+//   - records (or, in the optimized route, their pieces) are planned on the
+//     host into packed CTAs ("bundles") of equal slot size, longest first, so
+//     one launch covers a ragged batch;
 //   - the planner builds every table in the caller's staging buffer in place
 //     (no heap allocation), then enqueues one cudaMemcpyAsync.
 #include <algorithm>
@@ -27,6 +28,14 @@ namespace {
 thread_local std::string g_error;
 thread_local cudaEvent_t g_profile_before = nullptr;
 thread_local cudaEvent_t g_profile_after = nullptr;
+thread_local cudaEvent_t g_phase_events[FFA_PROFILE_POINTS] = {};
+thread_local bool g_phase_profiling = false;
+
+// Records the phase-boundary event `point` when phase profiling is on.
+cudaError_t mark_phase(int point, cudaStream_t stream) {
+  if (!g_phase_profiling) return cudaSuccess;
+  return cudaEventRecord(g_phase_events[point], stream);
+}
 
 int fail(int code, const std::string& message) {
   g_error = message;
@@ -35,50 +44,65 @@ int fail(int code, const std::string& message) {
 
 constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-int ceil_log2(int64_t x) {
-  int k = 0;
-  while ((int64_t{1} << k) < x) ++k;
-  return k;
-}
-
 struct Geometry {
+  bool chunked;  // optimized route: solved in pieces
   int K;         // states per thread
   int nw;        // warps for the DP
-  int slot_log2; // packing slot: 1 << slot_log2 warps
   int seg_log2;  // traceback segment length
   int64_t segments;
   int64_t bp_words;
   int64_t map_elems;
+  int64_t pieces;
+  int64_t frontier_elems;
 };
 
 // States per thread.  A record that has an SM to itself (at most one record
 // per SM in the batch) is latency-bound: its frame time is the per-frame
 // dependency chain, shortest with 4 states per thread and up to 16 warps
 // (measured: ~260 cycles per frame at 8 warps against ~280 for K = 8 at 4
-// warps).  Packed records share SMs, where fewer instructions per state win:
-// K = 8.
+// warps).  Packed records and pieces share SMs, where fewer instructions per
+// state win: K = 8.
 int choose_k(int64_t S, bool latency_bound) {
   if (latency_bound && S <= 32 * 4 * 16) return 4;
   return 8;
 }
 
-Geometry geometry(const ffa_record& r, bool latency_bound) {
+bool chunked_record(const ffa_record& r, bool optimized) {
+  return optimized && r.frames >= ffa::kPieceMinFrames;
+}
+
+// Pieces of kPieceFrames frames; the last one also takes a remainder shorter
+// than half a piece.
+int64_t piece_count(int64_t T) {
+  int64_t C = T / ffa::kPieceFrames;
+  if (T % ffa::kPieceFrames >= ffa::kPieceFrames / 2) ++C;
+  return std::max<int64_t>(C, 1);
+}
+
+Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
-  g.K = choose_k(S, latency_bound);
+  g.chunked = chunked_record(r, optimized);
+  g.K = g.chunked ? 8 : choose_k(S, latency_bound);
   g.nw = static_cast<int>((S + 32 * g.K - 1) / (32 * g.K));
-  g.slot_log2 = ceil_log2(g.nw);
-  // Segment length ~2*sqrt(T) balances the serial map walk (T/H steps) against
-  // the per-segment backpointer walk (H steps).
-  const double ideal = 2.0 * std::sqrt(static_cast<double>(r.frames));
-  g.seg_log2 = std::clamp(static_cast<int>(std::lround(std::log2(std::max(ideal, 1.0)))),
-                          ffa::kMinSegLog2, ffa::kMaxSegLog2);
+  if (g.chunked) {
+    g.seg_log2 = ffa::kPieceSegLog2;
+  } else {
+    // Segment length ~2*sqrt(T) balances the serial map walk (T/H steps)
+    // against the per-segment backpointer walk (H steps): the power of two
+    // nearest 2*sqrt(T) is 2^k for 2^(2k-3) <= T < 2^(2k-1).
+    g.seg_log2 = ffa::kMinSegLog2;
+    while (g.seg_log2 < ffa::kMaxSegLog2 && r.frames >= (int64_t{1} << (2 * (g.seg_log2 + 1) - 3)))
+      ++g.seg_log2;
+  }
   const int64_t H = int64_t{1} << g.seg_log2;
   g.segments = (r.frames + H - 1) / H;
   const int64_t nt = 32 * static_cast<int64_t>(g.nw);
   const int fpw = ffa::frames_per_word_host(g.K);
   g.bp_words = (r.frames + fpw - 1) / fpw * nt;
-  g.map_elems = (g.segments - 1) * nt * g.K;
+  g.map_elems = g.segments * nt * g.K;
+  g.pieces = g.chunked ? piece_count(r.frames) : 1;
+  g.frontier_elems = g.chunked ? g.pieces * nt * g.K : 0;
   return g;
 }
 
@@ -117,47 +141,126 @@ int device_sms() {
 // Byte layout of the staging buffer / the copy of it at the workspace start,
 // followed by the device-only arenas.
 struct AlignLayout {
-  size_t recs, bundles, order, fill, staging_bytes;
-  size_t bp, maps, anchors, workspace_bytes;
-  int64_t total_frames, bp_words, map_elems, segments, fill_items;
+  size_t recs, pieces, bundles, order, chunked, fill, copy_bytes, keys, staging_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, workspace_bytes;
+  int64_t total_frames, num_pieces, num_chunked, fill_items;
 };
 
-// One record per SM or fewer: every record's DP is latency-bound.
-bool latency_bound(int64_t count) { return count <= device_sms(); }
+bool latency_bound(int64_t slots) { return slots <= device_sms(); }
 
-int plan_align(const ffa_record* records, int64_t count, AlignLayout* L) {
+int64_t total_pieces(const ffa_record* records, int64_t count, bool optimized) {
+  int64_t n = 0;
+  for (int64_t i = 0; i < count; ++i)
+    n += chunked_record(records[i], optimized) ? piece_count(records[i].frames) : 1;
+  return n;
+}
+
+int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLayout* L) {
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
-  int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0;
-  const bool lat = latency_bound(count);
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
-    const Geometry g = geometry(records[i], lat);
+  }
+  const int64_t pieces = total_pieces(records, count, optimized);
+  const bool lat = latency_bound(pieces);
+  int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    const Geometry g = geometry(records[i], optimized, lat);
     frames += records[i].frames;
     bp_words += g.bp_words;
     map_elems += align_up(static_cast<size_t>(g.map_elems), 8);
     segments += g.segments;
     fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
+    frontier += g.frontier_elems;
+    chunked += g.chunked ? 1 : 0;
   }
-  if (segments > INT32_MAX || fill > INT32_MAX)
+  if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
   L->total_frames = frames;
-  L->bp_words = bp_words;
-  L->map_elems = map_elems;
-  L->segments = segments;
+  L->num_pieces = pieces;
+  L->num_chunked = chunked;
   L->fill_items = fill;
   size_t off = 0;
   L->recs = off; off = align_up(off + sizeof(ffa::RecordDev) * count, 16);
-  L->bundles = off; off = align_up(off + sizeof(ffa::Bundle) * count, 16);
-  L->order = off; off = align_up(off + sizeof(int32_t) * count, 16);
+  L->pieces = off; off = align_up(off + sizeof(ffa::PieceDev) * pieces, 16);
+  // First-pass bundles and slots: at most one slot per piece.
+  L->bundles = off; off = align_up(off + sizeof(ffa::Bundle) * pieces, 16);
+  L->order = off; off = align_up(off + sizeof(int32_t) * pieces, 16);
+  L->chunked = off; off = align_up(off + sizeof(int32_t) * chunked, 16);
   L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 256);
+  L->copy_bytes = off;  // uploaded; the rest of the staging buffer is host scratch
+  L->keys = off; off = align_up(off + 2 * sizeof(uint64_t) * count, 256);
   L->staging_bytes = off;
+  off = L->copy_bytes;  // the workspace holds the uploaded part only
   L->bp = off; off = align_up(off + sizeof(uint32_t) * bp_words, 256);
   L->maps = off; off = align_up(off + sizeof(uint16_t) * map_elems, 256);
   L->anchors = off; off = align_up(off + sizeof(int32_t) * segments, 256);
+  L->frontiers = off; off = align_up(off + sizeof(float) * frontier, 256);
+  L->pstates = off; off = align_up(off + sizeof(ffa::PieceState) * pieces, 256);
+  L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->workspace_bytes = off;
   return FFA_OK;
+}
+
+// Slot class of a record: row staging, route, states per thread and warps,
+// packed so that ascending order puts row-staged before gathered, pieces of
+// the optimized route before whole records, K = 4 before K = 8 and wider
+// slots (longer transcripts, usually longer records) first.
+uint32_t slot_class(const ffa::RecordDev& d) {
+  return (d.row_mode ? 0u : 1u) << 7 | (d.num_pieces > 1 ? 0u : 1u) << 6 | (d.kst == 4 ? 0u : 1u) << 5 |
+         static_cast<uint32_t>(ffa::kMaxWarps - d.nw);
+}
+int slot_group(uint32_t cls) { return static_cast<int>(cls >> 6); }  // 2 * !row + !chunked
+
+// Record order for packing: by slot class, then longest first.  Keys pack
+// (class, ~frames, index) in 64 bits and are sorted by an LSD radix sort over
+// bytes 2..7 (the index rides along); a byte every key shares is skipped, so
+// typical batches take two or three passes.  `tmp` has room for `count` keys.
+void sort_records(const ffa::RecordDev* recs, int64_t count, uint64_t* keys, uint64_t* tmp) {
+  for (int64_t i = 0; i < count; ++i)
+    keys[i] = static_cast<uint64_t>(slot_class(recs[i])) << 56 |
+              static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(recs[i].T)) << 16 |
+              static_cast<uint64_t>(i);
+  for (int shift = 16; shift < 64; shift += 8) {
+    int64_t hist[256] = {};
+    for (int64_t i = 0; i < count; ++i) ++hist[(keys[i] >> shift) & 0xff];
+    if (hist[(keys[0] >> shift) & 0xff] == count) continue;
+    int64_t sum = 0;
+    for (int b = 0; b < 256; ++b) { const int64_t h = hist[b]; hist[b] = sum; sum += h; }
+    for (int64_t i = 0; i < count; ++i) tmp[hist[(keys[i] >> shift) & 0xff]++] = keys[i];
+    std::memcpy(keys, tmp, sizeof(uint64_t) * count);
+  }
+}
+
+// Packs the slots listed in `order` (piece ids, already in packing order)
+// into bundles: runs of one slot class, at most `per_cta` slots and
+// kMaxWarps warps per CTA, a row-staged bundle also at most `row_slots`
+// rings.  Returns the bundle count; ranges[g] is the first bundle of slot
+// group g (ranges[4] = the count).
+template <typename ClassOf>
+int64_t make_bundles(const int32_t* order, int64_t n, ClassOf class_of, const ffa::RecordDev* recs,
+                     const ffa::PieceDev* pieces, int64_t per_cta, int64_t row_slots,
+                     ffa::Bundle* bundles, int64_t ranges[5], int64_t* max_row_slots) {
+  int64_t nb = 0;
+  int group = 0;
+  for (int g = 0; g < 5; ++g) ranges[g] = 0;
+  for (int64_t k = 0; k < n;) {
+    const uint32_t cls = class_of(order[k]);
+    const ffa::RecordDev& head = recs[pieces[order[k]].record];
+    const int g = slot_group(cls);
+    while (group < g) ranges[++group] = nb;
+    int64_t capacity = std::min<int64_t>(ffa::kMaxWarps / head.nw, per_cta);
+    if (head.row_mode) capacity = std::min(capacity, row_slots);
+    int64_t m = 1;
+    while (k + m < n && m < capacity && class_of(order[k + m]) == cls) ++m;
+    bundles[nb++] = ffa::Bundle{static_cast<int32_t>(k), head.nw, static_cast<uint8_t>(m), head.kst, 0};
+    if (head.row_mode) *max_row_slots = std::max(*max_row_slots, m);
+    k += m;
+  }
+  while (group < 4) ranges[++group] = nb;
+  return nb;
 }
 
 struct ScanLayout {
@@ -215,6 +318,23 @@ int ffa_profile_forward_events(void* before, void* after) {
   return FFA_OK;
 }
 
+int64_t ffa_launch_count(void) { return ffa::launches_so_far(); }
+
+int ffa_profile_phase_events(void* const* events, int count) {
+  if (events == nullptr && count == 0) {
+    g_phase_profiling = false;
+    return FFA_OK;
+  }
+  if (events == nullptr || count != FFA_PROFILE_POINTS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "pass FFA_PROFILE_POINTS events, or NULL and 0");
+  for (int k = 0; k < count; ++k) {
+    if (events[k] == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "profile events must not be NULL");
+    g_phase_events[k] = static_cast<cudaEvent_t>(events[k]);
+  }
+  g_phase_profiling = true;
+  return FFA_OK;
+}
+
 int ffa_align_query(const ffa_record* records, int64_t count, int mode, int flags,
                     ffa_sizes* sizes) {
   if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be NULL");
@@ -222,7 +342,7 @@ int ffa_align_query(const ffa_record* records, int64_t count, int mode, int flag
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
   if (flags & ~FFA_FLAG_CHECK_INPUTS) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
   AlignLayout L{};
-  const int rc = plan_align(records, count, &L);
+  const int rc = plan_align(records, count, mode == FFA_MODE_OPTIMIZED, &L);
   if (rc) return rc;
   sizes->staging_bytes = L.staging_bytes;
   sizes->workspace_bytes = L.workspace_bytes;
@@ -242,8 +362,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   if (mode != FFA_MODE_CONVENTIONAL && mode != FFA_MODE_OPTIMIZED)
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
   if (flags & ~FFA_FLAG_CHECK_INPUTS) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  const bool optimized = mode == FFA_MODE_OPTIMIZED;
   AlignLayout L{};
-  int rc = plan_align(records, count, &L);
+  int rc = plan_align(records, count, optimized, &L);
   if (rc) return rc;
   if (staging == nullptr || staging_bytes < L.staging_bytes)
     return fail(FFA_ERR_BUFFER_TOO_SMALL, "staging buffer smaller than ffa_align_query reports");
@@ -253,16 +374,22 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
 
   auto* host = static_cast<unsigned char*>(staging);
   auto* recs = reinterpret_cast<ffa::RecordDev*>(host + L.recs);
+  auto* pieces = reinterpret_cast<ffa::PieceDev*>(host + L.pieces);
   auto* bundles = reinterpret_cast<ffa::Bundle*>(host + L.bundles);
   auto* order = reinterpret_cast<int32_t*>(host + L.order);
+  auto* chunked = reinterpret_cast<int32_t*>(host + L.chunked);
   auto* fill = reinterpret_cast<ffa::FillItem*>(host + L.fill);
+  const int64_t P = L.num_pieces;
 
-  // Per-record descriptors and arena offsets.
-  int64_t out_off = 0, bp_off = 0, map_off = 0, seg_off = 0, nfill = 0;
-  const bool lat = latency_bound(count);
+  // Per-record descriptors, pieces and arena offsets.
+  int64_t out_off = 0, bp_off = 0, map_off = 0, seg_off = 0, nfill = 0, frontier_off = 0;
+  int64_t np = 0, nchunked = 0;
+  const bool lat = latency_bound(P);
+  unsigned max_row_vocab = 0;
+  int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
-    const Geometry g = geometry(r, lat);
+    const Geometry g = geometry(r, optimized, lat);
     ffa::RecordDev d{};
     d.emissions = r.emissions;
     d.targets = r.targets;
@@ -282,66 +409,89 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                   (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0)
                      ? 1
                      : 0;
+    d.frontier_off = frontier_off;
+    d.first_piece = static_cast<int32_t>(np);
+    d.num_pieces = static_cast<int32_t>(g.pieces);
     recs[i] = d;
+    if (d.row_mode) {
+      max_row_vocab = std::max<unsigned>(max_row_vocab, r.vocab);
+      row_vocab = (row_vocab < 0 || row_vocab == r.vocab) ? r.vocab : 0;
+    }
+    for (int64_t j = 0; j < g.pieces; ++j) {
+      const int64_t first = j * ffa::kPieceFrames;
+      const int64_t end = (j == g.pieces - 1) ? r.frames : first + ffa::kPieceFrames;
+      pieces[np + j] = ffa::PieceDev{static_cast<int32_t>(i), static_cast<int32_t>(g.chunked ? first : 0),
+                                     static_cast<int32_t>(g.chunked ? end : r.frames),
+                                     static_cast<int32_t>(j)};
+    }
+    if (g.chunked) ++nchunked;
+    np += g.pieces;
     for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
       fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
     out_off += r.frames;
     bp_off += g.bp_words;
     map_off += static_cast<int64_t>(align_up(static_cast<size_t>(g.map_elems), 8));
     seg_off += g.segments;
-    order[i] = static_cast<int32_t>(i);
+    frontier_off += g.frontier_elems;
   }
 
-  // Records are grouped by emission staging (TMA row rings vs per-thread
-  // column gather: one launch each), then by slot size, longest first.
-  unsigned max_row_vocab = 0;
-  int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
-  for (int64_t i = 0; i < count; ++i)
-    if (recs[i].row_mode) {
-      max_row_vocab = std::max<unsigned>(max_row_vocab, records[i].vocab);
-      row_vocab = (row_vocab < 0 || row_vocab == records[i].vocab) ? records[i].vocab : 0;
-    }
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
       align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4, 128));
   const int64_t row_slots =
       row_slot_bytes ? std::max<int64_t>(1, static_cast<int64_t>((ffa::kSmemBudget - header) / row_slot_bytes))
                      : ffa::kMaxWarps;
-
-  auto slot_of = [&](int32_t i) { return ceil_log2(recs[i].nw); };
-  std::sort(order, order + count, [&](int32_t a, int32_t b) {
-    if (recs[a].row_mode != recs[b].row_mode) return recs[a].row_mode > recs[b].row_mode;
-    if (recs[a].kst != recs[b].kst) return recs[a].kst < recs[b].kst;
-    const int sa = slot_of(a), sb = slot_of(b);
-    if (sa != sb) return sa < sb;
-    if (records[a].frames != records[b].frames) return records[a].frames > records[b].frames;
-    return a < b;
-  });
-  // Records per CTA grow only when the batch would otherwise need more than
-  // one wave; a row-staged slot also needs its ring to fit in shared memory.
+  // Pieces per first-pass slot: the fewest that let the pass fit the GPU in
+  // one wave of CTAs (each slot still restarts a relaxed DP every piece).
+  // A CTA holds slots of one width only, up to kMaxWarps warps (and, when
+  // row-staged, up to row_slots rings); one CTA runs per SM.
   const int64_t sms = device_sms();
-  const int64_t per_cta_target = std::max<int64_t>(1, (count + sms - 1) / sms);
-  int64_t nb = 0, n_row_bundles = 0, max_row_slots = 1;
-  for (int64_t k = 0; k < count;) {
-    const int cls = slot_of(order[k]);
-    const bool row = recs[order[k]].row_mode != 0;
-    const int kst = recs[order[k]].kst;
-    int64_t capacity = std::min(static_cast<int64_t>(ffa::kMaxWarps >> cls), per_cta_target);
-    if (row) capacity = std::min(capacity, row_slots);
-    int64_t n = 0;
-    while (k + n < count && n < capacity && slot_of(order[k + n]) == cls &&
-           (recs[order[k + n]].row_mode != 0) == row && recs[order[k + n]].kst == kst)
-      ++n;
-    bundles[nb++] = ffa::Bundle{static_cast<int32_t>(k), static_cast<uint8_t>(cls),
-                                static_cast<uint8_t>(n), static_cast<uint8_t>(kst), 0};
-    if (row) { ++n_row_bundles; max_row_slots = std::max(max_row_slots, n); }
-    k += n;
-  }
-  auto longest_first = [&](const ffa::Bundle& a, const ffa::Bundle& b) {
-    return records[order[a.first]].frames > records[order[b.first]].frames;
+  auto slots_per_cta = [&](const ffa::RecordDev& d) {
+    int64_t c = ffa::kMaxWarps / d.nw;
+    if (d.row_mode) c = std::min(c, row_slots);
+    return c;
   };
-  std::stable_sort(bundles, bundles + n_row_bundles, longest_first);
-  std::stable_sort(bundles + n_row_bundles, bundles + nb, longest_first);
+  int run_pieces = 1;
+  for (;; ++run_pieces) {
+    int64_t class_slots[256] = {};
+    for (int64_t i = 0; i < count; ++i)
+      class_slots[slot_class(recs[i])] += (recs[i].num_pieces + run_pieces - 1) / run_pieces;
+    int64_t ctas = 0;
+    for (int64_t i = 0; i < count; ++i) {
+      const uint32_t c = slot_class(recs[i]);
+      if (class_slots[c] == 0) continue;  // counted already
+      ctas += (class_slots[c] + slots_per_cta(recs[i]) - 1) / slots_per_cta(recs[i]);
+      class_slots[c] = 0;
+    }
+    if (ctas <= sms || run_pieces == ffa::kMaxRunPieces) break;
+  }
+  // Packing order: records by slot class, longest first; a record's pieces
+  // stay together.
+  auto* keys = reinterpret_cast<uint64_t*>(host + L.keys);
+  sort_records(recs, count, keys, keys + count);
+  int64_t n_first = 0;
+  for (int64_t k = 0; k < count; ++k) {
+    const ffa::RecordDev& d = recs[keys[k] & 0xffff];
+    for (int32_t j = 0; j < d.num_pieces; j += (d.num_pieces > 1 ? run_pieces : 1))
+      order[n_first++] = d.first_piece + j;
+  }
+  // Records of the optimized route, row-staged ones first (one finisher
+  // launch each kind).
+  int64_t n_chunked_row = 0, nc = 0;
+  for (int pass = 0; pass < 2; ++pass)
+    for (int64_t i = 0; i < count; ++i)
+      if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == (pass == 0)) {
+        chunked[nc++] = static_cast<int32_t>(i);
+        if (pass == 0) ++n_chunked_row;
+      }
+  auto class_of = [&](int32_t p) { return slot_class(recs[pieces[p].record]); };
+  // Slots per CTA grow only when the launch would otherwise need more than
+  // one wave (up to the full width once runs of pieces are in use).
+  int64_t ranges[5], max_row_slots = 1;
+  const int64_t nb = make_bundles(order, n_first, class_of, recs, pieces,
+                                  run_pieces > 1 ? ffa::kMaxWarps
+                                                 : std::max<int64_t>(1, (n_first + sms - 1) / sms),
+                                  row_slots, bundles, ranges, &max_row_slots);
   const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
   int max_gather_k = 8;
   for (int64_t i = 0; i < count; ++i)
@@ -350,41 +500,68 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
 
   auto* dev = static_cast<unsigned char*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(dev, host, L.staging_bytes, cudaMemcpyHostToDevice, s);
+  cudaError_t err = cudaMemcpyAsync(dev, host, L.copy_bytes, cudaMemcpyHostToDevice, s);
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
 
-  ffa::OutputsDev out{outputs->labels, outputs->scores, outputs->status, outputs->objective,
-                      outputs->stitched, outputs->repair_passes, outputs->repaired_frames,
-                      outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
-  const auto* drecs = reinterpret_cast<const ffa::RecordDev*>(dev + L.recs);
-  auto* bp = reinterpret_cast<uint32_t*>(dev + L.bp);
-  auto* anchors = reinterpret_cast<int32_t*>(dev + L.anchors);
-  // The optimized route currently resolves every record with the exact
-  // conventional DP, which satisfies its contract (stitched = 0 denotes the
-  // conventional route, alignment.py:101-104).
+  ffa::ForwardParams fp{};
+  fp.recs = reinterpret_cast<const ffa::RecordDev*>(dev + L.recs);
+  fp.pieces = reinterpret_cast<const ffa::PieceDev*>(dev + L.pieces);
+  fp.order = reinterpret_cast<const int32_t*>(dev + L.order);
+  fp.mask = emission_validity;
+  fp.check_inputs = (flags & FFA_FLAG_CHECK_INPUTS) ? 1 : 0;
+  fp.bp = reinterpret_cast<uint32_t*>(dev + L.bp);
+  fp.maps = reinterpret_cast<uint16_t*>(dev + L.maps);
+  fp.anchors = reinterpret_cast<int32_t*>(dev + L.anchors);
+  fp.frontiers = reinterpret_cast<float*>(dev + L.frontiers);
+  fp.pstates = reinterpret_cast<ffa::PieceState*>(dev + L.pstates);
+  fp.route = reinterpret_cast<int32_t*>(dev + L.route);
+  fp.fill_done = reinterpret_cast<int32_t*>(dev + L.fill_done);
+  fp.out = ffa::OutputsDev{outputs->labels, outputs->scores, outputs->status, outputs->objective,
+                           outputs->stitched, outputs->repair_passes, outputs->repaired_frames,
+                           outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
+  fp.row_slot_bytes = row_slot_bytes;
+  fp.run_pieces = run_pieces;
+  const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + L.bundles);
+  const int rv = row_vocab > 0 ? row_vocab : 0;
+
   if (g_profile_before != nullptr) {
     err = cudaEventRecord(g_profile_before, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
-  const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + L.bundles);
-  const auto* dorder = reinterpret_cast<const int32_t*>(dev + L.order);
-  auto* maps = reinterpret_cast<uint16_t*>(dev + L.maps);
-  const int check = (flags & FFA_FLAG_CHECK_INPUTS) ? 1 : 0;
-  err = ffa::launch_forward(drecs, dbundles, dorder, static_cast<int>(n_row_bundles), true,
-                            row_vocab > 0 ? row_vocab : 0, emission_validity, check, bp, maps,
-                            anchors, out, row_smem, row_slot_bytes, s);
+  auto mark = [&](int point) {
+    const cudaError_t e = mark_phase(point, s);
+    return e == cudaSuccess ? FFA_OK : cuda_fail(e, "profiling event");
+  };
+  if ((rc = mark(FFA_PROFILE_START))) return rc;
+  // First pass: every piece of every record (a one-piece record is the
+  // conventional DP).
+  fp.bundles = dbundles + ranges[0];
+  err = ffa::launch_forward(fp, static_cast<int>(ranges[2] - ranges[0]), true, rv, row_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
-  err = ffa::launch_forward(drecs, dbundles + n_row_bundles, dorder,
-                            static_cast<int>(nb - n_row_bundles), false, 0, emission_validity,
-                            check, bp, maps, anchors, out, gather_smem, 0, s);
+  fp.bundles = dbundles + ranges[2];
+  err = ffa::launch_forward(fp, static_cast<int>(ranges[4] - ranges[2]), false, 0, gather_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   if (g_profile_after != nullptr) {
     err = cudaEventRecord(g_profile_after, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
-  err = ffa::launch_fill(drecs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
-                         static_cast<int>(nfill), bp, anchors, out, s);
+  if ((rc = mark(FFA_PROFILE_FIRST))) return rc;
+  // The optimized route's seam plans, repairs and fallback: one CTA per record.
+  const auto* dchunked = reinterpret_cast<const int32_t*>(dev + L.chunked);
+  const int64_t finish_slots = std::min<int64_t>(
+      ffa::kMaxWarps - 1,
+      row_slot_bytes ? static_cast<int64_t>((ffa::kSmemBudget - 2048 - header) / row_slot_bytes) : 1);
+  const unsigned finish_row_smem = static_cast<unsigned>(header + finish_slots * row_slot_bytes);
+  err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), true, rv, finish_row_smem, s);
+  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), false, 0,
+                           gather_smem, s);
+  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
+  err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
+                         static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, s);
   if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
+  if ((rc = mark(FFA_PROFILE_FILL))) return rc;
   return FFA_OK;
 }
 

@@ -41,28 +41,72 @@ constexpr int kMinSegLog2 = 5;
 constexpr int kMaxSegLog2 = 10;
 constexpr int kFillWarps = 8;
 
-// Device-side descriptor of one record (64 bytes).
+// Device-side descriptor of one record (80 bytes).
 struct RecordDev {
   const float* emissions;   // [T, V] fp32, caller memory
   const int64_t* targets;   // [U] int64, caller memory (may be null if U == 0)
   int64_t out_off;          // first frame of this record in labels/scores
   int64_t bp_off;           // first uint32 word in the backpointer arena
-  int64_t map_off;          // first uint16 entry in the checkpoint-map arena
+  int64_t map_off;          // first uint16 entry in the segment-map arena
   int32_t T, V, U, blank;
   int32_t seg_off;          // first anchor (one per traceback segment)
   uint8_t nw;               // warps running this record's DP
   uint8_t kst;              // states per thread K
   uint8_t seg_log2;         // traceback segment length H = 1 << seg_log2
   uint8_t row_mode;         // 1: TMA row staging, 0: per-thread column gather
+  int64_t frontier_off;     // first float of the per-piece frontier arena
+  int32_t first_piece;      // this record's pieces are first_piece ..
+  int32_t num_pieces;       //   first_piece + num_pieces - 1
 };
-static_assert(sizeof(RecordDev) == 64, "RecordDev layout");
+static_assert(sizeof(RecordDev) == 80, "RecordDev layout");
 
-// One forward CTA ("bundle"): `count` records of the same slot size
-// (1 << slot_log2 warps each) and states per thread, listed at
+// Optimized route.  A record of at least kPieceMinFrames frames is cut into
+// pieces of kPieceFrames frames (the last one also takes a remainder shorter
+// than half a piece).  Each piece runs a relaxed DP -- free start state
+// (unless it is the record's first piece), best end state (unless it is the
+// last) -- and the pieces' paths are joined when every seam between them is a
+// legal CTC move.  A joined path then scores the sum of the per-piece maxima,
+// an upper bound on every legal path, so it is optimal.  Seams that fail
+// merge their two regions, and the merged region resumes from the left
+// region's end frontier (kRepairRounds rounds); records that still fail, or
+// whose pieces saw NaN, run the conventional DP.
+constexpr int kPieceFrames = 32;
+constexpr int kPieceMinFrames = 2 * kPieceFrames + 1;
+constexpr int kPieceSegLog2 = 5;
+constexpr int kRepairRounds = 2;
+// The first pass runs up to kMaxRunPieces consecutive pieces of a record in
+// one slot, back to back (each still a separate relaxed DP), so that its
+// set-up is paid once and the pass fits the GPU in about one wave.
+constexpr int kMaxRunPieces = 8;
+
+// One piece: frames [first, end) of a record; index is its rank in the record.
+struct PieceDev {
+  int32_t record;
+  int32_t first;
+  int32_t end;
+  int32_t index;
+};
+static_assert(sizeof(PieceDev) == 16, "PieceDev layout");
+
+// Device-written state of one piece.  `start` is valid on the first piece of
+// a region, `end` and `flags` on its last.
+struct PieceState {
+  int32_t start;
+  int32_t end;
+  int32_t flags;         // kPieceOk | kPieceFault
+  int32_t region_start;  // 1 if this piece begins a region
+};
+static_assert(sizeof(PieceState) == 16, "PieceState layout");
+enum : int32_t { kPieceOk = 1, kPieceFault = 2 };
+// Per-record route of the optimized mode (device-written).
+enum : int32_t { kRouteNone = 0, kRoutePending = 1, kRouteStitched = 2, kRouteFallback = 3 };
+
+// One forward CTA ("bundle"): `count` slots of `nw` warps, each running one
+// piece; all with the same states per thread, listed at
 // order[first .. first+count).
 struct Bundle {
   int32_t first;
-  uint8_t slot_log2;
+  uint8_t nw;
   uint8_t count;
   uint8_t kst;
   uint8_t reserved;
@@ -106,19 +150,44 @@ struct OutputsDev {
 constexpr unsigned gather_ring_bytes(int K) { return kGroup * (K / 2 + 1) * kCtaThreads * 4; }
 size_t forward_header_bytes();
 
+// Arguments of one forward launch.
+struct ForwardParams {
+  const RecordDev* recs;
+  const PieceDev* pieces;
+  const Bundle* bundles;
+  const int32_t* order;      // piece ids, grouped by bundle
+  const uint8_t* mask;       // emission-validity mask or null
+  int32_t check_inputs;
+  uint32_t* bp;
+  uint16_t* maps;
+  int32_t* anchors;
+  float* frontiers;
+  PieceState* pstates;
+  int32_t* route;            // per record: kRoute* (the finisher writes it)
+  OutputsDev out;
+  uint32_t row_slot_bytes;
+  int32_t run_pieces;        // kPhaseFirst: pieces per slot of the optimized route
+  int32_t* fill_done;        // per record: fill CTAs finished (zeroed by the first pass)
+};
+
 // row_vocab: the vocabulary shared by every row-staged record of the
 // launch, or 0 when they differ.
-cudaError_t launch_forward(const RecordDev* recs, const Bundle* bundles, const int32_t* order,
-                           int num_bundles, bool row_mode, int row_vocab, const uint8_t* mask,
-                           int check_inputs,
-                           uint32_t* bp, uint16_t* maps, int32_t* anchors,
-                           const OutputsDev& out, unsigned smem_bytes, unsigned row_slot_bytes,
-                           cudaStream_t stream);
+cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
+                           int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+// Everything after the first pass of the optimized route -- seam plans,
+// repair rounds, conventional fallback -- one CTA per listed record.
+cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
+                          bool row_mode, int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+// Traceback fill of every segment; for records of the optimized route the
+// last fill CTA of the record also folds the objective of a joined path.
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        cudaStream_t stream);
+                        const int32_t* route, int32_t* fill_done, cudaStream_t stream);
 cudaError_t launch_validity(const ScanRecord* recs, int64_t count, const ScanItem* items,
                             int64_t num_items, uint8_t* valid, cudaStream_t stream);
+
+// Kernels launched so far by the calling thread (ffa_kernels.cu).
+int64_t launches_so_far();
 
 // Sets the message ffa_last_error() returns on this thread (ffa_host.cpp).
 void set_last_error(const char* message);

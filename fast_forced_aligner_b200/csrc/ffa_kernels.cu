@@ -18,186 +18,76 @@
 // reproduces the reference bit for bit.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 
+#include "ffa_device.cuh"
 #include "ffa_internal.h"
 
 namespace ffa {
+using namespace dev;
 namespace {
 
-__device__ __forceinline__ void named_barrier(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ unsigned smem_u32(const void* p) {
-  return static_cast<unsigned>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait: gives up after kWaitNs nanoseconds and reports the failure
-// instead of hanging.  A caller that saw one failure makes no further waits.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity,
-                                          unsigned long long limit_ns = kWaitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long start = global_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (global_ns() - start > limit_ns) return false;
-  return true;
-}
-// One TMA bulk copy global -> shared (no tensor map, no multicast), completed
-// on `bar` with a transaction-byte count.
-__device__ __forceinline__ void tma_bulk_load(void* smem_dst, const void* gmem_src, unsigned bytes,
-                                              unsigned long long* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ int clamp_label(int64_t token, int V) {
-  // Only out-of-range IDs (rejected with status 3 when checks are on) are
-  // changed; clamping keeps unchecked calls from reading outside the row.
-  return token < 0 ? 0 : (token >= V ? V - 1 : static_cast<int>(token));
-}
-
-struct Boundary {
-  float alpha;  // score of a warp's last state
-  int delta;    // its ancestor delta
-};
-
-// Shared-memory header of one forward CTA; emission rings follow it.
-struct ForwardShared {
-  Boundary bnd[2][kMaxWarps];  // last-state hand-off between warps of a slot
-  Boundary edge;               // {-inf, 0}: the "left neighbour" of a record's first warp
-  int red_bad[kMaxWarps];
-  int red_rep[kMaxWarps];
-  float term_last[kMaxWarps];  // per slot: alpha[S-1], alpha[S-2]
-  float term_prev[kMaxWarps];
-  int slot_status[kMaxWarps];
-  int slot_fault[kMaxWarps];   // a bounded wait ran out (reported as status 5)
-  unsigned long long full[kMaxWarps][kRowRing];  // per slot: row group landed
-};
-
-// Emission rings start at this 128-byte aligned offset (TMA destinations
-// must be 16-byte aligned); the host planner uses the same value.
-constexpr size_t kForwardHeader = (sizeof(ForwardShared) + 127) / 128 * 128;
-static_assert(kForwardHeader % 128 == 0, "ring offset alignment");
-
-// One DP frame for this thread's K states (s = K*tl + k; odd k are tokens).
-// Selection: stay, then step if strictly greater, then skip if strictly
-// greater and legal (alignment.cu:418-424); one fp32 add per cell.  Also
-// advances the ancestor deltas d (distance back to the state at the end of the
-// previous traceback segment).  Returns the frame's backpointers as two bit
-// planes: bit k = "moved" (jump >= 1) of state k, bit K+q = "skipped"
-// (jump == 2) of token q = k/2, so jump = moved + skipped.
-template <int K>
-__device__ __forceinline__ unsigned dp_frame(float (&a)[K], int (&d)[K], float p1, int pd, float eb,
-                                             const float (&et)[K / 2], unsigned skip) {
-  float na[K];
-  int nd[K];
-  unsigned bits = 0;
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const float x1 = k >= 1 ? a[k - 1] : p1;
-    const int d1 = k >= 1 ? d[k - 1] : pd;
-    const bool c = x1 > a[k];
-    float b = c ? x1 : a[k];
-    int n = c ? d1 + 1 : d[k];
-    if (k & 1) {
-      const float x2 = k >= 2 ? a[k - 2] : p1;
-      const int d2 = k >= 2 ? d[k - 2] : pd;
-      const bool j2 = ((skip >> (k >> 1)) & 1u) && x2 > b;
-      b = j2 ? x2 : b;
-      n = j2 ? d2 + 2 : n;
-      bits |= (static_cast<unsigned>(c || j2) << k) | (static_cast<unsigned>(j2) << (K + (k >> 1)));
-      na[k] = __fadd_rn(b, et[k >> 1]);
-    } else {
-      bits |= static_cast<unsigned>(c) << k;
-      na[k] = __fadd_rn(b, eb);
-    }
-    nd[k] = n;
-  }
-#pragma unroll
-  for (int k = 0; k < K; ++k) { a[k] = na[k]; d[k] = nd[k]; }
-  return bits;
-}
-
-// Backpointer word geometry: 1.5*K bits per frame and thread, packed in
-// 16-bit lanes of 32-bit words when they fit (two frames per word).
-__host__ __device__ constexpr int frames_per_word(int K) { return 3 * K / 2 <= 16 ? 2 : 1; }
-
-// Jump of state s (owned by a thread with K states) from one frame's bits.
-__device__ __forceinline__ int jump_of(unsigned bits, int s, int K) {
-  const int k = s % K;
-  const unsigned moved = (bits >> k) & 1u;
-  const unsigned skipped = (k & 1) ? (bits >> (K + (k >> 1))) & 1u : 0u;
-  return static_cast<int>(moved + skipped);
-}
-
-// Per-record geometry shared by the DP body.
+// Per-slot geometry shared by the DP body.
 struct SlotCtx {
-  int tid, warp, lane, slot, lw, NT, tl, r;
-  bool single;
+  int tid, warp, lane, slot, lw, NT, tl, r, first_warp, bar;
   __device__ __forceinline__ void sync() const {
-    // Unconditional (a one-warp record uses a 32-thread barrier): a branch
+    // Unconditional (a one-warp slot uses a 32-thread barrier): a branch
     // here costs more than the barrier.
-    named_barrier(slot, NT);
+    named_barrier(bar, NT);
   }
 };
 
-// The DP of one record after its status checks: frame loop unrolled by
-// kGroup, terminal state, segment-map walk.  Thread tl owns states
+// How a run's first frame is seeded.
+enum : int {
+  kInitRecord = 0,    // frame 0 of the record: alpha[s] = e[0, l[s]] for s < 2
+  kInitFree = 1,      // free start: alpha[s] = e[t0, l[s]] on the reachable band
+  kInitFrontier = 2,  // alpha at t0-1 from a saved frontier
+};
+
+// One DP run over frames [t0, t1) of a record, made of `pieces` consecutive
+// pieces: piece k starts at t0 + k * kPieceFrames (the last one runs to t1),
+// and every piece after the first restarts with a free start.  A piece ends
+// at its best reachable state, or by the terminal rule at the record's last
+// frame.  a0 is the first frame of the region whose segment chain the single
+// piece of a one-piece run walks (a0 < t0 when a repair resumes a region).
+//   end_piece < 0   the whole record, with the conventional outputs;
+//   otherwise       piece k writes PieceState end_piece + k (its end state
+//                   and flags) and start_piece + k (its region's start).
+struct PieceRun {
+  int a0, t0, t1, init, pieces;
+  const float* frontier_in;
+  float* frontier_out;  // piece k's end frontier at frontier_out + k * NT*K
+  int end_piece, start_piece;
+  bool new_region;
+  // Row staging: emission chunks the slot's ring has already carried in
+  // earlier runs of this launch.  The ring's mbarriers are initialised once,
+  // by a slot's first run (chunk_base 0); later runs continue their phases.
+  int chunk_base;
+};
+
+// The DP of one run: frame loop unrolled by kGroup, emission staging, end
+// states, and the path's state at every segment end (anchors) and at the
+// region's first frame.  kMaps: ancestor deltas ride along with the DP and
+// segment maps are stored, so the anchors come from a walk over the maps
+// (whole records, where the fill traces segments in parallel); otherwise the
+// anchors come from warp traces over the backpointers after the DP (pieces,
+// one or two segments each, and repaired regions).  Thread tl owns states
 // K*tl .. K*tl+K-1 (odd offsets are tokens K/2*tl + k/2).
-template <int K, bool kRow, int kV>
-__device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec,
-                                          ForwardShared& sh, unsigned char* smem_raw,
-                                          uint32_t* __restrict__ bp_arena,
-                                          uint16_t* __restrict__ map_arena,
-                                          int32_t* __restrict__ anchors, const OutputsDev& out,
-                                          unsigned row_slot_bytes) {
+// Returns the number of emission chunks the run staged (row staging).
+template <int K, bool kRow, int kV, bool kMaps>
+__device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, const PieceRun& run,
+                                        ForwardShared& sh, unsigned char* smem_raw,
+                                        const ForwardParams& P) {
   constexpr int KT = K / 2;
   constexpr int FPW = frames_per_word(K);
+  constexpr int kGroupsPerPiece = kPieceFrames / kGroup;
   const int tl = x.tl, lane = x.lane, warp = x.warp, NT = x.NT, slot = x.slot;
   const int T = rec.T, U = rec.U, blank = rec.blank;
   const int V = kV > 0 ? kV : rec.V;
   const int S = 2 * U + 1;
+  const int t0 = run.t0, t1 = run.t1, nfr = t1 - t0;
   const int64_t* tgt = rec.targets;
 
   int col[KT];
@@ -216,26 +106,31 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
     }
   }
 
-  const float* e = rec.emissions;
-  const int ngroups = (T + kGroup - 1) / kGroup;
+  // Emission rows of this run, frame t0 first.
+  const float* e = rec.emissions + static_cast<int64_t>(t0) * V;
+  const int ngroups = (nfr + kGroup - 1) / kGroup;
   float* ring = reinterpret_cast<float*>(smem_raw + kForwardHeader) +
-                static_cast<size_t>(slot) * (row_slot_bytes / 4);
+                static_cast<size_t>(slot) * (P.row_slot_bytes / 4);
   float* gring = reinterpret_cast<float*>(smem_raw + kForwardHeader) + x.tid;
   unsigned long long* full = sh.full[slot];
   bool fault = false;
 
-  const int nchunks = (T + kChunkFrames - 1) / kChunkFrames;
-  auto issue_chunk = [&](int c) {  // kRow: by the record's thread 0
+  const int nchunks = (nfr + kChunkFrames - 1) / kChunkFrames;
+  const int cb = run.chunk_base;
+  // Chunk c of this run is the slot's chunk cb + c: ring entry and mbarrier
+  // (cb + c) % kRowRing, phase parity ((cb + c) / kRowRing) & 1.
+  auto issue_chunk = [&](int c) {  // kRow: by the slot's thread 0
     const int first = c * kChunkFrames;
-    const int rows = min(kChunkFrames, T - first);
+    const int rows = min(kChunkFrames, nfr - first);
     const unsigned bytes = static_cast<unsigned>(rows) * V * 4u;
-    unsigned long long* bar = &full[c % kRowRing];
+    unsigned long long* bar = &full[(cb + c) % kRowRing];
     mbar_expect_tx(bar, bytes);
-    tma_bulk_load(ring + (c % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(first) * V, bytes, bar);
+    tma_bulk_load(ring + ((cb + c) % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(first) * V,
+                  bytes, bar);
   };
-  auto gather = [&](int64_t f) {  // !kRow: KT + 1 private 4-byte copies
-    if (f < T) {
-      const float* row = e + f * V;
+  auto gather = [&](int f) {  // !kRow: KT + 1 private 4-byte copies of run frame f
+    if (f < nfr) {
+      const float* row = e + static_cast<int64_t>(f) * V;
       float* dst = gring + (f % kGroup) * (KT + 1) * kCtaThreads;
       cp_async4(dst, row + blank);
 #pragma unroll
@@ -245,31 +140,50 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
   };
   if constexpr (kRow) {
     if (tl == 0) {
-      for (int k = 0; k < kRowRing; ++k) mbar_init(&full[k], 1);
-      fence_mbar_init();
+      if (cb == 0) {
+        for (int k = 0; k < kRowRing; ++k) mbar_init(&full[k], 1);
+        fence_mbar_init();
+      } else {
+        // The ring's entries were read by the previous run (generic proxy)
+        // before this run's copies (async proxy) overwrite them.
+        fence_proxy_async();
+      }
       for (int c = 0; c < kRowRing && c < nchunks; ++c) issue_chunk(c);
     }
   } else {
 #pragma unroll
     for (int f = 0; f < kGroup - 1; ++f) gather(f);
   }
-  x.sync();
 
   float a[K];
-  int d[K];
+  int d[K];  // ancestor deltas (kMaps only)
 #pragma unroll
   for (int k = 0; k < K; ++k) { a[k] = -INFINITY; d[k] = 0; }
+  if (run.init == kInitFrontier) {
+    // Resume: alpha at frame t0-1 as the previous run left it.
+    const float4* src = reinterpret_cast<const float4*>(run.frontier_in + K * tl);
+#pragma unroll
+    for (int k = 0; k < K; k += 4) {
+      const float4 v = src[k / 4];
+      a[k] = v.x; a[k + 1] = v.y; a[k + 2] = v.z; a[k + 3] = v.w;
+    }
+    if (lane == 31) sh.bnd[t0 & 1][warp] = Boundary{a[K - 1], 0};
+  }
+  x.sync();
+
   const int hmask = (1 << rec.seg_log2) - 1;
-  uint32_t* bp = bp_arena + rec.bp_off + tl;
-  uint16_t* maps = map_arena + rec.map_off + K * tl;
+  uint32_t* bp = P.bp + rec.bp_off + tl;
+  uint16_t* maps = P.maps + rec.map_off + K * tl;
   const int64_t map_stride = static_cast<int64_t>(NT) * K;
   const Boundary* left = x.lw > 0 ? &sh.bnd[0][warp - 1] : &sh.edge;
   const int left_stride = x.lw > 0 ? kMaxWarps : 0;
   // Skip frames in which none of this warp's states lies in the reachable
-  // band [S - 2(T - t), 2t + 1]: states above it are still unreachable (-inf)
-  // and states below it can no longer reach the end, and in-band states read
-  // only in-band states, so skipping is exact.  Active iff
-  // band_lo <= 2t <= band_hi.
+  // band [S - 2(T - t), 2t + 1]: states below it can no longer reach the end,
+  // and in-band states read only in-band states, so skipping is exact.  States
+  // above the band are still unreachable: the reference holds -inf there,
+  // or NaN once an emission of NaN or +inf has landed on them (NaN then stays:
+  // no predecessor compares greater).  A skipped frame above the band keeps
+  // exactly that.  Active iff band_lo <= 2t <= band_hi.
   const int w_lo = x.lw * 32 * K;
   const int w_hi = w_lo + 32 * K - 1;
   const unsigned band_lo = static_cast<unsigned>(max(w_lo - 1, 0));
@@ -278,25 +192,25 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
   const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
   uint32_t word = 0;
 
-  auto load = [&](int t, int j, const float* rows, float& eb, float (&et)[KT]) {
+  auto load = [&](int f, int j, const float* rows, float& eb, float (&et)[KT]) {
     if constexpr (kRow) {
       const float* row = rows + j * V;
       eb = row[blank];
 #pragma unroll
       for (int q = 0; q < KT; ++q) et[q] = row[col[q]];
     } else {
-      gather(static_cast<int64_t>(t) + kGroup - 1);
+      gather(f + kGroup - 1);
       cp_async_wait<kGroup - 1>();
-      const float* cur = gring + (t & (kGroup - 1)) * (KT + 1) * kCtaThreads;
+      const float* cur = gring + (f & (kGroup - 1)) * (KT + 1) * kCtaThreads;
       eb = cur[0];
 #pragma unroll
       for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
     }
   };
   auto store_map = [&](int t) {
-    // Ancestor map of segment t/H: state at its last frame -> state at the
-    // last frame of the previous segment, as a delta.
-    uint32_t* dst = reinterpret_cast<uint32_t*>(maps + ((t >> rec.seg_log2) - 1) * map_stride);
+    // Map of segment t/H: state at its last frame -> state at the last frame
+    // of the previous segment (or at the region's first frame), as a delta.
+    uint32_t* dst = reinterpret_cast<uint32_t*>(maps + (t >> rec.seg_log2) * map_stride);
 #pragma unroll
     for (int q = 0; q < KT; ++q)
       dst[q] = static_cast<uint32_t>(d[2 * q]) | (static_cast<uint32_t>(d[2 * q + 1]) << 16);
@@ -307,19 +221,25 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
   };
   auto frame = [&](int t, int j, const float* rows) {
     float eb, et[KT];
-    load(t, j, rows, eb, et);
+    load(t - t0, j, rows, eb, et);
     // Left neighbour's last state at t-1 (s-1 for k=0, s-2 for k=1): from
     // lane-1, or for lane 0 from the warp on the left (branch-free).
     float p1 = __shfl_up_sync(0xffffffffu, a[K - 1], 1);
-    int pd = __shfl_up_sync(0xffffffffu, d[K - 1], 1);
     const Boundary nb = left[(t & 1) * left_stride];
-    if (lane == 0) { p1 = nb.alpha; pd = nb.delta; }
-    if (j == 0 && (t & hmask) == 0) {  // a new traceback segment starts at t
+    unsigned bits;
+    if constexpr (kMaps) {
+      int pd = __shfl_up_sync(0xffffffffu, d[K - 1], 1);
+      if (lane == 0) { p1 = nb.alpha; pd = nb.delta; }
+      if (j == 0 && (t & hmask) == 0) {  // a new traceback segment starts at t
 #pragma unroll
-      for (int k = 0; k < K; ++k) d[k] = 0;
-      pd = 0;
+        for (int k = 0; k < K; ++k) d[k] = 0;
+        pd = 0;
+      }
+      bits = dp_frame<K>(a, d, p1, pd, eb, et, skip);
+    } else {
+      if (lane == 0) p1 = nb.alpha;
+      bits = dp_frame_plain<K>(a, p1, eb, et, skip);
     }
-    const unsigned bits = dp_frame<K>(a, d, p1, pd, eb, et, skip);
     if constexpr (FPW == 2) {
       word |= bits << (16 * (t & 1));
       if (t & 1) store_word(t);
@@ -327,54 +247,122 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
       word = bits;
       store_word(t);
     }
-    if (j == kGroup - 1 && (t & hmask) == hmask && t > hmask) store_map(t);
-    if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], d[K - 1]};
+    if (kMaps && j == kGroup - 1 && (t & hmask) == hmask) store_map(t);
+    if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], kMaps ? d[K - 1] : 0};
     x.sync();
   };
+  // End of piece k at frame te (all threads, after te's barrier): the
+  // terminal states at the record's last frame, else this warp's best state
+  // on the band (lowest index among equals) and whether it holds NaN at or
+  // above the band; plus the frontier a later repair may resume from.
+  const int last = S - 1;  // even
+  auto piece_end = [&](int k, int te) {
+    if (te == T - 1) {
+      // One predicated store per state keeps a[] in registers (a runtime
+      // index would move it to local memory).
+#pragma unroll
+      for (int q = 0; q < K; ++q) {
+        const int s = K * tl + q;
+        if (s == last) sh.term_last[slot] = a[q];
+        if (s == last - 1) sh.term_prev[slot] = a[q];
+      }
+      return;
+    }
+    const int lo = max(0, S - 2 * (T - te));
+    const int hi = min(S - 1, 2 * te + 1);
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    bool nan = false;
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+      const int s = K * tl + q;
+      if (s >= lo && s <= hi && a[q] > bv) { bv = a[q]; bi = s; }
+      nan |= s >= lo && s < S && a[q] != a[q];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    nan = __any_sync(0xffffffffu, nan);
+    if (lane == 0) { sh.red_val[k][warp] = bv; sh.red_idx[k][warp] = bi; sh.red_nan[k][warp] = nan; }
+    if (run.frontier_out != nullptr) {
+      float4* dst = reinterpret_cast<float4*>(run.frontier_out + static_cast<int64_t>(k) * map_stride + K * tl);
+#pragma unroll
+      for (int q = 0; q < K; q += 4) dst[q / 4] = make_float4(a[q], a[q + 1], a[q + 2], a[q + 3]);
+    }
+  };
 
+  int piece = 0;  // current piece of the run
   for (int g = 0; g < ngroups; ++g) {
     const float* rows = nullptr;
     if constexpr (kRow) {
-      const int c = g / kChunkGroups;
+      const int c = cb + g / kChunkGroups;
       if (g % kChunkGroups == 0 && !fault && !mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1))
         fault = true;
       rows = ring + ((c % kRowRing) * kChunkFrames + (g % kChunkGroups) * kGroup) * V;
     }
-    const int t0 = g * kGroup;
+    const int tg = t0 + g * kGroup;
+    // A new piece of the run starts here: close the previous one, then seed
+    // this one with a free start.
+    const bool boundary = g > 0 && g % kGroupsPerPiece == 0 && piece + 1 < run.pieces;
+    if (boundary) piece_end(piece++, tg - 1);
+    const int init = g == 0 ? run.init : kInitFree;
+    const bool seeded = (g == 0 && run.init != kInitFrontier) || boundary;
     // The band test is made once per group: a group with at least one frame
     // in which this warp has in-band states runs every frame (the plain DP is
-    // exact everywhere); a group with none only keeps the barriers (and the
-    // gather ring) in step.  Its backpointers and maps are never read.
-    const unsigned g2 = 2u * static_cast<unsigned>(t0);
-    const bool group_active = g == 0 || (!never && g2 + 2u * (kGroup - 1) >= band_lo && g2 <= band_hi);
+    // exact everywhere); a group with none keeps the barriers (and the gather
+    // ring) in step.  Its backpointers and maps are never read.
+    const unsigned g2 = 2u * static_cast<unsigned>(tg);
+    const bool group_active = seeded || (!never && g2 + 2u * (kGroup - 1) >= band_lo && g2 <= band_hi);
     if (!group_active) {
+      const bool above = g2 + 2u * (kGroup - 1) < band_lo;
 #pragma unroll 1
-      for (int j = 0; j < kGroup && t0 + j < T; ++j) {
-        if constexpr (!kRow) {
+      for (int j = 0; j < kGroup && tg + j < t1; ++j) {
+        if (above || !kRow) {
           float eb, et[KT];
-          load(t0 + j, j, rows, eb, et);
+          load(tg + j - t0, j, rows, eb, et);
+          if (above) {
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+              if (poisons((k & 1) ? et[k >> 1] : eb)) a[k] = NAN;
+          }
         }
         x.sync();
       }
       if constexpr (FPW == 2) word = 0;
-    } else if (g == 0) {
-      // Frame 0: alpha[s] = e[0, l[s]] for s < 2, else -inf (alignment.cu:409).
+    } else if (seeded) {
       float eb, et[KT];
-      load(0, 0, rows, eb, et);
+      load(tg - t0, 0, rows, eb, et);
 #pragma unroll
       for (int k = 0; k < K; ++k) { a[k] = -INFINITY; d[k] = 0; }
-      if (tl == 0) {
-        a[0] = eb;
-        if (S > 1) a[1] = et[0];
+      if (init == kInitRecord) {
+        // Frame 0: alpha[s] = e[0, l[s]] for s < 2, else -inf (alignment.cu:409).
+        if (tl == 0) {
+          a[0] = eb;
+          if (S > 1) a[1] = et[0];
+        }
+      } else {
+        // Free start on the band of frame tg; above it, -inf (or NaN from a
+        // poisoning emission) as the full DP holds there.
+        const int lo0 = max(0, S - 2 * (T - tg));
+        const int hi0 = min(S - 1, 2 * tg + 1);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int s = K * tl + k;
+          const float ek = (k & 1) ? et[k >> 1] : eb;
+          a[k] = s < lo0 ? -INFINITY : (s <= hi0 ? ek : (poisons(ek) ? NAN : -INFINITY));
+        }
       }
-      if (lane == 31) sh.bnd[1][warp] = Boundary{a[K - 1], 0};
+      if (lane == 31) sh.bnd[(tg + 1) & 1][warp] = Boundary{a[K - 1], 0};
       x.sync();
 #pragma unroll 1
-      for (int j = 1; j < kGroup && j < T; ++j) frame(j, j, rows);
+      for (int j = 1; j < kGroup && tg + j < t1; ++j) frame(tg + j, j, rows);
     } else {
 #pragma unroll
       for (int j = 0; j < kGroup; ++j)
-        if (t0 + j < T) frame(t0 + j, j, rows);
+        if (tg + j < t1) frame(tg + j, j, rows);
     }
     if constexpr (kRow) {
       // Every thread has read this chunk's rows (the last barrier above), so
@@ -392,68 +380,110 @@ __device__ __forceinline__ void record_dp(const SlotCtx& x, const RecordDev& rec
     // After a failed wait, give the issuing thread's copies still in flight a
     // short, bounded chance to land before the CTA's shared memory goes away.
     if (fault && tl == 0)
-      for (int c = max(0, nchunks - kRowRing); c < nchunks; ++c)
+      for (int c = cb + max(0, nchunks - kRowRing); c < cb + nchunks; ++c)
         mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1, kDrainNs);
   }
   {  // a word or a map the last frame left open
-    const int tl_ = T - 1;
-    if (FPW == 2 && tl_ > 0 && (tl_ & 1) == 0) store_word(tl_);
-    if (tl_ > hmask && (tl_ & hmask) != hmask) store_map(tl_);
+    const int tl_ = t1 - 1;
+    if (FPW == 2 && (tl_ & 1) == 0 && tl_ > t0) store_word(tl_);
+    if (kMaps && (tl_ & hmask) != hmask) store_map(tl_);
   }
   if (fault) sh.slot_fault[slot] = 1;
-
-  // ---- terminal state (alignment.cu:497-510) ----
-  const int last = S - 1;  // even
-  // One predicated store per state keeps a[] in registers (a runtime index
-  // into it would move the array to local memory).
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int s = K * tl + k;
-    if (s == last) sh.term_last[slot] = a[k];
-    if (s == last - 1) sh.term_prev[slot] = a[k];
-  }
+  piece_end(piece, t1 - 1);
   x.sync();
-  if (tl == 0) {
-    const float vlast = sh.term_last[slot];
-    int terminal = last;
-    float objective = vlast;
-    if (S > 1) {
-      const float vprev = sh.term_prev[slot];
-      if (vprev >= vlast) { terminal = last - 1; objective = vprev; }
-    }
-    const bool ok = isfinite(objective);
-    out.objective[x.r] = objective;
-    out.status[x.r] = sh.slot_fault[slot] ? kStatusDeviceFault : (ok ? 0 : 1);
-    if (ok) {
-      // Walk the segment maps back from the terminal: one anchor per segment.
-      const int C = static_cast<int>((static_cast<int64_t>(T) + hmask) >> rec.seg_log2);
-      int32_t* anc = anchors + rec.seg_off;
-      const uint16_t* mp = map_arena + rec.map_off;
-      int s = terminal;
-      anc[C - 1] = s;
-      for (int c = C - 1; c >= 1; --c) {
-        s -= mp[static_cast<int64_t>(c - 1) * map_stride + s];
-        anc[c - 1] = s;
+
+  // Lane k of the slot's first warp finishes piece k: its end state and
+  // flags; then the path's anchors and region start come from the segment
+  // maps (kMaps) or from warp traces over the backpointers.
+  int32_t* anc = P.anchors + rec.seg_off;
+  if (x.lw == 0 && lane < run.pieces) {
+    const int k = lane;
+    const int first = t0 + k * kPieceFrames;
+    const int end = k + 1 < run.pieces ? first + kPieceFrames : t1;
+    int end_state;
+    float best;
+    bool nan = false;
+    if (end == T) {
+      const float vlast = sh.term_last[slot];
+      end_state = last;
+      best = vlast;
+      if (S > 1) {
+        const float vprev = sh.term_prev[slot];
+        if (vprev >= vlast) { end_state = last - 1; best = vprev; }
+      }
+    } else {
+      best = -INFINITY;
+      end_state = 0x7fffffff;
+      for (int w = x.first_warp; w < x.first_warp + rec.nw; ++w) {
+        const float v = sh.red_val[k][w];
+        const int i = sh.red_idx[k][w];
+        if (v > best || (v == best && i < end_state)) { best = v; end_state = i; }
+        nan |= sh.red_nan[k][w] != 0;
       }
     }
+    const bool slot_fault = sh.slot_fault[slot] != 0;
+    const bool finite = isfinite(best);
+    if (run.end_piece < 0) {
+      P.out.objective[x.r] = best;
+      P.out.status[x.r] = slot_fault ? kStatusDeviceFault : (finite ? 0 : 1);
+    } else {
+      PieceState& pe = P.pstates[run.end_piece + k];
+      pe.end = end_state;
+      pe.flags = (finite && !nan && !slot_fault ? kPieceOk : 0) | (slot_fault ? kPieceFault : 0);
+      if (run.new_region) pe.region_start = 1;
+    }
+    const bool trace = finite && !slot_fault && !(run.end_piece >= 0 && nan);
+    if constexpr (kMaps) {
+      if (trace) {
+        // (The clamp never acts on maps a completed DP wrote; it keeps every
+        // read inside the arena.)
+        const int a0 = run.pieces > 1 ? first : run.a0;
+        const uint16_t* mp = P.maps + rec.map_off;
+        int s = end_state;
+        for (int g = (end - 1) >> rec.seg_log2; g >= (a0 >> rec.seg_log2); --g) {
+          anc[g] = s;
+          s = min(max(s - mp[static_cast<int64_t>(g) * map_stride + s], 0), S - 1);
+        }
+        if (run.end_piece >= 0) P.pstates[run.start_piece + k].start = s;
+      }
+    } else {
+      sh.red_idx[k][x.first_warp] = trace ? end_state : -1;
+    }
   }
+  if constexpr (!kMaps) {
+    x.sync();
+    // Warp lw traces pieces lw, lw + nw, ...: from the end state back to the
+    // piece's (or the repaired region's) first frame.
+    const uint32_t* bpr = P.bp + rec.bp_off;
+    for (int k = x.lw; k < run.pieces; k += rec.nw) {
+      const int s_end = sh.red_idx[k][x.first_warp];
+      if (s_end < 0) continue;
+      const int first = t0 + k * kPieceFrames;
+      const int end = k + 1 < run.pieces ? first + kPieceFrames : t1;
+      const int a0 = run.pieces > 1 ? first : run.a0;
+      if (lane == 0) anc[(end - 1) >> rec.seg_log2] = s_end;
+      const int s0 = warp_trace(bpr, NT, K, s_end, end - 1, a0, lane, [&](int t, int s) {
+        if (lane == 0 && (t & hmask) == hmask) anc[t >> rec.seg_log2] = s;
+      });
+      if (lane == 0) P.pstates[run.start_piece + k].start = s0;
+    }
+  }
+  return nchunks;
 }
 
 }  // namespace
 
-// One CTA = one Bundle of records with the same slot size and the same states
-// per thread.  Warps of a slot run the record's DP in lock step with one named
-// barrier per frame (a one-warp slot needs only __syncwarp).  kRow: emission
-// rows arrive kGroup frames at a time by one TMA bulk copy into a
-// kRowRing-deep ring per record; otherwise each thread gathers its columns
-// with cp.async into a private ring (large vocabularies).
+// The first pass.  One CTA = one Bundle of slots of `nw` warps with the same
+// states per thread; a slot runs one whole record (conventional DP with its
+// outputs) or a run of consecutive pieces of one record of the optimized
+// route, and the first slot of each record also checks its inputs.  Warps of
+// a slot run the DP in lock step with one named barrier per frame.  kRow:
+// emission rows arrive kChunkFrames frames at a time by one TMA bulk copy
+// into a kRowRing-deep ring per slot; otherwise each thread gathers its
+// columns with cp.async into a private ring (large vocabularies).
 template <bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
-ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict__ bundles,
-                    const int32_t* __restrict__ order, const uint8_t* __restrict__ mask,
-                    int check_inputs, uint32_t* __restrict__ bp_arena,
-                    uint16_t* __restrict__ map_arena, int32_t* __restrict__ anchors,
-                    OutputsDev out, unsigned row_slot_bytes) {
+ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
 
@@ -461,78 +491,303 @@ ffa_viterbi_forward(const RecordDev* __restrict__ recs, const Bundle* __restrict
   x.tid = threadIdx.x;
   x.warp = x.tid >> 5;
   x.lane = x.tid & 31;
-  const Bundle bd = bundles[blockIdx.x];
-  x.slot = x.warp >> bd.slot_log2;
+  const Bundle bd = P.bundles[blockIdx.x];
+  x.slot = x.warp / bd.nw;
   if (x.tid == 0) sh.edge = Boundary{-INFINITY, 0};
   __syncthreads();
   if (x.slot >= bd.count) return;
-  x.r = order[bd.first + x.slot];
-  const RecordDev rec = recs[x.r];
-  x.lw = x.warp & ((1 << bd.slot_log2) - 1);  // warp within the record
+  const int p = P.order[bd.first + x.slot];
+  const PieceDev piece = P.pieces[p];
+  x.r = piece.record;
+  const RecordDev rec = P.recs[x.r];
+  x.first_warp = x.slot * bd.nw;
+  x.bar = x.slot;
+  x.lw = x.warp - x.first_warp;  // warp within the slot
   if (x.lw >= rec.nw) return;
   x.NT = rec.nw * 32;
-  x.tl = x.lw * 32 + x.lane;  // thread within the record
-  x.single = rec.nw == 1;
+  x.tl = x.lw * 32 + x.lane;  // thread within the slot
   const int tl = x.tl, lane = x.lane, warp = x.warp, r = x.r;
   const int T = rec.T, V = rec.V, U = rec.U, blank = rec.blank;
   const int64_t* tgt = rec.targets;
+  const bool chunked = rec.num_pieces > 1;
 
-  // ---- status: mask, then target validation (alignment.cu:836, 852-874) ----
-  int status = (mask != nullptr && !mask[r]) ? 2 : 0;
-  if (tl == 0) sh.slot_fault[x.slot] = 0;
-  if (check_inputs) {
-    int bad = 0, rep = 0;
-    for (int k = tl; k < U; k += x.NT) {
-      const int64_t token = tgt[k];
-      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
-      if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+  PieceRun run{0, 0, T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, 0};
+  {
+    const bool masked = P.mask != nullptr && !P.mask[r];
+    if (piece.index == 0) {
+      // ---- status: mask, then target validation (alignment.cu:836, 852-874) ----
+      int status = masked ? 2 : 0;
+      if (tl == 0) sh.slot_fault[x.slot] = 0;
+      if (P.check_inputs) {
+        int bad = 0, rep = 0;
+        for (int k = tl; k < U; k += x.NT) {
+          const int64_t token = tgt[k];
+          bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
+          if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+        }
+        bad = __reduce_or_sync(0xffffffffu, bad);
+        rep = __reduce_add_sync(0xffffffffu, rep);
+        if (lane == 0) { sh.chk_bad[warp] = bad; sh.chk_rep[warp] = rep; }
+        x.sync();
+        if (tl == 0) {
+          int b = 0, q = 0;
+          for (int w = 0; w < rec.nw; ++w) { b |= sh.chk_bad[warp + w]; q += sh.chk_rep[warp + w]; }
+          if (b) status = 3;
+          else if (static_cast<int64_t>(U) + q > T) status = 4;
+          sh.slot_status[x.slot] = status;
+        }
+        x.sync();
+        status = sh.slot_status[x.slot];
+      }
+      if (tl == 0) {
+        // Diagnostics start at zero (alignment.py:101-129); the optimized
+        // route's plan counts repairs and joins into them.
+        P.fill_done[r] = 0;
+        P.out.stitched[r] = 0;
+        P.out.repair_passes[r] = 0;
+        P.out.repaired_frames[r] = 0;
+        for (int j = 0; j < 3; ++j) { P.out.shortcut_stats[3 * r + j] = 0; P.out.routing_stats[3 * r + j] = 0; }
+        if (P.out.reuse_stats) for (int j = 0; j < 4; ++j) P.out.reuse_stats[4 * r + j] = 0;
+        if (status >= 2) P.out.objective[r] = -INFINITY;
+        if (status >= 2 || chunked) P.out.status[r] = status;
+      }
+      if (status >= 2) return;
+    } else {
+      if (masked) return;
+      if (tl == 0) sh.slot_fault[x.slot] = 0;
     }
-    bad = __reduce_or_sync(0xffffffffu, bad);
-    rep = __reduce_add_sync(0xffffffffu, rep);
-    if (lane == 0) { sh.red_bad[warp] = bad; sh.red_rep[warp] = rep; }
-    x.sync();
-    if (tl == 0) {
-      int b = 0, p = 0;
-      for (int w = 0; w < rec.nw; ++w) { b |= sh.red_bad[warp + w]; p += sh.red_rep[warp + w]; }
-      if (b) status = 3;
-      else if (static_cast<int64_t>(U) + p > T) status = 4;
-      sh.slot_status[x.slot] = status;
+    if (chunked) {
+      // Pieces index .. index+m-1 of the record, back to back.
+      const int m = min(P.run_pieces, rec.num_pieces - piece.index);
+      run.a0 = run.t0 = piece.first;
+      run.t1 = piece.index + m == rec.num_pieces ? T : piece.first + m * kPieceFrames;
+      run.pieces = m;
+      run.init = piece.first == 0 ? kInitRecord : kInitFree;
+      run.frontier_out = P.frontiers + rec.frontier_off + static_cast<int64_t>(piece.index) * x.NT * rec.kst;
+      run.end_piece = run.start_piece = p;
+      run.new_region = true;
     }
-    x.sync();
-    status = sh.slot_status[x.slot];
   }
-  if (tl == 0) {
-    // Diagnostics of the conventional route are all zero (alignment.py:101-129).
-    out.stitched[r] = 0;
-    out.repair_passes[r] = 0;
-    out.repaired_frames[r] = 0;
-    for (int j = 0; j < 3; ++j) { out.shortcut_stats[3 * r + j] = 0; out.routing_stats[3 * r + j] = 0; }
-    if (out.reuse_stats) for (int j = 0; j < 4; ++j) out.reuse_stats[4 * r + j] = 0;
-    if (status >= 2) { out.status[r] = status; out.objective[r] = -INFINITY; }
+
+  // Pieces of the optimized route (K = 8) find their anchors by tracing;
+  // whole records walk segment maps.
+  if (chunked)
+    piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+  else if (rec.kst == 4)
+    piece_dp<4, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+  else
+    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+}
+
+// Repair jobs of one round of one record (shared memory of the finisher).
+constexpr int kMaxJobs = 128;
+struct JobList {
+  int count;
+  int piece[kMaxJobs];  // first piece re-solved (resumes from the frontier of piece - 1)
+  int first[kMaxJobs];  // first piece of the merged region
+  int last[kMaxJobs];   // last piece of the merged region
+};
+
+// Seam check and repair planning of one round of one record, by one warp.  A
+// region is a run of pieces solved as one DP; a seam is legal when the right
+// region's start state follows the left region's end state by a CTC move
+// (stay, step, or a skip into a token that differs from the previous token
+// and from the blank).  Every run of consecutive failing seams becomes one
+// repair job: the merged region resumes from the end frontier of its first
+// region and re-solves the regions after it.  Returns the record's route:
+//   all seams legal, every region finite and NaN-free  -> joined (stitched)
+//   a region non-finite or with NaN                     -> conventional DP
+//   seams still failing after the last round            -> conventional DP
+__device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__ ps,
+                           int32_t* __restrict__ route, const OutputsDev& out, int round,
+                           bool final_round, JobList& jobs, int lane) {
+  if (out.status[r] != 0) {
+    if (lane == 0) route[r] = kRouteNone;
+    return kRouteNone;
   }
-  if (status >= 2) return;
+  const int C = rec.num_pieces, P0 = rec.first_piece;
+  if (lane == 0) jobs.count = 0;
+  __syncwarp();
 
-  switch (rec.kst) {
-    default:
-      record_dp<8, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
-      break;
-    case 4:
-      record_dp<4, kRow, kV>(x, rec, sh, smem_raw, bp_arena, map_arena, anchors, out, row_slot_bytes);
-      break;
+  auto col = [&](int u) { return clamp_label(rec.targets[u], rec.V); };
+  auto legal = [&](int from, int to) {
+    const int jump = to - from;
+    if (jump == 0 || jump == 1) return true;
+    if (jump != 2 || !(to & 1)) return false;
+    const int u = to >> 1;
+    return u >= 1 && col(u) != rec.blank && col(u) != col(u - 1);
+  };
 
+  bool bad = false, fault = false, any_fail = false, run_open = false, overflow = false;
+  int run_job = 0, run_first = 0, cur_first = 0, njobs = 0;
+  int64_t merged = 0, skipped = 0;
+  // Piece j covers frames [j * kPieceFrames, end_of(j)); the last one ends at T.
+  auto end_of = [&](int j) { return j == C - 1 ? rec.T : (j + 1) * kPieceFrames; };
+  auto emit = [&](int job, int last) {
+    // All lanes take the same decisions; lane 0 writes them.
+    merged += end_of(last) - run_first * kPieceFrames;
+    skipped += (job - run_first) * kPieceFrames;
+    if (njobs == kMaxJobs) overflow = true;
+    if (lane == 0 && !final_round && njobs < kMaxJobs) {
+      jobs.piece[njobs] = P0 + job;
+      jobs.first[njobs] = P0 + run_first;
+      jobs.last[njobs] = P0 + last;
+      for (int k = job; k <= last; ++k) ps[P0 + k].region_start = 0;
+    }
+    ++njobs;
+  };
+  for (int base = 0; base < C; base += 32) {
+    // Each lane checks the seam in front of its piece (if it starts a region)
+    // and whether its piece ends a region that failed.
+    const int j = base + lane;
+    bool seam = false, fail = false, region_bad = false, region_fault = false;
+    if (j < C) {
+      const PieceState mine = ps[P0 + j];
+      const bool next_rs = j + 1 >= C || ps[P0 + j + 1].region_start != 0;
+      seam = mine.region_start != 0 && j > 0;
+      if (seam) fail = !legal(ps[P0 + j - 1].end, mine.start);
+      region_bad = next_rs && (mine.flags & kPieceOk) == 0;
+      region_fault = next_rs && (mine.flags & kPieceFault) != 0;
+    }
+    unsigned seams = __ballot_sync(0xffffffffu, seam);
+    const unsigned fails = __ballot_sync(0xffffffffu, fail);
+    bad |= __any_sync(0xffffffffu, region_bad) != 0;
+    fault |= __any_sync(0xffffffffu, region_fault) != 0;
+    __syncwarp();
+    // Runs of consecutive failing seams, in piece order (uniform over lanes).
+    while (seams) {
+      const int q = __ffs(seams) - 1;
+      seams &= seams - 1;
+      const int jj = base + q;
+      if ((fails >> q) & 1u) {
+        any_fail = true;
+        if (!run_open) { run_open = true; run_job = jj; run_first = cur_first; }
+      } else {
+        if (run_open) { emit(run_job, jj - 1); run_open = false; }
+        cur_first = jj;
+      }
+    }
+  }
+  if (run_open) emit(run_job, C - 1);
+  int decision;
+  if (fault) decision = kRouteNone;
+  else if (bad || (any_fail && (final_round || overflow))) decision = kRouteFallback;
+  else if (!any_fail) decision = kRouteStitched;
+  else decision = kRoutePending;
+  if (lane == 0) {
+    route[r] = decision;
+    jobs.count = decision == kRoutePending ? njobs : 0;
+    if (fault) {
+      out.status[r] = kStatusDeviceFault;
+      out.objective[r] = -INFINITY;
+    } else if (decision == kRouteStitched) {
+      out.stitched[r] = 1;
+    } else if (decision == kRoutePending) {
+      out.repair_passes[r] += 1;
+      out.repaired_frames[r] += merged;
+      if (out.reuse_stats) {
+        // Frames the frontiers spared, and frontier values read.
+        out.reuse_stats[4 * r + 0] += skipped;
+        out.reuse_stats[4 * r + 3] += static_cast<int64_t>(njobs) * (2 * rec.U + 1);
+      }
+    }
+    if (round == 0 && out.reuse_stats)
+      out.reuse_stats[4 * r + 2] = static_cast<int64_t>(C - 1) * (2 * rec.U + 1);
+  }
+  __syncwarp();
+  return decision;
+}
 
+// The finisher's static shared memory (its job list) stays under 2 KiB; the
+// rest of the budget is dynamic.
+constexpr size_t kFinishDynamicSmem = kSmemBudget - 2048;
+static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
+
+// Everything after the first pass of one record of the optimized route, in
+// one CTA: kRepairRounds rounds of seam planning (warp 0) and repair jobs
+// (slots of nw warps, in parallel), the final plan, and the conventional DP
+// when the route cannot join the record.  Records need nothing from one
+// another, so no launch boundary separates the rounds.
+template <bool kRow, int kV>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
+  __shared__ JobList jobs;
+  __shared__ int route_s;
+  const int r = records[blockIdx.x];
+  const RecordDev rec = P.recs[r];
+  SlotCtx x;
+  x.tid = threadIdx.x;
+  x.warp = x.tid >> 5;
+  x.lane = x.tid & 31;
+  x.r = r;
+  const int nw = rec.nw;
+  // Slot barriers use ids 1.. (id 0 is __syncthreads); row-staged slots also
+  // need a ring each.
+  int nslots = min(kMaxWarps - 1, kMaxWarps / nw);
+  if (kRow) nslots = min(nslots, static_cast<int>((kFinishDynamicSmem - kForwardHeader) / P.row_slot_bytes));
+  x.slot = x.warp / nw;
+  x.lw = x.warp - x.slot * nw;
+  x.NT = nw * 32;
+  x.tl = x.lw * 32 + x.lane;
+  x.first_warp = x.slot * nw;
+  x.bar = x.slot + 1;
+  const bool in_slot = x.slot < nslots;
+  if (x.tid == 0) sh.edge = Boundary{-INFINITY, 0};
+  int chunk_base = 0;  // this slot's emission chunks so far (row staging)
+  for (int round = 0;; ++round) {
+    __syncthreads();
+    if (x.warp == 0) {
+      const int decision = plan_record(rec, r, P.pstates, P.route, P.out, round,
+                                       round == kRepairRounds, jobs, x.lane);
+      if (x.lane == 0) route_s = decision;
+    }
+    __syncthreads();
+    if (route_s != kRoutePending) break;
+    const int n = jobs.count;
+    const int64_t fstride = static_cast<int64_t>(x.NT) * rec.kst;
+    if (in_slot) {
+      for (int j = x.slot; j < n; j += nslots) {
+        const int p = jobs.piece[j];
+        const int idx = p - rec.first_piece;
+        const int last = jobs.last[j] - rec.first_piece;
+        PieceRun run{};
+        run.a0 = (jobs.first[j] - rec.first_piece) * kPieceFrames;
+        run.t0 = idx * kPieceFrames;
+        run.t1 = last == rec.num_pieces - 1 ? rec.T : (last + 1) * kPieceFrames;
+        run.init = kInitFrontier;
+        run.pieces = 1;
+        run.frontier_in = P.frontiers + rec.frontier_off + (idx - 1) * fstride;
+        run.frontier_out = run.t1 < rec.T ? P.frontiers + rec.frontier_off + last * fstride : nullptr;
+        run.end_piece = jobs.last[j];
+        run.start_piece = jobs.first[j];
+        run.new_region = false;
+        run.chunk_base = chunk_base;
+        if (x.tl == 0) sh.slot_fault[x.slot] = 0;
+        chunk_base += piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+      }
+    }
+  }
+  if (route_s == kRouteFallback && x.slot == 0) {
+    PieceRun run{0, 0, rec.T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, chunk_base};
+    if (x.tl == 0) sh.slot_fault[0] = 0;
+    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
   }
 }
 
-// One warp per traceback segment: lane 0 walks the 2-bit backpointers from the
+// One warp per traceback segment: the warp walks the backpointers from the
 // segment's anchor (path[t-1] = path[t] - bp[t, path[t]], alignment.cu:656-659),
-// then the warp maps states to labels and gathers the selected scores
+// then maps states to labels and gathers the selected scores
 // (alignment.cu:662-666).  Failed records get -1 / -inf (alignment.cu:650-652).
+// For a record of the optimized route, the record's last fill CTA to finish
+// (a counter per record) then folds the objective of a joined path.
 __global__ void __launch_bounds__(32 * kFillWarps)
 ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ items,
                const uint32_t* __restrict__ bp_arena, const int32_t* __restrict__ anchors,
-               OutputsDev out) {
+               OutputsDev out, const int32_t* __restrict__ route, int32_t* __restrict__ fill_done) {
   __shared__ int32_t path[kFillWarps][1 << kMaxSegLog2];
+  __shared__ int fold_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const FillItem item = items[blockIdx.x];
   const RecordDev rec = recs[item.record];
@@ -540,54 +795,75 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
   const int T = rec.T;
   const int H = 1 << rec.seg_log2;
   const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
-  if (c >= C) return;
-  const int a = c * H;
-  const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
   int64_t* labels = out.labels + rec.out_off;
   float* scores = out.scores + rec.out_off;
-  if (out.status[item.record] != 0) {
-    for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
-    return;
-  }
-  int32_t* p = path[warp];
-  {
-    // The path moves at most 2 states per frame, so over FB frames it stays
-    // within 2*FB/K + 2 threads' words: the warp loads those FB x NTH words
-    // in one round trip, then steps through them with shuffles.  Every lane
-    // tracks the same state.
-    const int NT = rec.nw * 32;
-    const int K = rec.kst;
-    const int fpw = frames_per_word(K);
-    const int FB = K >= 8 ? 8 : 6;
-    const int NTH = 2 * FB / K + 2;
-    const uint32_t* bp = bp_arena + rec.bp_off;
-    int s = anchors[rec.seg_off + c];
-    if (lane == 0) p[b - 1 - a] = s;
-    for (int t = b - 1; t > a;) {
-      const int f = lane / NTH, dd = lane % NTH;
-      const int tt = t - f;
-      const int th = s / K - dd;
-      uint32_t w = 0;
-      if (f < FB && tt > a && th >= 0) w = bp[static_cast<int64_t>(tt / fpw) * NT + th];
-      const int steps = min(FB, t - a);
-      const int th0 = s / K;
-      for (int i = 0; i < steps; ++i) {
-        const int ct = t - i;
-        const uint32_t word = __shfl_sync(0xffffffffu, w, i * NTH + (th0 - s / K));
-        s -= jump_of(fpw == 2 ? word >> (16 * (ct & 1)) : word, s, K);
-        if (lane == 0) p[ct - 1 - a] = s;
+  if (c < C) {
+    const int a = c * H;
+    const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
+    if (out.status[item.record] != 0) {
+      for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
+    } else {
+      int32_t* p = path[warp];
+      const int s_end = anchors[rec.seg_off + c];
+      if (lane == 0) p[b - 1 - a] = s_end;
+      warp_trace(bp_arena + rec.bp_off, rec.nw * 32, rec.kst, s_end, b - 1, a, lane,
+                 [&](int t, int s) { if (lane == 0) p[t - a] = s; });
+      __syncwarp();
+      const float* e = rec.emissions;
+      for (int t = a + lane; t < b; t += 32) {
+        const int s = p[t - a];
+        const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
+        labels[t] = label;
+        scores[t] = e[static_cast<int64_t>(t) * rec.V + label];
       }
-      t -= steps;
     }
   }
-  __syncwarp();
-  const float* e = rec.emissions;
-  for (int t = a + lane; t < b; t += 32) {
-    const int s = p[t - a];
-    const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
-    labels[t] = label;
-    scores[t] = e[static_cast<int64_t>(t) * rec.V + label];
+  if (rec.num_pieces <= 1) return;  // uniform over the CTA
+
+  // Objective of a joined record: the path's selected emissions summed in
+  // frame order with one fp32 add each -- the conventional DP's accumulation
+  // along the same path (alignment.cu:423), so equal paths give equal
+  // objectives.  A non-finite sum marks the record failed (alignment.cu:
+  // 507-510, 650-652).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int ctas = (C + kFillWarps - 1) / kFillWarps;
+    fold_flag = atomicAdd(&fill_done[item.record], 1) == ctas - 1 &&
+                route[item.record] == kRouteStitched;
   }
+  __syncthreads();
+  if (!fold_flag) return;
+  __threadfence();
+  float* window = reinterpret_cast<float*>(&path[0][0]);
+  constexpr int kWindow = kFillWarps << kMaxSegLog2;
+  float obj = -0.0f;  // -0 + x == x exactly for every x
+  for (int base = 0; base < T; base += kWindow) {
+    const int n = min(kWindow, T - base);
+    __syncthreads();
+#pragma unroll 4
+    for (int k = threadIdx.x; k < n; k += 32 * kFillWarps) window[k] = scores[base + k];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int k = 0;
+      for (; k + 8 <= n; k += 8) {
+        float x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) x[q] = window[k + q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, x[q]);
+      }
+      for (; k < n; ++k) obj = __fadd_rn(obj, window[k]);
+    }
+  }
+  if (threadIdx.x == 0) {
+    out.objective[item.record] = obj;
+    fold_flag = isfinite(obj) ? 1 : 0;
+    if (!isfinite(obj)) out.status[item.record] = 1;
+  }
+  __syncthreads();
+  if (fold_flag) return;
+  for (int t = threadIdx.x; t < T; t += 32 * kFillWarps) { labels[t] = -1; scores[t] = -INFINITY; }
 }
 
 // valid[r] was set to 1; any CTA finding NaN or +inf in its chunk clears it.
@@ -644,35 +920,72 @@ __global__ void ffa_fill_u8(uint8_t* p, int64_t n, uint8_t value) {
 
 size_t forward_header_bytes() { return kForwardHeader; }
 
-cudaError_t launch_forward(const RecordDev* recs, const Bundle* bundles, const int32_t* order,
-                           int num_bundles, bool row_mode, int row_vocab, const uint8_t* mask,
-                           int check_inputs,
-                           uint32_t* bp, uint16_t* maps, int32_t* anchors,
-                           const OutputsDev& out, unsigned smem_bytes, unsigned row_slot_bytes,
-                           cudaStream_t stream) {
+namespace {
+thread_local int64_t g_launches = 0;
+}  // namespace
+int64_t launches_so_far() { return g_launches; }
+
+cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
+                           int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
   if (num_bundles <= 0) return cudaSuccess;
   auto kernel = !row_mode ? ffa_viterbi_forward<false, 0>
                          : (row_vocab == 32 ? ffa_viterbi_forward<true, 32> : ffa_viterbi_forward<true, 0>);
-  // Opting in to >48 KiB of dynamic shared memory is per device; the call is
-  // cheap and idempotent, so it is repeated rather than cached.
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes));
+  // Opting in to >48 KiB of dynamic shared memory is per device and kernel:
+  // done once, to the whole budget, then every launch fits under it.
+  static std::atomic<uint64_t> opted[3];  // bit d: device d done
+  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
-  kernel<<<num_bundles, kCtaThreads, smem_bytes, stream>>>(
-      recs, bundles, order, mask, check_inputs, bp, maps, anchors, out, row_slot_bytes);
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmemBudget));
+    if (err != cudaSuccess) return err;
+    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
+  }
+  if (smem_bytes > kSmemBudget) return cudaErrorInvalidValue;
+  ++g_launches;
+  kernel<<<num_bundles, kCtaThreads, smem_bytes, stream>>>(params);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
+                          bool row_mode, int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  auto kernel = !row_mode ? ffa_finish_route<false, 0>
+                         : (row_vocab == 32 ? ffa_finish_route<true, 32> : ffa_finish_route<true, 0>);
+  static std::atomic<uint64_t> opted[3];  // bit d: device d opted in
+  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kFinishDynamicSmem));
+    if (err != cudaSuccess) return err;
+    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
+  }
+  if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
+  ++g_launches;
+  kernel<<<count, kCtaThreads, smem_bytes, stream>>>(params, records);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        cudaStream_t stream) {
+                        const int32_t* route, int32_t* fill_done, cudaStream_t stream) {
   if (num_items <= 0) return cudaSuccess;
-  ffa_trace_fill<<<num_items, 32 * kFillWarps, 0, stream>>>(recs, items, bp, anchors, out);
+  ++g_launches;
+  ffa_trace_fill<<<num_items, 32 * kFillWarps, 0, stream>>>(recs, items, bp, anchors, out, route,
+                                                             fill_done);
   return cudaGetLastError();
 }
 
 cudaError_t launch_check_targets(const RecordDev* recs, int64_t count, int32_t* status,
                                  cudaStream_t stream) {
+  ++g_launches;
   ffa_check_targets_kernel<<<static_cast<unsigned>((count + 7) / 8), 256, 0, stream>>>(recs, count, status);
   return cudaGetLastError();
 }
@@ -680,9 +993,11 @@ cudaError_t launch_check_targets(const RecordDev* recs, int64_t count, int32_t* 
 cudaError_t launch_validity(const ScanRecord* recs, int64_t count, const ScanItem* items,
                             int64_t num_items, uint8_t* valid, cudaStream_t stream) {
   const int fill_blocks = static_cast<int>((count + 255) / 256);
+  ++g_launches;
   ffa_fill_u8<<<fill_blocks, 256, 0, stream>>>(valid, count, 1);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess || num_items <= 0) return err;
+  ++g_launches;
   ffa_validity_scan<<<static_cast<unsigned>(num_items), kScanThreads, 0, stream>>>(recs, items, valid);
   return cudaGetLastError();
 }

@@ -1,20 +1,21 @@
 // ffa_torch.cpp -- thin PyTorch operator layer over the C ABI (libffa_b200.so).
 //
-// Registers torch.ops.ffa_b200.{align, align_packed, emission_validity}.  It
-// mirrors the reference's op layer (alignment.cu:893-1061,
+// Registers torch.ops.ffa_b200.{align, align_packed, emission_validity,
+// check_targets}.  It mirrors the reference's op layer (alignment.cu:893-1061,
 // TORCH_LIBRARY at alignment.cu:1064-1070): tensor metadata checks, stream
-// lifetime protection (recordStream on borrowed inputs), output allocation
-// from the caching allocator, and a pinned staging buffer whose reuse is
-// fenced with the host allocator's stream event.  Everything below the
-// ffa_* calls is plain pointers and sizes.
+// lifetime protection (recordStream on borrowed inputs) and output allocation
+// from the caching allocator.  Everything below the ffa_* calls is plain
+// pointers and sizes.  Per call it makes two caching-allocator requests (one
+// block holds every output tensor, one the workspace) and stages descriptors
+// in a reused host buffer, so the host cost stays a few microseconds.
 #include <ATen/ATen.h>
-#include <ATen/core/CachingHostAllocator.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
 #include <climits>
+#include <initializer_list>
 #include <optional>
 #include <tuple>
 #include <vector>
@@ -45,15 +46,58 @@ struct StreamRecorder {
   }
 };
 
-at::Tensor pinned_staging(size_t bytes) {
-  return at::empty({static_cast<int64_t>(std::max<size_t>(bytes, 1))},
-                   at::TensorOptions().dtype(at::kByte).device(at::kCPU).pinned_memory(true));
+// Host staging: a per-thread pageable buffer reused across calls.  A
+// host-to-device cudaMemcpyAsync from pageable memory copies the bytes out
+// before it returns, so the next call may refill the buffer at once.
+void* host_staging(size_t bytes) {
+  thread_local std::vector<unsigned char> buffer;
+  if (buffer.size() < bytes) buffer.resize(bytes);
+  return buffer.data();
 }
 
-void fence_staging(const at::Tensor& staging, c10::cuda::CUDAStream stream) {
-  at::getHostAllocator(at::kCUDA)->record_event(
-      staging.data_ptr(), staging.storage().data_ptr().get_context(), stream.unwrap());
+// Device scratch from the caching allocator on the current stream; returned
+// to the cache (stream-ordered) when the DataPtr goes away.
+c10::DataPtr device_scratch(size_t bytes) {
+  return c10::cuda::CUDACachingAllocator::get()->allocate(std::max<size_t>(bytes, 256));
 }
+
+// Several output tensors carved from one caching-allocator block: each is a
+// contiguous tensor on a shared storage at a 256-byte aligned offset, built
+// without a dispatcher round trip per tensor.
+class OutputBlock {
+ public:
+  template <typename T>
+  void add(std::initializer_list<int64_t> sizes) {
+    int64_t n = 1;
+    for (int64_t v : sizes) n *= v;
+    specs_.push_back({bytes_, std::vector<int64_t>(sizes), caffe2::TypeMeta::Make<T>()});
+    bytes_ = (bytes_ + static_cast<size_t>(n) * sizeof(T) + 255) / 256 * 256;
+  }
+  std::vector<at::Tensor> allocate() {
+    auto* allocator = c10::cuda::CUDACachingAllocator::get();
+    c10::Storage storage(c10::Storage::use_byte_size_t(), static_cast<int64_t>(bytes_),
+                         allocator->allocate(std::max<size_t>(bytes_, 256)), allocator, false);
+    std::vector<at::Tensor> out;
+    out.reserve(specs_.size());
+    for (const auto& spec : specs_) {
+      auto t = at::detail::make_tensor<c10::TensorImpl>(
+          c10::Storage(storage), c10::DispatchKeySet(c10::DispatchKey::CUDA), spec.dtype);
+      t.unsafeGetTensorImpl()->set_sizes_contiguous(spec.sizes);
+      t.unsafeGetTensorImpl()->set_storage_offset(static_cast<int64_t>(spec.offset / spec.dtype.itemsize()));
+      out.push_back(std::move(t));
+    }
+    return out;
+  }
+
+ private:
+  struct Spec {
+    size_t offset;
+    std::vector<int64_t> sizes;
+    caffe2::TypeMeta dtype;
+  };
+  std::vector<Spec> specs_;
+  size_t bytes_ = 0;
+};
 
 const uint8_t* check_mask(const std::optional<at::Tensor>& validity, const c10::Device& device,
                           int64_t count, StreamRecorder& rec) {
@@ -76,41 +120,32 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> run_align(
   ffa_sizes sizes{};
   check_status(ffa_align_query(recs.data(), count, cmode, flags, &sizes));
 
-  // One caching-allocator block per output (cheaper than carving typed views
-  // out of one block, which costs several dispatcher calls per view).
   const int64_t N = sizes.total_frames;
   int64_t max_frames = 0;
   for (const auto& r : recs) max_frames = std::max(max_frames, r.frames);
   const bool reuse = cmode == FFA_MODE_OPTIMIZED && max_frames >= 2048;
-  const auto opts = at::TensorOptions().device(device);
-  auto labels = at::empty({N}, opts.dtype(at::kLong));
-  auto scores = at::empty({N}, opts.dtype(at::kFloat));
-  auto status = at::empty({count}, opts.dtype(at::kInt));
-  auto objective = at::empty({count}, opts.dtype(at::kFloat));
-  auto stitched = at::empty({count}, opts.dtype(at::kInt));
-  auto passes = at::empty({count}, opts.dtype(at::kInt));
-  auto repaired = at::empty({count}, opts.dtype(at::kLong));
-  auto shortcut = at::empty({count, 3}, opts.dtype(at::kLong));
-  auto routing = at::empty({count, 3}, opts.dtype(at::kInt));
-  auto reuse_stats = at::empty({reuse ? count : 0, 4}, opts.dtype(at::kLong));
-
-  auto staging = pinned_staging(sizes.staging_bytes);
-  auto workspace = at::empty({static_cast<int64_t>(std::max<size_t>(sizes.workspace_bytes, 256))},
-                             opts.dtype(at::kByte));
-  ffa_outputs out{labels.data_ptr<int64_t>(), scores.data_ptr<float>(), status.data_ptr<int32_t>(),
-                  objective.data_ptr<float>(), stitched.data_ptr<int32_t>(),
-                  passes.data_ptr<int32_t>(), repaired.data_ptr<int64_t>(),
-                  shortcut.data_ptr<int64_t>(), routing.data_ptr<int32_t>(),
-                  reuse ? reuse_stats.data_ptr<int64_t>() : nullptr};
-  const int rc = ffa_align(recs.data(), count, cmode, flags, mask, &out, staging.data_ptr(),
-                           sizes.staging_bytes, workspace.data_ptr(),
-                           static_cast<size_t>(workspace.numel()),
+  OutputBlock block;
+  block.add<int64_t>({N});                        // labels
+  block.add<float>({N});                          // scores
+  block.add<int32_t>({count});                    // status
+  block.add<float>({count});                      // objective
+  block.add<int32_t>({count});                    // stitched
+  block.add<int32_t>({count});                    // repair_passes
+  block.add<int64_t>({count});                    // repaired_frames
+  block.add<int64_t>({count, 3});                 // shortcut_stats
+  block.add<int32_t>({count, 3});                 // routing_stats
+  block.add<int64_t>({reuse ? count : 0, 4});     // reuse_stats
+  std::vector<at::Tensor> t = block.allocate();
+  auto workspace = device_scratch(sizes.workspace_bytes);
+  ffa_outputs out{t[0].data_ptr<int64_t>(), t[1].data_ptr<float>(), t[2].data_ptr<int32_t>(),
+                  t[3].data_ptr<float>(), t[4].data_ptr<int32_t>(), t[5].data_ptr<int32_t>(),
+                  t[6].data_ptr<int64_t>(), t[7].data_ptr<int64_t>(), t[8].data_ptr<int32_t>(),
+                  reuse ? t[9].data_ptr<int64_t>() : nullptr};
+  const int rc = ffa_align(recs.data(), count, cmode, flags, mask, &out, host_staging(sizes.staging_bytes),
+                           sizes.staging_bytes, workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                            reinterpret_cast<ffa_stream_t>(stream.stream()));
-  fence_staging(staging, stream);
   check_status(rc);
-  return {{labels, scores, status, objective, stitched, passes, repaired, shortcut, routing,
-           reuse_stats},
-          std::move(lengths)};
+  return {std::move(t), std::move(lengths)};
 }
 
 void check_mode(int64_t mode) {
@@ -230,15 +265,12 @@ at::Tensor emission_validity(at::TensorList emissions) {
   ffa_sizes sizes{};
   check_status(ffa_emission_validity_query(recs.data(), count, &sizes));
   auto result = at::empty({count}, emissions[0].options().dtype(at::kBool));
-  auto staging = pinned_staging(sizes.staging_bytes);
-  auto workspace = at::empty({static_cast<int64_t>(std::max<size_t>(sizes.workspace_bytes, 256))},
-                             emissions[0].options().dtype(at::kByte));
+  auto workspace = device_scratch(sizes.workspace_bytes);
   const int rc = ffa_emission_validity(recs.data(), count,
                                        reinterpret_cast<uint8_t*>(result.data_ptr<bool>()),
-                                       staging.data_ptr(), sizes.staging_bytes, workspace.data_ptr(),
-                                       static_cast<size_t>(workspace.numel()),
+                                       host_staging(sizes.staging_bytes), sizes.staging_bytes,
+                                       workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                                        reinterpret_cast<ffa_stream_t>(stream.stream()));
-  fence_staging(staging, stream);
   check_status(rc);
   return result;
 }
@@ -277,14 +309,11 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
   ffa_sizes sizes{};
   check_status(ffa_check_targets_query(recs.data(), count, &sizes));
   auto status = at::empty({count}, emissions[0].options().dtype(at::kInt));
-  auto staging = pinned_staging(sizes.staging_bytes);
-  auto workspace = at::empty({static_cast<int64_t>(std::max<size_t>(sizes.workspace_bytes, 256))},
-                             emissions[0].options().dtype(at::kByte));
-  const int rc = ffa_check_targets(recs.data(), count, status.data_ptr<int32_t>(), staging.data_ptr(),
-                                   sizes.staging_bytes, workspace.data_ptr(),
-                                   static_cast<size_t>(workspace.numel()),
+  auto workspace = device_scratch(sizes.workspace_bytes);
+  const int rc = ffa_check_targets(recs.data(), count, status.data_ptr<int32_t>(),
+                                   host_staging(sizes.staging_bytes), sizes.staging_bytes,
+                                   workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                                    reinterpret_cast<ffa_stream_t>(stream.stream()));
-  fence_staging(staging, stream);
   check_status(rc);
   return status;
 }

@@ -173,9 +173,33 @@ FFA_API int ffa_align_noalloc(const ffa_record* records, int64_t count, int mode
 
 /* While set, ffa_align calls made on the calling thread record `before` and
  * `after` (two cudaEvent_t created by the caller) on their stream immediately
- * around the DP forward kernel, so the caller can read that kernel's device
- * time with cudaEventElapsedTime.  Pass NULL, NULL to clear. */
+ * around the first forward pass -- the launch that streams every emission row
+ * once (every piece of the optimized route, every record of the conventional
+ * one) -- so the caller can read its device time with cudaEventElapsedTime.
+ * Pass NULL, NULL to clear. */
 FFA_API int ffa_profile_forward_events(void* before, void* after);
+
+/* Number of CUDA kernels the ffa_* calls of the calling thread have launched
+ * so far (monotonic).  No reference counterpart: lets a benchmark report how
+ * many of this library's kernels ran in its timed region. */
+FFA_API int64_t ffa_launch_count(void);
+
+/* Phase boundaries of one ffa_align call, in launch order.  A conventional
+ * call has no finishing launch; its point is recorded where it would be, so
+ * that phase measures zero. */
+enum {
+  FFA_PROFILE_START = 0,   /* after the descriptor upload */
+  FFA_PROFILE_FIRST,       /* after the first forward pass (every piece / record) */
+  FFA_PROFILE_FINISH,      /* after the optimized route's seam plans, repairs and fallback */
+  FFA_PROFILE_FILL,        /* after the traceback fill (and objective fold) */
+  FFA_PROFILE_POINTS
+};
+
+/* While set, ffa_align calls made on the calling thread record events[k] (a
+ * cudaEvent_t created by the caller) at phase boundary k, for all
+ * FFA_PROFILE_POINTS boundaries.  No reference counterpart: a timing hook for
+ * benchmarks.  Pass NULL, 0 to clear; any other count is an error. */
+FFA_API int ffa_profile_phase_events(void* const* events, int count);
 
 /* ---- target validation (replaces the per-record checks of the reference's
  *      validate_inputs, alignment.py:255-309) ------------------------------- */
