@@ -188,8 +188,9 @@ __device__ __forceinline__ unsigned dp_frame_plain(float (&a)[K], float p1, floa
 __host__ __device__ constexpr int frames_per_word(int K) { return 3 * K / 2 <= 16 ? 2 : 1; }
 
 // Jump of state s (owned by a thread with K states) from one frame's bits.
-__device__ __forceinline__ int jump_of(unsigned bits, int s, int K) {
-  const int k = s % K;
+template <int K>
+__device__ __forceinline__ int jump_of(unsigned bits, int s) {
+  const int k = s & (K - 1);
   const unsigned moved = (bits >> k) & 1u;
   const unsigned skipped = (k & 1) ? (bits >> (K + (k >> 1))) & 1u : 0u;
   return static_cast<int>(moved + skipped);
@@ -203,26 +204,28 @@ __device__ __forceinline__ int jump_of(unsigned bits, int s, int K) {
 // every lane tracks the same state.  `at_frame(t, s)` is called (by every
 // lane) with the path's state at each frame t_hi-1 .. t_lo; returns the state
 // at t_lo.  bp: the record's backpointer words, NT threads per frame row.
-template <typename AtFrame>
-__device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int NT, int K, int s,
-                                          int t_hi, int t_lo, int lane, AtFrame at_frame) {
-  const int fpw = frames_per_word(K);
-  const int FB = K >= 8 ? 8 : 6;
-  const int NTH = 2 * FB / K + 2;
+template <int K, typename AtFrame>
+__device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int NT, int s, int t_hi,
+                                          int t_lo, int lane, AtFrame at_frame) {
+  constexpr int fpw = frames_per_word(K);
+  constexpr int FB = K >= 8 ? 8 : 6;
+  constexpr int NTH = 2 * FB / K + 2;
+  constexpr int kShift = K == 4 ? 2 : (K == 8 ? 3 : 4);
+  static_assert((1 << kShift) == K, "K is a power of two");
   for (int t = t_hi; t > t_lo;) {
     const int f = lane / NTH, dd = lane % NTH;
     const int tt = t - f;
-    const int th = s / K - dd;
+    const int th = (s >> kShift) - dd;
     uint32_t w = 0;
     if (f < FB && tt > t_lo && th >= 0) w = bp[static_cast<int64_t>(tt / fpw) * NT + th];
     const int steps = min(FB, t - t_lo);
-    const int th0 = s / K;
+    const int th0 = s >> kShift;
     for (int i = 0; i < steps; ++i) {
       const int ct = t - i;
-      const uint32_t word = __shfl_sync(0xffffffffu, w, i * NTH + (th0 - s / K));
+      const uint32_t word = __shfl_sync(0xffffffffu, w, i * NTH + (th0 - (s >> kShift)));
       // (The clamp never acts on backpointers a completed DP wrote; it keeps
       // every read inside the arena.)
-      s = max(s - jump_of(fpw == 2 ? word >> (16 * (ct & 1)) : word, s, K), 0);
+      s = max(s - jump_of<K>(fpw == 2 ? word >> (16 * (ct & 1)) : word, s), 0);
       at_frame(ct - 1, s);
     }
     t -= steps;

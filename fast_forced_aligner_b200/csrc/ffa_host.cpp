@@ -67,6 +67,14 @@ int choose_k(int64_t S, bool latency_bound) {
   return 8;
 }
 
+// States per thread for a record of the optimized route: whichever of 8 and
+// 16 runs fewer instructions per frame, modelled as warps x (fixed per-frame
+// cost + per-state cost x K), with warps = ceil(S / (32 K)).
+int piece_k(int64_t S) {
+  auto cost = [&](int64_t K) { return (S + 32 * K - 1) / (32 * K) * (24 + 6 * K); };
+  return cost(16) <= cost(8) ? 16 : 8;
+}
+
 bool chunked_record(const ffa_record& r, bool optimized) {
   return optimized && r.frames >= ffa::kPieceMinFrames;
 }
@@ -83,7 +91,7 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
   g.chunked = chunked_record(r, optimized);
-  g.K = g.chunked ? 8 : choose_k(S, latency_bound);
+  g.K = g.chunked ? piece_k(S) : choose_k(S, latency_bound);
   g.nw = static_cast<int>((S + 32 * g.K - 1) / (32 * g.K));
   if (g.chunked) {
     g.seg_log2 = ffa::kPieceSegLog2;
@@ -235,13 +243,13 @@ void sort_records(const ffa::RecordDev* recs, int64_t count, uint64_t* keys, uin
 }
 
 // Packs the slots listed in `order` (piece ids, already in packing order)
-// into bundles: runs of one slot class, at most `per_cta` slots and
-// kMaxWarps warps per CTA, a row-staged bundle also at most `row_slots`
-// rings.  Returns the bundle count; ranges[g] is the first bundle of slot
-// group g (ranges[4] = the count).
+// into bundles: runs of one slot class, about `warps_per_cta` warps per CTA
+// (at least one slot, at most kMaxWarps warps), a row-staged bundle also at
+// most `row_slots` rings.  Returns the bundle count; ranges[g] is the first
+// bundle of slot group g (ranges[4] = the count).
 template <typename ClassOf>
 int64_t make_bundles(const int32_t* order, int64_t n, ClassOf class_of, const ffa::RecordDev* recs,
-                     const ffa::PieceDev* pieces, int64_t per_cta, int64_t row_slots,
+                     const ffa::PieceDev* pieces, int64_t warps_per_cta, int64_t row_slots,
                      ffa::Bundle* bundles, int64_t ranges[5], int64_t* max_row_slots) {
   int64_t nb = 0;
   int group = 0;
@@ -251,7 +259,7 @@ int64_t make_bundles(const int32_t* order, int64_t n, ClassOf class_of, const ff
     const ffa::RecordDev& head = recs[pieces[order[k]].record];
     const int g = slot_group(cls);
     while (group < g) ranges[++group] = nb;
-    int64_t capacity = std::min<int64_t>(ffa::kMaxWarps / head.nw, per_cta);
+    int64_t capacity = std::min<int64_t>(ffa::kMaxWarps / head.nw, std::max<int64_t>(1, warps_per_cta / head.nw));
     if (head.row_mode) capacity = std::min(capacity, row_slots);
     int64_t m = 1;
     while (k + m < n && m < capacity && class_of(order[k + m]) == cls) ++m;
@@ -485,13 +493,41 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
         if (pass == 0) ++n_chunked_row;
       }
   auto class_of = [&](int32_t p) { return slot_class(recs[pieces[p].record]); };
-  // Slots per CTA grow only when the launch would otherwise need more than
-  // one wave (up to the full width once runs of pieces are in use).
+  // Warps per CTA: the launch's warps spread evenly over the SMs (one CTA
+  // runs per SM): the smallest per-CTA target whose packing still fits one
+  // wave, so that every SM gets a share and none gets more than it must.
+  int64_t first_warps = 0;
+  for (int64_t k = 0; k < n_first; ++k) first_warps += recs[pieces[order[k]].record].nw;
+  // Slots of one class are contiguous in `order`: count CTAs per class run.
+  struct ClassRun {
+    int64_t slots;
+    int nw;
+    bool row;
+  };
+  ClassRun runs[256];
+  int nruns = 0;
+  for (int64_t k = 0; k < n_first;) {
+    const uint32_t cls = class_of(order[k]);
+    const ffa::RecordDev& head = recs[pieces[order[k]].record];
+    int64_t m = 1;
+    while (k + m < n_first && class_of(order[k + m]) == cls) ++m;
+    if (nruns < 256) runs[nruns++] = ClassRun{m, head.nw, head.row_mode != 0};
+    k += m;
+  }
+  auto ctas_for = [&](int64_t target) {
+    int64_t ctas = 0;
+    for (int c = 0; c < nruns; ++c) {
+      int64_t cap = std::min<int64_t>(ffa::kMaxWarps / runs[c].nw, std::max<int64_t>(1, target / runs[c].nw));
+      if (runs[c].row) cap = std::min(cap, row_slots);
+      ctas += (runs[c].slots + cap - 1) / cap;
+    }
+    return ctas;
+  };
+  int64_t target = std::min<int64_t>(ffa::kMaxWarps, (first_warps + sms - 1) / sms);
+  while (target < ffa::kMaxWarps && ctas_for(target) > sms) ++target;
   int64_t ranges[5], max_row_slots = 1;
-  const int64_t nb = make_bundles(order, n_first, class_of, recs, pieces,
-                                  run_pieces > 1 ? ffa::kMaxWarps
-                                                 : std::max<int64_t>(1, (n_first + sms - 1) / sms),
-                                  row_slots, bundles, ranges, &max_row_slots);
+  const int64_t nb = make_bundles(order, n_first, class_of, recs, pieces, target, row_slots, bundles,
+                                  ranges, &max_row_slots);
   const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
   int max_gather_k = 8;
   for (int64_t i = 0; i < count; ++i)

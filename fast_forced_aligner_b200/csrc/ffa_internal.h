@@ -78,6 +78,10 @@ constexpr int kRepairRounds = 2;
 // one slot, back to back (each still a separate relaxed DP), so that its
 // set-up is paid once and the pass fits the GPU in about one wave.
 constexpr int kMaxRunPieces = 8;
+// States per thread of the DPs of a record of the optimized route (pieces,
+// repairs, fallback share the record's backpointer layout): 8 or 16, chosen
+// per record for the fewest instructions (wider threads amortise the
+// per-frame overhead; narrower ones pad fewer states).
 
 // One piece: frames [first, end) of a record; index is its rank in the record.
 struct PieceDev {
@@ -95,8 +99,10 @@ struct PieceState {
   int32_t end;
   int32_t flags;         // kPieceOk | kPieceFault
   int32_t region_start;  // 1 if this piece begins a region
+  int32_t start_skip;    // 1 if a skip into `start` is a legal CTC move
+  int32_t reserved[3];
 };
-static_assert(sizeof(PieceState) == 16, "PieceState layout");
+static_assert(sizeof(PieceState) == 32, "PieceState layout");
 enum : int32_t { kPieceOk = 1, kPieceFault = 2 };
 // Per-record route of the optimized mode (device-written).
 enum : int32_t { kRouteNone = 0, kRoutePending = 1, kRouteStitched = 2, kRouteFallback = 3 };

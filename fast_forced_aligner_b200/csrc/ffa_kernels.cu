@@ -462,10 +462,22 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
       const int end = k + 1 < run.pieces ? first + kPieceFrames : t1;
       const int a0 = run.pieces > 1 ? first : run.a0;
       if (lane == 0) anc[(end - 1) >> rec.seg_log2] = s_end;
-      const int s0 = warp_trace(bpr, NT, K, s_end, end - 1, a0, lane, [&](int t, int s) {
+      const int s0 = warp_trace<K>(bpr, NT, s_end, end - 1, a0, lane, [&](int t, int s) {
         if (lane == 0 && (t & hmask) == hmask) anc[t >> rec.seg_log2] = s;
       });
-      if (lane == 0) P.pstates[run.start_piece + k].start = s0;
+      if (lane == 0 && run.end_piece >= 0) {
+        // Whether a skip into the region's first state is legal: it is a
+        // token that differs from the previous token and from the blank.
+        bool skip_in = false;
+        if ((s0 & 1) && s0 >= 3) {
+          const int u = s0 >> 1;
+          const int cu = clamp_label(tgt[u], V);
+          skip_in = cu != blank && cu != clamp_label(tgt[u - 1], V);
+        }
+        PieceState& ps = P.pstates[run.start_piece + k];
+        ps.start = s0;
+        ps.start_skip = skip_in ? 1 : 0;
+      }
     }
   }
   return nchunks;
@@ -569,9 +581,11 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
     }
   }
 
-  // Pieces of the optimized route (K = 8) find their anchors by tracing;
-  // whole records walk segment maps.
-  if (chunked)
+  // Pieces of the optimized route (K = 8 or 16) find their anchors by
+  // tracing; whole records walk segment maps.
+  if (chunked && rec.kst == 16)
+    piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+  else if (chunked)
     piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
   else if (rec.kst == 4)
     piece_dp<4, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
@@ -588,45 +602,39 @@ struct JobList {
   int last[kMaxJobs];   // last piece of the merged region
 };
 
+// What one round's plan adds to a record's diagnostics.
+struct PlanStats {
+  int64_t merged = 0;   // frames of the merged regions
+  int64_t skipped = 0;  // frames the saved frontiers spared
+  int jobs = 0;
+};
+
 // Seam check and repair planning of one round of one record, by one warp.  A
 // region is a run of pieces solved as one DP; a seam is legal when the right
 // region's start state follows the left region's end state by a CTC move
 // (stay, step, or a skip into a token that differs from the previous token
-// and from the blank).  Every run of consecutive failing seams becomes one
-// repair job: the merged region resumes from the end frontier of its first
-// region and re-solves the regions after it.  Returns the record's route:
+// and from the blank -- precomputed for each region's start).  Every run of
+// consecutive failing seams becomes one repair job: the merged region
+// resumes from the end frontier of its first region and re-solves the
+// regions after it.  Returns the record's route:
 //   all seams legal, every region finite and NaN-free  -> joined (stitched)
 //   a region non-finite or with NaN                     -> conventional DP
 //   seams still failing after the last round            -> conventional DP
+//   a bounded wait gave up                               -> none (status 5)
+// Status >= 2 (rejected inputs) -> none.
 __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__ ps,
-                           int32_t* __restrict__ route, const OutputsDev& out, int round,
-                           bool final_round, JobList& jobs, int lane) {
-  if (out.status[r] != 0) {
-    if (lane == 0) route[r] = kRouteNone;
-    return kRouteNone;
-  }
+                           const OutputsDev& out, bool final_round, JobList& jobs, int lane,
+                           PlanStats& stats) {
   const int C = rec.num_pieces, P0 = rec.first_piece;
-  if (lane == 0) jobs.count = 0;
-  __syncwarp();
-
-  auto col = [&](int u) { return clamp_label(rec.targets[u], rec.V); };
-  auto legal = [&](int from, int to) {
-    const int jump = to - from;
-    if (jump == 0 || jump == 1) return true;
-    if (jump != 2 || !(to & 1)) return false;
-    const int u = to >> 1;
-    return u >= 1 && col(u) != rec.blank && col(u) != col(u - 1);
-  };
-
+  const int status = out.status[r];
   bool bad = false, fault = false, any_fail = false, run_open = false, overflow = false;
   int run_job = 0, run_first = 0, cur_first = 0, njobs = 0;
-  int64_t merged = 0, skipped = 0;
   // Piece j covers frames [j * kPieceFrames, end_of(j)); the last one ends at T.
   auto end_of = [&](int j) { return j == C - 1 ? rec.T : (j + 1) * kPieceFrames; };
   auto emit = [&](int job, int last) {
     // All lanes take the same decisions; lane 0 writes them.
-    merged += end_of(last) - run_first * kPieceFrames;
-    skipped += (job - run_first) * kPieceFrames;
+    stats.merged += end_of(last) - run_first * kPieceFrames;
+    stats.skipped += (job - run_first) * kPieceFrames;
     if (njobs == kMaxJobs) overflow = true;
     if (lane == 0 && !final_round && njobs < kMaxJobs) {
       jobs.piece[njobs] = P0 + job;
@@ -644,16 +652,20 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
     if (j < C) {
       const PieceState mine = ps[P0 + j];
       const bool next_rs = j + 1 >= C || ps[P0 + j + 1].region_start != 0;
+      const int prev_end = j > 0 ? ps[P0 + j - 1].end : 0;
       seam = mine.region_start != 0 && j > 0;
-      if (seam) fail = !legal(ps[P0 + j - 1].end, mine.start);
+      if (seam) {
+        const int jump = mine.start - prev_end;
+        fail = !(jump == 0 || jump == 1 || (jump == 2 && mine.start_skip));
+      }
       region_bad = next_rs && (mine.flags & kPieceOk) == 0;
       region_fault = next_rs && (mine.flags & kPieceFault) != 0;
     }
+    if (status != 0) break;  // rejected inputs: nothing to plan
     unsigned seams = __ballot_sync(0xffffffffu, seam);
     const unsigned fails = __ballot_sync(0xffffffffu, fail);
     bad |= __any_sync(0xffffffffu, region_bad) != 0;
     fault |= __any_sync(0xffffffffu, region_fault) != 0;
-    __syncwarp();
     // Runs of consecutive failing seams, in piece order (uniform over lanes).
     while (seams) {
       const int q = __ffs(seams) - 1;
@@ -668,32 +680,19 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
       }
     }
   }
+  if (status != 0) {
+    if (lane == 0) jobs.count = 0;
+    __syncwarp();
+    return kRouteNone;
+  }
   if (run_open) emit(run_job, C - 1);
   int decision;
   if (fault) decision = kRouteNone;
   else if (bad || (any_fail && (final_round || overflow))) decision = kRouteFallback;
   else if (!any_fail) decision = kRouteStitched;
   else decision = kRoutePending;
-  if (lane == 0) {
-    route[r] = decision;
-    jobs.count = decision == kRoutePending ? njobs : 0;
-    if (fault) {
-      out.status[r] = kStatusDeviceFault;
-      out.objective[r] = -INFINITY;
-    } else if (decision == kRouteStitched) {
-      out.stitched[r] = 1;
-    } else if (decision == kRoutePending) {
-      out.repair_passes[r] += 1;
-      out.repaired_frames[r] += merged;
-      if (out.reuse_stats) {
-        // Frames the frontiers spared, and frontier values read.
-        out.reuse_stats[4 * r + 0] += skipped;
-        out.reuse_stats[4 * r + 3] += static_cast<int64_t>(njobs) * (2 * rec.U + 1);
-      }
-    }
-    if (round == 0 && out.reuse_stats)
-      out.reuse_stats[4 * r + 2] = static_cast<int64_t>(C - 1) * (2 * rec.U + 1);
-  }
+  stats.jobs = njobs;
+  if (lane == 0) jobs.count = decision == kRoutePending ? njobs : 0;
   __syncwarp();
   return decision;
 }
@@ -736,11 +735,20 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   const bool in_slot = x.slot < nslots;
   if (x.tid == 0) sh.edge = Boundary{-INFINITY, 0};
   int chunk_base = 0;  // this slot's emission chunks so far (row staging)
+  // Warp 0 keeps the record's diagnostics and writes them once at the end.
+  int passes = 0;
+  int64_t repaired = 0, spared = 0, frontier_reads = 0;
   for (int round = 0;; ++round) {
     __syncthreads();
     if (x.warp == 0) {
-      const int decision = plan_record(rec, r, P.pstates, P.route, P.out, round,
-                                       round == kRepairRounds, jobs, x.lane);
+      PlanStats stats;
+      const int decision = plan_record(rec, r, P.pstates, P.out, round == kRepairRounds, jobs, x.lane, stats);
+      if (decision == kRoutePending) {
+        ++passes;
+        repaired += stats.merged;
+        spared += stats.skipped;
+        frontier_reads += static_cast<int64_t>(stats.jobs) * (2 * rec.U + 1);
+      }
       if (x.lane == 0) route_s = decision;
     }
     __syncthreads();
@@ -765,14 +773,37 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
         run.new_region = false;
         run.chunk_base = chunk_base;
         if (x.tl == 0) sh.slot_fault[x.slot] = 0;
-        chunk_base += piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+        chunk_base += rec.kst == 16 ? piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P)
+                                    : piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
       }
+    }
+  }
+  if (x.tid == 0) {
+    // Route and diagnostics (alignment.py:101-129).
+    const int route = route_s;
+    P.route[r] = route;
+    if (route == kRouteNone && P.out.status[r] == 0) {
+      P.out.status[r] = kStatusDeviceFault;
+      P.out.objective[r] = -INFINITY;
+    }
+    if (route == kRouteStitched) P.out.stitched[r] = 1;
+    P.out.repair_passes[r] = passes;
+    P.out.repaired_frames[r] = repaired;
+    if (P.out.reuse_stats) {
+      P.out.reuse_stats[4 * r + 0] = spared;
+      P.out.reuse_stats[4 * r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
+      P.out.reuse_stats[4 * r + 3] = frontier_reads;
     }
   }
   if (route_s == kRouteFallback && x.slot == 0) {
     PieceRun run{0, 0, rec.T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, chunk_base};
     if (x.tl == 0) sh.slot_fault[0] = 0;
-    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+    // The record's backpointers use the pieces' layout (the record's states
+    // per thread), so its anchors come from traces as well.
+    if (rec.kst == 16)
+      piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+    else
+      piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
   }
 }
 
@@ -806,8 +837,11 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
       int32_t* p = path[warp];
       const int s_end = anchors[rec.seg_off + c];
       if (lane == 0) p[b - 1 - a] = s_end;
-      warp_trace(bp_arena + rec.bp_off, rec.nw * 32, rec.kst, s_end, b - 1, a, lane,
-                 [&](int t, int s) { if (lane == 0) p[t - a] = s; });
+      auto keep = [&](int t, int s) { if (lane == 0) p[t - a] = s; };
+      const uint32_t* bpr = bp_arena + rec.bp_off;
+      if (rec.kst == 4) warp_trace<4>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
+      else if (rec.kst == 8) warp_trace<8>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
+      else warp_trace<16>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
       __syncwarp();
       const float* e = rec.emissions;
       for (int t = a + lane; t < b; t += 32) {
@@ -845,13 +879,22 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
     for (int k = threadIdx.x; k < n; k += 32 * kFillWarps) window[k] = scores[base + k];
     __syncthreads();
     if (threadIdx.x == 0) {
+      // The next 8 values load while the current 8 are added.
       int k = 0;
-      for (; k + 8 <= n; k += 8) {
-        float x[8];
+      float cur[8], nxt[8];
+      if (n >= 8) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) x[q] = window[k + q];
+        for (int q = 0; q < 8; ++q) cur[q] = window[q];
+        for (k = 8; k + 8 <= n; k += 8) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, x[q]);
+          for (int q = 0; q < 8; ++q) nxt[q] = window[k + q];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
       }
       for (; k < n; ++k) obj = __fadd_rn(obj, window[k]);
     }

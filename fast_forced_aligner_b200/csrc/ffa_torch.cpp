@@ -7,7 +7,7 @@
 // from the caching allocator.  Everything below the ffa_* calls is plain
 // pointers and sizes.  Per call it makes two caching-allocator requests (one
 // block holds every output tensor, one the workspace) and stages descriptors
-// in a reused host buffer, so the host cost stays a few microseconds.
+// in a reused pinned host buffer, so the host cost stays a few microseconds.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDACachingAllocator.h>
@@ -46,13 +46,64 @@ struct StreamRecorder {
   }
 };
 
-// Host staging: a per-thread pageable buffer reused across calls.  A
-// host-to-device cudaMemcpyAsync from pageable memory copies the bytes out
-// before it returns, so the next call may refill the buffer at once.
-void* host_staging(size_t bytes) {
-  thread_local std::vector<unsigned char> buffer;
-  if (buffer.size() < bytes) buffer.resize(bytes);
-  return buffer.data();
+// Host staging for the descriptor upload: pinned, so that the upload is a
+// plain DMA (from pageable memory the driver copies the bytes itself first,
+// which costs tens of microseconds of host time).  Each thread keeps a small
+// ring of pinned buffers per device; a buffer is reused once the event
+// recorded after its upload has completed, and a buffer is (re)allocated only
+// while the ring grows to the batch sizes in use.
+class PinnedStaging {
+ public:
+  // A buffer of at least `bytes`, not in use by an upload still pending.
+  void* acquire(size_t bytes) {
+    for (int tries = 0; tries < 2 * kSlots; ++tries) {
+      Slot& slot = slots_[next_];
+      current_ = next_;
+      next_ = (next_ + 1) % kSlots;
+      if (slot.pending && cudaEventQuery(slot.done) != cudaSuccess) continue;
+      slot.pending = false;
+      if (slot.capacity < bytes) {
+        if (slot.ptr != nullptr) cudaFreeHost(slot.ptr);
+        slot.ptr = nullptr;
+        slot.capacity = 0;
+        const size_t cap = std::max<size_t>(bytes, size_t{64} << 10);
+        TORCH_CHECK(cudaHostAlloc(&slot.ptr, cap, cudaHostAllocPortable) == cudaSuccess,
+                    "fast_forced_aligner_b200: cannot allocate pinned staging");
+        slot.capacity = cap;
+      }
+      if (slot.done == nullptr)
+        TORCH_CHECK(cudaEventCreateWithFlags(&slot.done, cudaEventDisableTiming) == cudaSuccess,
+                    "fast_forced_aligner_b200: cannot create a staging event");
+      return slot.ptr;
+    }
+    // Every buffer still pending: wait for the oldest.
+    Slot& slot = slots_[next_];
+    cudaEventSynchronize(slot.done);
+    slot.pending = false;
+    return acquire(bytes);
+  }
+  // Marks the buffer handed out last as in use until the stream passes here.
+  void release(cudaStream_t stream) {
+    Slot& slot = slots_[current_];
+    if (cudaEventRecord(slot.done, stream) == cudaSuccess) slot.pending = true;
+  }
+
+ private:
+  static constexpr int kSlots = 4;
+  struct Slot {
+    void* ptr = nullptr;
+    size_t capacity = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+  };
+  Slot slots_[kSlots];
+  int next_ = 0, current_ = 0;
+};
+
+PinnedStaging& staging_for(int device) {
+  thread_local PinnedStaging rings[64];
+  TORCH_CHECK(device >= 0 && device < 64, "fast_forced_aligner_b200: device index out of range");
+  return rings[device];
 }
 
 // Device scratch from the caching allocator on the current stream; returned
@@ -141,9 +192,11 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> run_align(
                   t[3].data_ptr<float>(), t[4].data_ptr<int32_t>(), t[5].data_ptr<int32_t>(),
                   t[6].data_ptr<int64_t>(), t[7].data_ptr<int64_t>(), t[8].data_ptr<int32_t>(),
                   reuse ? t[9].data_ptr<int64_t>() : nullptr};
-  const int rc = ffa_align(recs.data(), count, cmode, flags, mask, &out, host_staging(sizes.staging_bytes),
+  PinnedStaging& staging = staging_for(device.index());
+  const int rc = ffa_align(recs.data(), count, cmode, flags, mask, &out, staging.acquire(sizes.staging_bytes),
                            sizes.staging_bytes, workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                            reinterpret_cast<ffa_stream_t>(stream.stream()));
+  if (rc == FFA_OK) staging.release(stream.stream());
   check_status(rc);
   return {std::move(t), std::move(lengths)};
 }
@@ -266,11 +319,13 @@ at::Tensor emission_validity(at::TensorList emissions) {
   check_status(ffa_emission_validity_query(recs.data(), count, &sizes));
   auto result = at::empty({count}, emissions[0].options().dtype(at::kBool));
   auto workspace = device_scratch(sizes.workspace_bytes);
+  PinnedStaging& staging = staging_for(device.index());
   const int rc = ffa_emission_validity(recs.data(), count,
                                        reinterpret_cast<uint8_t*>(result.data_ptr<bool>()),
-                                       host_staging(sizes.staging_bytes), sizes.staging_bytes,
+                                       staging.acquire(sizes.staging_bytes), sizes.staging_bytes,
                                        workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                                        reinterpret_cast<ffa_stream_t>(stream.stream()));
+  if (rc == FFA_OK) staging.release(stream.stream());
   check_status(rc);
   return result;
 }
@@ -310,10 +365,12 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
   check_status(ffa_check_targets_query(recs.data(), count, &sizes));
   auto status = at::empty({count}, emissions[0].options().dtype(at::kInt));
   auto workspace = device_scratch(sizes.workspace_bytes);
+  PinnedStaging& staging = staging_for(device.index());
   const int rc = ffa_check_targets(recs.data(), count, status.data_ptr<int32_t>(),
-                                   host_staging(sizes.staging_bytes), sizes.staging_bytes,
+                                   staging.acquire(sizes.staging_bytes), sizes.staging_bytes,
                                    workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
                                    reinterpret_cast<ffa_stream_t>(stream.stream()));
+  if (rc == FFA_OK) staging.release(stream.stream());
   check_status(rc);
   return status;
 }
