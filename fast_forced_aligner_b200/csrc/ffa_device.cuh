@@ -120,15 +120,15 @@ static_assert(kForwardHeader % 128 == 0, "ring offset alignment");
 // Selection: stay, then step if strictly greater, then skip if strictly
 // greater and legal (alignment.cu:418-424); one fp32 add per cell.  Also
 // advances the ancestor deltas d (distance back to the state at the end of the
-// previous traceback segment).  Returns the frame's backpointers as two bit
-// planes: bit k = "moved" (jump >= 1) of state k, bit K+q = "skipped"
-// (jump == 2) of token q = k/2, so jump = moved + skipped.
+// previous traceback segment).  Returns the frame's 2K-bit jump codes; the
+// states' selections are independent of one another within a frame, and
+// their codes are gathered by a balanced OR tree.
 template <int K>
 __device__ __forceinline__ unsigned dp_frame(float (&a)[K], int (&d)[K], float p1, int pd, float eb,
                                              const float (&et)[K / 2], unsigned skip) {
   float na[K];
   int nd[K];
-  unsigned bits = 0;
+  unsigned m[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     const float x1 = k >= 1 ? a[k - 1] : p1;
@@ -142,17 +142,21 @@ __device__ __forceinline__ unsigned dp_frame(float (&a)[K], int (&d)[K], float p
       const bool j2 = ((skip >> (k >> 1)) & 1u) && x2 > b;
       b = j2 ? x2 : b;
       n = j2 ? d2 + 2 : n;
-      bits |= (static_cast<unsigned>(c || j2) << k) | (static_cast<unsigned>(j2) << (K + (k >> 1)));
+      m[k] = (j2 ? 2u : (c ? 1u : 0u)) << (2 * k);
       na[k] = __fadd_rn(b, et[k >> 1]);
     } else {
-      bits |= static_cast<unsigned>(c) << k;
+      m[k] = (c ? 1u : 0u) << (2 * k);
       na[k] = __fadd_rn(b, eb);
     }
     nd[k] = n;
   }
 #pragma unroll
+  for (int w = 1; w < K; w *= 2)
+#pragma unroll
+    for (int k = 0; k + w < K; k += 2 * w) m[k] |= m[k + w];
+#pragma unroll
   for (int k = 0; k < K; ++k) { a[k] = na[k]; d[k] = nd[k]; }
-  return bits;
+  return m[0];
 }
 
 // The same frame step without ancestor deltas, for runs whose path is found
@@ -161,7 +165,7 @@ template <int K>
 __device__ __forceinline__ unsigned dp_frame_plain(float (&a)[K], float p1, float eb,
                                                    const float (&et)[K / 2], unsigned skip) {
   float na[K];
-  unsigned bits = 0;
+  unsigned m[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     const float x1 = k >= 1 ? a[k - 1] : p1;
@@ -171,61 +175,56 @@ __device__ __forceinline__ unsigned dp_frame_plain(float (&a)[K], float p1, floa
       const float x2 = k >= 2 ? a[k - 2] : p1;
       const bool j2 = ((skip >> (k >> 1)) & 1u) && x2 > b;
       b = j2 ? x2 : b;
-      bits |= (static_cast<unsigned>(c || j2) << k) | (static_cast<unsigned>(j2) << (K + (k >> 1)));
+      m[k] = (j2 ? 2u : (c ? 1u : 0u)) << (2 * k);
       na[k] = __fadd_rn(b, et[k >> 1]);
     } else {
-      bits |= static_cast<unsigned>(c) << k;
+      m[k] = (c ? 1u : 0u) << (2 * k);
       na[k] = __fadd_rn(b, eb);
     }
   }
 #pragma unroll
+  for (int w = 1; w < K; w *= 2)
+#pragma unroll
+    for (int k = 0; k + w < K; k += 2 * w) m[k] |= m[k + w];
+#pragma unroll
   for (int k = 0; k < K; ++k) a[k] = na[k];
-  return bits;
+  return m[0];
 }
 
-// Backpointer word geometry: 1.5*K bits per frame and thread, packed in
-// 16-bit lanes of 32-bit words when they fit (two frames per word).
-__host__ __device__ constexpr int frames_per_word(int K) { return 3 * K / 2 <= 16 ? 2 : 1; }
-
-// Jump of state s (owned by a thread with K states) from one frame's bits.
+// Stores one thread's 2K jump-code bits of a frame into its row (K = 4, 8,
+// 16: a byte, a halfword or a word at state K*tl).
 template <int K>
-__device__ __forceinline__ int jump_of(unsigned bits, int s) {
-  const int k = s & (K - 1);
-  const unsigned moved = (bits >> k) & 1u;
-  const unsigned skipped = (k & 1) ? (bits >> (K + (k >> 1))) & 1u : 0u;
-  return static_cast<int>(moved + skipped);
+__device__ __forceinline__ void store_codes(uint8_t* row, int tl, unsigned bits) {
+  if constexpr (K == 16) reinterpret_cast<uint32_t*>(row)[tl] = bits;
+  else if constexpr (K == 8) reinterpret_cast<uint16_t*>(row)[tl] = static_cast<uint16_t>(bits);
+  else reinterpret_cast<uint8_t*>(row)[tl] = static_cast<uint8_t>(bits);
 }
 
 // One warp walks a path back through the backpointers, from state s at frame
 // t_hi down to frame t_lo (path[t-1] = path[t] - jump(t, path[t]),
 // alignment.cu:656-659).  The path moves at most 2 states per frame, so over
-// FB frames it stays within 2*FB/K + 2 threads' words: the warp loads those
-// FB x NTH words in one round trip, then steps through them with shuffles;
-// every lane tracks the same state.  `at_frame(t, s)` is called (by every
-// lane) with the path's state at each frame t_hi-1 .. t_lo; returns the state
-// at t_lo.  bp: the record's backpointer words, NT threads per frame row.
-template <int K, typename AtFrame>
-__device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int NT, int s, int t_hi,
-                                          int t_lo, int lane, AtFrame at_frame) {
-  constexpr int fpw = frames_per_word(K);
-  constexpr int FB = K >= 8 ? 8 : 6;
-  constexpr int NTH = 2 * FB / K + 2;
-  constexpr int kShift = K == 4 ? 2 : (K == 8 ? 3 : 4);
-  static_assert((1 << kShift) == K, "K is a power of two");
+// FB = 10 frames it stays within 3 words of the start word: the warp loads
+// those FB x 3 words in one round trip, then steps through them with
+// shuffles; every lane tracks the same state.  `at_frame(t, s)` is called (by
+// every lane) with the path's state at each frame t_hi-1 .. t_lo; returns the
+// state at t_lo.  bp: the record's rows, row_words words per frame.
+template <typename AtFrame>
+__device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int row_words, int s,
+                                          int t_hi, int t_lo, int lane, AtFrame at_frame) {
+  constexpr int FB = 10, NW = 3;
   for (int t = t_hi; t > t_lo;) {
-    const int f = lane / NTH, dd = lane % NTH;
+    const int f = lane / NW, dd = lane % NW;
     const int tt = t - f;
-    const int th = (s >> kShift) - dd;
+    const int w0 = s >> 4;
     uint32_t w = 0;
-    if (f < FB && tt > t_lo && th >= 0) w = bp[static_cast<int64_t>(tt / fpw) * NT + th];
+    if (f < FB && tt > t_lo && w0 - dd >= 0) w = bp[static_cast<int64_t>(tt) * row_words + (w0 - dd)];
     const int steps = min(FB, t - t_lo);
-    const int th0 = s >> kShift;
     for (int i = 0; i < steps; ++i) {
       const int ct = t - i;
-      const uint32_t word = __shfl_sync(0xffffffffu, w, i * NTH + (th0 - (s >> kShift)));
+      const uint32_t word = __shfl_sync(0xffffffffu, w, i * NW + (w0 - (s >> 4)));
       // (The clamp never acts on backpointers a completed DP wrote; it keeps
       // every read inside the arena.)
-      s = max(s - jump_of<K>(fpw == 2 ? word >> (16 * (ct & 1)) : word, s), 0);
+      s = max(s - static_cast<int>((word >> (2 * (s & 15))) & 3u), 0);
       at_frame(ct - 1, s);
     }
     t -= steps;

@@ -105,12 +105,12 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   }
   const int64_t H = int64_t{1} << g.seg_log2;
   g.segments = (r.frames + H - 1) / H;
-  const int64_t nt = 32 * static_cast<int64_t>(g.nw);
-  const int fpw = ffa::frames_per_word_host(g.K);
-  g.bp_words = (r.frames + fpw - 1) / fpw * nt;
-  g.map_elems = g.segments * nt * g.K;
+  // Backpointer rows, frontiers and maps do not depend on the thread layout.
+  const int S32 = static_cast<int>(S);
+  g.bp_words = r.frames * ffa::bp_row_words(S32);
+  g.map_elems = g.segments * ffa::state_stride(S32);
   g.pieces = g.chunked ? piece_count(r.frames) : 1;
-  g.frontier_elems = g.chunked ? g.pieces * nt * g.K : 0;
+  g.frontier_elems = g.chunked ? g.pieces * ffa::state_stride(S32) : 0;
   return g;
 }
 
@@ -588,11 +588,18 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       ffa::kMaxWarps - 1,
       row_slot_bytes ? static_cast<int64_t>((ffa::kSmemBudget - 2048 - header) / row_slot_bytes) : 1);
   const unsigned finish_row_smem = static_cast<unsigned>(header + finish_slots * row_slot_bytes);
-  err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), true, rv, finish_row_smem, s);
-  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
-  err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), false, 0,
-                           gather_smem, s);
-  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  // Round 0 spreads each record's repair jobs over up to four CTAs while the
+  // records leave SMs free; later rounds take one CTA per record.
+  const int spread = static_cast<int>(std::clamp<int64_t>(sms / std::max<int64_t>(nchunked, 1), 1, 4));
+  for (int phase = 0; phase < 2; ++phase) {
+    const int per = phase == 0 ? spread : 1;
+    err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), phase, per, true, rv,
+                             finish_row_smem, s);
+    if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+    err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), phase,
+                             per, false, 0, gather_smem, s);
+    if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  }
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
   err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
                          static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, s);

@@ -33,10 +33,16 @@ constexpr unsigned long long kDrainNs = 50000000ull;   // 50 ms
 // Per-record status written when a bounded device wait gave up.
 constexpr int kStatusDeviceFault = 5;
 constexpr size_t kSmemBudget = 227 * 1024;
-// Backpointers: 1.5*K bits per frame and thread (a "moved" bit per state and
-// a "skipped" bit per token), two frames per 32-bit word when they fit.
-constexpr int frames_per_word_host(int K) { return 3 * K / 2 <= 16 ? 2 : 1; }
-// Traceback segment length bounds (power of two, multiple of kFramesPerWord).
+// Backpointers: a 2-bit jump code per state and frame (0 stay, 1 step from
+// s-1, 2 skip from s-2), in one row per frame of bp_row_words(S) 32-bit
+// words, state s at bits 2*(s % 16) of word s / 16.  The layout does not
+// depend on how states are spread over threads, so different DPs of one
+// record (wide threads for throughput, narrow ones for latency) share it.
+__host__ __device__ constexpr int bp_row_words(int S) { return (S + 63) / 64 * 4; }
+// Per-state arrays (frontiers, segment maps) of a record: one stride for all
+// thread layouts (K <= 16, 32 threads per warp).
+__host__ __device__ constexpr int state_stride(int S) { return (S + 511) / 512 * 512; }
+// Traceback segment length bounds (power of two).
 constexpr int kMinSegLog2 = 5;
 constexpr int kMaxSegLog2 = 10;
 constexpr int kFillWarps = 8;
@@ -46,7 +52,7 @@ struct RecordDev {
   const float* emissions;   // [T, V] fp32, caller memory
   const int64_t* targets;   // [U] int64, caller memory (may be null if U == 0)
   int64_t out_off;          // first frame of this record in labels/scores
-  int64_t bp_off;           // first uint32 word in the backpointer arena
+  int64_t bp_off;           // first uint32 word of the record's backpointer rows
   int64_t map_off;          // first uint16 entry in the segment-map arena
   int32_t T, V, U, blank;
   int32_t seg_off;          // first anchor (one per traceback segment)
@@ -97,10 +103,13 @@ static_assert(sizeof(PieceDev) == 16, "PieceDev layout");
 struct PieceState {
   int32_t start;
   int32_t end;
-  int32_t flags;         // kPieceOk | kPieceFault
-  int32_t region_start;  // 1 if this piece begins a region
-  int32_t start_skip;    // 1 if a skip into `start` is a legal CTC move
-  int32_t reserved[3];
+  int32_t flags;            // kPieceOk | kPieceFault
+  int32_t start_skip;       // 1 if a skip into `start` is a legal CTC move
+  // 1 if this piece begins a region, as planned by round k (region_start[0]:
+  // after the first pass).  Round k reads entry k and writes entry k + 1, so
+  // CTAs that plan the same round concurrently only write equal values into
+  // an entry that nobody reads during that round.
+  int32_t region_start[4];
 };
 static_assert(sizeof(PieceState) == 32, "PieceState layout");
 enum : int32_t { kPieceOk = 1, kPieceFault = 2 };
@@ -181,9 +190,11 @@ struct ForwardParams {
 cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
                            int row_vocab, unsigned smem_bytes, cudaStream_t stream);
 // Everything after the first pass of the optimized route -- seam plans,
-// repair rounds, conventional fallback -- one CTA per listed record.
+// repair rounds, conventional fallback: phase 0 (round 0, ctas_per_record
+// CTAs per listed record), then phase 1 (the rest, one CTA per record).
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          bool row_mode, int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+                          int phase, int ctas_per_record, bool row_mode, int row_vocab,
+                          unsigned smem_bytes, cudaStream_t stream);
 // Traceback fill of every segment; for records of the optimized route the
 // last fill CTA of the record also folds the objective of a joined path.
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,

@@ -81,7 +81,6 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
                                         ForwardShared& sh, unsigned char* smem_raw,
                                         const ForwardParams& P) {
   constexpr int KT = K / 2;
-  constexpr int FPW = frames_per_word(K);
   constexpr int kGroupsPerPiece = kPieceFrames / kGroup;
   const int tl = x.tl, lane = x.lane, warp = x.warp, NT = x.NT, slot = x.slot;
   const int T = rec.T, U = rec.U, blank = rec.blank;
@@ -172,9 +171,13 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   x.sync();
 
   const int hmask = (1 << rec.seg_log2) - 1;
-  uint32_t* bp = P.bp + rec.bp_off + tl;
+  // Backpointer rows (a 2-bit code per state, bp_row_words(S) words per
+  // frame); a thread whose states start past the row has none to store.
+  const int row_words = bp_row_words(S);
+  uint8_t* bp_rows = reinterpret_cast<uint8_t*>(P.bp + rec.bp_off);
+  const bool stores_codes = K * tl < row_words * 16;
   uint16_t* maps = P.maps + rec.map_off + K * tl;
-  const int64_t map_stride = static_cast<int64_t>(NT) * K;
+  const int64_t map_stride = state_stride(S);
   const Boundary* left = x.lw > 0 ? &sh.bnd[0][warp - 1] : &sh.edge;
   const int left_stride = x.lw > 0 ? kMaxWarps : 0;
   // Skip frames in which none of this warp's states lies in the reachable
@@ -190,8 +193,6 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   const int64_t hi64 = static_cast<int64_t>(w_hi) - S + 2 * static_cast<int64_t>(T);
   const bool never = hi64 < 0;
   const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
-  uint32_t word = 0;
-
   auto load = [&](int f, int j, const float* rows, float& eb, float (&et)[KT]) {
     if constexpr (kRow) {
       const float* row = rows + j * V;
@@ -215,9 +216,8 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
     for (int q = 0; q < KT; ++q)
       dst[q] = static_cast<uint32_t>(d[2 * q]) | (static_cast<uint32_t>(d[2 * q + 1]) << 16);
   };
-  auto store_word = [&](int t) {
-    bp[static_cast<int64_t>(t / FPW) * NT] = word;
-    word = 0;
+  auto store_codes_at = [&](int t, unsigned bits) {
+    if (stores_codes) store_codes<K>(bp_rows + static_cast<int64_t>(t) * row_words * 4, tl, bits);
   };
   auto frame = [&](int t, int j, const float* rows) {
     float eb, et[KT];
@@ -240,13 +240,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
       if (lane == 0) p1 = nb.alpha;
       bits = dp_frame_plain<K>(a, p1, eb, et, skip);
     }
-    if constexpr (FPW == 2) {
-      word |= bits << (16 * (t & 1));
-      if (t & 1) store_word(t);
-    } else {
-      word = bits;
-      store_word(t);
-    }
+    store_codes_at(t, bits);
     if (kMaps && j == kGroup - 1 && (t & hmask) == hmask) store_map(t);
     if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], kMaps ? d[K - 1] : 0};
     x.sync();
@@ -331,7 +325,6 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
         }
         x.sync();
       }
-      if constexpr (FPW == 2) word = 0;
     } else if (seeded) {
       float eb, et[KT];
       load(tg - t0, 0, rows, eb, et);
@@ -383,9 +376,8 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
       for (int c = cb + max(0, nchunks - kRowRing); c < cb + nchunks; ++c)
         mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1, kDrainNs);
   }
-  {  // a word or a map the last frame left open
+  {  // a map the last frame left open
     const int tl_ = t1 - 1;
-    if (FPW == 2 && (tl_ & 1) == 0 && tl_ > t0) store_word(tl_);
     if (kMaps && (tl_ & hmask) != hmask) store_map(tl_);
   }
   if (fault) sh.slot_fault[slot] = 1;
@@ -414,7 +406,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
     } else {
       best = -INFINITY;
       end_state = 0x7fffffff;
-      for (int w = x.first_warp; w < x.first_warp + rec.nw; ++w) {
+      for (int w = x.first_warp; w < x.first_warp + NT / 32; ++w) {
         const float v = sh.red_val[k][w];
         const int i = sh.red_idx[k][w];
         if (v > best || (v == best && i < end_state)) { best = v; end_state = i; }
@@ -430,7 +422,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
       PieceState& pe = P.pstates[run.end_piece + k];
       pe.end = end_state;
       pe.flags = (finite && !nan && !slot_fault ? kPieceOk : 0) | (slot_fault ? kPieceFault : 0);
-      if (run.new_region) pe.region_start = 1;
+      if (run.new_region) pe.region_start[0] = 1;
     }
     const bool trace = finite && !slot_fault && !(run.end_piece >= 0 && nan);
     if constexpr (kMaps) {
@@ -455,14 +447,14 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
     // Warp lw traces pieces lw, lw + nw, ...: from the end state back to the
     // piece's (or the repaired region's) first frame.
     const uint32_t* bpr = P.bp + rec.bp_off;
-    for (int k = x.lw; k < run.pieces; k += rec.nw) {
+    for (int k = x.lw; k < run.pieces; k += NT / 32) {
       const int s_end = sh.red_idx[k][x.first_warp];
       if (s_end < 0) continue;
       const int first = t0 + k * kPieceFrames;
       const int end = k + 1 < run.pieces ? first + kPieceFrames : t1;
       const int a0 = run.pieces > 1 ? first : run.a0;
       if (lane == 0) anc[(end - 1) >> rec.seg_log2] = s_end;
-      const int s0 = warp_trace<K>(bpr, NT, s_end, end - 1, a0, lane, [&](int t, int s) {
+      const int s0 = warp_trace(bpr, row_words, s_end, end - 1, a0, lane, [&](int t, int s) {
         if (lane == 0 && (t & hmask) == hmask) anc[t >> rec.seg_log2] = s;
       });
       if (lane == 0 && run.end_piece >= 0) {
@@ -575,7 +567,7 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
       run.t1 = piece.index + m == rec.num_pieces ? T : piece.first + m * kPieceFrames;
       run.pieces = m;
       run.init = piece.first == 0 ? kInitRecord : kInitFree;
-      run.frontier_out = P.frontiers + rec.frontier_off + static_cast<int64_t>(piece.index) * x.NT * rec.kst;
+      run.frontier_out = P.frontiers + rec.frontier_off + static_cast<int64_t>(piece.index) * state_stride(2 * U + 1);
       run.end_piece = run.start_piece = p;
       run.new_region = true;
     }
@@ -622,9 +614,11 @@ struct PlanStats {
 //   seams still failing after the last round            -> conventional DP
 //   a bounded wait gave up                               -> none (status 5)
 // Status >= 2 (rejected inputs) -> none.
+// write_regions: this warp records the next round's region starts (one
+// planner per record does; others that plan the same round only read).
 __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__ ps,
-                           const OutputsDev& out, bool final_round, JobList& jobs, int lane,
-                           PlanStats& stats) {
+                           const OutputsDev& out, int round, bool final_round, bool write_regions,
+                           JobList& jobs, int lane, PlanStats& stats) {
   const int C = rec.num_pieces, P0 = rec.first_piece;
   const int status = out.status[r];
   bool bad = false, fault = false, any_fail = false, run_open = false, overflow = false;
@@ -640,7 +634,6 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
       jobs.piece[njobs] = P0 + job;
       jobs.first[njobs] = P0 + run_first;
       jobs.last[njobs] = P0 + last;
-      for (int k = job; k <= last; ++k) ps[P0 + k].region_start = 0;
     }
     ++njobs;
   };
@@ -651,9 +644,11 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
     bool seam = false, fail = false, region_bad = false, region_fault = false;
     if (j < C) {
       const PieceState mine = ps[P0 + j];
-      const bool next_rs = j + 1 >= C || ps[P0 + j + 1].region_start != 0;
+      const bool next_rs = j + 1 >= C || ps[P0 + j + 1].region_start[round] != 0;
       const int prev_end = j > 0 ? ps[P0 + j - 1].end : 0;
-      seam = mine.region_start != 0 && j > 0;
+      seam = mine.region_start[round] != 0 && j > 0;
+      // The next round's regions start as this round's; merges clear below.
+      if (!final_round && write_regions) ps[P0 + j].region_start[round + 1] = mine.region_start[round];
       if (seam) {
         const int jump = mine.start - prev_end;
         fail = !(jump == 0 || jump == 1 || (jump == 2 && mine.start_skip));
@@ -692,6 +687,14 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
   else if (!any_fail) decision = kRouteStitched;
   else decision = kRoutePending;
   stats.jobs = njobs;
+  // Merge the failing runs into the next round's regions only when there is
+  // a next round for this record: a record already routed keeps its regions,
+  // so a later planner of it sees the same bad or joined regions again.
+  __syncwarp();  // the lanes' copies above land before lane 0 clears
+  if (lane == 0 && decision == kRoutePending && write_regions) {
+    for (int q = 0; q < njobs && q < kMaxJobs; ++q)
+      for (int k = jobs.piece[q]; k <= jobs.last[q]; ++k) ps[k].region_start[round + 1] = 0;
+  }
   if (lane == 0) jobs.count = decision == kRoutePending ? njobs : 0;
   __syncwarp();
   return decision;
@@ -702,26 +705,35 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
 constexpr size_t kFinishDynamicSmem = kSmemBudget - 2048;
 static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
 
-// Everything after the first pass of one record of the optimized route, in
-// one CTA: kRepairRounds rounds of seam planning (warp 0) and repair jobs
-// (slots of nw warps, in parallel), the final plan, and the conventional DP
-// when the route cannot join the record.  Records need nothing from one
-// another, so no launch boundary separates the rounds.
+// Everything after the first pass of the optimized route, in two launches
+// (records need nothing from one another):
+//   phase 0  R CTAs per record: each plans round 0 (the same plan) and runs
+//            the round's repair jobs j with j % R == its index, so a record's
+//            jobs spread over R SMs;
+//   phase 1  one CTA per record: rounds 1 .. kRepairRounds of planning
+//            (warp 0) and repairs (slots of nw warps, in parallel), the final
+//            plan, the conventional DP when the route cannot join the record,
+//            and the record's route and diagnostics.
 template <bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
-ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records) {
+ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records, int phase,
+                 int ctas_per_record) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
   __shared__ JobList jobs;
   __shared__ int route_s;
-  const int r = records[blockIdx.x];
+  const int part = static_cast<int>(blockIdx.x % ctas_per_record);
+  const int r = records[blockIdx.x / ctas_per_record];
   const RecordDev rec = P.recs[r];
   SlotCtx x;
   x.tid = threadIdx.x;
   x.warp = x.tid >> 5;
   x.lane = x.tid & 31;
   x.r = r;
-  const int nw = rec.nw;
+  // Repairs and the fallback run 8 states per thread (shorter per-frame
+  // chains than the first pass's 16): the backpointer rows do not depend on
+  // the thread layout.
+  const int nw = (2 * rec.U + 1 + 255) / 256;
   // Slot barriers use ids 1.. (id 0 is __syncthreads); row-staged slots also
   // need a ring each.
   int nslots = min(kMaxWarps - 1, kMaxWarps / nw);
@@ -738,11 +750,14 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   // Warp 0 keeps the record's diagnostics and writes them once at the end.
   int passes = 0;
   int64_t repaired = 0, spared = 0, frontier_reads = 0;
-  for (int round = 0;; ++round) {
+  const int first_round = phase == 0 ? 0 : 1;
+  const int last_round = phase == 0 ? 0 : kRepairRounds;
+  for (int round = first_round; round <= last_round; ++round) {
     __syncthreads();
     if (x.warp == 0) {
       PlanStats stats;
-      const int decision = plan_record(rec, r, P.pstates, P.out, round == kRepairRounds, jobs, x.lane, stats);
+      const int decision = plan_record(rec, r, P.pstates, P.out, round, round == kRepairRounds, part == 0,
+                                       jobs, x.lane, stats);
       if (decision == kRoutePending) {
         ++passes;
         repaired += stats.merged;
@@ -754,9 +769,9 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
     __syncthreads();
     if (route_s != kRoutePending) break;
     const int n = jobs.count;
-    const int64_t fstride = static_cast<int64_t>(x.NT) * rec.kst;
+    const int64_t fstride = state_stride(2 * rec.U + 1);
     if (in_slot) {
-      for (int j = x.slot; j < n; j += nslots) {
+      for (int j = part + x.slot * ctas_per_record; j < n; j += nslots * ctas_per_record) {
         const int p = jobs.piece[j];
         const int idx = p - rec.first_piece;
         const int last = jobs.last[j] - rec.first_piece;
@@ -773,13 +788,25 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
         run.new_region = false;
         run.chunk_base = chunk_base;
         if (x.tl == 0) sh.slot_fault[x.slot] = 0;
-        chunk_base += rec.kst == 16 ? piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P)
-                                    : piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+        chunk_base += piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
       }
     }
   }
+  if (phase == 0) {
+    // Round 0's share of the diagnostics, once per record.
+    if (x.tid == 0 && part == 0) {
+      P.out.repair_passes[r] = passes;
+      P.out.repaired_frames[r] = repaired;
+      if (P.out.reuse_stats) {
+        P.out.reuse_stats[4 * r + 0] = spared;
+        P.out.reuse_stats[4 * r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
+        P.out.reuse_stats[4 * r + 3] = frontier_reads;
+      }
+    }
+    return;
+  }
   if (x.tid == 0) {
-    // Route and diagnostics (alignment.py:101-129).
+    // Route and diagnostics (alignment.py:101-129), adding to round 0's.
     const int route = route_s;
     P.route[r] = route;
     if (route == kRouteNone && P.out.status[r] == 0) {
@@ -787,23 +814,17 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
       P.out.objective[r] = -INFINITY;
     }
     if (route == kRouteStitched) P.out.stitched[r] = 1;
-    P.out.repair_passes[r] = passes;
-    P.out.repaired_frames[r] = repaired;
+    P.out.repair_passes[r] += passes;
+    P.out.repaired_frames[r] += repaired;
     if (P.out.reuse_stats) {
-      P.out.reuse_stats[4 * r + 0] = spared;
-      P.out.reuse_stats[4 * r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
-      P.out.reuse_stats[4 * r + 3] = frontier_reads;
+      P.out.reuse_stats[4 * r + 0] += spared;
+      P.out.reuse_stats[4 * r + 3] += frontier_reads;
     }
   }
   if (route_s == kRouteFallback && x.slot == 0) {
     PieceRun run{0, 0, rec.T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, chunk_base};
     if (x.tl == 0) sh.slot_fault[0] = 0;
-    // The record's backpointers use the pieces' layout (the record's states
-    // per thread), so its anchors come from traces as well.
-    if (rec.kst == 16)
-      piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
-    else
-      piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
   }
 }
 
@@ -837,11 +858,8 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
       int32_t* p = path[warp];
       const int s_end = anchors[rec.seg_off + c];
       if (lane == 0) p[b - 1 - a] = s_end;
-      auto keep = [&](int t, int s) { if (lane == 0) p[t - a] = s; };
-      const uint32_t* bpr = bp_arena + rec.bp_off;
-      if (rec.kst == 4) warp_trace<4>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
-      else if (rec.kst == 8) warp_trace<8>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
-      else warp_trace<16>(bpr, rec.nw * 32, s_end, b - 1, a, lane, keep);
+      warp_trace(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
+                 [&](int t, int s) { if (lane == 0) p[t - a] = s; });
       __syncwarp();
       const float* e = rec.emissions;
       for (int t = a + lane; t < b; t += 32) {
@@ -994,7 +1012,8 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 }
 
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          bool row_mode, int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+                          int phase, int ctas_per_record, bool row_mode, int row_vocab,
+                          unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
   auto kernel = !row_mode ? ffa_finish_route<false, 0>
                          : (row_vocab == 32 ? ffa_finish_route<true, 32> : ffa_finish_route<true, 0>);
@@ -1012,7 +1031,8 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   }
   if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
   ++g_launches;
-  kernel<<<count, kCtaThreads, smem_bytes, stream>>>(params, records);
+  kernel<<<count * ctas_per_record, kCtaThreads, smem_bytes, stream>>>(params, records, phase,
+                                                                      ctas_per_record);
   return cudaGetLastError();
 }
 
