@@ -9,6 +9,9 @@ One step = one ``align`` call over one synthetic batch of BASELINE.json's
 configs[C] (default cfg1, the config the 1-GPU metric is quoted on).  Under
 torchrun each rank aligns its own independent batch of that shape on its own
 GPU (records are independent: no collective on the data path; weak scaling).
+With --split every rank draws the same batch and aligns its share of a
+length-balanced partition of its records instead (strong scaling: the
+multi-GPU configuration's whole-box measurement).
 
 impl=ours            this package: device-resident timing (``value``), an
                      end-to-end host->device->host timing (``e2e``), the live
@@ -51,6 +54,8 @@ def parse_args():
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--mode", default="optimized", choices=["optimized", "conventional"])
     p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
+    p.add_argument("--split", action="store_true",
+                   help="partition one batch over the ranks (strong scaling) instead of one batch per rank")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU work in the cpu_baseline sample")
     args = p.parse_args()
@@ -199,6 +204,7 @@ def run_ours(args):
     import fast_forced_aligner_b200 as ffa
     from fast_forced_aligner_b200 import workloads
     from fast_forced_aligner_b200.build import LIB
+    from fast_forced_aligner_b200.sharding import reduce_over_ranks, shard_of_rank
 
     rank, world, local = rank_info()
     device = torch.device("cuda", local)
@@ -212,21 +218,20 @@ def run_ours(args):
             dist.barrier()
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_over_ranks(x, "max", device)
 
     def sum_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce_over_ranks(x, "sum", device)
 
     ffa.load_extension()
-    wl = workloads.config(args.config, shard=rank)
+    if args.split:
+        pool = workloads.config(args.config)
+        wl = pool.subset(shard_of_rank(pool.lengths, pool.target_lengths, rank, world))
+        parallelism = f"one batch LPT-partitioned over {world} GPU(s) by record cost, no collective"
+    else:
+        wl = workloads.config(args.config, shard=rank)
+        parallelism = f"records sharded, {world} independent GPU(s), no collective"
+    records_total = int(sum_over_ranks(wl.batch))
     frames = int(wl.lengths.sum())
     frame_list, token_list = wl.lengths.tolist(), wl.target_lengths.tolist()
     e_host = torch.from_numpy(wl.emissions).pin_memory()
@@ -337,13 +342,15 @@ def run_ours(args):
     line = {
         "metric": "aligned frames/sec", "value": value, "unit": "frames/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if args.split else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl.name, "records_per_gpu": wl.batch, "frames_per_gpu": frames,
+                   "records_total": records_total, "frames_total": int(all_frames),
                    "vocab": wl.vocab, "mode": args.mode, "check_inputs": True,
                    "inputs": "packed device-resident fp32 [sum T, V] + int64 targets",
                    "l2": "flushed (256 MiB write) before every timed step",
-                   "parallelism": f"records sharded, {world} independent GPU(s), no collective"},
+                   "parallelism": parallelism},
         "e2e": {"value": e2e_value, "unit": "frames/s",
                 "h2d_bytes_per_step": int(e_host.numel() * 4 + t_host.numel() * 8),
                 "d2h_bytes_per_step": int(frames * 12 + wl.batch * 4),

@@ -61,7 +61,7 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned pari
     if (global_ns() - start > limit_ns) return false;
   return true;
 }
-// One TMA bulk copy global -> shared (no tensor map, no multicast), completed
+// One TMA bulk copy global -> shared (no tensor map; this CTA's shared memory only), completed
 // on `bar` with a transaction-byte count.
 __device__ __forceinline__ void tma_bulk_load(void* smem_dst, const void* gmem_src, unsigned bytes,
                                               unsigned long long* bar) {
