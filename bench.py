@@ -241,7 +241,7 @@ def run_ours(args):
     ffa.validate_inputs(list(e_dev.split(frame_list)), list(t_dev.split(token_list)), blank_id=wl.blank)
 
     def step(e, t):
-        return ffa.align_packed(e, frame_list, t, token_list, blank_id=wl.blank, mode=args.mode)
+        return ffa.align_packed(e, wl.lengths, t, wl.target_lengths, blank_id=wl.blank, mode=args.mode)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     import ctypes

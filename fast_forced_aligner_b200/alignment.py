@@ -15,6 +15,7 @@ from functools import lru_cache
 from pathlib import Path
 from typing import Literal
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -276,9 +277,22 @@ def align(
     return AlignmentBatch(tuple(lengths), *tensors)
 
 
+def _host_counts(values, what: str) -> Tensor:
+    """A 1-D CPU int64 tensor of counts from a sequence, array or tensor."""
+    if isinstance(values, Tensor):
+        if values.ndim != 1 or values.dtype.is_floating_point or values.dtype.is_complex \
+                or values.dtype == torch.bool:
+            raise ValueError(f"{what} must be a 1-D sequence of ints")
+        return values.to("cpu", torch.int64).contiguous()
+    array = np.asarray(values)
+    if array.ndim != 1 or (array.size and array.dtype.kind not in "iu"):
+        raise ValueError(f"{what} must be a 1-D sequence of ints")
+    return torch.from_numpy(np.ascontiguousarray(array, dtype=np.int64))
+
+
 @torch.inference_mode()
 def align_packed(
-    emissions: Tensor, frames: Sequence[int], targets: Tensor, tokens: Sequence[int], *,
+    emissions: Tensor, frames, targets: Tensor, tokens, *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
     check_inputs: bool = True, emission_validity: Tensor | None = None,
 ) -> AlignmentBatch:
@@ -287,19 +301,30 @@ def align_packed(
     Record ``i`` is rows ``[sum(frames[:i]), sum(frames[:i+1]))`` of one
     contiguous CUDA float32 ``(N, V)`` matrix and tokens
     ``[sum(tokens[:i]), sum(tokens[:i+1]))`` of one contiguous CUDA int64
-    vector.  Results and errors are those of ``align`` on the same records.
+    vector.  ``frames``, ``tokens`` and a per-record ``blank_id`` may be
+    Python sequences, NumPy integer arrays or integer tensors (arrays and
+    tensors skip the per-record Python work).  Results and errors are those
+    of ``align`` on the same records.
     """
     code = _mode(mode, check_inputs)
-    frames = [int(f) for f in frames]
-    tokens = [int(u) for u in tokens]
-    if not 0 < len(frames) <= 65535 or len(tokens) != len(frames):
+    frames_t = _host_counts(frames, "frames")
+    tokens_t = _host_counts(tokens, "tokens")
+    count = frames_t.numel()
+    if not 0 < count <= 65535 or tokens_t.numel() != count:
         raise ValueError("provide 1..65535 matching frame counts, token counts and blanks")
-    blanks = _blanks(len(frames), blank_id)
+    if type(blank_id) is int:
+        blanks_t = torch.tensor([blank_id], dtype=torch.int64)
+    elif not isinstance(blank_id, (Sequence, np.ndarray, Tensor)):
+        raise TypeError("blank_id must be an int or a sequence of ints")  # as align's list(blank_id)
+    else:
+        blanks_t = _host_counts(blank_id, "blank_id")
+        if blanks_t.numel() != count:
+            raise ValueError("provide one blank ID per record")
     if not isinstance(emissions, Tensor) or emissions.device.type != "cuda":
         raise ValueError("inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device")
-    _check_mask(emission_validity, emissions.device, len(frames))
+    _check_mask(emission_validity, emissions.device, count)
     load_extension()
     # The op runs under a device guard for the inputs' device.
-    tensors, lengths = torch.ops.ffa_b200.align_packed(
-        emissions, frames, targets, tokens, blanks, code, emission_validity, check_inputs)
-    return AlignmentBatch(tuple(lengths), *tensors)
+    tensors = torch.ops.ffa_b200.align_packed(
+        emissions, frames_t, targets, tokens_t, blanks_t, code, emission_validity, check_inputs)
+    return AlignmentBatch(tuple(frames_t.tolist()), *tensors)

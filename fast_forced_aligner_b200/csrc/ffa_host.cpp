@@ -17,6 +17,8 @@
 #include <cstdint>
 #include <cstring>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -71,8 +73,8 @@ int choose_k(int64_t S, bool latency_bound) {
 // 16 runs fewer instructions per frame, modelled as warps x (fixed per-frame
 // cost + per-state cost x K), with warps = ceil(S / (32 K)).
 int piece_k(int64_t S) {
-  auto cost = [&](int64_t K) { return (S + 32 * K - 1) / (32 * K) * (24 + 6 * K); };
-  return cost(16) <= cost(8) ? 16 : 8;
+  const int64_t cost16 = ((S + 511) >> 9) * (24 + 6 * 16), cost8 = ((S + 255) >> 8) * (24 + 6 * 8);
+  return cost16 <= cost8 ? 16 : 8;
 }
 
 bool chunked_record(const ffa_record& r, bool optimized) {
@@ -92,7 +94,8 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
   g.chunked = chunked_record(r, optimized);
   g.K = g.chunked ? piece_k(S) : choose_k(S, latency_bound);
-  g.nw = static_cast<int>((S + 32 * g.K - 1) / (32 * g.K));
+  const int slot_log2 = g.K == 4 ? 7 : g.K == 8 ? 8 : 9;  // log2(32 K): states per warp
+  g.nw = static_cast<int>((S + (int64_t{1} << slot_log2) - 1) >> slot_log2);
   if (g.chunked) {
     g.seg_log2 = ffa::kPieceSegLog2;
   } else {
@@ -103,8 +106,7 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
     while (g.seg_log2 < ffa::kMaxSegLog2 && r.frames >= (int64_t{1} << (2 * (g.seg_log2 + 1) - 3)))
       ++g.seg_log2;
   }
-  const int64_t H = int64_t{1} << g.seg_log2;
-  g.segments = (r.frames + H - 1) / H;
+  g.segments = (r.frames + (int64_t{1} << g.seg_log2) - 1) >> g.seg_log2;
   // Backpointer rows, frontiers and maps do not depend on the thread layout.
   const int S32 = static_cast<int>(S);
   g.bp_words = r.frames * ffa::bp_row_words(S32);
@@ -147,34 +149,29 @@ int device_sms() {
 }
 
 // Byte layout of the staging buffer / the copy of it at the workspace start,
-// followed by the device-only arenas.
+// followed by the device-only arenas.  The slot region holds the first-pass
+// slot list and its bundles, packed back to back once their counts are known
+// (it reserves room for one slot and one bundle per piece); the upload stops
+// at their end.
 struct AlignLayout {
-  size_t recs, pieces, bundles, order, chunked, fill, copy_bytes, keys, staging_bytes;
+  size_t recs, chunked, fill, slots, keys, classes, staging_bytes;
   size_t bp, maps, anchors, frontiers, pstates, route, fill_done, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, fill_items;
 };
 
 bool latency_bound(int64_t slots) { return slots <= device_sms(); }
 
-int64_t total_pieces(const ffa_record* records, int64_t count, bool optimized) {
-  int64_t n = 0;
-  for (int64_t i = 0; i < count; ++i)
-    n += chunked_record(records[i], optimized) ? piece_count(records[i].frames) : 1;
-  return n;
-}
-
+// Sizes of one call.  Everything here is independent of the thread layout
+// (states per thread), so one pass over the records suffices.
 int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLayout* L) {
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
+  int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
+          pieces = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
-  }
-  const int64_t pieces = total_pieces(records, count, optimized);
-  const bool lat = latency_bound(pieces);
-  int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0;
-  for (int64_t i = 0; i < count; ++i) {
-    const Geometry g = geometry(records[i], optimized, lat);
+    const Geometry g = geometry(records[i], optimized, false);
     frames += records[i].frames;
     bp_words += g.bp_words;
     map_elems += align_up(static_cast<size_t>(g.map_elems), 8);
@@ -182,6 +179,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
     fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
     frontier += g.frontier_elems;
     chunked += g.chunked ? 1 : 0;
+    pieces += g.pieces;
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
@@ -191,16 +189,14 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->fill_items = fill;
   size_t off = 0;
   L->recs = off; off = align_up(off + sizeof(ffa::RecordDev) * count, 16);
-  L->pieces = off; off = align_up(off + sizeof(ffa::PieceDev) * pieces, 16);
-  // First-pass bundles and slots: at most one slot per piece.
-  L->bundles = off; off = align_up(off + sizeof(ffa::Bundle) * pieces, 16);
-  L->order = off; off = align_up(off + sizeof(int32_t) * pieces, 16);
   L->chunked = off; off = align_up(off + sizeof(int32_t) * chunked, 16);
-  L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 256);
-  L->copy_bytes = off;  // uploaded; the rest of the staging buffer is host scratch
-  L->keys = off; off = align_up(off + 2 * sizeof(uint64_t) * count, 256);
+  L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 16);
+  L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 16, 256);
+  const size_t device_part = off;  // the most that is uploaded
+  L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
+  L->classes = off; off = align_up(off + count, 256);
   L->staging_bytes = off;
-  off = L->copy_bytes;  // the workspace holds the uploaded part only
+  off = device_part;
   L->bp = off; off = align_up(off + sizeof(uint32_t) * bp_words, 256);
   L->maps = off; off = align_up(off + sizeof(uint16_t) * map_elems, 256);
   L->anchors = off; off = align_up(off + sizeof(int32_t) * segments, 256);
@@ -216,60 +212,111 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
 // packed so that ascending order puts row-staged before gathered, pieces of
 // the optimized route before whole records, K = 4 before K = 8 and wider
 // slots (longer transcripts, usually longer records) first.
-uint32_t slot_class(const ffa::RecordDev& d) {
-  return (d.row_mode ? 0u : 1u) << 7 | (d.num_pieces > 1 ? 0u : 1u) << 6 | (d.kst == 4 ? 0u : 1u) << 5 |
-         static_cast<uint32_t>(ffa::kMaxWarps - d.nw);
+uint8_t slot_class(const ffa::RecordDev& d) {
+  return static_cast<uint8_t>((d.row_mode ? 0u : 1u) << 7 | (d.num_pieces > 1 ? 0u : 1u) << 6 |
+                              (d.kst == 4 ? 0u : 1u) << 5 | static_cast<uint32_t>(ffa::kMaxWarps - d.nw));
 }
-int slot_group(uint32_t cls) { return static_cast<int>(cls >> 6); }  // 2 * !row + !chunked
+bool class_row(uint8_t cls) { return (cls >> 7) == 0; }
+int class_warps(uint8_t cls) { return ffa::kMaxWarps - (cls & 31); }
 
-// Record order for packing: by slot class, then longest first.  Keys pack
-// (class, ~frames, index) in 64 bits and are sorted by an LSD radix sort over
-// bytes 2..7 (the index rides along); a byte every key shares is skipped, so
-// typical batches take two or three passes.  `tmp` has room for `count` keys.
-void sort_records(const ffa::RecordDev* recs, int64_t count, uint64_t* keys, uint64_t* tmp) {
-  for (int64_t i = 0; i < count; ++i)
-    keys[i] = static_cast<uint64_t>(slot_class(recs[i])) << 56 |
-              static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(recs[i].T)) << 16 |
-              static_cast<uint64_t>(i);
-  for (int shift = 16; shift < 64; shift += 8) {
-    int64_t hist[256] = {};
-    for (int64_t i = 0; i < count; ++i) ++hist[(keys[i] >> shift) & 0xff];
-    if (hist[(keys[0] >> shift) & 0xff] == count) continue;
-    int64_t sum = 0;
-    for (int b = 0; b < 256; ++b) { const int64_t h = hist[b]; hist[b] = sum; sum += h; }
-    for (int64_t i = 0; i < count; ++i) tmp[hist[(keys[i] >> shift) & 0xff]++] = keys[i];
-    std::memcpy(keys, tmp, sizeof(uint64_t) * count);
-  }
+// Length bucket of a record: 16 buckets per power of two (about 6% wide),
+// exact below 16 frames; always below kLengthBuckets.
+constexpr int kLengthBuckets = 512;
+inline int length_bucket(uint32_t T) {
+  if (T < 16) return static_cast<int>(T);
+  const int msb = 31 - __builtin_clz(T);
+  return (msb - 3) << 4 | static_cast<int>((T >> (msb - 4)) & 15);
 }
 
-// Packs the slots listed in `order` (piece ids, already in packing order)
-// into bundles: runs of one slot class, about `warps_per_cta` warps per CTA
-// (at least one slot, at most kMaxWarps warps), a row-staged bundle also at
-// most `row_slots` rings.  Returns the bundle count; ranges[g] is the first
-// bundle of slot group g (ranges[4] = the count).
-template <typename ClassOf>
-int64_t make_bundles(const int32_t* order, int64_t n, ClassOf class_of, const ffa::RecordDev* recs,
-                     const ffa::PieceDev* pieces, int64_t warps_per_cta, int64_t row_slots,
-                     ffa::Bundle* bundles, int64_t ranges[5], int64_t* max_row_slots) {
-  int64_t nb = 0;
-  int group = 0;
-  for (int g = 0; g < 5; ++g) ranges[g] = 0;
-  for (int64_t k = 0; k < n;) {
-    const uint32_t cls = class_of(order[k]);
-    const ffa::RecordDev& head = recs[pieces[order[k]].record];
-    const int g = slot_group(cls);
-    while (group < g) ranges[++group] = nb;
-    int64_t capacity = std::min<int64_t>(ffa::kMaxWarps / head.nw, std::max<int64_t>(1, warps_per_cta / head.nw));
-    if (head.row_mode) capacity = std::min(capacity, row_slots);
-    int64_t m = 1;
-    while (k + m < n && m < capacity && class_of(order[k + m]) == cls) ++m;
-    bundles[nb++] = ffa::Bundle{static_cast<int32_t>(k), head.nw, static_cast<uint8_t>(m), head.kst, 0};
-    if (head.row_mode) *max_row_slots = std::max(*max_row_slots, m);
-    k += m;
-  }
-  while (group < 4) ranges[++group] = nb;
-  return nb;
+// Record order for packing: by slot class, then longest first (by length
+// bucket; ties keep index order), written to `sorted`.  A counting sort over
+// the (class, bucket) cells of the classes present: the cells of consecutive
+// records differ, so no pass is serialised on one counter the way a radix
+// pass over a few classes is.
+void sort_records(const ffa::RecordDev* recs, const uint8_t* classes, int64_t count, int32_t* sorted) {
+  int16_t index[256];
+  std::fill_n(index, 256, static_cast<int16_t>(-1));
+  for (int64_t i = 0; i < count; ++i) index[classes[i]] = 0;
+  int used = 0;
+  for (int c = 0; c < 256; ++c)
+    if (index[c] == 0) index[c] = static_cast<int16_t>(used++);
+  thread_local std::vector<int32_t> cells;
+  cells.assign(static_cast<size_t>(used) * kLengthBuckets, 0);
+  auto cell = [&](int64_t i) {
+    return static_cast<size_t>(index[classes[i]]) * kLengthBuckets +
+           (kLengthBuckets - 1 - length_bucket(static_cast<uint32_t>(recs[i].T)));
+  };
+  for (int64_t i = 0; i < count; ++i) ++cells[cell(i)];
+  int32_t sum = 0;
+  for (int32_t& c : cells) { const int32_t h = c; c = sum; sum += h; }
+  for (int64_t i = 0; i < count; ++i) sorted[cells[cell(i)]++] = static_cast<int32_t>(i);
 }
+
+// Slots of the optimized route's records per slot class, as a function of
+// the run length M (pieces per slot): a record of P pieces takes ceil(P / M)
+// slots.  Piece counts below kBins are histogrammed per class, so evaluating
+// one M costs O(classes x largest count) rather than O(records).
+class RunLengthModel {
+ public:
+  static constexpr int kBins = 256;
+  RunLengthModel() { std::fill_n(index_, 256, static_cast<int16_t>(-1)); }
+  void reset() {
+    for (int c = 0; c < nused_; ++c) index_[used_[c]] = -1;
+    nused_ = 0;
+    big_.clear();
+  }
+  void add(uint8_t cls, int64_t pieces) {
+    const int k = slot(cls);
+    if (pieces < kBins) {
+      ++hist_[static_cast<size_t>(k) * kBins + pieces];
+      maxp_[k] = std::max<int>(maxp_[k], static_cast<int>(pieces));
+    } else {
+      big_.push_back({k, pieces});
+    }
+  }
+  void add_whole(uint8_t cls) { ++whole_[slot(cls)]; }
+  // CTAs of the first pass at run length m when a CTA holds at most
+  // capacity(cls) slots of its class.
+  template <typename Capacity>
+  int64_t ctas(int m, Capacity capacity) const {
+    int64_t slots[256];
+    for (int c = 0; c < nused_; ++c) {
+      int64_t n = whole_[c];
+      const int32_t* h = hist_.data() + static_cast<size_t>(c) * kBins;
+      for (int p = 1; p <= maxp_[c]; ++p) n += h[p] * ((p + m - 1) / m);
+      slots[c] = n;
+    }
+    for (const auto& b : big_) slots[b.first] += (b.second + m - 1) / m;
+    int64_t total = 0;
+    for (int c = 0; c < nused_; ++c) {
+      const int64_t cap = capacity(used_[c]);
+      total += (slots[c] + cap - 1) / cap;
+    }
+    return total;
+  }
+
+ private:
+  int slot(uint8_t cls) {
+    if (index_[cls] < 0) {
+      index_[cls] = static_cast<int16_t>(nused_);
+      used_[nused_] = cls;
+      whole_[nused_] = 0;
+      maxp_[nused_] = 0;
+      if (hist_.size() < static_cast<size_t>(nused_ + 1) * kBins)
+        hist_.resize(static_cast<size_t>(nused_ + 1) * kBins);
+      std::fill_n(hist_.begin() + static_cast<size_t>(nused_) * kBins, kBins, 0);
+      ++nused_;
+    }
+    return index_[cls];
+  }
+  int16_t index_[256];
+  uint8_t used_[256] = {};
+  int64_t whole_[256] = {};
+  int maxp_[256] = {};
+  int nused_ = 0;
+  std::vector<int32_t> hist_;
+  std::vector<std::pair<int, int64_t>> big_;
+};
 
 struct ScanLayout {
   size_t recs, items, staging_bytes, workspace_bytes;
@@ -382,19 +429,19 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
 
   auto* host = static_cast<unsigned char*>(staging);
   auto* recs = reinterpret_cast<ffa::RecordDev*>(host + L.recs);
-  auto* pieces = reinterpret_cast<ffa::PieceDev*>(host + L.pieces);
-  auto* bundles = reinterpret_cast<ffa::Bundle*>(host + L.bundles);
-  auto* order = reinterpret_cast<int32_t*>(host + L.order);
   auto* chunked = reinterpret_cast<int32_t*>(host + L.chunked);
   auto* fill = reinterpret_cast<ffa::FillItem*>(host + L.fill);
+  auto* classes = reinterpret_cast<uint8_t*>(host + L.classes);
   const int64_t P = L.num_pieces;
 
-  // Per-record descriptors, pieces and arena offsets.
+  // Per-record descriptors, fill items and arena offsets.
   int64_t out_off = 0, bp_off = 0, map_off = 0, seg_off = 0, nfill = 0, frontier_off = 0;
   int64_t np = 0, nchunked = 0;
   const bool lat = latency_bound(P);
   unsigned max_row_vocab = 0;
   int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
+  thread_local RunLengthModel runs_model;
+  runs_model.reset();
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, lat);
@@ -421,18 +468,18 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     d.first_piece = static_cast<int32_t>(np);
     d.num_pieces = static_cast<int32_t>(g.pieces);
     recs[i] = d;
+    const uint8_t cls = slot_class(d);
+    classes[i] = cls;
     if (d.row_mode) {
       max_row_vocab = std::max<unsigned>(max_row_vocab, r.vocab);
       row_vocab = (row_vocab < 0 || row_vocab == r.vocab) ? r.vocab : 0;
     }
-    for (int64_t j = 0; j < g.pieces; ++j) {
-      const int64_t first = j * ffa::kPieceFrames;
-      const int64_t end = (j == g.pieces - 1) ? r.frames : first + ffa::kPieceFrames;
-      pieces[np + j] = ffa::PieceDev{static_cast<int32_t>(i), static_cast<int32_t>(g.chunked ? first : 0),
-                                     static_cast<int32_t>(g.chunked ? end : r.frames),
-                                     static_cast<int32_t>(j)};
+    if (g.chunked) {
+      ++nchunked;
+      runs_model.add(cls, g.pieces);
+    } else {
+      runs_model.add_whole(cls);
     }
-    if (g.chunked) ++nchunked;
     np += g.pieces;
     for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
       fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
@@ -451,37 +498,39 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                      : ffa::kMaxWarps;
   // Pieces per first-pass slot: the fewest that let the pass fit the GPU in
   // one wave of CTAs (each slot still restarts a relaxed DP every piece).
-  // A CTA holds slots of one width only, up to kMaxWarps warps (and, when
+  // A CTA holds slots of one class only, up to kMaxWarps warps (and, when
   // row-staged, up to row_slots rings); one CTA runs per SM.
   const int64_t sms = device_sms();
-  auto slots_per_cta = [&](const ffa::RecordDev& d) {
-    int64_t c = ffa::kMaxWarps / d.nw;
-    if (d.row_mode) c = std::min(c, row_slots);
+  auto slots_per_cta = [&](uint8_t cls) {
+    int64_t c = ffa::kMaxWarps / class_warps(cls);
+    if (class_row(cls)) c = std::min(c, row_slots);
     return c;
   };
   int run_pieces = 1;
-  for (;; ++run_pieces) {
-    int64_t class_slots[256] = {};
-    for (int64_t i = 0; i < count; ++i)
-      class_slots[slot_class(recs[i])] += (recs[i].num_pieces + run_pieces - 1) / run_pieces;
-    int64_t ctas = 0;
-    for (int64_t i = 0; i < count; ++i) {
-      const uint32_t c = slot_class(recs[i]);
-      if (class_slots[c] == 0) continue;  // counted already
-      ctas += (class_slots[c] + slots_per_cta(recs[i]) - 1) / slots_per_cta(recs[i]);
-      class_slots[c] = 0;
-    }
-    if (ctas <= sms || run_pieces == ffa::kMaxRunPieces) break;
-  }
+  if (nchunked > 0)
+    while (run_pieces < ffa::kMaxRunPieces && runs_model.ctas(run_pieces, slots_per_cta) > sms) ++run_pieces;
+
   // Packing order: records by slot class, longest first; a record's pieces
-  // stay together.
-  auto* keys = reinterpret_cast<uint64_t*>(host + L.keys);
-  sort_records(recs, count, keys, keys + count);
+  // stay together.  Slots of one class form one contiguous run.
+  auto* sorted = reinterpret_cast<int32_t*>(host + L.keys);
+  sort_records(recs, classes, count, sorted);
+  struct ClassRun {
+    int64_t first, slots;
+    uint8_t cls, kst;
+  };
+  thread_local std::vector<ClassRun> runs;
+  runs.clear();
+  auto* order = reinterpret_cast<ffa::SlotRef*>(host + L.slots);
   int64_t n_first = 0;
   for (int64_t k = 0; k < count; ++k) {
-    const ffa::RecordDev& d = recs[keys[k] & 0xffff];
-    for (int32_t j = 0; j < d.num_pieces; j += (d.num_pieces > 1 ? run_pieces : 1))
-      order[n_first++] = d.first_piece + j;
+    const int32_t i = sorted[k];
+    const ffa::RecordDev& d = recs[i];
+    const int64_t before = n_first;
+    const int32_t step = d.num_pieces > 1 ? run_pieces : 1;
+    for (int32_t j = 0; j < d.num_pieces; j += step) order[n_first++] = ffa::SlotRef{i, j};
+    if (runs.empty() || runs.back().cls != classes[i])
+      runs.push_back(ClassRun{before, 0, classes[i], d.kst});
+    runs.back().slots += n_first - before;
   }
   // Records of the optimized route, row-staged ones first (one finisher
   // launch each kind).
@@ -492,57 +541,58 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
         chunked[nc++] = static_cast<int32_t>(i);
         if (pass == 0) ++n_chunked_row;
       }
-  auto class_of = [&](int32_t p) { return slot_class(recs[pieces[p].record]); };
   // Warps per CTA: the launch's warps spread evenly over the SMs (one CTA
   // runs per SM): the smallest per-CTA target whose packing still fits one
   // wave, so that every SM gets a share and none gets more than it must.
   int64_t first_warps = 0;
-  for (int64_t k = 0; k < n_first; ++k) first_warps += recs[pieces[order[k]].record].nw;
-  // Slots of one class are contiguous in `order`: count CTAs per class run.
-  struct ClassRun {
-    int64_t slots;
-    int nw;
-    bool row;
+  for (const ClassRun& run : runs) first_warps += run.slots * class_warps(run.cls);
+  auto capacity = [&](const ClassRun& run, int64_t target) {
+    const int nw = class_warps(run.cls);
+    int64_t cap = std::min<int64_t>(ffa::kMaxWarps / nw, std::max<int64_t>(1, target / nw));
+    if (class_row(run.cls)) cap = std::min(cap, row_slots);
+    return cap;
   };
-  ClassRun runs[256];
-  int nruns = 0;
-  for (int64_t k = 0; k < n_first;) {
-    const uint32_t cls = class_of(order[k]);
-    const ffa::RecordDev& head = recs[pieces[order[k]].record];
-    int64_t m = 1;
-    while (k + m < n_first && class_of(order[k + m]) == cls) ++m;
-    if (nruns < 256) runs[nruns++] = ClassRun{m, head.nw, head.row_mode != 0};
-    k += m;
-  }
   auto ctas_for = [&](int64_t target) {
     int64_t ctas = 0;
-    for (int c = 0; c < nruns; ++c) {
-      int64_t cap = std::min<int64_t>(ffa::kMaxWarps / runs[c].nw, std::max<int64_t>(1, target / runs[c].nw));
-      if (runs[c].row) cap = std::min(cap, row_slots);
-      ctas += (runs[c].slots + cap - 1) / cap;
+    for (const ClassRun& run : runs) {
+      const int64_t cap = capacity(run, target);
+      ctas += (run.slots + cap - 1) / cap;
     }
     return ctas;
   };
   int64_t target = std::min<int64_t>(ffa::kMaxWarps, (first_warps + sms - 1) / sms);
   while (target < ffa::kMaxWarps && ctas_for(target) > sms) ++target;
-  int64_t ranges[5], max_row_slots = 1;
-  const int64_t nb = make_bundles(order, n_first, class_of, recs, pieces, target, row_slots, bundles,
-                                  ranges, &max_row_slots);
-  const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
+  // Bundles: each class run cut into CTAs of at most `capacity` slots; the
+  // row-staged runs come first (one launch each kind).
+  const size_t bundles_off = align_up(L.slots + sizeof(ffa::SlotRef) * n_first, 16);
+  auto* bundles = reinterpret_cast<ffa::Bundle*>(host + bundles_off);
+  int64_t nb = 0, nb_row = 0, max_row_slots = 1;
   int max_gather_k = 8;
+  for (const ClassRun& run : runs) {
+    const int64_t cap = capacity(run, target);
+    const int nw = class_warps(run.cls);
+    for (int64_t off = 0; off < run.slots; off += cap) {
+      const int64_t m = std::min(cap, run.slots - off);
+      bundles[nb++] = ffa::Bundle{static_cast<int32_t>(run.first + off), static_cast<uint8_t>(nw),
+                                  static_cast<uint8_t>(m), run.kst, 0};
+      if (class_row(run.cls)) max_row_slots = std::max(max_row_slots, m);
+    }
+    if (class_row(run.cls)) nb_row = nb;
+  }
   for (int64_t i = 0; i < count; ++i)
     if (!recs[i].row_mode) max_gather_k = std::max<int>(max_gather_k, recs[i].kst);
+  const size_t upload_bytes = bundles_off + sizeof(ffa::Bundle) * nb;
+  const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
   const unsigned gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(max_gather_k));
 
   auto* dev = static_cast<unsigned char*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(dev, host, L.copy_bytes, cudaMemcpyHostToDevice, s);
+  cudaError_t err = cudaMemcpyAsync(dev, host, upload_bytes, cudaMemcpyHostToDevice, s);
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
 
   ffa::ForwardParams fp{};
   fp.recs = reinterpret_cast<const ffa::RecordDev*>(dev + L.recs);
-  fp.pieces = reinterpret_cast<const ffa::PieceDev*>(dev + L.pieces);
-  fp.order = reinterpret_cast<const int32_t*>(dev + L.order);
+  fp.order = reinterpret_cast<const ffa::SlotRef*>(dev + L.slots);
   fp.mask = emission_validity;
   fp.check_inputs = (flags & FFA_FLAG_CHECK_INPUTS) ? 1 : 0;
   fp.bp = reinterpret_cast<uint32_t*>(dev + L.bp);
@@ -557,7 +607,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                            outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
   fp.row_slot_bytes = row_slot_bytes;
   fp.run_pieces = run_pieces;
-  const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + L.bundles);
+  const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + bundles_off);
   const int rv = row_vocab > 0 ? row_vocab : 0;
 
   if (g_profile_before != nullptr) {
@@ -571,11 +621,11 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   if ((rc = mark(FFA_PROFILE_START))) return rc;
   // First pass: every piece of every record (a one-piece record is the
   // conventional DP).
-  fp.bundles = dbundles + ranges[0];
-  err = ffa::launch_forward(fp, static_cast<int>(ranges[2] - ranges[0]), true, rv, row_smem, s);
+  fp.bundles = dbundles;
+  err = ffa::launch_forward(fp, static_cast<int>(nb_row), true, rv, row_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
-  fp.bundles = dbundles + ranges[2];
-  err = ffa::launch_forward(fp, static_cast<int>(ranges[4] - ranges[2]), false, 0, gather_smem, s);
+  fp.bundles = dbundles + nb_row;
+  err = ffa::launch_forward(fp, static_cast<int>(nb - nb_row), false, 0, gather_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   if (g_profile_after != nullptr) {
     err = cudaEventRecord(g_profile_after, s);

@@ -89,14 +89,15 @@ constexpr int kMaxRunPieces = 8;
 // per record for the fewest instructions (wider threads amortise the
 // per-frame overhead; narrower ones pad fewer states).
 
-// One piece: frames [first, end) of a record; index is its rank in the record.
-struct PieceDev {
+// One first-pass slot: piece `piece` of record `record` (frames
+// [32 piece, ...) of a record of the optimized route; piece 0 = the whole
+// record otherwise).  Its piece id -- the index of its PieceState -- is the
+// record's first_piece + piece.
+struct SlotRef {
   int32_t record;
-  int32_t first;
-  int32_t end;
-  int32_t index;
+  int32_t piece;
 };
-static_assert(sizeof(PieceDev) == 16, "PieceDev layout");
+static_assert(sizeof(SlotRef) == 8, "SlotRef layout");
 
 // Device-written state of one piece.  `start` is valid on the first piece of
 // a region, `end` and `flags` on its last.
@@ -168,9 +169,8 @@ size_t forward_header_bytes();
 // Arguments of one forward launch.
 struct ForwardParams {
   const RecordDev* recs;
-  const PieceDev* pieces;
   const Bundle* bundles;
-  const int32_t* order;      // piece ids, grouped by bundle
+  const SlotRef* order;      // first-pass slots, grouped by bundle
   const uint8_t* mask;       // emission-validity mask or null
   int32_t check_inputs;
   uint32_t* bp;

@@ -500,10 +500,12 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
   if (x.tid == 0) sh.edge = Boundary{-INFINITY, 0};
   __syncthreads();
   if (x.slot >= bd.count) return;
-  const int p = P.order[bd.first + x.slot];
-  const PieceDev piece = P.pieces[p];
-  x.r = piece.record;
+  const SlotRef ref = P.order[bd.first + x.slot];
+  x.r = ref.record;
   const RecordDev rec = P.recs[x.r];
+  const int pidx = ref.piece;                // rank of the slot's first piece in the record
+  const int p = rec.first_piece + pidx;      // its piece id
+  const int pfirst = pidx * kPieceFrames;    // its first frame (0 for a whole record)
   x.first_warp = x.slot * bd.nw;
   x.bar = x.slot;
   x.lw = x.warp - x.first_warp;  // warp within the slot
@@ -518,7 +520,7 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
   PieceRun run{0, 0, T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, 0};
   {
     const bool masked = P.mask != nullptr && !P.mask[r];
-    if (piece.index == 0) {
+    if (pidx == 0) {
       // ---- status: mask, then target validation (alignment.cu:836, 852-874) ----
       int status = masked ? 2 : 0;
       if (tl == 0) sh.slot_fault[x.slot] = 0;
@@ -562,12 +564,12 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
     }
     if (chunked) {
       // Pieces index .. index+m-1 of the record, back to back.
-      const int m = min(P.run_pieces, rec.num_pieces - piece.index);
-      run.a0 = run.t0 = piece.first;
-      run.t1 = piece.index + m == rec.num_pieces ? T : piece.first + m * kPieceFrames;
+      const int m = min(P.run_pieces, rec.num_pieces - pidx);
+      run.a0 = run.t0 = pfirst;
+      run.t1 = pidx + m == rec.num_pieces ? T : pfirst + m * kPieceFrames;
       run.pieces = m;
-      run.init = piece.first == 0 ? kInitRecord : kInitFree;
-      run.frontier_out = P.frontiers + rec.frontier_off + static_cast<int64_t>(piece.index) * state_stride(2 * U + 1);
+      run.init = pfirst == 0 ? kInitRecord : kInitFree;
+      run.frontier_out = P.frontiers + rec.frontier_off + static_cast<int64_t>(pidx) * state_stride(2 * U + 1);
       run.end_piece = run.start_piece = p;
       run.new_region = true;
     }

@@ -245,22 +245,36 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align(
   return run_align(recs, device, mode, mask, check_inputs, stream, std::move(lengths));
 }
 
-// align_packed(Tensor emissions, int[] frames, Tensor targets, int[] tokens,
-//              int[] blanks, int mode, Tensor? emission_validity,
-//              bool check_inputs) -> (Tensor[], int[])
+// CPU int64 [n] view of a count vector (frames, tokens, blank IDs).
+const int64_t* host_counts(const at::Tensor& t, int64_t n, const char* what) {
+  TORCH_CHECK_VALUE(t.device().is_cpu() && t.scalar_type() == at::kLong && t.dim() == 1 &&
+                        t.is_contiguous() && t.numel() == n,
+                    what);
+  return t.data_ptr<int64_t>();
+}
+
+// align_packed(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens,
+//              Tensor blanks, int mode, Tensor? emission_validity,
+//              bool check_inputs) -> Tensor[]
 // Packed varlen form: record i is rows [sum frames[:i], +frames[i]) of a
 // contiguous fp32 [N, V] matrix and tokens [sum tokens[:i], +tokens[i]) of a
-// contiguous int64 vector.  One storage each, so no per-record tensors.
-std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align_packed(
-    const at::Tensor& emissions, at::IntArrayRef frames, const at::Tensor& targets,
-    at::IntArrayRef tokens, at::IntArrayRef blanks, int64_t mode,
+// contiguous int64 vector.  One storage each, so no per-record tensors; the
+// counts are CPU int64 vectors (blanks: one entry, or one per record), so no
+// per-record Python objects either.
+std::vector<at::Tensor> align_packed(
+    const at::Tensor& emissions, const at::Tensor& frames_t, const at::Tensor& targets,
+    const at::Tensor& tokens_t, const at::Tensor& blanks_t, int64_t mode,
     const std::optional<at::Tensor>& emission_validity, bool check_inputs) {
   check_mode(mode);
-  const int64_t count = static_cast<int64_t>(frames.size());
-  TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS &&
-                        static_cast<int64_t>(tokens.size()) == count &&
-                        static_cast<int64_t>(blanks.size()) == count,
+  const int64_t count = frames_t.numel();
+  TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS && tokens_t.numel() == count &&
+                        (blanks_t.numel() == count || blanks_t.numel() == 1),
                     "provide 1..65535 matching frame counts, token counts and blanks");
+  const char* counts_msg = "frame counts, token counts and blanks must be 1-D CPU int64 vectors";
+  const int64_t* frames = host_counts(frames_t, count, counts_msg);
+  const int64_t* tokens = host_counts(tokens_t, count, counts_msg);
+  const int64_t* blanks = host_counts(blanks_t, blanks_t.numel(), counts_msg);
+  const int64_t blank_step = blanks_t.numel() == 1 ? 0 : 1;
   const auto device = emissions.device();
   TORCH_CHECK_VALUE(device.is_cuda() && targets.device() == device &&
                         emissions.scalar_type() == at::kFloat && targets.scalar_type() == at::kLong &&
@@ -274,25 +288,25 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align_packed(
   StreamRecorder rec{stream};
   rec(emissions);
   rec(targets);
-  std::vector<ffa_record> recs(count);
-  std::vector<int64_t> lengths(frames.begin(), frames.end());
+  thread_local std::vector<ffa_record> recs;
+  recs.resize(count);
   int64_t row = 0, tok = 0;
   const float* ebase = emissions.numel() ? emissions.data_ptr<float>() : nullptr;
   const int64_t* tbase = targets.numel() ? targets.data_ptr<int64_t>() : nullptr;
+  const int64_t rows = emissions.size(0), ntok = targets.numel();
   for (int64_t i = 0; i < count; ++i) {
-    TORCH_CHECK_VALUE(frames[i] > 0 && frames[i] <= INT_MAX && tokens[i] >= 0 && tokens[i] <= 2047 &&
-                          blanks[i] >= 0 && blanks[i] < V,
+    const int64_t T = frames[i], U = tokens[i], blank = blanks[i * blank_step];
+    TORCH_CHECK_VALUE(T > 0 && T <= INT_MAX && U >= 0 && U <= 2047 && blank >= 0 && blank < V,
                       "unsupported frame count, target length, or blank ID");
-    TORCH_CHECK_VALUE(row + frames[i] <= emissions.size(0) && tok + tokens[i] <= targets.numel(),
+    TORCH_CHECK_VALUE(row + T <= rows && tok + U <= ntok,
                       "frame or token counts exceed the packed tensors");
-    recs[i] = ffa_record{ebase + row * V, tokens[i] ? tbase + tok : nullptr, frames[i],
-                         static_cast<int32_t>(V), static_cast<int32_t>(tokens[i]),
-                         static_cast<int32_t>(blanks[i]), 0};
-    row += frames[i];
-    tok += tokens[i];
+    recs[i] = ffa_record{ebase + row * V, U ? tbase + tok : nullptr, T, static_cast<int32_t>(V),
+                         static_cast<int32_t>(U), static_cast<int32_t>(blank), 0};
+    row += T;
+    tok += U;
   }
   const uint8_t* mask = check_mask(emission_validity, device, count, rec);
-  return run_align(recs, device, mode, mask, check_inputs, stream, std::move(lengths));
+  return std::get<0>(run_align(recs, device, mode, mask, check_inputs, stream, {}));
 }
 
 // emission_validity(Tensor[] emissions) -> Tensor   (alignment.cu:893-917)
@@ -380,8 +394,8 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
 TORCH_LIBRARY(ffa_b200, m) {
   m.def("align(Tensor[] emissions, Tensor[] targets, int[] blanks, int mode, "
         "Tensor? emission_validity=None, bool check_inputs=True) -> (Tensor[], int[])");
-  m.def("align_packed(Tensor emissions, int[] frames, Tensor targets, int[] tokens, int[] blanks, "
-        "int mode, Tensor? emission_validity=None, bool check_inputs=True) -> (Tensor[], int[])");
+  m.def("align_packed(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens, Tensor blanks, "
+        "int mode, Tensor? emission_validity=None, bool check_inputs=True) -> Tensor[]");
   m.def("emission_validity(Tensor[] emissions) -> Tensor");
   m.def("check_targets(Tensor[] emissions, Tensor[] targets, int[] blanks) -> Tensor");
 }

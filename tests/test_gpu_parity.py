@@ -80,6 +80,11 @@ def test_packed_form_equals_list_form(cuda, mode):
     packed = ffa.align_packed(e, wl.lengths.tolist(), t, wl.target_lengths.tolist(),
                               blank_id=wl.blank, mode=mode)
     assert_matches_oracle(packed, ref, "packed cfg1")
+    # Counts as NumPy arrays, as tensors, and per-record blanks as an array.
+    arrays = ffa.align_packed(e, wl.lengths, t, torch.from_numpy(wl.target_lengths),
+                              blank_id=np.full(wl.batch, wl.blank), mode=mode)
+    assert_matches_oracle(arrays, ref, "packed cfg1 from arrays")
+    assert arrays.lengths == packed.lengths
 
 
 def test_tie_records_are_exact_in_conventional_mode(cuda):

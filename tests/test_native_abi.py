@@ -4,6 +4,7 @@ import ctypes
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 from torch.utils import cpp_extension
@@ -174,3 +175,26 @@ def test_argument_contract_without_gpu():
         ffa.emission_validity([])
     with pytest.raises(ValueError):
         ffa.emission_validity([e])
+
+
+def test_packed_argument_contract_without_gpu():
+    e = torch.zeros(12, 6)
+    t = torch.tensor([1, 2])
+    with pytest.raises(ValueError, match="frames"):
+        ffa.align_packed(e, [6.0, 6.0], t, [1, 1])
+    with pytest.raises(ValueError, match="tokens"):
+        ffa.align_packed(e, [6, 6], t, np.array([[1, 1]]))
+    with pytest.raises(ValueError, match="matching"):
+        ffa.align_packed(e, [6, 6], t, [2])
+    with pytest.raises(ValueError, match="matching"):
+        ffa.align_packed(e, [], t, [])
+    with pytest.raises(ValueError, match="blank"):
+        ffa.align_packed(e, [6, 6], t, [1, 1], blank_id=[0])
+    with pytest.raises(TypeError):
+        ffa.align_packed(e, [6, 6], t, [1, 1], blank_id=True)
+    with pytest.raises(ValueError, match="frames"):
+        ffa.align_packed(e, torch.tensor([6.0, 6.0]), t, [1, 1])
+    with pytest.raises(ValueError, match="mode"):
+        ffa.align_packed(e, [6, 6], t, [1, 1], mode="fast")
+    with pytest.raises(ValueError, match="CUDA"):
+        ffa.align_packed(e, np.array([6, 6]), t, torch.tensor([1, 1]), blank_id=np.array([0, 0]))
