@@ -1,12 +1,20 @@
 // ffa_kernels.cu -- sm_100a kernels of the B200-native CTC forced aligner.
 //
-//   ffa_viterbi_forward   conventional max-plus Viterbi forward pass, one
-//                         record per warp group, packed into 512-thread CTAs;
-//                         writes 2-bit backpointers and per-segment ancestor
-//                         maps, then walks the maps from the terminal state
-//                         (semantics: reference alignment.cu:354-523)
+//   ffa_viterbi_forward   the first pass: max-plus Viterbi forward over every
+//                         whole record (conventional DP, semantics of the
+//                         reference's alignment.cu:354-523) and over every
+//                         32-frame piece of a record of the optimized route
+//                         (relaxed DPs, free start, best end); slots of warps
+//                         packed into 512-thread CTAs, emission rows staged by
+//                         TMA bulk copies; writes 2-bit backpointer rows,
+//                         segment anchors and, for pieces, end frontiers
+//   ffa_finish_route      the optimized route after the first pass: seam
+//                         plans, repairs of merged regions resumed from saved
+//                         frontiers, the conventional DP as fallback, routes
+//                         and diagnostics (alignment.cu:157-228, 525-592)
 //   ffa_trace_fill        parallel traceback of every segment of every
-//                         record + label/score gather (alignment.cu:597-667)
+//                         record + label/score gather (alignment.cu:597-667),
+//                         and the objective of joined records
 //   ffa_validity_scan     NaN/+inf scan of the emissions (alignment.cu:879-891)
 //   ffa_check_targets     target-ID and frame-feasibility checks alone
 //
