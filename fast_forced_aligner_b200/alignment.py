@@ -243,7 +243,8 @@ def align(
             ``1 <= B <= 65535``, ``1 <= T_i <= 2**31 - 1``, ``1 <= V_i <= 8192``.
         targets: ``B`` contiguous CUDA int64 ``(U_i,)`` tensors on the same
             device, IDs in ``[0, V_i)`` and different from the blank,
-            ``0 <= U_i <= 2047``.
+            ``0 <= U_i <= 32767`` (the reference stops at 2047; longer
+            transcripts run the conventional DP on a thread-block cluster).
         blank_id: one Python int or ``B`` Python ints (bools rejected).
         mode: ``"optimized"`` (default) or ``"conventional"``.  Conventional
             runs the exact max-plus Viterbi DP (stay > step > skip tie rule).

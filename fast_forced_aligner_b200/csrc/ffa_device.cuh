@@ -78,6 +78,46 @@ __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// ---- thread-block clusters (long records: one cluster per record) ----------
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ unsigned cluster_size() {
+  unsigned n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  return n;
+}
+// Address of this CTA's shared variable `p` in the shared memory of cluster
+// CTA `rank` (a shared::cluster address).
+__device__ __forceinline__ unsigned cluster_addr(const void* p, unsigned rank) {
+  unsigned a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void st_cluster_u64(unsigned cluster_address, unsigned long long v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.b64 [%0], %1;" ::"r"(cluster_address), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(unsigned cluster_address, float v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.f32 [%0], %1;" ::"r"(cluster_address), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(unsigned cluster_address, unsigned v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_address), "r"(v) : "memory");
+}
+// A load of this CTA's shared memory that sees stores other CTAs of the
+// cluster made to it.
+__device__ __forceinline__ unsigned long long ld_cluster_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.cluster.shared::cta.b64 %0, [%1];" : "=l"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+// Every thread of every CTA of the cluster; orders shared and global memory
+// accesses before it with those after it, cluster-wide.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // An emission that turns an unreachable state (-inf) into NaN: -inf + NaN and
 // -inf + inf are both NaN.
 __device__ __forceinline__ bool poisons(float e) { return e != e || e == INFINITY; }

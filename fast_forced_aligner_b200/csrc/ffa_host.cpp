@@ -48,6 +48,7 @@ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Geometry {
   bool chunked;  // optimized route: solved in pieces
+  int cluster;   // > 0: a long record, solved by a cluster of this many CTAs
   int K;         // states per thread
   int nw;        // warps for the DP
   int seg_log2;  // traceback segment length
@@ -92,10 +93,17 @@ int64_t piece_count(int64_t T) {
 Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
-  g.chunked = chunked_record(r, optimized);
-  g.K = g.chunked ? piece_k(S) : choose_k(S, latency_bound);
-  const int slot_log2 = g.K == 4 ? 7 : g.K == 8 ? 8 : 9;  // log2(32 K): states per warp
-  g.nw = static_cast<int>((S + (int64_t{1} << slot_log2) - 1) >> slot_log2);
+  if (S > ffa::kMaxStates) {
+    // Long record: the conventional DP on a cluster of 4096-state CTAs.
+    g.cluster = static_cast<int>((S + ffa::kLongStatesPerCta - 1) / ffa::kLongStatesPerCta);
+    g.K = ffa::kLongK;
+    g.nw = ffa::kMaxWarps;
+  } else {
+    g.chunked = chunked_record(r, optimized);
+    g.K = g.chunked ? piece_k(S) : choose_k(S, latency_bound);
+    const int slot_log2 = g.K == 4 ? 7 : g.K == 8 ? 8 : 9;  // log2(32 K): states per warp
+    g.nw = static_cast<int>((S + (int64_t{1} << slot_log2) - 1) >> slot_log2);
+  }
   if (g.chunked) {
     g.seg_log2 = ffa::kPieceSegLog2;
   } else {
@@ -127,7 +135,7 @@ int check_record(const ffa_record& r, int64_t i, bool need_targets) {
   if (!need_targets) return FFA_OK;
   if (r.tokens < 0 || (r.tokens > 0 && r.targets == nullptr))
     return fail(FFA_ERR_INVALID_ARGUMENT, "record " + std::to_string(i) + ": missing targets");
-  if (2 * static_cast<int64_t>(r.tokens) + 1 > ffa::kMaxStates || r.blank < 0 || r.blank >= r.vocab)
+  if (2 * static_cast<int64_t>(r.tokens) + 1 > ffa::kMaxLongStates || r.blank < 0 || r.blank >= r.vocab)
     return fail(FFA_ERR_UNSUPPORTED, "record " + std::to_string(i) +
                                          ": unsupported target length or blank ID");
   return FFA_OK;
@@ -154,9 +162,9 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, fill, slots, keys, classes, staging_bytes;
+  size_t recs, chunked, longs, fill, slots, keys, classes, staging_bytes;
   size_t bp, maps, anchors, frontiers, pstates, route, fill_done, workspace_bytes;
-  int64_t total_frames, num_pieces, num_chunked, fill_items;
+  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
 };
 
 bool latency_bound(int64_t slots) { return slots <= device_sms(); }
@@ -167,7 +175,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0;
+          pieces = 0, longs = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
@@ -179,6 +187,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
     fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
     frontier += g.frontier_elems;
     chunked += g.chunked ? 1 : 0;
+    longs += g.cluster > 0 ? 1 : 0;
     pieces += g.pieces;
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
@@ -186,10 +195,12 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->total_frames = frames;
   L->num_pieces = pieces;
   L->num_chunked = chunked;
+  L->num_long = longs;
   L->fill_items = fill;
   size_t off = 0;
   L->recs = off; off = align_up(off + sizeof(ffa::RecordDev) * count, 16);
   L->chunked = off; off = align_up(off + sizeof(int32_t) * chunked, 16);
+  L->longs = off; off = align_up(off + sizeof(int32_t) * longs, 16);
   L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 16);
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 16, 256);
   const size_t device_part = off;  // the most that is uploaded
@@ -430,6 +441,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   auto* host = static_cast<unsigned char*>(staging);
   auto* recs = reinterpret_cast<ffa::RecordDev*>(host + L.recs);
   auto* chunked = reinterpret_cast<int32_t*>(host + L.chunked);
+  auto* longs = reinterpret_cast<int32_t*>(host + L.longs);
   auto* fill = reinterpret_cast<ffa::FillItem*>(host + L.fill);
   auto* classes = reinterpret_cast<uint8_t*>(host + L.classes);
   const int64_t P = L.num_pieces;
@@ -442,6 +454,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
   thread_local RunLengthModel runs_model;
   runs_model.reset();
+  // Long records, keyed for their launches: (gathered, cluster size, index).
+  thread_local std::vector<uint64_t> long_keys;
+  long_keys.clear();
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, lat);
@@ -474,7 +489,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       max_row_vocab = std::max<unsigned>(max_row_vocab, r.vocab);
       row_vocab = (row_vocab < 0 || row_vocab == r.vocab) ? r.vocab : 0;
     }
-    if (g.chunked) {
+    if (g.cluster > 0) {
+      long_keys.push_back(static_cast<uint64_t>(d.row_mode ? 0 : 1) << 40 |
+                          static_cast<uint64_t>(g.cluster) << 32 | static_cast<uint64_t>(i));
+    } else if (g.chunked) {
       ++nchunked;
       runs_model.add(cls, g.pieces);
     } else {
@@ -525,6 +543,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   for (int64_t k = 0; k < count; ++k) {
     const int32_t i = sorted[k];
     const ffa::RecordDev& d = recs[i];
+    if (2 * d.U + 1 > ffa::kMaxStates) continue;  // long records run on clusters
     const int64_t before = n_first;
     const int32_t step = d.num_pieces > 1 ? run_pieces : 1;
     for (int32_t j = 0; j < d.num_pieces; j += step) order[n_first++] = ffa::SlotRef{i, j};
@@ -581,6 +600,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   }
   for (int64_t i = 0; i < count; ++i)
     if (!recs[i].row_mode) max_gather_k = std::max<int>(max_gather_k, recs[i].kst);
+  // Long records by launch: row-staged first, then by cluster size.
+  std::sort(long_keys.begin(), long_keys.end());
+  for (size_t k = 0; k < long_keys.size(); ++k) longs[k] = static_cast<int32_t>(long_keys[k] & 0xffffffffu);
   const size_t upload_bytes = bundles_off + sizeof(ffa::Bundle) * nb;
   const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
   const unsigned gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(max_gather_k));
@@ -619,6 +641,39 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return e == cudaSuccess ? FFA_OK : cuda_fail(e, "profiling event");
   };
   if ((rc = mark(FFA_PROFILE_START))) return rc;
+  // Long records: the conventional DP on one cluster each, one launch per
+  // (staging kind, cluster size).
+  if (!long_keys.empty()) {
+    ffa::LongParams lp{};
+    lp.recs = fp.recs;
+    lp.mask = fp.mask;
+    lp.check_inputs = fp.check_inputs;
+    lp.bp = fp.bp;
+    lp.maps = fp.maps;
+    lp.anchors = fp.anchors;
+    lp.out = fp.out;
+    const auto* dlongs = reinterpret_cast<const int32_t*>(dev + L.longs);
+    const size_t long_header = ffa::long_header_bytes();
+    for (size_t k = 0; k < long_keys.size();) {
+      const uint64_t group = long_keys[k] >> 32;
+      size_t m = 1;
+      while (k + m < long_keys.size() && (long_keys[k + m] >> 32) == group) ++m;
+      const bool row = (group >> 8) == 0;
+      const int cluster = static_cast<int>(group & 0xff);
+      const unsigned smem = static_cast<unsigned>(
+          long_header + (row ? static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4
+                             : ffa::gather_ring_bytes(ffa::kLongK)));
+      lp.records = dlongs + k;
+      err = ffa::launch_long(lp, static_cast<int>(m), cluster, row, rv, smem, s);
+      if (err == cudaErrorInvalidClusterSize)
+        return fail(FFA_ERR_UNSUPPORTED, "this GPU cannot co-schedule a cluster of " + std::to_string(cluster) +
+                                             " CTAs, which records of " +
+                                             std::to_string(cluster * ffa::kLongStatesPerCta) +
+                                             " states or fewer need");
+      if (err != cudaSuccess) return cuda_fail(err, "long-record launch");
+      k += m;
+    }
+  }
   // First pass: every piece of every record (a one-piece record is the
   // conventional DP).
   fp.bundles = dbundles;

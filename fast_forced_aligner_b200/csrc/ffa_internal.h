@@ -42,6 +42,16 @@ __host__ __device__ constexpr int bp_row_words(int S) { return (S + 63) / 64 * 4
 // Per-state arrays (frontiers, segment maps) of a record: one stride for all
 // thread layouts (K <= 16, 32 threads per warp).
 __host__ __device__ constexpr int state_stride(int S) { return (S + 511) / 512 * 512; }
+// Long records (kMaxStates < S <= kMaxLongStates, beyond the reference's own
+// limit): one thread-block cluster per record, CTA c of the cluster owning
+// the kLongStatesPerCta consecutive states from c * kLongStatesPerCta, K =
+// kLongK per thread.  Each frame, the last state of CTA c reaches CTA c + 1
+// through a kLinkRing-frame ring in CTA c + 1's shared memory.
+constexpr int kLongK = 8;
+constexpr int kLongStatesPerCta = kCtaThreads * kLongK;  // 4096
+constexpr int kMaxClusterCtas = 16;
+constexpr int kMaxLongStates = kMaxClusterCtas * kLongStatesPerCta;  // 65536
+constexpr int kLinkRing = 64;
 // Traceback segment length bounds (power of two).
 constexpr int kMinSegLog2 = 5;
 constexpr int kMaxSegLog2 = 10;
@@ -203,8 +213,30 @@ cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_it
 cudaError_t launch_validity(const ScanRecord* recs, int64_t count, const ScanItem* items,
                             int64_t num_items, uint8_t* valid, cudaStream_t stream);
 
-// Kernels launched so far by the calling thread (ffa_kernels.cu).
+// Arguments of one long-record launch: `count` records, one cluster of
+// `cluster` CTAs each.
+struct LongParams {
+  const RecordDev* recs;
+  const int32_t* records;    // indices of the launch's records
+  const uint8_t* mask;       // emission-validity mask or null
+  int32_t check_inputs;
+  uint32_t* bp;
+  uint16_t* maps;
+  int32_t* anchors;
+  OutputsDev out;
+};
+// Conventional DP of long records (ffa_long.cu).  Returns
+// cudaErrorInvalidClusterSize when the device cannot run one cluster of
+// that many CTAs.
+cudaError_t launch_long(const LongParams& params, int count, int cluster, bool row_mode,
+                        int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+// Dynamic shared memory a long-record CTA needs besides its emission ring.
+size_t long_header_bytes();
+
+// Kernels launched so far by the calling thread (ffa_kernels.cu), and the
+// hook every launcher calls.
 int64_t launches_so_far();
+void count_launch();
 
 // Sets the message ffa_last_error() returns on this thread (ffa_host.cpp).
 void set_last_error(const char* message);

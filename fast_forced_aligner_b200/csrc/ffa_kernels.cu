@@ -995,6 +995,7 @@ namespace {
 thread_local int64_t g_launches = 0;
 }  // namespace
 int64_t launches_so_far() { return g_launches; }
+void count_launch() { ++g_launches; }
 
 cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
                            int row_vocab, unsigned smem_bytes, cudaStream_t stream) {

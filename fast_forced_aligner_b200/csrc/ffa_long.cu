@@ -1,0 +1,445 @@
+// ffa_long.cu -- conventional DP of long records on thread-block clusters.
+//
+// A record with more CTC states than one CTA holds (kMaxStates < S <=
+// kMaxLongStates; the reference stops at S = 4095, alignment.py:250) runs on
+// one cluster of C = ceil(S / 4096) CTAs: CTA c owns states [4096 c,
+// 4096 (c + 1)), 8 per thread.  Each CTA runs, frame by frame, the same
+// max-plus step as every other DP of this library (dp_frame: stay > step >
+// skip by strict '>', one fp32 add per cell, alignment.cu:418-424, with the
+// ancestor deltas of the segment maps).  The only dependence between CTAs is
+// the left neighbour's last state at the previous frame (a state reads s-1
+// and s-2, and a CTA's first state is a blank, which has no skip), so:
+//   - after each frame, CTA c's last thread publishes that state for CTA c+1:
+//     one 8-byte store into a kLinkRing-frame ring in CTA c+1's shared
+//     memory (distributed shared memory, no global round trip);
+//   - CTA c+1's first thread reads it when it steps the next frame, and
+//     reports the frames it has consumed back into CTA c's shared memory once
+//     per frame group, so a producer runs at most kLinkRing frames ahead.
+// Every wait is bounded (kWaitNs); a CTA whose wait gave up stops waiting and
+// the record ends with status 5.  After the last frame the terminal states
+// and any failure reach the last CTA, which applies the terminal rule
+// (alignment.cu:496-510) and walks the segment maps into the anchors; the
+// traceback fill then runs as for any whole record.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+
+#include "ffa_device.cuh"
+#include "ffa_internal.h"
+
+namespace ffa {
+using namespace dev;
+namespace {
+
+constexpr int K = kLongK;
+constexpr int KT = K / 2;
+constexpr unsigned kFull = 0xffffffffu;
+
+struct LongShared {
+  Boundary bnd[2][kMaxWarps];  // last-state hand-off between the CTA's warps
+  int chk_bad[kMaxWarps];
+  int chk_rep[kMaxWarps];
+  int status;
+  unsigned cta_fault;          // a wait of this CTA gave up
+  unsigned fault;              // last CTA: a wait of some CTA of the cluster gave up
+  float term_last, term_prev;  // last CTA: alpha[S-1], alpha[S-2] at the last frame
+  unsigned long long link[kLinkRing];  // left neighbour's last state, frame t at t % kLinkRing
+  unsigned long long ack;              // frames the right neighbour has consumed
+  unsigned long long full[kRowRing];   // emission chunk landed (row staging)
+};
+constexpr size_t kLongHeader = (sizeof(LongShared) + 127) / 128 * 128;
+
+// One frame's boundary as a 64-bit word: alpha's bits, the ancestor delta
+// (at most 2 states per frame over a segment of at most 1024 frames: < 2^12)
+// and the frame number's low 20 bits.  A CTA runs ahead of its left
+// neighbour only while its first warp is above the reachable band, i.e. for
+// fewer than 32768 frames, so a slot never holds a stale word whose frame
+// bits equal those of the frame its reader waits for.
+constexpr unsigned kFrameBits = 20;
+constexpr unsigned kFrameMask = (1u << kFrameBits) - 1;
+__device__ __forceinline__ unsigned long long pack_link(int t, float alpha, int delta) {
+  return static_cast<unsigned long long>(__float_as_uint(alpha)) << 32 |
+         static_cast<unsigned long long>(static_cast<unsigned>(delta) & 0xfffu) << kFrameBits |
+         (static_cast<unsigned>(t) & kFrameMask);
+}
+
+template <bool kRow, int kV>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+ffa_long_forward(const __grid_constant__ LongParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  LongShared& sh = *reinterpret_cast<LongShared*>(smem_raw);
+  const unsigned rank = cluster_rank(), C = cluster_size();
+  const int r = P.records[blockIdx.x / C];
+  const RecordDev rec = P.recs[r];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = rec.T, U = rec.U, blank = rec.blank;
+  const int V = kV > 0 ? kV : rec.V;
+  const int S = 2 * U + 1;
+  const int64_t* tgt = rec.targets;
+  // Thread index within the record: thread g owns states K g .. K g + K-1.
+  const int g = static_cast<int>(rank) * kCtaThreads + tid;
+
+  // ---- status: mask, then target validation (alignment.cu:836, 852-874).
+  // Every CTA computes it, so the whole cluster agrees without exchanging it.
+  int status = P.mask != nullptr && !P.mask[r] ? 2 : 0;
+  if (P.check_inputs) {
+    int bad = 0, rep = 0;
+    for (int k = tid; k < U; k += kCtaThreads) {
+      const int64_t token = tgt[k];
+      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
+      if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+    }
+    bad = __reduce_or_sync(kFull, bad);
+    rep = __reduce_add_sync(kFull, rep);
+    if (lane == 0) { sh.chk_bad[warp] = bad; sh.chk_rep[warp] = rep; }
+    __syncthreads();
+    if (tid == 0) {
+      int b = 0;
+      int64_t q = 0;
+      for (int w = 0; w < kMaxWarps; ++w) { b |= sh.chk_bad[w]; q += sh.chk_rep[w]; }
+      sh.status = b ? 3 : (static_cast<int64_t>(U) + q > T ? 4 : status);
+    }
+    __syncthreads();
+    status = sh.status;
+  }
+  if (rank == 0 && tid == 0) {
+    // Diagnostics start at zero (alignment.py:101-129): long records always
+    // take the conventional DP.
+    P.out.stitched[r] = 0;
+    P.out.repair_passes[r] = 0;
+    P.out.repaired_frames[r] = 0;
+    for (int j = 0; j < 3; ++j) { P.out.shortcut_stats[3 * r + j] = 0; P.out.routing_stats[3 * r + j] = 0; }
+    if (P.out.reuse_stats) for (int j = 0; j < 4; ++j) P.out.reuse_stats[4 * r + j] = 0;
+    if (status >= 2) { P.out.objective[r] = -INFINITY; P.out.status[r] = status; }
+  }
+  if (status >= 2) return;  // every CTA of the cluster returns here
+
+  // Labels of this thread's states (odd k: token K/2 g + k/2) and which of
+  // them a skip may enter (alignment.cu:407).
+  int col[KT];
+  unsigned skip = 0;
+  {
+    const int first = KT * g;
+    int prev = (first >= 1 && first - 1 < U) ? clamp_label(tgt[first - 1], V) : -1;
+#pragma unroll
+    for (int q = 0; q < KT; ++q) {
+      const int u = first + q;
+      col[q] = u < U ? clamp_label(tgt[u], V) : blank;
+      if (u < U && u >= 1 && col[q] != blank && col[q] != prev) skip |= 1u << q;
+      prev = col[q];
+    }
+  }
+
+  // Emission rows: TMA bulk copies of kChunkFrames rows into a kRowRing ring
+  // (row staging), or per-thread cp.async gathers of the thread's columns.
+  const float* e = rec.emissions;
+  float* ring = reinterpret_cast<float*>(smem_raw + kLongHeader);
+  float* gring = ring + tid;
+  const int nchunks = (T + kChunkFrames - 1) / kChunkFrames;
+  auto issue_chunk = [&](int c) {  // kRow: by thread 0
+    const int rows = min(kChunkFrames, T - c * kChunkFrames);
+    const unsigned bytes = static_cast<unsigned>(rows) * V * 4u;
+    unsigned long long* bar = &sh.full[c % kRowRing];
+    mbar_expect_tx(bar, bytes);
+    tma_bulk_load(ring + (c % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(c) * kChunkFrames * V,
+                  bytes, bar);
+  };
+  auto gather = [&](int f) {  // !kRow: KT + 1 private 4-byte copies of frame f
+    if (f < T) {
+      const float* row = e + static_cast<int64_t>(f) * V;
+      float* dst = gring + (f % kGroup) * (KT + 1) * kCtaThreads;
+      cp_async4(dst, row + blank);
+#pragma unroll
+      for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
+    }
+    cp_async_commit();
+  };
+
+  if (tid == 0) {
+    // No frame has arrived: a frame field no reader can be waiting for.
+    for (int k = 0; k < kLinkRing; ++k) sh.link[k] = pack_link(static_cast<int>(kFrameMask), -INFINITY, 0);
+    sh.ack = 0;
+    sh.cta_fault = 0;
+    sh.fault = 0;
+    sh.term_last = -INFINITY;
+    sh.term_prev = -INFINITY;
+    if constexpr (kRow) {
+      for (int k = 0; k < kRowRing; ++k) mbar_init(&sh.full[k], 1);
+      fence_mbar_init();
+      for (int c = 0; c < kRowRing && c < nchunks; ++c) issue_chunk(c);
+    }
+  }
+  if constexpr (!kRow) {
+#pragma unroll
+    for (int f = 0; f < kGroup - 1; ++f) gather(f);
+  }
+  // Every CTA's ring is initialised before any neighbour writes into it.
+  cluster_sync();
+
+  const bool consumer = rank > 0 && tid == 0;
+  const bool producer = rank + 1 < C && tid == kCtaThreads - 1;
+  const unsigned right_link = producer ? cluster_addr(&sh.link[0], rank + 1) : 0u;
+  const unsigned left_ack = consumer ? cluster_addr(&sh.ack, rank - 1) : 0u;
+  bool tma_fault = false, link_fault = false;
+
+  // Producer: frame t's last state into the right neighbour's ring, once that
+  // neighbour has consumed frame t - kLinkRing from the same slot.
+  auto link_put = [&](int t, float alpha, int delta) {
+    const long long need = static_cast<long long>(t) - kLinkRing + 1;
+    if (need > 0 && !link_fault && static_cast<long long>(ld_cluster_u64(&sh.ack)) < need) {
+      const unsigned long long start = global_ns();
+      while (static_cast<long long>(ld_cluster_u64(&sh.ack)) < need)
+        if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+    }
+    st_cluster_u64(right_link + static_cast<unsigned>(t % kLinkRing) * 8u, pack_link(t, alpha, delta));
+  };
+  // Consumer: the left neighbour's last state at frame t.
+  auto link_get = [&](int t, float& alpha, int& delta) {
+    const unsigned long long* slot = &sh.link[t % kLinkRing];
+    const unsigned want = static_cast<unsigned>(t) & kFrameMask;
+    unsigned long long w = ld_cluster_u64(slot);
+    if ((static_cast<unsigned>(w) & kFrameMask) != want && !link_fault) {
+      const unsigned long long start = global_ns();
+      while (((w = ld_cluster_u64(slot)) & kFrameMask) != want)
+        if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+    }
+    alpha = __uint_as_float(static_cast<unsigned>(w >> 32));
+    delta = static_cast<int>((w >> kFrameBits) & 0xfffu);
+  };
+
+  float a[K];
+  int d[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) { a[k] = -INFINITY; d[k] = 0; }
+  const int hmask = (1 << rec.seg_log2) - 1;
+  const int row_words = bp_row_words(S);
+  uint8_t* bp_rows = reinterpret_cast<uint8_t*>(P.bp + rec.bp_off);
+  const bool stores_codes = K * g < row_words * 16;
+  const int64_t map_stride = state_stride(S);
+  const bool stores_maps = K * g < map_stride;
+  uint16_t* maps = P.maps + rec.map_off + K * g;
+  // Reachable band [S - 2(T - t), 2t + 1], tested per warp and frame group
+  // exactly as in the first pass; warps wholly past the last state never run.
+  const int w_lo = K * (g - lane);
+  const int w_hi = w_lo + 32 * K - 1;
+  const unsigned band_lo = static_cast<unsigned>(max(w_lo - 1, 0));
+  const int64_t hi64 = static_cast<int64_t>(w_hi) - S + 2 * static_cast<int64_t>(T);
+  const bool never = hi64 < 0 || w_lo >= S;
+  const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
+
+  auto load = [&](int f, int j, const float* rows, float& eb, float (&et)[KT]) {
+    if constexpr (kRow) {
+      const float* row = rows + j * V;
+      eb = row[blank];
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = row[col[q]];
+    } else {
+      gather(f + kGroup - 1);
+      cp_async_wait<kGroup - 1>();
+      const float* cur = gring + (f & (kGroup - 1)) * (KT + 1) * kCtaThreads;
+      eb = cur[0];
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+    }
+  };
+  auto store_map = [&](int t) {
+    if (!stores_maps) return;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(maps + static_cast<int64_t>(t >> rec.seg_log2) * map_stride);
+#pragma unroll
+    for (int q = 0; q < KT; ++q)
+      dst[q] = static_cast<uint32_t>(d[2 * q]) | (static_cast<uint32_t>(d[2 * q + 1]) << 16);
+  };
+  auto frame = [&](int t, int j, const float* rows) {
+    float eb, et[KT];
+    load(t, j, rows, eb, et);
+    float p1 = __shfl_up_sync(kFull, a[K - 1], 1);
+    int pd = __shfl_up_sync(kFull, d[K - 1], 1);
+    if (lane == 0) {
+      if (warp > 0) {
+        const Boundary nb = sh.bnd[t & 1][warp - 1];
+        p1 = nb.alpha;
+        pd = nb.delta;
+      } else if (consumer) {
+        link_get(t - 1, p1, pd);
+      } else {
+        p1 = -INFINITY;
+        pd = 0;
+      }
+    }
+    if (j == 0 && (t & hmask) == 0) {  // a new traceback segment starts at t
+#pragma unroll
+      for (int k = 0; k < K; ++k) d[k] = 0;
+      pd = 0;
+    }
+    const unsigned bits = dp_frame<K>(a, d, p1, pd, eb, et, skip);
+    if (stores_codes) store_codes<K>(bp_rows + static_cast<int64_t>(t) * row_words * 4, g, bits);
+    if (j == kGroup - 1 && (t & hmask) == hmask) store_map(t);
+    if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], d[K - 1]};
+    if (producer) link_put(t, a[K - 1], d[K - 1]);
+    __syncthreads();
+  };
+
+  const int ngroups = (T + kGroup - 1) / kGroup;
+  for (int gi = 0; gi < ngroups; ++gi) {
+    const float* rows = nullptr;
+    if constexpr (kRow) {
+      const int c = gi / kChunkGroups;
+      if (gi % kChunkGroups == 0 && !tma_fault && !mbar_wait(&sh.full[c % kRowRing], (c / kRowRing) & 1))
+        tma_fault = true;
+      rows = ring + ((c % kRowRing) * kChunkFrames + (gi % kChunkGroups) * kGroup) * V;
+    }
+    const int tg = gi * kGroup;
+    const unsigned g2 = 2u * static_cast<unsigned>(tg);
+    const bool seeded = gi == 0;
+    const bool group_active = seeded || (!never && g2 + 2u * (kGroup - 1) >= band_lo && g2 <= band_hi);
+    if (!group_active) {
+      // Out of band: above it the states stay -inf, or turn NaN for good on
+      // a NaN or +inf emission (as the full DP holds them); below it they
+      // can no longer reach the end.  The producer still publishes every
+      // frame, so its neighbour never waits on a frame it skipped.
+      const bool above = !never && g2 + 2u * (kGroup - 1) < band_lo;
+#pragma unroll 1
+      for (int j = 0; j < kGroup && tg + j < T; ++j) {
+        if (above || !kRow) {
+          float eb, et[KT];
+          load(tg + j, j, rows, eb, et);
+          if (above) {
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+              if (poisons((k & 1) ? et[k >> 1] : eb)) a[k] = NAN;
+          }
+        }
+        if (producer) link_put(tg + j, a[K - 1], d[K - 1]);
+        __syncthreads();
+      }
+    } else if (seeded) {
+      // Frame 0: alpha[s] = e[0, l[s]] for s < 2, else -inf (alignment.cu:409).
+      float eb, et[KT];
+      load(0, 0, rows, eb, et);
+      if (g == 0) {
+        a[0] = eb;
+        if (S > 1) a[1] = et[0];
+      }
+      if (lane == 31) sh.bnd[1][warp] = Boundary{a[K - 1], 0};
+      if (producer) link_put(0, a[K - 1], 0);
+      __syncthreads();
+#pragma unroll 1
+      for (int j = 1; j < kGroup && j < T; ++j) frame(j, j, rows);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kGroup; ++j)
+        if (tg + j < T) frame(tg + j, j, rows);
+    }
+    // Frames below tg + kGroup - 1 are consumed: their ring slots may be reused.
+    if (consumer) st_cluster_u64(left_ack, static_cast<unsigned long long>(tg + kGroup - 1));
+    if constexpr (kRow) {
+      const int c = gi / kChunkGroups;
+      if (tid == 0 && (gi % kChunkGroups == kChunkGroups - 1 || gi == ngroups - 1) && c + kRowRing < nchunks) {
+        fence_proxy_async();
+        issue_chunk(c + kRowRing);
+      }
+    }
+  }
+  if constexpr (!kRow) cp_async_wait<0>();
+  if constexpr (kRow) {
+    // After a failed wait, give the copies still in flight a short, bounded
+    // chance to land before the CTA's shared memory goes away.
+    if (tma_fault && tid == 0)
+      for (int c = max(0, nchunks - kRowRing); c < nchunks; ++c)
+        mbar_wait(&sh.full[c % kRowRing], (c / kRowRing) & 1, kDrainNs);
+  }
+  if (((T - 1) & hmask) != hmask) store_map(T - 1);  // the last, partial segment
+
+  // Terminal states and failures to the last CTA.
+  const int last = S - 1;
+#pragma unroll
+  for (int q = 0; q < K; ++q) {
+    const int s = K * g + q;
+    if (s == last) st_cluster_f32(cluster_addr(&sh.term_last, C - 1), a[q]);
+    if (s == last - 1) st_cluster_f32(cluster_addr(&sh.term_prev, C - 1), a[q]);
+  }
+  if (tma_fault || link_fault) atomicOr(&sh.cta_fault, 1u);
+  __syncthreads();
+  if (tid == 0 && sh.cta_fault) st_cluster_u32(cluster_addr(&sh.fault, C - 1), 1u);
+  __threadfence();  // backpointers and maps visible to the last CTA's walk
+  cluster_sync();
+  if (rank != C - 1 || tid != 0) return;
+
+  // Terminal rule: S-1 unless S>1 and alpha[S-2] >= alpha[S-1]
+  // (alignment.cu:497-499); status from the objective (:507-510).
+  int end_state = last;
+  float best = sh.term_last;
+  if (S > 1 && sh.term_prev >= best) { end_state = last - 1; best = sh.term_prev; }
+  const bool fault = sh.fault != 0;
+  const bool finite = isfinite(best);
+  P.out.objective[r] = best;
+  P.out.status[r] = fault ? kStatusDeviceFault : (finite ? 0 : 1);
+  if (!finite || fault) return;
+  // The path's state at every segment end, from the maps (the clamp never
+  // acts on maps a completed DP wrote; it keeps every read in the arena).
+  const uint16_t* mp = P.maps + rec.map_off;
+  int32_t* anc = P.anchors + rec.seg_off;
+  int s = end_state;
+  for (int seg = (T - 1) >> rec.seg_log2; seg >= 0; --seg) {
+    anc[seg] = s;
+    s = min(max(s - mp[static_cast<int64_t>(seg) * map_stride + s], 0), S - 1);
+  }
+}
+
+}  // namespace
+
+size_t long_header_bytes() { return kLongHeader; }
+
+cudaError_t launch_long(const LongParams& params, int count, int cluster, bool row_mode,
+                        int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  if (cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget) return cudaErrorInvalidValue;
+  auto kernel = !row_mode ? ffa_long_forward<false, 0>
+                         : (row_vocab == 32 ? ffa_long_forward<true, 32> : ffa_long_forward<true, 0>);
+  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  // Per device and kernel variant, once: the shared-memory budget and
+  // clusters beyond the portable 8 CTAs; then, per cluster size, whether one
+  // cluster fits the device at all (cached: 1 yes, -1 no).
+  static std::atomic<uint64_t> opted[3];
+  static std::atomic<int> fits[3][64][kMaxClusterCtas + 1];
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmemBudget));
+    if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err != cudaSuccess) return err;
+    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(count * cluster));
+  cfg.blockDim = dim3(kCtaThreads);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int dev_slot = device < 64 ? device : 63;
+  int known = fits[variant][dev_slot][cluster].load(std::memory_order_acquire);
+  if (known == 0 || device >= 64) {
+    int clusters = 0;
+    err = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+    if (err != cudaSuccess) return err;
+    known = clusters >= 1 ? 1 : -1;
+    if (device < 64) fits[variant][dev_slot][cluster].store(known, std::memory_order_release);
+  }
+  if (known < 0) return cudaErrorInvalidClusterSize;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+}  // namespace ffa

@@ -231,7 +231,7 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align(
                           e.dim() == 2 && t.dim() == 1 && e.is_contiguous() && t.is_contiguous(),
                       "inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device");
     TORCH_CHECK_VALUE(e.size(0) > 0 && e.size(0) <= INT_MAX && e.size(1) > 0 &&
-                          e.size(1) <= FFA_MAX_VOCAB && t.numel() <= 2047 && blanks[i] >= 0 &&
+                          e.size(1) <= FFA_MAX_VOCAB && t.numel() <= FFA_MAX_TOKENS && blanks[i] >= 0 &&
                           blanks[i] < e.size(1),
                       "unsupported frame count, vocabulary, target length, or blank ID");
     recs[i] = ffa_record{e.data_ptr<float>(), t.numel() ? t.data_ptr<int64_t>() : nullptr,
@@ -296,7 +296,7 @@ std::vector<at::Tensor> align_packed(
   const int64_t rows = emissions.size(0), ntok = targets.numel();
   for (int64_t i = 0; i < count; ++i) {
     const int64_t T = frames[i], U = tokens[i], blank = blanks[i * blank_step];
-    TORCH_CHECK_VALUE(T > 0 && T <= INT_MAX && U >= 0 && U <= 2047 && blank >= 0 && blank < V,
+    TORCH_CHECK_VALUE(T > 0 && T <= INT_MAX && U >= 0 && U <= FFA_MAX_TOKENS && blank >= 0 && blank < V,
                       "unsupported frame count, target length, or blank ID");
     TORCH_CHECK_VALUE(row + T <= rows && tok + U <= ntok,
                       "frame or token counts exceed the packed tensors");
@@ -367,7 +367,7 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
                           e.dim() == 2 && t.dim() == 1 && e.is_contiguous() && t.is_contiguous(),
                       msg);
     TORCH_CHECK_VALUE(e.size(0) > 0 && e.size(0) <= INT_MAX && e.size(1) > 0 &&
-                          e.size(1) <= FFA_MAX_VOCAB && t.numel() <= 2047 && blanks[i] >= 0 &&
+                          e.size(1) <= FFA_MAX_VOCAB && t.numel() <= FFA_MAX_TOKENS && blanks[i] >= 0 &&
                           blanks[i] < e.size(1),
                       "unsupported frame count, vocabulary, target length, or blank ID");
     recs[i] = ffa_record{e.data_ptr<float>(), t.numel() ? t.data_ptr<int64_t>() : nullptr,

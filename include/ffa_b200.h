@@ -65,10 +65,13 @@ enum {
   FFA_FLAG_CHECK_INPUTS = 1 /* validate target IDs and frame feasibility on the device */
 };
 
-/* Limits (alignment.py:237, 249-250; the state limit is this build's). */
+/* Limits (alignment.py:237, 249-250).  The reference stops at 2047 tokens
+ * (4095 states); this build also aligns longer transcripts, up to 65536 states,
+ * on thread-block clusters. */
 #define FFA_MAX_RECORDS 65535
 #define FFA_MAX_VOCAB 8192
 #define FFA_MAX_FRAMES 2147483647LL
+#define FFA_MAX_TOKENS 32767
 
 /* One record: a device-resident fp32 [frames, vocab] row-major emission
  * matrix and an int64 [tokens] transcript (reference: one entry of the

@@ -71,9 +71,19 @@ def test_align_query_sizes(lib):
     assert sizes.workspace_bytes >= (600 * 201 + 7 + 2305 * 4095) // 4
 
 
+def test_align_query_sizes_long_records(lib):
+    # 32767 tokens (65535 states, a 16-CTA cluster): backpointers alone take
+    # 2 bits per cell.
+    recs = records((34000, 32, 32767, 0), (90000, 32, 27000, 0))
+    sizes = Sizes()
+    assert lib.ffa_align_query(recs, 2, 1, 1, ctypes.byref(sizes)) == 0
+    assert sizes.total_frames == 34000 + 90000
+    assert sizes.workspace_bytes >= (34000 * 65535 + 90000 * 54001) // 4
+
+
 @pytest.mark.parametrize("spec, code", [
     ((0, 32, 1, 0), -2), ((10, 0, 1, 0), -2), ((10, 8193, 1, 0), -2),
-    ((10, 32, 2048, 0), -2), ((10, 32, 1, 32), -2), ((10, 32, 1, -1), -2),
+    ((10, 32, 32768, 0), -2), ((10, 32, 1, 32), -2), ((10, 32, 1, -1), -2),
 ])
 def test_align_query_rejects_unsupported_metadata(lib, spec, code):
     sizes = Sizes()
