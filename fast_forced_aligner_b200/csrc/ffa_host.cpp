@@ -95,8 +95,10 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
   if (S > ffa::kMaxStates) {
     // Long record: the conventional DP on a cluster of 4096-state CTAs.
-    g.cluster = static_cast<int>((S + ffa::kLongStatesPerCta - 1) / ffa::kLongStatesPerCta);
-    g.K = ffa::kLongK;
+    // (8 states per thread here; ffa_align may choose 16 for a batch whose
+    // records would not all fit the GPU at once.)
+    g.cluster = static_cast<int>((S + 8 * ffa::kCtaThreads - 1) / (8 * ffa::kCtaThreads));
+    g.K = 8;
     g.nw = ffa::kMaxWarps;
   } else {
     g.chunked = chunked_record(r, optimized);
@@ -454,7 +456,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
   thread_local RunLengthModel runs_model;
   runs_model.reset();
-  // Long records, keyed for their launches: (gathered, cluster size, index).
+  // Long records, keyed for their launches: (gathered, K = 16, cluster size,
+  // index).
   thread_local std::vector<uint64_t> long_keys;
   long_keys.clear();
   for (int64_t i = 0; i < count; ++i) {
@@ -490,8 +493,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       row_vocab = (row_vocab < 0 || row_vocab == r.vocab) ? r.vocab : 0;
     }
     if (g.cluster > 0) {
-      long_keys.push_back(static_cast<uint64_t>(d.row_mode ? 0 : 1) << 40 |
-                          static_cast<uint64_t>(g.cluster) << 32 | static_cast<uint64_t>(i));
+      long_keys.push_back(static_cast<uint64_t>(i));  // keyed below, once the batch is known
     } else if (g.chunked) {
       ++nchunked;
       runs_model.add(cls, g.pieces);
@@ -600,7 +602,36 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   }
   for (int64_t i = 0; i < count; ++i)
     if (!recs[i].row_mode) max_gather_k = std::max<int>(max_gather_k, recs[i].kst);
-  // Long records by launch: row-staged first, then by cluster size.
+  // Long records: 8 states per thread, unless the device cannot run the
+  // clusters of all of the batch's long records of one staging kind at once
+  // and 16 states per thread (half the cluster size) fits more of them.
+  const size_t long_header = ffa::long_header_bytes();
+  auto long_smem = [&](int k, bool row) {
+    return static_cast<unsigned>(
+        long_header + (row ? static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4
+                           : ffa::gather_ring_bytes(k)));
+  };
+  const int rv_long = row_vocab > 0 ? row_vocab : 0;
+  int64_t n_long_row = 0;
+  for (uint64_t key : long_keys) n_long_row += recs[key].row_mode ? 1 : 0;
+  for (uint64_t& key : long_keys) {
+    ffa::RecordDev& d = recs[key];
+    const bool row = d.row_mode != 0;
+    const int64_t n = row ? n_long_row : static_cast<int64_t>(long_keys.size()) - n_long_row;
+    const int64_t S = 2 * static_cast<int64_t>(d.U) + 1;
+    const int c8 = static_cast<int>((S + 8 * ffa::kCtaThreads - 1) / (8 * ffa::kCtaThreads));
+    const int c16 = static_cast<int>((S + 16 * ffa::kCtaThreads - 1) / (16 * ffa::kCtaThreads));
+    int k = 8, c = c8;
+    const int cap8 = ffa::long_capacity(8, c8, row, rv_long, long_smem(8, row));
+    if (cap8 < n && ffa::long_capacity(16, c16, row, rv_long, long_smem(16, row)) > cap8) {
+      k = 16;
+      c = c16;
+    }
+    d.kst = static_cast<uint8_t>(k);
+    key = static_cast<uint64_t>(row ? 0 : 1) << 44 | static_cast<uint64_t>(k == 16 ? 1 : 0) << 40 |
+          static_cast<uint64_t>(c) << 32 | key;
+  }
+  // By launch: row-staged first, then by states per thread and cluster size.
   std::sort(long_keys.begin(), long_keys.end());
   for (size_t k = 0; k < long_keys.size(); ++k) longs[k] = static_cast<int32_t>(long_keys[k] & 0xffffffffu);
   const size_t upload_bytes = bundles_off + sizeof(ffa::Bundle) * nb;
@@ -642,7 +673,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   };
   if ((rc = mark(FFA_PROFILE_START))) return rc;
   // Long records: the conventional DP on one cluster each, one launch per
-  // (staging kind, cluster size).
+  // (staging kind, states per thread, cluster size).
   if (!long_keys.empty()) {
     ffa::LongParams lp{};
     lp.recs = fp.recs;
@@ -653,23 +684,19 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     lp.anchors = fp.anchors;
     lp.out = fp.out;
     const auto* dlongs = reinterpret_cast<const int32_t*>(dev + L.longs);
-    const size_t long_header = ffa::long_header_bytes();
     for (size_t k = 0; k < long_keys.size();) {
       const uint64_t group = long_keys[k] >> 32;
       size_t m = 1;
       while (k + m < long_keys.size() && (long_keys[k + m] >> 32) == group) ++m;
-      const bool row = (group >> 8) == 0;
+      const bool row = ((group >> 12) & 1) == 0;
+      const int kst = ((group >> 8) & 1) ? 16 : 8;
       const int cluster = static_cast<int>(group & 0xff);
-      const unsigned smem = static_cast<unsigned>(
-          long_header + (row ? static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4
-                             : ffa::gather_ring_bytes(ffa::kLongK)));
       lp.records = dlongs + k;
-      err = ffa::launch_long(lp, static_cast<int>(m), cluster, row, rv, smem, s);
+      err = ffa::launch_long(lp, static_cast<int>(m), cluster, kst, row, rv, long_smem(kst, row), s);
       if (err == cudaErrorInvalidClusterSize)
         return fail(FFA_ERR_UNSUPPORTED, "this GPU cannot co-schedule a cluster of " + std::to_string(cluster) +
-                                             " CTAs, which records of " +
-                                             std::to_string(cluster * ffa::kLongStatesPerCta) +
-                                             " states or fewer need");
+                                             " CTAs, which records of up to " +
+                                             std::to_string(cluster * kst * ffa::kCtaThreads) + " states need");
       if (err != cudaSuccess) return cuda_fail(err, "long-record launch");
       k += m;
     }

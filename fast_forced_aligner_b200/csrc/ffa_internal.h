@@ -44,13 +44,11 @@ __host__ __device__ constexpr int bp_row_words(int S) { return (S + 63) / 64 * 4
 __host__ __device__ constexpr int state_stride(int S) { return (S + 511) / 512 * 512; }
 // Long records (kMaxStates < S <= kMaxLongStates, beyond the reference's own
 // limit): one thread-block cluster per record, CTA c of the cluster owning
-// the kLongStatesPerCta consecutive states from c * kLongStatesPerCta, K =
-// kLongK per thread.  Each frame, the last state of CTA c reaches CTA c + 1
+// the kCtaThreads * K consecutive states from c * kCtaThreads * K, K = 8 or
+// 16 per thread.  Each frame, the last state of CTA c reaches CTA c + 1
 // through a kLinkRing-frame ring in CTA c + 1's shared memory.
-constexpr int kLongK = 8;
-constexpr int kLongStatesPerCta = kCtaThreads * kLongK;  // 4096
 constexpr int kMaxClusterCtas = 16;
-constexpr int kMaxLongStates = kMaxClusterCtas * kLongStatesPerCta;  // 65536
+constexpr int kMaxLongStates = kMaxClusterCtas * kCtaThreads * 8;  // 65536
 constexpr int kLinkRing = 64;
 // Traceback segment length bounds (power of two).
 constexpr int kMinSegLog2 = 5;
@@ -225,11 +223,13 @@ struct LongParams {
   int32_t* anchors;
   OutputsDev out;
 };
-// Conventional DP of long records (ffa_long.cu).  Returns
-// cudaErrorInvalidClusterSize when the device cannot run one cluster of
-// that many CTAs.
-cudaError_t launch_long(const LongParams& params, int count, int cluster, bool row_mode,
+// Conventional DP of long records (ffa_long.cu), K states per thread (8 or
+// 16).  Returns cudaErrorInvalidClusterSize when the device cannot run one
+// cluster of that many CTAs.
+cudaError_t launch_long(const LongParams& params, int count, int cluster, int k, bool row_mode,
                         int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+// How many such clusters the current device runs at once (0: none fit).
+int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned smem_bytes);
 // Dynamic shared memory a long-record CTA needs besides its emission ring.
 size_t long_header_bytes();
 

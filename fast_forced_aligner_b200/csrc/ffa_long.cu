@@ -2,8 +2,10 @@
 //
 // A record with more CTC states than one CTA holds (kMaxStates < S <=
 // kMaxLongStates; the reference stops at S = 4095, alignment.py:250) runs on
-// one cluster of C = ceil(S / 4096) CTAs: CTA c owns states [4096 c,
-// 4096 (c + 1)), 8 per thread.  Each CTA runs, frame by frame, the same
+// one cluster of C = ceil(S / 512 K) CTAs: CTA c owns states [512 K c,
+// 512 K (c + 1)), K per thread (8, or 16 where that lets every record of the
+// launch run at once: clusters of more than 9 CTAs fit only 7 at a time on a
+// B200).  Each CTA runs, frame by frame, the same
 // max-plus step as every other DP of this library (dp_frame: stay > step >
 // skip by strict '>', one fp32 add per cell, alignment.cu:418-424, with the
 // ancestor deltas of the segment maps).  The only dependence between CTAs is
@@ -33,8 +35,6 @@ namespace ffa {
 using namespace dev;
 namespace {
 
-constexpr int K = kLongK;
-constexpr int KT = K / 2;
 constexpr unsigned kFull = 0xffffffffu;
 
 struct LongShared {
@@ -65,9 +65,10 @@ __device__ __forceinline__ unsigned long long pack_link(int t, float alpha, int 
          (static_cast<unsigned>(t) & kFrameMask);
 }
 
-template <bool kRow, int kV>
+template <int K, bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_long_forward(const __grid_constant__ LongParams P) {
+  constexpr int KT = K / 2;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   LongShared& sh = *reinterpret_cast<LongShared*>(smem_raw);
   const unsigned rank = cluster_rank(), C = cluster_size();
@@ -185,28 +186,43 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
   bool tma_fault = false, link_fault = false;
 
   // Producer: frame t's last state into the right neighbour's ring, once that
-  // neighbour has consumed frame t - kLinkRing from the same slot.
+  // neighbour has consumed frame t - kLinkRing from the same slot (the
+  // neighbour's count is re-read only when the copy last read is too old).
+  long long acked = 0;
   auto link_put = [&](int t, float alpha, int delta) {
     const long long need = static_cast<long long>(t) - kLinkRing + 1;
-    if (need > 0 && !link_fault && static_cast<long long>(ld_cluster_u64(&sh.ack)) < need) {
-      const unsigned long long start = global_ns();
-      while (static_cast<long long>(ld_cluster_u64(&sh.ack)) < need)
-        if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+    if (need > acked) {
+      acked = static_cast<long long>(ld_cluster_u64(&sh.ack));
+      if (need > acked && !link_fault) {
+        const unsigned long long start = global_ns();
+        while ((acked = static_cast<long long>(ld_cluster_u64(&sh.ack))) < need)
+          if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+      }
     }
     st_cluster_u64(right_link + static_cast<unsigned>(t % kLinkRing) * 8u, pack_link(t, alpha, delta));
   };
-  // Consumer: the left neighbour's last state at frame t.
-  auto link_get = [&](int t, float& alpha, int& delta) {
+  // Consumer, warp 0: lane l < kGroup holds the word of frame tg - 1 + l as it
+  // stood when the group started (the producer usually runs ahead, so a
+  // group's boundaries cost one load per lane); lane 0 waits only for a frame
+  // that had not arrived.
+  const bool link_warp = rank > 0 && warp == 0;
+  unsigned long long linkw = 0;
+  auto link_prefetch = [&](int tg) {
+    const int f = tg - 1 + lane;
+    linkw = (lane < kGroup && f >= 0) ? ld_cluster_u64(&sh.link[f % kLinkRing]) : 0ull;
+  };
+  auto link_wait = [&](int t, unsigned long long w) {
     const unsigned long long* slot = &sh.link[t % kLinkRing];
     const unsigned want = static_cast<unsigned>(t) & kFrameMask;
-    unsigned long long w = ld_cluster_u64(slot);
-    if ((static_cast<unsigned>(w) & kFrameMask) != want && !link_fault) {
-      const unsigned long long start = global_ns();
-      while (((w = ld_cluster_u64(slot)) & kFrameMask) != want)
-        if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+    if ((static_cast<unsigned>(w) & kFrameMask) != want) {
+      w = ld_cluster_u64(slot);
+      if ((static_cast<unsigned>(w) & kFrameMask) != want && !link_fault) {
+        const unsigned long long start = global_ns();
+        while (((w = ld_cluster_u64(slot)) & kFrameMask) != want)
+          if (global_ns() - start > kWaitNs) { link_fault = true; break; }
+      }
     }
-    alpha = __uint_as_float(static_cast<unsigned>(w >> 32));
-    delta = static_cast<int>((w >> kFrameBits) & 0xfffu);
+    return w;
   };
 
   float a[K];
@@ -256,13 +272,17 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
     load(t, j, rows, eb, et);
     float p1 = __shfl_up_sync(kFull, a[K - 1], 1);
     int pd = __shfl_up_sync(kFull, d[K - 1], 1);
+    unsigned long long lw = 0;
+    if (link_warp) lw = __shfl_sync(kFull, linkw, j);  // frame t - 1's word as prefetched
     if (lane == 0) {
       if (warp > 0) {
         const Boundary nb = sh.bnd[t & 1][warp - 1];
         p1 = nb.alpha;
         pd = nb.delta;
       } else if (consumer) {
-        link_get(t - 1, p1, pd);
+        lw = link_wait(t - 1, lw);
+        p1 = __uint_as_float(static_cast<unsigned>(lw >> 32));
+        pd = static_cast<int>((lw >> kFrameBits) & 0xfffu);
       } else {
         p1 = -INFINITY;
         pd = 0;
@@ -277,6 +297,8 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
     if (stores_codes) store_codes<K>(bp_rows + static_cast<int64_t>(t) * row_words * 4, g, bits);
     if (j == kGroup - 1 && (t & hmask) == hmask) store_map(t);
     if (lane == 31) sh.bnd[(t + 1) & 1][warp] = Boundary{a[K - 1], d[K - 1]};
+    // Published before the barrier (measured faster than after it from three
+    // CTAs per cluster on: the neighbour's group prefetch then finds it).
     if (producer) link_put(t, a[K - 1], d[K - 1]);
     __syncthreads();
   };
@@ -325,9 +347,11 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
       if (lane == 31) sh.bnd[1][warp] = Boundary{a[K - 1], 0};
       if (producer) link_put(0, a[K - 1], 0);
       __syncthreads();
+      if (link_warp) link_prefetch(0);
 #pragma unroll 1
       for (int j = 1; j < kGroup && j < T; ++j) frame(j, j, rows);
     } else {
+      if (link_warp) link_prefetch(tg);
 #pragma unroll
       for (int j = 0; j < kGroup; ++j)
         if (tg + j < T) frame(tg + j, j, rows);
@@ -392,52 +416,81 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
 
 size_t long_header_bytes() { return kLongHeader; }
 
-cudaError_t launch_long(const LongParams& params, int count, int cluster, bool row_mode,
-                        int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
-  if (count <= 0) return cudaSuccess;
-  if (cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget) return cudaErrorInvalidValue;
-  auto kernel = !row_mode ? ffa_long_forward<false, 0>
-                         : (row_vocab == 32 ? ffa_long_forward<true, 32> : ffa_long_forward<true, 0>);
-  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
-  int device = 0;
-  cudaError_t err = cudaGetDevice(&device);
-  if (err != cudaSuccess) return err;
-  // Per device and kernel variant, once: the shared-memory budget and
-  // clusters beyond the portable 8 CTAs; then, per cluster size, whether one
-  // cluster fits the device at all (cached: 1 yes, -1 no).
-  static std::atomic<uint64_t> opted[3];
-  static std::atomic<int> fits[3][64][kMaxClusterCtas + 1];
-  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
-  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kSmemBudget));
-    if (err != cudaSuccess) return err;
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (err != cudaSuccess) return err;
-    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
-  }
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+namespace {
+using LongKernel = void (*)(LongParams);
+// Kernel variant and its index among the six (K, staging) instantiations.
+LongKernel long_kernel(int k, bool row_mode, int row_vocab, int* variant) {
+  const int v = (k == 16 ? 3 : 0) + (!row_mode ? 0 : (row_vocab == 32 ? 2 : 1));
+  *variant = v;
+  static const LongKernel table[6] = {
+      ffa_long_forward<8, false, 0>,  ffa_long_forward<8, true, 0>,  ffa_long_forward<8, true, 32>,
+      ffa_long_forward<16, false, 0>, ffa_long_forward<16, true, 0>, ffa_long_forward<16, true, 32>};
+  return table[v];
+}
+cudaLaunchConfig_t long_config(int count, int cluster, unsigned smem, cudaStream_t stream,
+                               cudaLaunchAttribute* attr) {
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(count * cluster));
   cfg.blockDim = dim3(kCtaThreads);
-  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const int dev_slot = device < 64 ? device : 63;
-  int known = fits[variant][dev_slot][cluster].load(std::memory_order_acquire);
-  if (known == 0 || device >= 64) {
-    int clusters = 0;
-    err = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
-    if (err != cudaSuccess) return err;
-    known = clusters >= 1 ? 1 : -1;
-    if (device < 64) fits[variant][dev_slot][cluster].store(known, std::memory_order_release);
+  return cfg;
+}
+// Per device and variant, once: the shared-memory budget and clusters beyond
+// the portable 8 CTAs.
+cudaError_t prepare_long(LongKernel kernel, int variant, int device) {
+  static std::atomic<uint64_t> opted[6];
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit != 0 && (opted[variant].load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBudget));
+  if (err != cudaSuccess) return err;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (err != cudaSuccess) return err;
+  if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
+}  // namespace
+
+int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned smem_bytes) {
+  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget) return 0;
+  int variant = 0;
+  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, &variant);
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 0;
+  // Cached per (device, variant, cluster size): the count + 1 (0 = unknown).
+  static std::atomic<int> known[6][64][kMaxClusterCtas + 1];
+  const int slot = device < 64 ? device : 63;
+  const int cached = known[variant][slot][cluster].load(std::memory_order_acquire);
+  if (cached > 0 && device < 64) return cached - 1;
+  if (prepare_long(kernel, variant, device) != cudaSuccess) return 0;
+  cudaLaunchAttribute attr;
+  cudaLaunchConfig_t cfg = long_config(1, cluster, smem_bytes, nullptr, &attr);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    clusters = 0;
   }
-  if (known < 0) return cudaErrorInvalidClusterSize;
+  if (device < 64) known[variant][slot][cluster].store(clusters + 1, std::memory_order_release);
+  return clusters;
+}
+
+cudaError_t launch_long(const LongParams& params, int count, int cluster, int k, bool row_mode,
+                        int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget)
+    return cudaErrorInvalidValue;
+  if (long_capacity(k, cluster, row_mode, row_vocab, smem_bytes) < 1) return cudaErrorInvalidClusterSize;
+  int variant = 0;
+  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, &variant);
+  cudaLaunchAttribute attr;
+  cudaLaunchConfig_t cfg = long_config(count, cluster, smem_bytes, stream, &attr);
   count_launch();
   return cudaLaunchKernelEx(&cfg, kernel, params);
 }

@@ -52,6 +52,16 @@ def test_every_cluster_size_matches_oracle(cuda, mode):
     assert_matches_oracle(result, ref, f"cluster sizes {mode}")
 
 
+def test_sixteen_states_per_thread_when_clusters_do_not_all_fit(cuda):
+    # 12 records of S = 37001 need 10-CTA clusters at 8 states per thread, of
+    # which a B200 runs 11 at a time: the batch takes 16 states per thread
+    # (5-CTA clusters) instead.
+    rng = np.random.default_rng(5)
+    es, ts = zip(*(long_record(rng, 19000, 18500) for _ in range(12)))
+    result = ffa.align(*cuda_records(es, ts), blank_id=0, mode="conventional")
+    assert_matches_oracle(result, oracle.align(list(es), list(ts), 0, threads=THREADS), "K=16 batch")
+
+
 def test_gathered_long_record_matches_oracle(cuda):
     # V = 1025 rows are gathered per thread (no row staging); blank 1024.
     rng = np.random.default_rng(7)
