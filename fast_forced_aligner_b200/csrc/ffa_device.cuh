@@ -248,8 +248,10 @@ __device__ __forceinline__ void store_codes(uint8_t* row, int tl, unsigned bits)
 // shuffles; every lane tracks the same state.  `at_frame(t, s)` is called (by
 // every lane) with the path's state at each frame t_hi-1 .. t_lo; returns the
 // state at t_lo.  bp: the record's rows, row_words words per frame.
+// Rows are read through L2 (ld.global.cg): a trace may follow rows that
+// another CTA of the same launch wrote.
 template <typename AtFrame>
-__device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int row_words, int s,
+__device__ __forceinline__ int warp_trace(const uint32_t* bp, int row_words, int s,
                                           int t_hi, int t_lo, int lane, AtFrame at_frame) {
   constexpr int FB = 10, NW = 3;
   for (int t = t_hi; t > t_lo;) {
@@ -257,7 +259,7 @@ __device__ __forceinline__ int warp_trace(const uint32_t* __restrict__ bp, int r
     const int tt = t - f;
     const int w0 = s >> 4;
     uint32_t w = 0;
-    if (f < FB && tt > t_lo && w0 - dd >= 0) w = bp[static_cast<int64_t>(tt) * row_words + (w0 - dd)];
+    if (f < FB && tt > t_lo && w0 - dd >= 0) w = __ldcg(bp + static_cast<int64_t>(tt) * row_words + (w0 - dd));
     const int steps = min(FB, t - t_lo);
     for (int i = 0; i < steps; ++i) {
       const int ct = t - i;

@@ -165,7 +165,7 @@ int device_sms() {
 // at their end.
 struct AlignLayout {
   size_t recs, chunked, longs, fill, slots, keys, classes, staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, workspace_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
 };
 
@@ -217,6 +217,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->pstates = off; off = align_up(off + sizeof(ffa::PieceState) * pieces, 256);
   L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  L->finish_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->workspace_bytes = off;
   return FFA_OK;
 }
@@ -655,6 +656,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   fp.pstates = reinterpret_cast<ffa::PieceState*>(dev + L.pstates);
   fp.route = reinterpret_cast<int32_t*>(dev + L.route);
   fp.fill_done = reinterpret_cast<int32_t*>(dev + L.fill_done);
+  fp.finish_done = reinterpret_cast<int32_t*>(dev + L.finish_done);
   fp.out = ffa::OutputsDev{outputs->labels, outputs->scores, outputs->status, outputs->objective,
                            outputs->stitched, outputs->repair_passes, outputs->repaired_frames,
                            outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
@@ -721,17 +723,13 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       row_slot_bytes ? static_cast<int64_t>((ffa::kSmemBudget - 2048 - header) / row_slot_bytes) : 1);
   const unsigned finish_row_smem = static_cast<unsigned>(header + finish_slots * row_slot_bytes);
   // Round 0 spreads each record's repair jobs over up to four CTAs while the
-  // records leave SMs free; later rounds take one CTA per record.
+  // records leave SMs free; the rest of a record runs on the last of them.
   const int spread = static_cast<int>(std::clamp<int64_t>(sms / std::max<int64_t>(nchunked, 1), 1, 4));
-  for (int phase = 0; phase < 2; ++phase) {
-    const int per = phase == 0 ? spread : 1;
-    err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), phase, per, true, rv,
-                             finish_row_smem, s);
-    if (err != cudaSuccess) return cuda_fail(err, "finish launch");
-    err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), phase,
-                             per, false, 0, gather_smem, s);
-    if (err != cudaSuccess) return cuda_fail(err, "finish launch");
-  }
+  err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), spread, true, rv, finish_row_smem, s);
+  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), spread,
+                           false, 0, gather_smem, s);
+  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
   err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
                          static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, s);

@@ -143,9 +143,11 @@ struct FillItem {
   int32_t first_seg;
 };
 
-// Emission-validity scan: one CTA per 16 KiB-aligned chunk of one record.
+// Emission-validity scan: one CTA per 64 KiB chunk (16-byte aligned) of one
+// record, kScanBatch float4 loads in flight per thread.
 constexpr int kScanThreads = 256;
-constexpr int kScanChunkBytes = 16384;
+constexpr int kScanChunkBytes = 65536;
+constexpr int kScanBatch = 8;
 struct ScanRecord {
   const float* data;
   int64_t count;  // elements
@@ -191,6 +193,7 @@ struct ForwardParams {
   uint32_t row_slot_bytes;
   int32_t run_pieces;        // kPhaseFirst: pieces per slot of the optimized route
   int32_t* fill_done;        // per record: fill CTAs finished (zeroed by the first pass)
+  int32_t* finish_done;      // per record: finisher CTAs through round 0 (zeroed by the first pass)
 };
 
 // row_vocab: the vocabulary shared by every row-staged record of the
@@ -198,10 +201,10 @@ struct ForwardParams {
 cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
                            int row_vocab, unsigned smem_bytes, cudaStream_t stream);
 // Everything after the first pass of the optimized route -- seam plans,
-// repair rounds, conventional fallback: phase 0 (round 0, ctas_per_record
-// CTAs per listed record), then phase 1 (the rest, one CTA per record).
+// repair rounds, conventional fallback -- in one launch: round 0's repairs on
+// ctas_per_record CTAs per listed record, the rest on the last of them.
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          int phase, int ctas_per_record, bool row_mode, int row_vocab,
+                          int ctas_per_record, bool row_mode, int row_vocab,
                           unsigned smem_bytes, cudaStream_t stream);
 // Traceback fill of every segment; for records of the optimized route the
 // last fill CTA of the record also folds the objective of a joined path.

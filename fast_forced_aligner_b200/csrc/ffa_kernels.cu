@@ -171,7 +171,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
     const float4* src = reinterpret_cast<const float4*>(run.frontier_in + K * tl);
 #pragma unroll
     for (int k = 0; k < K; k += 4) {
-      const float4 v = src[k / 4];
+      const float4 v = __ldcg(src + k / 4);  // through L2: another CTA may have written it
       a[k] = v.x; a[k + 1] = v.y; a[k + 2] = v.z; a[k + 3] = v.w;
     }
     if (lane == 31) sh.bnd[t0 & 1][warp] = Boundary{a[K - 1], 0};
@@ -557,6 +557,7 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
         // Diagnostics start at zero (alignment.py:101-129); the optimized
         // route's plan counts repairs and joins into them.
         P.fill_done[r] = 0;
+        P.finish_done[r] = 0;
         P.out.stitched[r] = 0;
         P.out.repair_passes[r] = 0;
         P.out.repaired_frames[r] = 0;
@@ -611,6 +612,17 @@ struct PlanStats {
   int jobs = 0;
 };
 
+// A piece's state as other CTAs of the running launch may have left it:
+// loaded through L2 (ld.global.cg), never from a stale L1 line.
+__device__ __forceinline__ PieceState load_piece_state(const PieceState* p) {
+  const int4 a = __ldcg(reinterpret_cast<const int4*>(p));
+  const int4 b = __ldcg(reinterpret_cast<const int4*>(p) + 1);
+  PieceState s;
+  s.start = a.x; s.end = a.y; s.flags = a.z; s.start_skip = a.w;
+  s.region_start[0] = b.x; s.region_start[1] = b.y; s.region_start[2] = b.z; s.region_start[3] = b.w;
+  return s;
+}
+
 // Seam check and repair planning of one round of one record, by one warp.  A
 // region is a run of pieces solved as one DP; a seam is legal when the right
 // region's start state follows the left region's end state by a CTC move
@@ -653,9 +665,9 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
     const int j = base + lane;
     bool seam = false, fail = false, region_bad = false, region_fault = false;
     if (j < C) {
-      const PieceState mine = ps[P0 + j];
-      const bool next_rs = j + 1 >= C || ps[P0 + j + 1].region_start[round] != 0;
-      const int prev_end = j > 0 ? ps[P0 + j - 1].end : 0;
+      const PieceState mine = load_piece_state(ps + P0 + j);
+      const bool next_rs = j + 1 >= C || __ldcg(&ps[P0 + j + 1].region_start[round]) != 0;
+      const int prev_end = j > 0 ? __ldcg(&ps[P0 + j - 1].end) : 0;
       seam = mine.region_start[round] != 0 && j > 0;
       // The next round's regions start as this round's; merges clear below.
       if (!final_round && write_regions) ps[P0 + j].region_start[round + 1] = mine.region_start[round];
@@ -715,24 +727,27 @@ __device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__
 constexpr size_t kFinishDynamicSmem = kSmemBudget - 2048;
 static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
 
-// Everything after the first pass of the optimized route, in two launches
-// (records need nothing from one another):
-//   phase 0  R CTAs per record: each plans round 0 (the same plan) and runs
-//            the round's repair jobs j with j % R == its index, so a record's
-//            jobs spread over R SMs;
-//   phase 1  one CTA per record: rounds 1 .. kRepairRounds of planning
-//            (warp 0) and repairs (slots of nw warps, in parallel), the final
-//            plan, the conventional DP when the route cannot join the record,
-//            and the record's route and diagnostics.
+// Everything after the first pass of the optimized route, in one launch
+// (records need nothing from one another).  R CTAs per record each plan
+// round 0 (the same plan) and run the round's repair jobs j with j % R == its
+// index, so a record's first jobs spread over R SMs; the record's last CTA to
+// finish them (a counter per record) then continues alone: rounds 1 ..
+// kRepairRounds of planning (warp 0) and repairs (slots of nw warps, in
+// parallel), the final plan, the conventional DP when the route cannot join
+// the record, and the record's route and diagnostics.  A record that round 0
+// already routes is finished by its CTA 0.  Data other CTAs of this launch
+// wrote (piece states, frontiers, backpointer rows) is read through L2.
 template <bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
-ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records, int phase,
+ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records,
                  int ctas_per_record) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
   __shared__ JobList jobs;
   __shared__ int route_s;
-  const int part = static_cast<int>(blockIdx.x % ctas_per_record);
+  __shared__ int last_s;
+  int part = static_cast<int>(blockIdx.x % ctas_per_record);
+  int parts = ctas_per_record;
   const int r = records[blockIdx.x / ctas_per_record];
   const RecordDev rec = P.recs[r];
   SlotCtx x;
@@ -760,9 +775,7 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   // Warp 0 keeps the record's diagnostics and writes them once at the end.
   int passes = 0;
   int64_t repaired = 0, spared = 0, frontier_reads = 0;
-  const int first_round = phase == 0 ? 0 : 1;
-  const int last_round = phase == 0 ? 0 : kRepairRounds;
-  for (int round = first_round; round <= last_round; ++round) {
+  for (int round = 0; round <= kRepairRounds; ++round) {
     __syncthreads();
     if (x.warp == 0) {
       PlanStats stats;
@@ -781,7 +794,7 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
     const int n = jobs.count;
     const int64_t fstride = state_stride(2 * rec.U + 1);
     if (in_slot) {
-      for (int j = part + x.slot * ctas_per_record; j < n; j += nslots * ctas_per_record) {
+      for (int j = part + x.slot * parts; j < n; j += nslots * parts) {
         const int p = jobs.piece[j];
         const int idx = p - rec.first_piece;
         const int last = jobs.last[j] - rec.first_piece;
@@ -801,22 +814,26 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
         chunk_base += piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
       }
     }
-  }
-  if (phase == 0) {
-    // Round 0's share of the diagnostics, once per record.
-    if (x.tid == 0 && part == 0) {
-      P.out.repair_passes[r] = passes;
-      P.out.repaired_frames[r] = repaired;
-      if (P.out.reuse_stats) {
-        P.out.reuse_stats[4 * r + 0] = spared;
-        P.out.reuse_stats[4 * r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
-        P.out.reuse_stats[4 * r + 3] = frontier_reads;
+    if (parts > 1) {
+      // The record's CTAs ran round 0's jobs between them; the last one to
+      // finish continues alone (release: every CTA's results before its
+      // count; acquire: the counts before the continuing CTA's reads).
+      __syncthreads();
+      if (x.tid == 0) {
+        __threadfence();
+        last_s = atomicAdd(&P.finish_done[r], 1) == parts - 1;
+        __threadfence();
       }
+      __syncthreads();
+      if (!last_s) return;
+      part = 0;
+      parts = 1;
     }
-    return;
   }
+  // Round 0 routed the record: every CTA planned it, CTA 0 finishes it.
+  if (part != 0) return;
   if (x.tid == 0) {
-    // Route and diagnostics (alignment.py:101-129), adding to round 0's.
+    // Route and diagnostics (alignment.py:101-129).
     const int route = route_s;
     P.route[r] = route;
     if (route == kRouteNone && P.out.status[r] == 0) {
@@ -824,11 +841,12 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
       P.out.objective[r] = -INFINITY;
     }
     if (route == kRouteStitched) P.out.stitched[r] = 1;
-    P.out.repair_passes[r] += passes;
-    P.out.repaired_frames[r] += repaired;
+    P.out.repair_passes[r] = passes;
+    P.out.repaired_frames[r] = repaired;
     if (P.out.reuse_stats) {
-      P.out.reuse_stats[4 * r + 0] += spared;
-      P.out.reuse_stats[4 * r + 3] += frontier_reads;
+      P.out.reuse_stats[4 * r + 0] = spared;
+      P.out.reuse_stats[4 * r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
+      P.out.reuse_stats[4 * r + 3] = frontier_reads;
     }
   }
   if (route_s == kRouteFallback && x.slot == 0) {
@@ -938,10 +956,15 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
 }
 
 // valid[r] was set to 1; any CTA finding NaN or +inf in its chunk clears it.
-// Chunks are 16 KiB windows aligned to 16 bytes, so interior loads are float4.
+// Chunks are kScanChunkBytes windows aligned to 16 bytes.  Each thread keeps
+// kScanBatch float4 loads in flight (streaming, evict-first) before it tests
+// any, so the read stream has the memory parallelism HBM needs; only the two
+// edge chunks of a record test every element against the record's bounds.
 __global__ void __launch_bounds__(kScanThreads)
 ffa_validity_scan(const ScanRecord* __restrict__ recs, const ScanItem* __restrict__ items,
                   uint8_t* __restrict__ valid) {
+  constexpr int kPerThread = kScanChunkBytes / (16 * kScanThreads);
+  static_assert(kPerThread % kScanBatch == 0, "scan batches");
   const ScanItem item = items[blockIdx.x];
   const ScanRecord rec = recs[item.record];
   const uintptr_t base = reinterpret_cast<uintptr_t>(rec.data);
@@ -949,15 +972,31 @@ ffa_validity_scan(const ScanRecord* __restrict__ recs, const ScanItem* __restric
   const uintptr_t end = base + static_cast<uintptr_t>(rec.count) * 4;
   const uintptr_t lo = aligned + static_cast<uintptr_t>(item.chunk) * kScanChunkBytes;
   const uintptr_t hi = lo + kScanChunkBytes < end ? lo + kScanChunkBytes : end;
+  const bool interior = lo >= base && hi == lo + kScanChunkBytes;
+  auto poisoned = [](float x) { return isnan(x) || x == INFINITY; };
   bool bad = false;
-  for (uintptr_t p = lo + 16 * threadIdx.x; p < hi; p += 16 * kScanThreads) {
-    // Whole 16-byte blocks are read; lanes outside [base, end) are ignored.
-    const float4 v = __ldcs(reinterpret_cast<const float4*>(p));
-    const float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uintptr_t q = p + 4 * k;
-      if (q >= base && q < end) bad |= isnan(x[k]) || x[k] == INFINITY;
+  for (int b = 0; b < kPerThread; b += kScanBatch) {
+    float4 v[kScanBatch];
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      // Whole 16-byte blocks are read; lanes outside [base, end) are ignored.
+      const uintptr_t p = lo + 16 * (threadIdx.x + static_cast<uintptr_t>(b + u) * kScanThreads);
+      v[u] = p < hi ? __ldcs(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kScanBatch; ++u) {
+      const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (interior) {
+        bad |= poisoned(x[0]) || poisoned(x[1]) || poisoned(x[2]) || poisoned(x[3]);
+      } else {
+        const uintptr_t p = lo + 16 * (threadIdx.x + static_cast<uintptr_t>(b + u) * kScanThreads);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uintptr_t q = p + 4 * k;
+          if (q >= base && q < end) bad |= poisoned(x[k]);
+        }
+      }
     }
   }
   if (__syncthreads_or(bad) && threadIdx.x == 0) valid[item.record] = 0;
@@ -1023,7 +1062,7 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 }
 
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          int phase, int ctas_per_record, bool row_mode, int row_vocab,
+                          int ctas_per_record, bool row_mode, int row_vocab,
                           unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
   auto kernel = !row_mode ? ffa_finish_route<false, 0>
@@ -1042,8 +1081,7 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   }
   if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
   ++g_launches;
-  kernel<<<count * ctas_per_record, kCtaThreads, smem_bytes, stream>>>(params, records, phase,
-                                                                      ctas_per_record);
+  kernel<<<count * ctas_per_record, kCtaThreads, smem_bytes, stream>>>(params, records, ctas_per_record);
   return cudaGetLastError();
 }
 

@@ -368,3 +368,27 @@ def test_emission_validity_scans_unaligned_views_and_large_records(cuda):
     big[-1, -1] = torch.inf
     big[3, 0] = torch.nan
     assert ffa.emission_validity([big[1:], big[4:], big[:3], big[:4]]).tolist() == [False, False, True, False]
+
+
+def test_emission_validity_random_views_and_chunk_edges(cuda):
+    # Views start at arbitrary element offsets (not 16-byte aligned) and end
+    # anywhere; NaN, +inf and -inf land at random positions, some right at
+    # 64 KiB chunk and view edges.  The mask must equal a host scan.
+    rng = np.random.default_rng(99)
+    n = 3_000_000
+    host = rng.standard_normal(n).astype(np.float32)
+    spots = np.r_[rng.integers(0, n, 40), np.arange(16383, n, 16384)[:20], [0, n - 1]]
+    host[spots] = rng.choice(np.array([np.nan, np.inf, -np.inf], np.float32), spots.size)
+    flat = torch.from_numpy(host).to(cuda)
+    starts = rng.integers(0, n - 1, 300)
+    sizes = np.minimum(rng.integers(1, 400_000, 300), n - starts)
+    widths = rng.choice([1, 3, 4, 32, 33], 300)
+    views, expect = [], []
+    for s0, size, w in zip(starts, sizes, widths):
+        rows = max(1, int(size) // int(w))
+        if s0 + rows * w > n:
+            rows = (n - s0) // w
+        views.append(flat[s0:s0 + rows * w].view(rows, int(w)))
+        chunk = host[s0:s0 + rows * w]
+        expect.append(not (np.isnan(chunk).any() or np.isposinf(chunk).any()))
+    assert ffa.emission_validity(views).tolist() == expect
