@@ -117,6 +117,18 @@ def test_piece_boundary_lengths(cuda, mode):
     es, ts = zip(*(synthetic(rng, T, ratio=0.25) for T in lengths))
     result, ref = run_both(list(es), list(ts), 0, mode)
     assert_matches_oracle(result, ref, mode)
+    # The same lengths with the last frame on the last token (terminal state
+    # S-2, odd), so that every record's last frame carries a token label.
+    ends = []
+    for e, t in zip(es, ts):
+        e = e.copy()
+        e[-1, :] = -30.0
+        e[-1, t[-1]] = 0.0
+        ends.append(e)
+    result, ref = run_both(ends, list(ts), 0, mode)
+    last = np.cumsum([e.shape[0] for e in ends]) - 1
+    assert (ref.labels[last] != 0).all()
+    assert_matches_oracle(result, ref, mode + " token-ended")
 
 
 def test_mixed_row_and_gather_vocabularies(cuda):
