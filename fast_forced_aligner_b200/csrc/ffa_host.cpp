@@ -554,15 +554,23 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       runs.push_back(ClassRun{before, 0, classes[i], d.kst});
     runs.back().slots += n_first - before;
   }
-  // Records of the optimized route, row-staged ones first (one finisher
-  // launch each kind).
-  int64_t n_chunked_row = 0, nc = 0;
-  for (int pass = 0; pass < 2; ++pass)
+  // Records of the optimized route for the finisher, one launch per group:
+  // row-staged before gathered, and, when the records outnumber the SMs (the
+  // finisher is then throughput-bound), records whose repairs need at most 8
+  // warps (8 states per thread) on 256-thread CTAs, two per SM, before the
+  // wider ones on 512-thread CTAs.
+  const bool many_chunked = nchunked > sms;
+  auto finish_narrow = [&](const ffa::RecordDev& d) {
+    return many_chunked && (2 * d.U + 1 + 255) / 256 <= ffa::kMaxWarps / 2;
+  };
+  int64_t finish_end[4] = {0, 0, 0, 0}, nc = 0;
+  for (int grp = 0; grp < 4; ++grp) {
+    const bool row = grp < 2, narrow = (grp & 1) == 0;
     for (int64_t i = 0; i < count; ++i)
-      if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == (pass == 0)) {
+      if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == row && finish_narrow(recs[i]) == narrow)
         chunked[nc++] = static_cast<int32_t>(i);
-        if (pass == 0) ++n_chunked_row;
-      }
+    finish_end[grp] = nc;
+  }
   // Warps per CTA: the launch's warps spread evenly over the SMs (one CTA
   // runs per SM): the smallest per-CTA target whose packing still fits one
   // wave, so that every SM gets a share and none gets more than it must.
@@ -716,20 +724,30 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
   if ((rc = mark(FFA_PROFILE_FIRST))) return rc;
-  // The optimized route's seam plans, repairs and fallback: one CTA per record.
+  // The optimized route's seam plans, repairs and fallback: a CTA per record
+  // (the first round spread over up to four while the records leave SMs
+  // free), the groups planned above.  Repairs run 8 states per thread, so a
+  // gathered CTA needs that ring only; a 256-thread CTA keeps under half the
+  // shared memory so that two share an SM.
   const auto* dchunked = reinterpret_cast<const int32_t*>(dev + L.chunked);
-  const int64_t finish_slots = std::min<int64_t>(
-      ffa::kMaxWarps - 1,
-      row_slot_bytes ? static_cast<int64_t>((ffa::kSmemBudget - 2048 - header) / row_slot_bytes) : 1);
-  const unsigned finish_row_smem = static_cast<unsigned>(header + finish_slots * row_slot_bytes);
-  // Round 0 spreads each record's repair jobs over up to four CTAs while the
-  // records leave SMs free; the rest of a record runs on the last of them.
   const int spread = static_cast<int>(std::clamp<int64_t>(sms / std::max<int64_t>(nchunked, 1), 1, 4));
-  err = ffa::launch_finish(fp, dchunked, static_cast<int>(n_chunked_row), spread, true, rv, finish_row_smem, s);
-  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
-  err = ffa::launch_finish(fp, dchunked + n_chunked_row, static_cast<int>(nchunked - n_chunked_row), spread,
-                           false, 0, gather_smem, s);
-  if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  const unsigned finish_gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(8));
+  for (int grp = 0; grp < 4; ++grp) {
+    const int64_t first = grp == 0 ? 0 : finish_end[grp - 1];
+    const int64_t n = finish_end[grp] - first;
+    if (n == 0) continue;
+    const bool row = grp < 2, narrow = (grp & 1) == 0;
+    const int threads = narrow ? ffa::kCtaThreads / 2 : ffa::kCtaThreads;
+    unsigned smem = finish_gather_smem;
+    if (row) {
+      const size_t budget = narrow ? ffa::kSmemBudget / 2 - 4096 : ffa::kSmemBudget - 2048;
+      const int64_t slots = std::max<int64_t>(1, std::min<int64_t>(threads / 32 - 1,
+                                                                   static_cast<int64_t>((budget - header) / row_slot_bytes)));
+      smem = static_cast<unsigned>(header + slots * row_slot_bytes);
+    }
+    err = ffa::launch_finish(fp, dchunked + first, static_cast<int>(n), spread, threads, row, row ? rv : 0, smem, s);
+    if (err != cudaSuccess) return cuda_fail(err, "finish launch");
+  }
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
   err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
                          static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, s);

@@ -740,7 +740,7 @@ static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
 template <bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records,
-                 int ctas_per_record) {
+                 int ctas_per_record, unsigned dynamic_smem) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
   __shared__ JobList jobs;
@@ -760,9 +760,11 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   // the thread layout.
   const int nw = (2 * rec.U + 1 + 255) / 256;
   // Slot barriers use ids 1.. (id 0 is __syncthreads); row-staged slots also
-  // need a ring each.
-  int nslots = min(kMaxWarps - 1, kMaxWarps / nw);
-  if (kRow) nslots = min(nslots, static_cast<int>((kFinishDynamicSmem - kForwardHeader) / P.row_slot_bytes));
+  // need a ring each.  The CTA has 8 or 16 warps (8 when many records share
+  // the GPU: two such CTAs fit an SM).
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
+  int nslots = min(kMaxWarps - 1, nwarps / nw);
+  if (kRow) nslots = min(nslots, static_cast<int>((dynamic_smem - kForwardHeader) / P.row_slot_bytes));
   x.slot = x.warp / nw;
   x.lw = x.warp - x.slot * nw;
   x.NT = nw * 32;
@@ -1062,7 +1064,7 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 }
 
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          int ctas_per_record, bool row_mode, int row_vocab,
+                          int ctas_per_record, int threads, bool row_mode, int row_vocab,
                           unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
   auto kernel = !row_mode ? ffa_finish_route<false, 0>
@@ -1081,7 +1083,8 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   }
   if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
   ++g_launches;
-  kernel<<<count * ctas_per_record, kCtaThreads, smem_bytes, stream>>>(params, records, ctas_per_record);
+  if (threads != kCtaThreads && threads != kCtaThreads / 2) return cudaErrorInvalidValue;
+  kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, ctas_per_record, smem_bytes);
   return cudaGetLastError();
 }
 

@@ -63,13 +63,15 @@ class PinnedStaging {
       if (slot.pending && cudaEventQuery(slot.done) != cudaSuccess) continue;
       slot.pending = false;
       if (slot.capacity < bytes) {
-        if (slot.ptr != nullptr) cudaFreeHost(slot.ptr);
-        slot.ptr = nullptr;
-        slot.capacity = 0;
-        const size_t cap = std::max<size_t>(bytes, size_t{64} << 10);
-        TORCH_CHECK(cudaHostAlloc(&slot.ptr, cap, cudaHostAllocPortable) == cudaSuccess,
-                    "fast_forced_aligner_b200: cannot allocate pinned staging");
-        slot.capacity = cap;
+        // Pinning memory is slow (milliseconds) and can synchronise: grow
+        // every idle buffer now, so that later calls of this size never do.
+        for (Slot& other : slots_) {
+          if (other.capacity >= bytes || (&other != &slot && other.pending &&
+                                          cudaEventQuery(other.done) != cudaSuccess))
+            continue;
+          other.pending = false;
+          grow(other, bytes);
+        }
       }
       if (slot.done == nullptr)
         TORCH_CHECK(cudaEventCreateWithFlags(&slot.done, cudaEventDisableTiming) == cudaSuccess,
@@ -96,6 +98,15 @@ class PinnedStaging {
     cudaEvent_t done = nullptr;
     bool pending = false;
   };
+  static void grow(Slot& slot, size_t bytes) {
+    if (slot.ptr != nullptr) cudaFreeHost(slot.ptr);
+    slot.ptr = nullptr;
+    slot.capacity = 0;
+    const size_t cap = std::max<size_t>(bytes, size_t{64} << 10);
+    TORCH_CHECK(cudaHostAlloc(&slot.ptr, cap, cudaHostAllocPortable) == cudaSuccess,
+                "fast_forced_aligner_b200: cannot allocate pinned staging");
+    slot.capacity = cap;
+  }
   Slot slots_[kSlots];
   int next_ = 0, current_ = 0;
 };
