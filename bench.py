@@ -394,7 +394,8 @@ def run_ours(args):
         "metric": "aligned frames/sec", "value": value, "unit": "frames/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total_ms / args.steps, "latency_ms_per_call": latency_ms,
-        "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms), "max": max(step_ms)},
+        "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms), "max": max(step_ms),
+                    "slowest": int(np.argmax(step_ms))},
         "higher_is_better": True,
         "scaling": "strong" if args.split else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",

@@ -556,18 +556,23 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   }
   // Records of the optimized route for the finisher, one launch per group:
   // row-staged before gathered, and, when the records outnumber the SMs (the
-  // finisher is then throughput-bound), records whose repairs need at most 8
-  // warps (8 states per thread) on 256-thread CTAs, two per SM, before the
-  // wider ones on 512-thread CTAs.
+  // finisher is then throughput-bound), by the warps their repairs need at 8
+  // states per thread: at most 4 on 128-thread CTAs (four per SM), at most 8
+  // on 256-thread CTAs (two per SM), the rest on 512-thread CTAs.
   const bool many_chunked = nchunked > sms;
-  auto finish_narrow = [&](const ffa::RecordDev& d) {
-    return many_chunked && (2 * d.U + 1 + 255) / 256 <= ffa::kMaxWarps / 2;
+  auto finish_threads = [&](const ffa::RecordDev& d) {
+    const int nw8 = (2 * d.U + 1 + 255) / 256;
+    if (!many_chunked) return ffa::kCtaThreads;
+    return nw8 <= ffa::kMaxWarps / 4 ? ffa::kCtaThreads / 4
+                                     : (nw8 <= ffa::kMaxWarps / 2 ? ffa::kCtaThreads / 2 : ffa::kCtaThreads);
   };
-  int64_t finish_end[4] = {0, 0, 0, 0}, nc = 0;
-  for (int grp = 0; grp < 4; ++grp) {
-    const bool row = grp < 2, narrow = (grp & 1) == 0;
+  static constexpr int kFinishGroups = 6;  // (row, gathered) x (128, 256, 512 threads)
+  auto group_threads = [](int grp) { return ffa::kCtaThreads >> (2 - grp % 3); };
+  int64_t finish_end[kFinishGroups] = {}, nc = 0;
+  for (int grp = 0; grp < kFinishGroups; ++grp) {
+    const bool row = grp < 3;
     for (int64_t i = 0; i < count; ++i)
-      if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == row && finish_narrow(recs[i]) == narrow)
+      if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == row && finish_threads(recs[i]) == group_threads(grp))
         chunked[nc++] = static_cast<int32_t>(i);
     finish_end[grp] = nc;
   }
@@ -732,16 +737,17 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   const auto* dchunked = reinterpret_cast<const int32_t*>(dev + L.chunked);
   const int spread = static_cast<int>(std::clamp<int64_t>(sms / std::max<int64_t>(nchunked, 1), 1, 4));
   const unsigned finish_gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(8));
-  for (int grp = 0; grp < 4; ++grp) {
+  for (int grp = 0; grp < kFinishGroups; ++grp) {
     const int64_t first = grp == 0 ? 0 : finish_end[grp - 1];
     const int64_t n = finish_end[grp] - first;
     if (n == 0) continue;
-    const bool row = grp < 2, narrow = (grp & 1) == 0;
-    const int threads = narrow ? ffa::kCtaThreads / 2 : ffa::kCtaThreads;
+    const bool row = grp < 3;
+    const int threads = group_threads(grp);
+    const int per_sm = ffa::kCtaThreads / threads;  // CTAs that share an SM
     unsigned smem = finish_gather_smem;
     if (row) {
-      const size_t budget = narrow ? ffa::kSmemBudget / 2 - 4096 : ffa::kSmemBudget - 2048;
-      const int64_t slots = std::max<int64_t>(1, std::min<int64_t>(threads / 32 - 1,
+      const size_t budget = (ffa::kSmemBudget - 2048) / per_sm - (per_sm > 1 ? 2048 : 0);
+      const int64_t slots = std::max<int64_t>(1, std::min<int64_t>(std::max(1, threads / 32 - 1),
                                                                    static_cast<int64_t>((budget - header) / row_slot_bytes)));
       smem = static_cast<unsigned>(header + slots * row_slot_bytes);
     }

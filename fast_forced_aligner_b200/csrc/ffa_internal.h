@@ -203,8 +203,8 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 // Everything after the first pass of the optimized route -- seam plans,
 // repair rounds, conventional fallback -- in one launch: round 0's repairs on
 // ctas_per_record CTAs per listed record, the rest on the last of them.
-// `threads`: 512, or 256 (records of at most 8 warps at 8 states per thread)
-// when many records share the GPU and two CTAs per SM pay.
+// `threads`: 512, or 256 / 128 (records of at most 8 / 4 warps at 8 states
+// per thread) when many records share the GPU and two / four CTAs per SM pay.
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
                           int ctas_per_record, int threads, bool row_mode, int row_vocab,
                           unsigned smem_bytes, cudaStream_t stream);

@@ -760,8 +760,8 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   // the thread layout.
   const int nw = (2 * rec.U + 1 + 255) / 256;
   // Slot barriers use ids 1.. (id 0 is __syncthreads); row-staged slots also
-  // need a ring each.  The CTA has 8 or 16 warps (8 when many records share
-  // the GPU: two such CTAs fit an SM).
+  // need a ring each.  The CTA has 4, 8 or 16 warps (fewer when many records
+  // share the GPU: four or two such CTAs fit an SM).
   const int nwarps = static_cast<int>(blockDim.x >> 5);
   int nslots = min(kMaxWarps - 1, nwarps / nw);
   if (kRow) nslots = min(nslots, static_cast<int>((dynamic_smem - kForwardHeader) / P.row_slot_bytes));
@@ -1083,7 +1083,8 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   }
   if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
   ++g_launches;
-  if (threads != kCtaThreads && threads != kCtaThreads / 2) return cudaErrorInvalidValue;
+  if (threads != kCtaThreads && threads != kCtaThreads / 2 && threads != kCtaThreads / 4)
+    return cudaErrorInvalidValue;
   kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, ctas_per_record, smem_bytes);
   return cudaGetLastError();
 }
