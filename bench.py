@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--mode", default="optimized", choices=["optimized", "conventional"])
     p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
+    p.add_argument("--scale", type=float, default=1.0,
+                   help="shrink the config's record count (and cfg2's frames) for small profiling runs")
     p.add_argument("--split", action="store_true",
                    help="partition one batch over the ranks (strong scaling) instead of one batch per rank")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -256,11 +258,11 @@ def run_ours(args):
 
     ffa.load_extension()
     if args.split:
-        pool = workloads.config(args.config)
+        pool = workloads.config(args.config, scale=args.scale)
         wl = pool.subset(shard_of_rank(pool.lengths, pool.target_lengths, rank, world))
         parallelism = f"one batch LPT-partitioned over {world} GPU(s) by record cost, no collective"
     else:
-        wl = workloads.config(args.config, shard=rank)
+        wl = workloads.config(args.config, scale=args.scale, shard=rank)
         parallelism = f"records sharded, {world} independent GPU(s), no collective"
     records_total = int(sum_over_ranks(wl.batch))
     frames = int(wl.lengths.sum())
