@@ -401,7 +401,8 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": "strong" if args.split else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "records_per_gpu": wl.batch, "frames_per_gpu": frames,
+        "config": {"workload": wl.name if args.scale == 1.0 else f"{wl.name} at scale {args.scale}",
+                   "records_per_gpu": wl.batch, "frames_per_gpu": frames,
                    "records_total": records_total, "frames_total": int(all_frames),
                    "vocab": wl.vocab, "mode": args.mode, "check_inputs": True,
                    "inputs": "packed device-resident fp32 [sum T, V] + int64 targets",

@@ -329,3 +329,48 @@ def align_packed(
     tensors = torch.ops.ffa_b200.align_packed(
         emissions, frames_t, targets, tokens_t, blanks_t, code, emission_validity, check_inputs)
     return AlignmentBatch(tuple(frames_t.tolist()), *tensors)
+
+
+@torch.inference_mode()
+def token_spans(batch: AlignmentBatch, tokens, *, blank_id: int | Sequence[int] = 0) -> Tensor:
+    """Frame span of every target token, from an AlignmentBatch's labels.
+
+    The conversion the reference's README describes (README.md:509-517),
+    done on the GPU: each record's path is split into runs of equal labels,
+    blank runs are dropped, and the k-th remaining run is the k-th target
+    token (a repeated token keeps its blank-separated occurrences apart).
+
+    Args:
+        batch: the result of ``align``/``align_packed``.
+        tokens: the records' target lengths ``U_i`` (sequence, array or tensor).
+        blank_id: the blank of every record, or one per record.
+
+    Returns:
+        CUDA int64 ``(sum(U), 2)``: ``[start, end)`` frames per token in record
+        order (``.split(tokens)`` gives each record's); ``-1`` in every row of
+        a record whose path does not hold ``U_i`` non-blank runs (failed
+        records).  Stream-ordered; nothing is read back.
+    """
+    tokens_t = _host_counts(tokens, "tokens")
+    count = len(batch.lengths)
+    if tokens_t.numel() != count:
+        raise ValueError("provide one token count per record")
+    if type(blank_id) is int:
+        blanks_t = torch.tensor([blank_id], dtype=torch.int64)
+    elif not isinstance(blank_id, (Sequence, np.ndarray, Tensor)):
+        raise TypeError("blank_id must be an int or a sequence of ints")
+    else:
+        blanks_t = _host_counts(blank_id, "blank_id")
+    frames_t = torch.tensor(batch.lengths, dtype=torch.int64)
+    load_extension()
+    return torch.ops.ffa_b200.token_spans(batch.labels, frames_t, tokens_t, blanks_t)
+
+
+def token_timestamps(batch: AlignmentBatch, tokens, frame_seconds: float, *,
+                     blank_id: int | Sequence[int] = 0) -> Tensor:
+    """``token_spans`` in seconds: float64 ``(sum(U), 2)`` start and end times
+    (frames times ``frame_seconds``, e.g. a model's
+    ``inputs_to_logits_ratio / sample_rate``); NaN rows for failed records."""
+    spans = token_spans(batch, tokens, blank_id=blank_id)
+    seconds = spans.to(torch.float64) * float(frame_seconds)
+    return torch.where(spans < 0, torch.full_like(seconds, float("nan")), seconds)

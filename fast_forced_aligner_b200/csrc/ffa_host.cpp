@@ -373,6 +373,22 @@ int cuda_fail(cudaError_t err, const char* what) {
 
 void ffa::set_last_error(const char* message) { g_error = message; }
 
+namespace {
+int check_spans(const int64_t* frames, const int32_t* tokens, int64_t count, int64_t* total) {
+  if (frames == nullptr || tokens == nullptr || count < 1 || count > FFA_MAX_RECORDS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 frame and token counts");
+  int64_t n = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    if (frames[i] < 1 || frames[i] > INT32_MAX || tokens[i] < 0 || tokens[i] > FFA_MAX_TOKENS)
+      return fail(FFA_ERR_UNSUPPORTED, "record " + std::to_string(i) + ": unsupported frame or token count");
+    n += frames[i];
+  }
+  *total = n;
+  return FFA_OK;
+}
+size_t spans_bytes(int64_t count) { return align_up(sizeof(ffa::SpanRecord) * static_cast<size_t>(count), 256); }
+}  // namespace
+
 extern "C" {
 
 int ffa_abi_version(void) { return FFA_ABI_VERSION; }
@@ -854,6 +870,51 @@ int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
   err = ffa::launch_check_targets(static_cast<const ffa::RecordDev*>(workspace), count, status, s);
   if (err != cudaSuccess) return cuda_fail(err, "target check launch");
+  return FFA_OK;
+}
+
+
+int ffa_token_spans_query(const int64_t* frames, const int32_t* tokens, int64_t count, ffa_sizes* sizes) {
+  if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be null");
+  int64_t total = 0;
+  const int rc = check_spans(frames, tokens, count, &total);
+  if (rc) return rc;
+  sizes->staging_bytes = spans_bytes(count);
+  sizes->workspace_bytes = spans_bytes(count);
+  sizes->total_frames = total;
+  return FFA_OK;
+}
+
+int ffa_token_spans(const int64_t* labels, const int64_t* frames, const int32_t* tokens,
+                    const int32_t* blanks, int64_t count, int64_t* spans,
+                    void* staging, size_t staging_bytes,
+                    void* workspace, size_t workspace_bytes, ffa_stream_t stream) {
+  int64_t total = 0;
+  int rc = check_spans(frames, tokens, count, &total);
+  if (rc) return rc;
+  if (labels == nullptr || blanks == nullptr)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "labels and blanks are required");
+  const size_t need = spans_bytes(count);
+  if (staging == nullptr || staging_bytes < need)
+    return fail(FFA_ERR_BUFFER_TOO_SMALL, "staging buffer smaller than ffa_token_spans_query reports");
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(FFA_ERR_BUFFER_TOO_SMALL, "workspace missing, too small or not 256-byte aligned");
+  auto* recs = static_cast<ffa::SpanRecord*>(staging);
+  int64_t frame_off = 0, token_off = 0, total_tokens = 0;
+  for (int64_t i = 0; i < count; ++i) total_tokens += tokens[i];
+  if (total_tokens > 0 && spans == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "spans output is required");
+  for (int64_t i = 0; i < count; ++i) {
+    if (blanks[i] < 0) return fail(FFA_ERR_UNSUPPORTED, "record " + std::to_string(i) + ": negative blank ID");
+    recs[i] = ffa::SpanRecord{labels + frame_off, spans + 2 * token_off, static_cast<int32_t>(frames[i]),
+                              tokens[i], blanks[i], 0};
+    frame_off += frames[i];
+    token_off += tokens[i];
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaMemcpyAsync(workspace, staging, sizeof(ffa::SpanRecord) * count, cudaMemcpyHostToDevice, s);
+  if (err != cudaSuccess) return cuda_fail(err, "span descriptor upload");
+  err = ffa::launch_spans(static_cast<const ffa::SpanRecord*>(workspace), count, s);
+  if (err != cudaSuccess) return cuda_fail(err, "span launch");
   return FFA_OK;
 }
 

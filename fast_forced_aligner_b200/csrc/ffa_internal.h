@@ -238,6 +238,14 @@ int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned sme
 // Dynamic shared memory a long-record CTA needs besides its emission ring.
 size_t long_header_bytes();
 
+// Token spans: one warp per record.
+struct SpanRecord {
+  const int64_t* labels;  // the record's frames of an ffa_align labels output
+  int64_t* spans;         // its [U, 2] rows of the spans output
+  int32_t T, U, blank, reserved;
+};
+cudaError_t launch_spans(const SpanRecord* recs, int64_t count, cudaStream_t stream);
+
 // Kernels launched so far by the calling thread (ffa_kernels.cu), and the
 // hook every launcher calls.
 int64_t launches_so_far();

@@ -1004,6 +1004,51 @@ ffa_validity_scan(const ScanRecord* __restrict__ recs, const ScanItem* __restric
   if (__syncthreads_or(bad) && threadIdx.x == 0) valid[item.record] = 0;
 }
 
+// Token spans of aligned paths, one warp per record (the conversion the
+// reference's README describes, README.md:509-517): the path's equal-label
+// runs, blank runs dropped; run k of a record is its k-th token, as the path
+// collapses to the transcript.  Each 32-frame chunk finds run starts and ends
+// by comparing every label with its predecessor; a ballot and a population
+// count number them.  A record whose non-blank run count is not U -- a failed
+// record (labels -1) among them -- gets -1 for every span.
+__global__ void __launch_bounds__(256)
+ffa_token_spans_kernel(const SpanRecord* __restrict__ recs, int64_t count) {
+  const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= count) return;
+  const SpanRecord rec = recs[r];
+  const int64_t* labels = rec.labels;
+  int64_t* spans = rec.spans;
+  const unsigned lt = (1u << lane) - 1u;
+  int runs = 0;            // non-blank runs started before this chunk
+  int64_t carry = -1;      // label of the chunk's previous frame (-1: none)
+  bool invalid = false;
+  for (int base = 0; base < rec.T; base += 32) {
+    const int t = base + lane;
+    int64_t lab = t < rec.T ? labels[t] : rec.blank;
+    if (lab < 0) { invalid = true; lab = rec.blank; }
+    int64_t prev = __shfl_up_sync(0xffffffffu, lab, 1);
+    if (lane == 0) prev = carry;
+    const bool start = t < rec.T && lab != rec.blank && lab != prev;
+    const bool end = t < rec.T && prev >= 0 && prev != rec.blank && lab != prev;
+    const unsigned starts = __ballot_sync(0xffffffffu, start);
+    const int before = runs + __popc(starts & lt);  // runs started before frame t
+    if (start && before < rec.U) spans[2 * before] = t;
+    if (end && before - 1 < rec.U) spans[2 * (before - 1) + 1] = t;
+    runs += __popc(starts);
+    carry = __shfl_sync(0xffffffffu, lab, 31);
+  }
+  // The last run ends with the record (past a partial last chunk, `carry`
+  // holds padding, so the last frame's label is read again).
+  if (lane == 0 && rec.T > 0) {
+    const int64_t last = labels[rec.T - 1];
+    if (last >= 0 && last != rec.blank && runs >= 1 && runs <= rec.U) spans[2 * (runs - 1) + 1] = rec.T;
+  }
+  invalid = __any_sync(0xffffffffu, invalid) || runs != rec.U;
+  if (!invalid) return;
+  for (int k = lane; k < 2 * rec.U; k += 32) spans[k] = -1;
+}
+
 // One warp per record: the target checks of the forward kernel without the DP.
 __global__ void __launch_bounds__(256)
 ffa_check_targets_kernel(const RecordDev* __restrict__ recs, int64_t count,
@@ -1036,6 +1081,14 @@ namespace {
 thread_local int64_t g_launches = 0;
 }  // namespace
 int64_t launches_so_far() { return g_launches; }
+
+cudaError_t launch_spans(const SpanRecord* recs, int64_t count, cudaStream_t stream) {
+  if (count <= 0) return cudaSuccess;
+  ++g_launches;
+  const unsigned blocks = static_cast<unsigned>((count * 32 + 255) / 256);
+  ffa_token_spans_kernel<<<blocks, 256, 0, stream>>>(recs, count);
+  return cudaGetLastError();
+}
 void count_launch() { ++g_launches; }
 
 cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,

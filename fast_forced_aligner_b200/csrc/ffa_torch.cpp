@@ -400,6 +400,54 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
   return status;
 }
 
+// token_spans(Tensor labels, Tensor frames, Tensor tokens, Tensor blanks) -> Tensor
+// labels: CUDA int64 [sum frames] (an align output); frames, tokens: CPU int64
+// [B]; blanks: CPU int64 [1] or [B].  Returns CUDA int64 [sum tokens, 2].
+at::Tensor token_spans(const at::Tensor& labels, const at::Tensor& frames_t, const at::Tensor& tokens_t,
+                       const at::Tensor& blanks_t) {
+  const int64_t count = frames_t.numel();
+  TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS && tokens_t.numel() == count &&
+                        (blanks_t.numel() == 1 || blanks_t.numel() == count),
+                    "provide 1..65535 matching frame counts, token counts and blanks");
+  const char* counts_msg = "frame counts, token counts and blanks must be 1-D CPU int64 vectors";
+  const int64_t* frames = host_counts(frames_t, count, counts_msg);
+  const int64_t* tokens64 = host_counts(tokens_t, count, counts_msg);
+  const int64_t* blanks64 = host_counts(blanks_t, blanks_t.numel(), counts_msg);
+  TORCH_CHECK_VALUE(labels.device().is_cuda() && labels.scalar_type() == at::kLong && labels.dim() == 1 &&
+                        labels.is_contiguous(),
+                    "labels must be a contiguous CUDA int64 vector");
+  std::vector<int32_t> tokens(count), blanks(count);
+  int64_t frames_total = 0, tokens_total = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    TORCH_CHECK_VALUE(tokens64[i] >= 0 && tokens64[i] <= FFA_MAX_TOKENS, "unsupported token count");
+    const int64_t b = blanks64[blanks_t.numel() == 1 ? 0 : i];
+    TORCH_CHECK_VALUE(b >= 0 && b <= INT_MAX, "unsupported blank ID");
+    tokens[i] = static_cast<int32_t>(tokens64[i]);
+    blanks[i] = static_cast<int32_t>(b);
+    frames_total += frames[i];
+    tokens_total += tokens64[i];
+  }
+  TORCH_CHECK_VALUE(frames_total == labels.numel(), "frame counts must add up to the labels' length");
+  const auto device = labels.device();
+  c10::cuda::CUDAGuard guard(device);
+  const auto stream = c10::cuda::getCurrentCUDAStream();
+  StreamRecorder rec{stream};
+  rec(labels);
+  ffa_sizes sizes{};
+  check_status(ffa_token_spans_query(frames, tokens.data(), count, &sizes));
+  auto spans = at::empty({tokens_total, 2}, labels.options());
+  auto workspace = device_scratch(sizes.workspace_bytes);
+  PinnedStaging& staging = staging_for(device.index());
+  const int rc = ffa_token_spans(labels.data_ptr<int64_t>(), frames, tokens.data(), blanks.data(), count,
+                                 tokens_total ? spans.data_ptr<int64_t>() : nullptr,
+                                 staging.acquire(sizes.staging_bytes), sizes.staging_bytes, workspace.get(),
+                                 std::max<size_t>(sizes.workspace_bytes, 256),
+                                 reinterpret_cast<ffa_stream_t>(stream.stream()));
+  if (rc == FFA_OK) staging.release(stream.stream());
+  check_status(rc);
+  return spans;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(ffa_b200, m) {
@@ -409,6 +457,7 @@ TORCH_LIBRARY(ffa_b200, m) {
         "int mode, Tensor? emission_validity=None, bool check_inputs=True) -> Tensor[]");
   m.def("emission_validity(Tensor[] emissions) -> Tensor");
   m.def("check_targets(Tensor[] emissions, Tensor[] targets, int[] blanks) -> Tensor");
+  m.def("token_spans(Tensor labels, Tensor frames, Tensor tokens, Tensor blanks) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(ffa_b200, CUDA, m) {
@@ -416,4 +465,5 @@ TORCH_LIBRARY_IMPL(ffa_b200, CUDA, m) {
   m.impl("align_packed", &align_packed);
   m.impl("emission_validity", &emission_validity);
   m.impl("check_targets", &check_targets);
+  m.impl("token_spans", &token_spans);
 }

@@ -218,6 +218,26 @@ FFA_API int ffa_check_targets(const ffa_record* records, int64_t count, int32_t*
                               void* staging, size_t staging_bytes,
                               void* workspace, size_t workspace_bytes, ffa_stream_t stream);
 
+/* ---- token spans (no op in the reference: its README describes the
+ *      conversion, README.md:509-517) ------------------------------------- */
+
+/* Host only: sizes for ffa_token_spans (total_frames = sum of frames). */
+FFA_API int ffa_token_spans_query(const int64_t* frames, const int32_t* tokens, int64_t count,
+                                  ffa_sizes* sizes);
+
+/* From the labels ffa_align wrote (device int64 [sum frames], record i's
+ * frames[i] rows in record order), each record's token spans: the frame
+ * range [start, end) of its k-th run of equal non-blank labels, the frames
+ * its k-th target token occupies.  spans: device int64 [sum tokens, 2], record
+ * i's tokens[i] rows in record order.  A record whose non-blank run count is
+ * not tokens[i] (a failed record: labels -1) gets -1 in all of its rows.
+ * frames, tokens, blanks: host arrays of count entries.  Same staging /
+ * workspace contract as ffa_align. */
+FFA_API int ffa_token_spans(const int64_t* labels, const int64_t* frames, const int32_t* tokens,
+                            const int32_t* blanks, int64_t count, int64_t* spans,
+                            void* staging, size_t staging_bytes,
+                            void* workspace, size_t workspace_bytes, ffa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -126,7 +126,7 @@ def test_validity_and_target_queries(lib):
 
 def test_torch_ops_register_without_a_gpu():
     torch.ops.load_library(str(SHIM))
-    for name in ("align", "align_packed", "emission_validity", "check_targets"):
+    for name in ("align", "align_packed", "emission_validity", "check_targets", "token_spans"):
         assert hasattr(torch.ops.ffa_b200, name)
 
 
