@@ -242,17 +242,54 @@ __device__ __forceinline__ void store_codes(uint8_t* row, int tl, unsigned bits)
 
 // One warp walks a path back through the backpointers, from state s at frame
 // t_hi down to frame t_lo (path[t-1] = path[t] - jump(t, path[t]),
-// alignment.cu:656-659).  The path moves at most 2 states per frame, so over
-// FB = 10 frames it stays within 3 words of the start word: the warp loads
-// those FB x 3 words in one round trip, then steps through them with
-// shuffles; every lane tracks the same state.  `at_frame(t, s)` is called (by
+// alignment.cu:656-659).  The path drops at most 2 states per frame, so over
+// 32 frames it stays within the 4-word block holding its starting state and
+// the block before it: lane l loads those two 16-byte blocks of frame t - l
+// (rows are whole multiples of 4 words, so the loads are aligned) in one
+// round trip, and the warp then steps through the 32 frames with a shuffle
+// each; every lane tracks the same state.  `at_frame(t, s)` is called (by
 // every lane) with the path's state at each frame t_hi-1 .. t_lo; returns the
-// state at t_lo.  bp: the record's rows, row_words words per frame.
-// Rows are read through L2 (ld.global.cg): a trace may follow rows that
-// another CTA of the same launch wrote.
+// state at t_lo.  bp: the record's rows, row_words words per frame.  Rows are
+// read through L2 (ld.global.cg): a trace may follow rows that another CTA of
+// the same launch wrote.
 template <typename AtFrame>
 __device__ __forceinline__ int warp_trace(const uint32_t* bp, int row_words, int s,
                                           int t_hi, int t_lo, int lane, AtFrame at_frame) {
+  for (int t = t_hi; t > t_lo;) {
+    const int steps = min(32, t - t_lo);
+    const int qb = (s >> 6) << 2;  // first word of the block holding s
+    uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
+    if (lane < steps) {
+      const uint4* row = reinterpret_cast<const uint4*>(bp + static_cast<int64_t>(t - lane) * row_words + qb);
+      hi = __ldcg(row);
+      if (qb >= 4) lo = __ldcg(row - 1);
+    }
+    for (int i = 0; i < steps; ++i) {
+      // Word (s >> 4) is qb + d with d in [-4, 3]: position d + 4 of lo:hi
+      // (the same position on every lane), taken from lane i (frame t - i).
+      const int idx = (s >> 4) - qb + 4;
+      const bool b0 = idx & 1, b1 = idx & 2, b2 = idx & 4;
+      const uint32_t x = b1 ? (b0 ? lo.w : lo.z) : (b0 ? lo.y : lo.x);
+      const uint32_t y = b1 ? (b0 ? hi.w : hi.z) : (b0 ? hi.y : hi.x);
+      const uint32_t word = __shfl_sync(0xffffffffu, b2 ? y : x, i);
+      // (The clamp never acts on backpointers a completed DP wrote; it keeps
+      // every read inside the arena.)
+      s = max(s - static_cast<int>((word >> (2 * (s & 15))) & 3u), 0);
+      at_frame(t - i - 1, s);
+    }
+    t -= steps;
+  }
+  return s;
+}
+
+// The same walk with fewer bytes per frame: FB = 10 frames over 3 words
+// around the path's word per round trip (lanes f*3 + dd load word w0 - dd of
+// frame t - f).  Where many warps walk at once (the traceback fill of every
+// segment) the memory traffic, not one walk's latency, bounds the kernel, and
+// this variant moves 4 bytes per lane instead of 32.
+template <typename AtFrame>
+__device__ __forceinline__ int warp_trace_lean(const uint32_t* bp, int row_words, int s,
+                                               int t_hi, int t_lo, int lane, AtFrame at_frame) {
   constexpr int FB = 10, NW = 3;
   for (int t = t_hi; t > t_lo;) {
     const int f = lane / NW, dd = lane % NW;
@@ -264,8 +301,6 @@ __device__ __forceinline__ int warp_trace(const uint32_t* bp, int row_words, int
     for (int i = 0; i < steps; ++i) {
       const int ct = t - i;
       const uint32_t word = __shfl_sync(0xffffffffu, w, i * NW + (w0 - (s >> 4)));
-      // (The clamp never acts on backpointers a completed DP wrote; it keeps
-      // every read inside the arena.)
       s = max(s - static_cast<int>((word >> (2 * (s & 15))) & 3u), 0);
       at_frame(ct - 1, s);
     }

@@ -888,8 +888,8 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
       int32_t* p = path[warp];
       const int s_end = anchors[rec.seg_off + c];
       if (lane == 0) p[b - 1 - a] = s_end;
-      warp_trace(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
-                 [&](int t, int s) { if (lane == 0) p[t - a] = s; });
+      warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
+                      [&](int t, int s) { if (lane == 0) p[t - a] = s; });
       __syncwarp();
       const float* e = rec.emissions;
       for (int t = a + lane; t < b; t += 32) {
