@@ -82,7 +82,7 @@ def peaks():
 
 
 def algorithmic_bytes(wl):
-    """Per SURVEY 8(d): 32 B for every sector of a row holding a label column
+    """The path's algorithmic bytes: 32 B for every sector of a row holding a label column
     of the record (sectors counted from a 32 B-aligned record base), plus 12 B
     of output per frame and the 8 B int64 targets.  Returns (emission+target
     bytes read by the DP, full B_alg)."""

@@ -191,7 +191,7 @@ struct ForwardParams {
   int32_t* route;            // per record: kRoute* (the finisher writes it)
   OutputsDev out;
   uint32_t row_slot_bytes;
-  int32_t run_pieces;        // kPhaseFirst: pieces per slot of the optimized route
+  int32_t run_pieces;        // first pass: consecutive pieces per slot of the optimized route
   int32_t* fill_done;        // per record: fill CTAs finished (zeroed by the first pass)
   int32_t* finish_done;      // per record: finisher CTAs through round 0 (zeroed by the first pass)
 };
