@@ -164,7 +164,7 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, longs, fill, slots, keys, classes, staging_bytes;
+  size_t recs, chunked, longs, fill, counters, slots, keys, classes, staging_bytes;
   size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
 };
@@ -204,6 +204,9 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->chunked = off; off = align_up(off + sizeof(int32_t) * chunked, 16);
   L->longs = off; off = align_up(off + sizeof(int32_t) * longs, 16);
   L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 16);
+  // Zeroed counters of round 0's plan in the first pass (per record, then
+  // per finisher group), uploaded with the descriptors.
+  L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups), 16);
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 16, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
@@ -527,6 +530,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     frontier_off += g.frontier_elems;
   }
 
+  std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups));
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
       align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4, 128));
@@ -586,10 +590,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     if (nw8 <= ffa::kMaxWarps / 4) return ffa::kCtaThreads / 4;
     return nw8 <= ffa::kMaxWarps / 2 ? ffa::kCtaThreads / 2 : ffa::kCtaThreads;
   };
-  static constexpr int kFinishGroups = 6;  // (row, gathered) x (128, 256, 512 threads)
   auto group_threads = [](int grp) { return ffa::kCtaThreads >> (2 - grp % 3); };
-  int64_t finish_end[kFinishGroups] = {}, nc = 0;
-  for (int grp = 0; grp < kFinishGroups; ++grp) {
+  int64_t finish_end[ffa::kFinishGroups] = {}, nc = 0;
+  for (int grp = 0; grp < ffa::kFinishGroups; ++grp) {
     const bool row = grp < 3;
     for (int64_t i = 0; i < count; ++i)
       if (recs[i].num_pieces > 1 && (recs[i].row_mode != 0) == row && finish_threads(recs[i]) == group_threads(grp))
@@ -690,6 +693,18 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   fp.route = reinterpret_cast<int32_t*>(dev + L.route);
   fp.fill_done = reinterpret_cast<int32_t*>(dev + L.fill_done);
   fp.finish_done = reinterpret_cast<int32_t*>(dev + L.finish_done);
+  // Round 0 is planned in the first pass when the records outnumber the SMs
+  // but the finisher still gives each its own 512-thread CTA: records joined
+  // there never occupy one.  (cfg4 shards on one B200, first pass + finisher
+  // with and without: 1031 records 565 vs 606 us, 2063: 914 vs 1016, 4128:
+  // 1747 vs 1842; 8256 records, on the finisher's small CTAs: 3274 vs 3240.)
+  fp.plan_first = nchunked > sms && !many_chunked ? 1 : 0;
+  fp.finish_narrow = many_chunked ? 1 : 0;
+  fp.slot_done = reinterpret_cast<int32_t*>(dev + L.counters);
+  fp.finish_count = fp.slot_done + count;
+  fp.finish_list = reinterpret_cast<int32_t*>(dev + L.chunked);
+  for (int grp = 0; grp < ffa::kFinishGroups; ++grp)
+    fp.finish_base[grp] = static_cast<int32_t>(grp == 0 ? 0 : finish_end[grp - 1]);
   fp.out = ffa::OutputsDev{outputs->labels, outputs->scores, outputs->status, outputs->objective,
                            outputs->stitched, outputs->repair_passes, outputs->repaired_frames,
                            outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
@@ -757,7 +772,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   const auto* dchunked = reinterpret_cast<const int32_t*>(dev + L.chunked);
   const int spread = static_cast<int>(std::clamp<int64_t>(sms / std::max<int64_t>(nchunked, 1), 1, 4));
   const unsigned finish_gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(8));
-  for (int grp = 0; grp < kFinishGroups; ++grp) {
+  for (int grp = 0; grp < ffa::kFinishGroups; ++grp) {
     const int64_t first = grp == 0 ? 0 : finish_end[grp - 1];
     const int64_t n = finish_end[grp] - first;
     if (n == 0) continue;
@@ -771,7 +786,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                                                                    static_cast<int64_t>((budget - header) / row_slot_bytes)));
       smem = static_cast<unsigned>(header + slots * row_slot_bytes);
     }
-    err = ffa::launch_finish(fp, dchunked + first, static_cast<int>(n), spread, threads, row, row ? rv : 0, smem, s);
+    err = ffa::launch_finish(fp, dchunked + first, static_cast<int>(n), fp.plan_first ? fp.finish_count + grp : nullptr,
+                             spread, threads, row, row ? rv : 0, smem, s);
     if (err != cudaSuccess) return cuda_fail(err, "finish launch");
   }
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;

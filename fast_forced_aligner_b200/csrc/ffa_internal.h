@@ -176,6 +176,9 @@ struct OutputsDev {
 constexpr unsigned gather_ring_bytes(int K) { return kGroup * (K / 2 + 1) * kCtaThreads * 4; }
 size_t forward_header_bytes();
 
+// Finisher launch groups: (row-staged, gathered) x (128, 256, 512 threads).
+constexpr int kFinishGroups = 6;
+
 // Arguments of one forward launch.
 struct ForwardParams {
   const RecordDev* recs;
@@ -194,6 +197,17 @@ struct ForwardParams {
   int32_t run_pieces;        // first pass: consecutive pieces per slot of the optimized route
   int32_t* fill_done;        // per record: fill CTAs finished (zeroed by the first pass)
   int32_t* finish_done;      // per record: finisher CTAs through round 0 (zeroed by the first pass)
+  // Round 0's plan in the first pass (set when the optimized route's records
+  // outnumber the SMs): the record's last slot to finish plans it; a record
+  // it joins is done, the others go to the finisher's list of their group
+  // (finish_list + finish_base[g], finish_count[g] entries).  slot_done and
+  // finish_count arrive zeroed with the descriptor upload.
+  int32_t plan_first;
+  int32_t finish_narrow;     // the finisher's 128/256-thread CTA groups are in use
+  int32_t* slot_done;        // per record: first-pass slots finished
+  int32_t* finish_list;
+  int32_t* finish_count;     // [kFinishGroups]
+  int32_t finish_base[kFinishGroups];
 };
 
 // row_vocab: the vocabulary shared by every row-staged record of the
@@ -205,9 +219,11 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 // ctas_per_record CTAs per listed record, the rest on the last of them.
 // `threads`: 512, or 256 / 128 (records of at most 8 / 4 warps at 8 states
 // per thread) when many records share the GPU and two / four CTAs per SM pay.
+// `device_count` (or null): the number of listed records, written by the
+// first pass; CTAs past it exit at once (`count` is then the list's room).
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          int ctas_per_record, int threads, bool row_mode, int row_vocab,
-                          unsigned smem_bytes, cudaStream_t stream);
+                          const int32_t* device_count, int ctas_per_record, int threads, bool row_mode,
+                          int row_vocab, unsigned smem_bytes, cudaStream_t stream);
 // Traceback fill of every segment; for records of the optimized route the
 // last fill CTA of the record also folds the objective of a joined path.
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,

@@ -485,6 +485,173 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
 
 }  // namespace
 
+// Repair jobs of one round of one record (shared memory of the finisher).
+constexpr int kMaxJobs = 128;
+struct JobList {
+  int count;
+  int piece[kMaxJobs];  // first piece re-solved (resumes from the frontier of piece - 1)
+  int first[kMaxJobs];  // first piece of the merged region
+  int last[kMaxJobs];   // last piece of the merged region
+};
+
+// What one round's plan adds to a record's diagnostics.
+struct PlanStats {
+  int64_t merged = 0;   // frames of the merged regions
+  int64_t skipped = 0;  // frames the saved frontiers spared
+  int jobs = 0;
+};
+
+// A piece's state as other CTAs of the running launch may have left it:
+// loaded through L2 (ld.global.cg), never from a stale L1 line.
+__device__ __forceinline__ PieceState load_piece_state(const PieceState* p) {
+  const int4 a = __ldcg(reinterpret_cast<const int4*>(p));
+  const int4 b = __ldcg(reinterpret_cast<const int4*>(p) + 1);
+  PieceState s;
+  s.start = a.x; s.end = a.y; s.flags = a.z; s.start_skip = a.w;
+  s.region_start[0] = b.x; s.region_start[1] = b.y; s.region_start[2] = b.z; s.region_start[3] = b.w;
+  return s;
+}
+
+// Seam check and repair planning of one round of one record, by one warp.  A
+// region is a run of pieces solved as one DP; a seam is legal when the right
+// region's start state follows the left region's end state by a CTC move
+// (stay, step, or a skip into a token that differs from the previous token
+// and from the blank -- precomputed for each region's start).  Every run of
+// consecutive failing seams becomes one repair job: the merged region
+// resumes from the end frontier of its first region and re-solves the
+// regions after it.  Returns the record's route:
+//   all seams legal, every region finite and NaN-free  -> joined (stitched)
+//   a region non-finite or with NaN                     -> conventional DP
+//   seams still failing after the last round            -> conventional DP
+//   a bounded wait gave up                               -> none (status 5)
+// Status >= 2 (rejected inputs) -> none.
+// write_regions: this warp records the next round's region starts (one
+// planner per record does; others that plan the same round only read).
+__device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__ ps,
+                           const OutputsDev& out, int round, bool final_round, bool write_regions,
+                           JobList* jobs, int lane, PlanStats& stats) {
+  const int C = rec.num_pieces, P0 = rec.first_piece;
+  const int status = out.status[r];
+  bool bad = false, fault = false, any_fail = false, run_open = false, overflow = false;
+  int run_job = 0, run_first = 0, cur_first = 0, njobs = 0;
+  // Piece j covers frames [j * kPieceFrames, end_of(j)); the last one ends at T.
+  auto end_of = [&](int j) { return j == C - 1 ? rec.T : (j + 1) * kPieceFrames; };
+  auto emit = [&](int job, int last) {
+    // All lanes take the same decisions; lane 0 writes them.
+    stats.merged += end_of(last) - run_first * kPieceFrames;
+    stats.skipped += (job - run_first) * kPieceFrames;
+    if (njobs == kMaxJobs) overflow = true;
+    if (lane == 0 && jobs != nullptr && !final_round && njobs < kMaxJobs) {
+      jobs->piece[njobs] = P0 + job;
+      jobs->first[njobs] = P0 + run_first;
+      jobs->last[njobs] = P0 + last;
+    }
+    ++njobs;
+  };
+  for (int base = 0; base < C; base += 32) {
+    // Each lane checks the seam in front of its piece (if it starts a region)
+    // and whether its piece ends a region that failed.
+    const int j = base + lane;
+    bool seam = false, fail = false, region_bad = false, region_fault = false;
+    if (j < C) {
+      const PieceState mine = load_piece_state(ps + P0 + j);
+      const bool next_rs = j + 1 >= C || __ldcg(&ps[P0 + j + 1].region_start[round]) != 0;
+      const int prev_end = j > 0 ? __ldcg(&ps[P0 + j - 1].end) : 0;
+      seam = mine.region_start[round] != 0 && j > 0;
+      // The next round's regions start as this round's; merges clear below.
+      if (!final_round && write_regions) ps[P0 + j].region_start[round + 1] = mine.region_start[round];
+      if (seam) {
+        const int jump = mine.start - prev_end;
+        fail = !(jump == 0 || jump == 1 || (jump == 2 && mine.start_skip));
+      }
+      region_bad = next_rs && (mine.flags & kPieceOk) == 0;
+      region_fault = next_rs && (mine.flags & kPieceFault) != 0;
+    }
+    if (status != 0) break;  // rejected inputs: nothing to plan
+    unsigned seams = __ballot_sync(0xffffffffu, seam);
+    const unsigned fails = __ballot_sync(0xffffffffu, fail);
+    bad |= __any_sync(0xffffffffu, region_bad) != 0;
+    fault |= __any_sync(0xffffffffu, region_fault) != 0;
+    // Runs of consecutive failing seams, in piece order (uniform over lanes).
+    while (seams) {
+      const int q = __ffs(seams) - 1;
+      seams &= seams - 1;
+      const int jj = base + q;
+      if ((fails >> q) & 1u) {
+        any_fail = true;
+        if (!run_open) { run_open = true; run_job = jj; run_first = cur_first; }
+      } else {
+        if (run_open) { emit(run_job, jj - 1); run_open = false; }
+        cur_first = jj;
+      }
+    }
+  }
+  if (status != 0) {
+    if (lane == 0 && jobs != nullptr) jobs->count = 0;
+    __syncwarp();
+    return kRouteNone;
+  }
+  if (run_open) emit(run_job, C - 1);
+  int decision;
+  if (fault) decision = kRouteNone;
+  else if (bad || (any_fail && (final_round || overflow))) decision = kRouteFallback;
+  else if (!any_fail) decision = kRouteStitched;
+  else decision = kRoutePending;
+  stats.jobs = njobs;
+  // Merge the failing runs into the next round's regions only when there is
+  // a next round for this record: a record already routed keeps its regions,
+  // so a later planner of it sees the same bad or joined regions again.
+  __syncwarp();  // the lanes' copies above land before lane 0 clears
+  if (lane == 0 && jobs != nullptr && decision == kRoutePending && write_regions) {
+    for (int q = 0; q < njobs && q < kMaxJobs; ++q)
+      for (int k = jobs->piece[q]; k <= jobs->last[q]; ++k) ps[k].region_start[round + 1] = 0;
+  }
+  if (lane == 0 && jobs != nullptr) jobs->count = decision == kRoutePending ? njobs : 0;
+  __syncwarp();
+  return decision;
+}
+
+// The finisher group of a record of the optimized route (the host planner's
+// rule, ffa_host.cpp): row-staged before gathered, then the CTA size its
+// repairs get: 128 / 256 threads for at most 4 / 8 warps at 8 states per
+// thread when the narrow groups are in use, else 512.
+__device__ __forceinline__ int finish_group(const RecordDev& rec, bool narrow) {
+  const int nw8 = (2 * rec.U + 1 + 255) / 256;
+  const int size = !narrow ? 2 : (nw8 <= kMaxWarps / 4 ? 0 : (nw8 <= kMaxWarps / 2 ? 1 : 2));
+  return (rec.row_mode ? 0 : 3) + size;
+}
+
+// Round 0's plan in the first pass: every slot of a record counts itself out
+// once its pieces' states are written; the last one plans round 0 with its
+// first warp.  A joined record is done here (route and diagnostics; the fill
+// folds its objective); any other goes to the finisher's list.  Called by
+// every thread of the slot.
+__device__ void plan_round0(const SlotCtx& x, const RecordDev& rec, ForwardShared& sh,
+                            const ForwardParams& P) {
+  x.sync();  // the slot's traces have written its pieces' states
+  if (x.tl == 0) {
+    __threadfence();
+    const int slots = (rec.num_pieces + P.run_pieces - 1) / P.run_pieces;
+    sh.slot_status[x.slot] = atomicAdd(&P.slot_done[x.r], 1) == slots - 1 ? 1 : 0;
+    __threadfence();
+  }
+  x.sync();
+  if (!sh.slot_status[x.slot] || x.lw != 0) return;
+  PlanStats stats;
+  const int decision = plan_record(rec, x.r, P.pstates, P.out, 0, false, false, nullptr, x.lane, stats);
+  if (x.lane != 0) return;
+  if (decision == kRouteStitched) {
+    // Diagnostics of a record joined without repairs (the rest stay zero).
+    P.route[x.r] = kRouteStitched;
+    P.out.stitched[x.r] = 1;
+    if (P.out.reuse_stats)
+      P.out.reuse_stats[4 * x.r + 2] = static_cast<int64_t>(rec.num_pieces - 1) * (2 * rec.U + 1);
+  } else {
+    const int g = finish_group(rec, P.finish_narrow != 0);
+    P.finish_list[P.finish_base[g] + atomicAdd(&P.finish_count[g], 1)] = x.r;
+  }
+}
+
 // The first pass.  One CTA = one Bundle of slots of `nw` warps with the same
 // states per thread; a slot runs one whole record (conventional DP with its
 // outputs) or a run of consecutive pieces of one record of the optimized
@@ -566,9 +733,15 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
         if (status >= 2) P.out.objective[r] = -INFINITY;
         if (status >= 2 || chunked) P.out.status[r] = status;
       }
-      if (status >= 2) return;
+      if (status >= 2) {
+        if (chunked && P.plan_first) plan_round0(x, rec, sh, P);
+        return;
+      }
     } else {
-      if (masked) return;
+      if (masked) {
+        if (chunked && P.plan_first) plan_round0(x, rec, sh, P);
+        return;
+      }
       if (tl == 0) sh.slot_fault[x.slot] = 0;
     }
     if (chunked) {
@@ -594,132 +767,7 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
     piece_dp<4, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
   else
     piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
-}
-
-// Repair jobs of one round of one record (shared memory of the finisher).
-constexpr int kMaxJobs = 128;
-struct JobList {
-  int count;
-  int piece[kMaxJobs];  // first piece re-solved (resumes from the frontier of piece - 1)
-  int first[kMaxJobs];  // first piece of the merged region
-  int last[kMaxJobs];   // last piece of the merged region
-};
-
-// What one round's plan adds to a record's diagnostics.
-struct PlanStats {
-  int64_t merged = 0;   // frames of the merged regions
-  int64_t skipped = 0;  // frames the saved frontiers spared
-  int jobs = 0;
-};
-
-// A piece's state as other CTAs of the running launch may have left it:
-// loaded through L2 (ld.global.cg), never from a stale L1 line.
-__device__ __forceinline__ PieceState load_piece_state(const PieceState* p) {
-  const int4 a = __ldcg(reinterpret_cast<const int4*>(p));
-  const int4 b = __ldcg(reinterpret_cast<const int4*>(p) + 1);
-  PieceState s;
-  s.start = a.x; s.end = a.y; s.flags = a.z; s.start_skip = a.w;
-  s.region_start[0] = b.x; s.region_start[1] = b.y; s.region_start[2] = b.z; s.region_start[3] = b.w;
-  return s;
-}
-
-// Seam check and repair planning of one round of one record, by one warp.  A
-// region is a run of pieces solved as one DP; a seam is legal when the right
-// region's start state follows the left region's end state by a CTC move
-// (stay, step, or a skip into a token that differs from the previous token
-// and from the blank -- precomputed for each region's start).  Every run of
-// consecutive failing seams becomes one repair job: the merged region
-// resumes from the end frontier of its first region and re-solves the
-// regions after it.  Returns the record's route:
-//   all seams legal, every region finite and NaN-free  -> joined (stitched)
-//   a region non-finite or with NaN                     -> conventional DP
-//   seams still failing after the last round            -> conventional DP
-//   a bounded wait gave up                               -> none (status 5)
-// Status >= 2 (rejected inputs) -> none.
-// write_regions: this warp records the next round's region starts (one
-// planner per record does; others that plan the same round only read).
-__device__ int plan_record(const RecordDev& rec, int r, PieceState* __restrict__ ps,
-                           const OutputsDev& out, int round, bool final_round, bool write_regions,
-                           JobList& jobs, int lane, PlanStats& stats) {
-  const int C = rec.num_pieces, P0 = rec.first_piece;
-  const int status = out.status[r];
-  bool bad = false, fault = false, any_fail = false, run_open = false, overflow = false;
-  int run_job = 0, run_first = 0, cur_first = 0, njobs = 0;
-  // Piece j covers frames [j * kPieceFrames, end_of(j)); the last one ends at T.
-  auto end_of = [&](int j) { return j == C - 1 ? rec.T : (j + 1) * kPieceFrames; };
-  auto emit = [&](int job, int last) {
-    // All lanes take the same decisions; lane 0 writes them.
-    stats.merged += end_of(last) - run_first * kPieceFrames;
-    stats.skipped += (job - run_first) * kPieceFrames;
-    if (njobs == kMaxJobs) overflow = true;
-    if (lane == 0 && !final_round && njobs < kMaxJobs) {
-      jobs.piece[njobs] = P0 + job;
-      jobs.first[njobs] = P0 + run_first;
-      jobs.last[njobs] = P0 + last;
-    }
-    ++njobs;
-  };
-  for (int base = 0; base < C; base += 32) {
-    // Each lane checks the seam in front of its piece (if it starts a region)
-    // and whether its piece ends a region that failed.
-    const int j = base + lane;
-    bool seam = false, fail = false, region_bad = false, region_fault = false;
-    if (j < C) {
-      const PieceState mine = load_piece_state(ps + P0 + j);
-      const bool next_rs = j + 1 >= C || __ldcg(&ps[P0 + j + 1].region_start[round]) != 0;
-      const int prev_end = j > 0 ? __ldcg(&ps[P0 + j - 1].end) : 0;
-      seam = mine.region_start[round] != 0 && j > 0;
-      // The next round's regions start as this round's; merges clear below.
-      if (!final_round && write_regions) ps[P0 + j].region_start[round + 1] = mine.region_start[round];
-      if (seam) {
-        const int jump = mine.start - prev_end;
-        fail = !(jump == 0 || jump == 1 || (jump == 2 && mine.start_skip));
-      }
-      region_bad = next_rs && (mine.flags & kPieceOk) == 0;
-      region_fault = next_rs && (mine.flags & kPieceFault) != 0;
-    }
-    if (status != 0) break;  // rejected inputs: nothing to plan
-    unsigned seams = __ballot_sync(0xffffffffu, seam);
-    const unsigned fails = __ballot_sync(0xffffffffu, fail);
-    bad |= __any_sync(0xffffffffu, region_bad) != 0;
-    fault |= __any_sync(0xffffffffu, region_fault) != 0;
-    // Runs of consecutive failing seams, in piece order (uniform over lanes).
-    while (seams) {
-      const int q = __ffs(seams) - 1;
-      seams &= seams - 1;
-      const int jj = base + q;
-      if ((fails >> q) & 1u) {
-        any_fail = true;
-        if (!run_open) { run_open = true; run_job = jj; run_first = cur_first; }
-      } else {
-        if (run_open) { emit(run_job, jj - 1); run_open = false; }
-        cur_first = jj;
-      }
-    }
-  }
-  if (status != 0) {
-    if (lane == 0) jobs.count = 0;
-    __syncwarp();
-    return kRouteNone;
-  }
-  if (run_open) emit(run_job, C - 1);
-  int decision;
-  if (fault) decision = kRouteNone;
-  else if (bad || (any_fail && (final_round || overflow))) decision = kRouteFallback;
-  else if (!any_fail) decision = kRouteStitched;
-  else decision = kRoutePending;
-  stats.jobs = njobs;
-  // Merge the failing runs into the next round's regions only when there is
-  // a next round for this record: a record already routed keeps its regions,
-  // so a later planner of it sees the same bad or joined regions again.
-  __syncwarp();  // the lanes' copies above land before lane 0 clears
-  if (lane == 0 && decision == kRoutePending && write_regions) {
-    for (int q = 0; q < njobs && q < kMaxJobs; ++q)
-      for (int k = jobs.piece[q]; k <= jobs.last[q]; ++k) ps[k].region_start[round + 1] = 0;
-  }
-  if (lane == 0) jobs.count = decision == kRoutePending ? njobs : 0;
-  __syncwarp();
-  return decision;
+  if (chunked && P.plan_first) plan_round0(x, rec, sh, P);
 }
 
 // The finisher's static shared memory (its job list) stays under 2 KiB; the
@@ -740,7 +788,8 @@ static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
 template <bool kRow, int kV>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records,
-                 int ctas_per_record, unsigned dynamic_smem) {
+                 const int32_t* __restrict__ device_count, int ctas_per_record, unsigned dynamic_smem) {
+  if (device_count != nullptr && static_cast<int>(blockIdx.x) / ctas_per_record >= *device_count) return;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
   __shared__ JobList jobs;
@@ -782,7 +831,7 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
     if (x.warp == 0) {
       PlanStats stats;
       const int decision = plan_record(rec, r, P.pstates, P.out, round, round == kRepairRounds, part == 0,
-                                       jobs, x.lane, stats);
+                                       &jobs, x.lane, stats);
       if (decision == kRoutePending) {
         ++passes;
         repaired += stats.merged;
@@ -1117,8 +1166,8 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 }
 
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
-                          int ctas_per_record, int threads, bool row_mode, int row_vocab,
-                          unsigned smem_bytes, cudaStream_t stream) {
+                          const int32_t* device_count, int ctas_per_record, int threads, bool row_mode,
+                          int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
   auto kernel = !row_mode ? ffa_finish_route<false, 0>
                          : (row_vocab == 32 ? ffa_finish_route<true, 32> : ffa_finish_route<true, 0>);
@@ -1138,7 +1187,8 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   ++g_launches;
   if (threads != kCtaThreads && threads != kCtaThreads / 2 && threads != kCtaThreads / 4)
     return cudaErrorInvalidValue;
-  kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, ctas_per_record, smem_bytes);
+  kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, device_count, ctas_per_record,
+                                                                  smem_bytes);
   return cudaGetLastError();
 }
 

@@ -200,3 +200,33 @@ def test_flat_ties_on_long_records(cuda):
     assert_same_optimum(result, ref, es, ts, 0, "flat")
     conv, _ = run_both(es, ts, 0, "conventional")
     assert_matches_oracle(conv, ref, "flat conventional")
+
+
+def test_many_records_with_masks_and_rejections(cuda):
+    # More records than SMs: round 0 is planned in the first pass, records it
+    # joins skip the finisher, and the finisher's lists are built on the
+    # device.  Masked records (status 2), invalid targets (3) and infeasible
+    # lengths (4) must still get their routes and outputs.
+    wl = workloads.config(1, scale=5)  # 320 records
+    es, ts = [list(x) for x in wl.records()]
+    rng = np.random.default_rng(12)
+    for i in rng.choice(wl.batch, 12, replace=False):
+        ts[i] = ts[i].copy()
+        ts[i][len(ts[i]) // 2] = wl.blank          # status 3
+    for i in rng.choice(wl.batch, 6, replace=False):
+        es[i] = es[i][: max(1, len(ts[i]) - 3)]    # status 4
+    mask = np.ones(wl.batch, bool)
+    mask[rng.choice(wl.batch, 20, replace=False)] = False
+    ref = oracle.align(es, ts, wl.blank, validity=mask.astype(np.uint8))
+    d_es, d_ts = cuda_records(es, ts)
+    validity = torch.from_numpy(mask).to(cuda)
+    for mode in ("optimized", "conventional"):
+        result = ffa.align(d_es, d_ts, blank_id=wl.blank, mode=mode, emission_validity=validity)
+        assert set(np.unique(ref.status)) >= {0, 2, 3}
+        if mode == "conventional":
+            assert_matches_oracle(result, ref, mode)
+        else:
+            assert_same_optimum(result, ref, es, ts, wl.blank, mode)
+            stitched = result.stitched.cpu().numpy()
+            assert stitched[ref.status == 0].mean() > 0.9
+            assert (stitched[ref.status != 0] == 0).all()
