@@ -207,7 +207,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   // Zeroed counters of round 0's plan in the first pass (per record, then
   // per finisher group), uploaded with the descriptors.
   L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups), 16);
-  L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 16, 256);
+  L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
   L->classes = off; off = align_up(off + count, 256);
@@ -366,6 +366,21 @@ int plan_scan(const ffa_record* records, int64_t count, ScanLayout* L) {
   L->staging_bytes = off;
   L->workspace_bytes = off;
   return FFA_OK;
+}
+
+// The descriptor upload.  From pinned staging a small kernel reads the bytes
+// through the buffer's device mapping, so the upload never waits in a copy
+// engine's queue behind a large copy another stream has submitted (the next
+// batch's emissions, say); from any other staging it is a plain
+// cudaMemcpyAsync.  The workspace has room for the upload rounded up to 16
+// bytes, and so has the staging buffer.
+cudaError_t upload_descriptors(void* dst, const void* staging, size_t bytes, cudaStream_t s) {
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, staging) == cudaSuccess && attr.type == cudaMemoryTypeHost &&
+      attr.devicePointer != nullptr && (reinterpret_cast<uintptr_t>(attr.devicePointer) & 15) == 0)
+    return ffa::launch_upload(attr.devicePointer, dst, bytes, s);
+  (void)cudaGetLastError();  // a failed attribute query leaves no error behind
+  return cudaMemcpyAsync(dst, staging, bytes, cudaMemcpyHostToDevice, s);
 }
 
 int cuda_fail(cudaError_t err, const char* what) {
@@ -677,7 +692,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
 
   auto* dev = static_cast<unsigned char*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(dev, host, upload_bytes, cudaMemcpyHostToDevice, s);
+  cudaError_t err = upload_descriptors(dev, host, upload_bytes, s);
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
 
   ffa::ForwardParams fp{};

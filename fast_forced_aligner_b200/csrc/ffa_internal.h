@@ -254,6 +254,10 @@ int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned sme
 // Dynamic shared memory a long-record CTA needs besides its emission ring.
 size_t long_header_bytes();
 
+// The descriptor upload by a kernel that reads pinned host memory through
+// its device mapping (no copy-engine queue); `bytes` rounded up to 16.
+cudaError_t launch_upload(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream);
+
 // Token spans: one warp per record.
 struct SpanRecord {
   const int64_t* labels;  // the record's frames of an ffa_align labels output

@@ -26,6 +26,7 @@
 // reproduces the reference bit for bit.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -1130,6 +1131,24 @@ namespace {
 thread_local int64_t g_launches = 0;
 }  // namespace
 int64_t launches_so_far() { return g_launches; }
+
+// Copies 16-byte blocks from pinned host memory (read over the bus) to the
+// device, many blocks in flight per thread.
+__global__ void __launch_bounds__(256) ffa_upload_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                         int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+cudaError_t launch_upload(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>((bytes + 15) / 16);
+  if (n == 0) return cudaSuccess;
+  ++g_launches;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1184));
+  ffa_upload_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint4*>(mapped_src), static_cast<uint4*>(dst), n);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_spans(const SpanRecord* recs, int64_t count, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
