@@ -10,7 +10,9 @@
 //     host into packed CTAs ("bundles") of equal slot size, longest first, so
 //     one launch covers a ragged batch;
 //   - the planner builds every table in the caller's staging buffer in place
-//     (no heap allocation), then enqueues one cudaMemcpyAsync.
+//     (no heap allocation), then enqueues one upload of it: a small kernel
+//     reading pinned staging through its device mapping, or a cudaMemcpyAsync
+//     from any other memory.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -849,7 +851,7 @@ int ffa_emission_validity(const ffa_record* records, int64_t count, uint8_t* val
   }
   auto* dev = static_cast<unsigned char*>(workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(dev, host, L.staging_bytes, cudaMemcpyHostToDevice, s);
+  cudaError_t err = upload_descriptors(dev, host, L.staging_bytes, s);
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
   err = ffa::launch_validity(reinterpret_cast<const ffa::ScanRecord*>(dev + L.recs), count,
                              reinterpret_cast<const ffa::ScanItem*>(dev + L.items), n, valid, s);
@@ -896,8 +898,7 @@ int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
     recs[i] = d;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(workspace, staging, sizes.staging_bytes,
-                                    cudaMemcpyHostToDevice, s);
+  cudaError_t err = upload_descriptors(workspace, staging, sizes.staging_bytes, s);
   if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
   err = ffa::launch_check_targets(static_cast<const ffa::RecordDev*>(workspace), count, status, s);
   if (err != cudaSuccess) return cuda_fail(err, "target check launch");
@@ -942,7 +943,7 @@ int ffa_token_spans(const int64_t* labels, const int64_t* frames, const int32_t*
     token_off += tokens[i];
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t err = cudaMemcpyAsync(workspace, staging, sizeof(ffa::SpanRecord) * count, cudaMemcpyHostToDevice, s);
+  cudaError_t err = upload_descriptors(workspace, staging, sizeof(ffa::SpanRecord) * count, s);
   if (err != cudaSuccess) return cuda_fail(err, "span descriptor upload");
   err = ffa::launch_spans(static_cast<const ffa::SpanRecord*>(workspace), count, s);
   if (err != cudaSuccess) return cuda_fail(err, "span launch");
