@@ -60,6 +60,9 @@ def parse_args():
                    help="partition one batch over the ranks (strong scaling) instead of one batch per rank")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU work in the cpu_baseline sample")
+    p.add_argument("--input", default="log-probs", choices=["log-probs", "logits-f32", "logits-bf16"],
+                   help="what the batch holds: fp32 log-probabilities (the reference's input), or a "
+                        "model's logits aligned as their log_softmax inside the kernels (from_logits)")
     args = p.parse_args()
     if args.warmup < 3:
         p.error("--warmup must be >= 3")
@@ -81,19 +84,20 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def algorithmic_bytes(wl):
+def algorithmic_bytes(wl, element_bytes=4):
     """The path's algorithmic bytes: 32 B for every sector of a row holding a label column
     of the record (sectors counted from a 32 B-aligned record base), plus 12 B
     of output per frame and the 8 B int64 targets.  Returns (emission+target
     bytes read by the DP, full B_alg)."""
     read = 0
     out = 0
+    per_sector = 32 // element_bytes
     for i in range(wl.batch):
         e, t = wl.record(i)
         T, V = e.shape
         cols = np.unique(np.r_[t, wl.blank])
-        per_residue = np.array([np.unique((r + cols) // 8).size for r in range(8)])
-        residues = (np.arange(T, dtype=np.int64) * V) % 8
+        per_residue = np.array([np.unique((r + cols) // per_sector).size for r in range(per_sector)])
+        residues = (np.arange(T, dtype=np.int64) * V) % per_sector
         read += 32 * int(per_residue[residues].sum()) + 8 * t.size
         out += 12 * T
     return read, read + out
@@ -195,6 +199,30 @@ def validity_scan_roofline(ffa, e_dev, frame_list, vocab, warmup, min_bytes=512 
             "ms": ms, "achieved": nbytes / (ms / 1e3) / 1e9, "unit": "GB/s", "all_valid": ok}
 
 
+def unfused_logits_ms(ffa, e_dev, t_dev, wl, args, flush):
+    """Device time per step of what a caller without fused logits runs:
+    torch.log_softmax in fp32, then the align on the materialised
+    log-probabilities; queued and flushed as the value loop is."""
+    import torch
+
+    def step():
+        emissions = torch.log_softmax(e_dev.float(), dim=-1)
+        return ffa.align_packed(emissions, wl.lengths, t_dev, wl.target_lengths, blank_id=wl.blank, mode=args.mode)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(20_000_000)
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        step()
+        b.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / args.steps
+
+
 def cpu_reference_runner(wl):
     """The reference's corrected C++ comparator (oracle/_ref) over all host
     threads, one record per task with the GIL released, as in its benchmark
@@ -267,14 +295,25 @@ def run_ours(args):
     records_total = int(sum_over_ranks(wl.batch))
     frames = int(wl.lengths.sum())
     frame_list, token_list = wl.lengths.tolist(), wl.target_lengths.tolist()
-    e_host = torch.from_numpy(wl.emissions).pin_memory()
+    from_logits = args.input != "log-probs"
+    if from_logits:
+        # Logits whose log_softmax is the workload's log-probabilities up to
+        # rounding: each row shifted by a seeded offset, as a model's rows are.
+        offsets = np.random.default_rng(1234).uniform(-8.0, 8.0, (wl.emissions.shape[0], 1)).astype(np.float32)
+        e_host = torch.from_numpy(wl.emissions + offsets)
+        if args.input == "logits-bf16":
+            e_host = e_host.to(torch.bfloat16)
+        e_host = e_host.pin_memory()
+    else:
+        e_host = torch.from_numpy(wl.emissions).pin_memory()
     t_host = torch.from_numpy(wl.targets).pin_memory()
     e_dev = e_host.to(device)
     t_dev = t_host.to(device)
     ffa.validate_inputs(list(e_dev.split(frame_list)), list(t_dev.split(token_list)), blank_id=wl.blank)
 
     def step(e, t):
-        return ffa.align_packed(e, wl.lengths, t, wl.target_lengths, blank_id=wl.blank, mode=args.mode)
+        return ffa.align_packed(e, wl.lengths, t, wl.target_lengths, blank_id=wl.blank, mode=args.mode,
+                                from_logits=from_logits)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     import ctypes
@@ -344,7 +383,7 @@ def run_ours(args):
 
         def e2e_step():
             return astream.submit(e_host, wl.lengths, t_host, wl.target_lengths, blank_id=wl.blank,
-                                  mode=args.mode)
+                                  mode=args.mode, from_logits=from_logits)
         for _ in range(args.warmup):
             pending = e2e_step()
         pending.result()
@@ -386,13 +425,16 @@ def run_ours(args):
     phases = {name: round(statistics.median(v), 2) for name, v in phase_us.items()}
     launches = per_call[-1] * 2 * args.steps  # device-resident + end-to-end timed loops
     status_ok = bool((result.status == 0).all().item()) and bool((host_result.status == 0).all().item())
-    scan = validity_scan_roofline(ffa, e_dev, frame_list, wl.vocab, args.warmup)
+    # The validity scan reads fp32 records.
+    scan = validity_scan_roofline(ffa, e_dev, frame_list, wl.vocab, args.warmup) \
+        if e_dev.dtype == torch.float32 else None
+    unfused = unfused_logits_ms(ffa, e_dev, t_dev, wl, args, flush) if from_logits else None
 
     all_frames = sum_over_ranks(frames)
     value = all_frames * args.steps / (total_ms / 1e3)
     e2e_value = all_frames * args.steps / (e2e_ms / 1e3)
     fwd_avg_ms = max_over_ranks(statistics.fmean(fwd_ms))
-    read_bytes, alg_bytes = algorithmic_bytes(wl)
+    read_bytes, alg_bytes = algorithmic_bytes(wl, e_dev.element_size())
     peak, peak_kind = peaks()
     achieved = read_bytes / (fwd_avg_ms / 1e3) / 1e9
     traffic = traffic_from_profile(wl.name)
@@ -410,14 +452,16 @@ def run_ours(args):
                    "records_per_gpu": wl.batch, "frames_per_gpu": frames,
                    "records_total": records_total, "frames_total": int(all_frames),
                    "vocab": wl.vocab, "mode": args.mode, "check_inputs": True,
-                   "inputs": "packed device-resident fp32 [sum T, V] + int64 targets",
+                   "inputs": ("packed device-resident fp32 [sum T, V] log-probabilities" if not from_logits
+                              else f"packed device-resident {args.input[7:]} [sum T, V] logits, aligned as their "
+                                   "log_softmax inside the kernels (from_logits)") + " + int64 targets",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "timing": "steps queued back to back (no host sync between them); per-step device time "
                              "from events around each align call; latency_ms_per_call = one synced call, "
                              "host and device",
                    "parallelism": parallelism},
         "e2e": {"value": e2e_value, "unit": "frames/s",
-                "h2d_bytes_per_step": int(e_host.numel() * 4 + t_host.numel() * 8),
+                "h2d_bytes_per_step": int(e_host.numel() * e_host.element_size() + t_host.numel() * 8),
                 "d2h_bytes_per_step": int(frames * 12 + wl.batch * 8),
                 "api": "fast_forced_aligner_b200.AlignStream.submit (align_packed, the torch op over the "
                        "C ABI, with host copies overlapped on separate streams)"},
@@ -433,13 +477,18 @@ def run_ours(args):
                "first_pass_cells_per_s": cells / (fwd_avg_ms / 1e3), "cells": cells},
         "phases_us": phases,
         "validity_scan": dict(scan, peak=peak, frac=scan["achieved"] / peak,
-                              peak_source=f"{peak_kind} hbm_gbs"),
+                              peak_source=f"{peak_kind} hbm_gbs") if scan else None,
         "b_alg_bytes": alg_bytes,
         "gpu_launches": launches,
         "gpu_launches_note": f"{per_call[-1]} kernels of libffa_b200 per align call (counted by "
                              "ffa_launch_count), in the device-resident and the end-to-end timed loops",
         "status_ok": status_ok,
     }
+    if unfused is not None:
+        line["unfused"] = {"ms_per_step": unfused, "value": frames * world / (unfused / 1e3),
+                           "pipeline": "torch.log_softmax(logits.float(), -1) then align_packed on the "
+                                       "fp32 log-probabilities (the reference's example pipeline), device-"
+                                       "resident, timed as value"}
     clock = clocks.summary()
     line["clocks"] = clock
     if rank == 0 and world == 1:
@@ -449,7 +498,9 @@ def run_ours(args):
             pool.shutdown()
         line["cpu_baseline"] = {"value": cpu_value, "unit": "frames/s", "cores": threads, "kind": kind,
                                 "sample": f"{passes} passes over the {wl.name} batch "
-                                          f"({wl.batch} records, {frames} frames) in {seconds:.1f} s"}
+                                          f"({wl.batch} records, {frames} frames) in {seconds:.1f} s"
+                                          + (" (as fp32 log-probabilities: the reference takes no logits)"
+                                             if from_logits else "")}
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:

@@ -219,12 +219,72 @@ def emission_validity(emissions: Sequence[Tensor]) -> Tensor:
         return torch.ops.ffa_b200.emission_validity(list(emissions))
 
 
-def _mode(mode, check_inputs) -> int:
+def _mode(mode, check_inputs, from_logits=False) -> int:
     if mode not in _MODES:
         raise ValueError("mode must be 'optimized' or 'conventional'")
     if type(check_inputs) is not bool:
         raise TypeError("check_inputs must be bool")
+    if type(from_logits) is not bool:
+        raise TypeError("from_logits must be bool")
     return _MODES[mode]
+
+
+def _input_format(first, from_logits: bool) -> int:
+    """The C ABI's input format (ffa_input_format) for a call's inputs."""
+    if not from_logits:
+        return 0
+    dtype = first.dtype if isinstance(first, Tensor) else None
+    if dtype == torch.float32:
+        return 1
+    if dtype == torch.bfloat16:
+        return 2
+    raise ValueError("logits must be contiguous CUDA float32 or bfloat16 tensors")
+
+
+@torch.inference_mode()
+def row_logsumexp(logits: Tensor | Sequence[Tensor]) -> Tensor:
+    """Each row's log-sum-exp, as ``align(..., from_logits=True)`` uses it.
+
+    ``z[t] = m + log(sum_v exp(x[t, v] - m))`` with ``m`` the row maximum, in
+    fp32 on the GPU (``torch.ops.ffa_b200.row_logsumexp``).  A row holding NaN
+    or +inf, or only -inf, gets NaN.
+
+    Args:
+        logits: one contiguous CUDA float32 or bfloat16 ``(T, V)`` tensor, or a
+            sequence of them (one dtype, one device).
+
+    Returns:
+        CUDA float32 ``(sum T,)``: the rows of every tensor, in order.
+    """
+    items = [logits] if isinstance(logits, Tensor) else list(logits)
+    if not 0 < len(items) <= 65535 or not isinstance(items[0], Tensor) or items[0].device.type != "cuda":
+        raise ValueError("logits must be contiguous CUDA float32 or bfloat16 [T,V] tensors of one dtype on one device")
+    with torch.cuda.device(items[0].device):
+        load_extension()
+        return torch.ops.ffa_b200.row_logsumexp(items)
+
+
+@torch.inference_mode()
+def log_softmax(logits: Tensor | Sequence[Tensor]) -> Tensor | list[Tensor]:
+    """The emission matrices ``align(logits, ..., from_logits=True)`` aligns.
+
+    ``x - z[:, None]`` in fp32 (one rounded subtraction per element, bf16
+    logits widened exactly first), with ``z`` from ``row_logsumexp``: within
+    a few fp32 ulps of ``torch.log_softmax(x.float(), -1)``, and exactly the
+    values the fused path reads.  Aligning these log-probabilities gives the
+    fused path's results bit for bit.
+
+    Returns:
+        A float32 tensor for a tensor argument, else a list of them.
+    """
+    single = isinstance(logits, Tensor)
+    items = [logits] if single else list(logits)
+    z = row_logsumexp(items)
+    out, row = [], 0
+    for x in items:
+        out.append(x.float() - z[row:row + x.shape[0], None])
+        row += x.shape[0]
+    return out[0] if single else out
 
 
 @torch.inference_mode()
@@ -232,6 +292,7 @@ def align(
     emissions: Sequence[Tensor], targets: Sequence[Tensor], *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
     check_inputs: bool = True, emission_validity: Tensor | None = None,
+    from_logits: bool = False,
 ) -> AlignmentBatch:
     """Align known CTC targets to resident emissions; return CUDA frame paths.
 
@@ -258,23 +319,31 @@ def align(
             (status 4) on the GPU; must be a Python bool.
         emission_validity: optional CUDA bool ``[B]`` mask; False gives status
             2 unless target validation fails.
+        from_logits: the ``emissions`` are a model's logits (float32 or
+            bfloat16, one dtype for the batch), aligned as their log_softmax
+            without writing it out: each kernel reads the logits it needs and
+            subtracts the row's log-sum-exp (``log_softmax`` returns the same
+            matrices, for inspection).  Not in the reference, whose examples
+            call ``torch.log_softmax`` first.
 
     Returns:
         AlignmentBatch with packed CUDA outputs.  Failures are recorded in
-        ``status`` and do not raise; call ``raise_for_status``.
+        ``status`` and do not raise; call ``raise_for_status``.  ``scores``
+        hold the selected log_softmax values when ``from_logits``.
 
     Raises:
         ValueError: invalid mode, metadata, blank IDs or mask metadata.
-        TypeError: ``check_inputs`` is not a bool.
+        TypeError: ``check_inputs`` or ``from_logits`` is not a bool.
         RuntimeError: the native library is unavailable or CUDA fails.
     """
-    code = _mode(mode, check_inputs)
+    code = _mode(mode, check_inputs, from_logits)
     blanks = _metadata(emissions, targets, blank_id)
+    fmt = _input_format(emissions[0], from_logits)
     _check_mask(emission_validity, emissions[0].device, len(emissions))
     load_extension()
     # The op runs under a device guard for the inputs' device.
     tensors, lengths = torch.ops.ffa_b200.align(
-        list(emissions), list(targets), blanks, code, emission_validity, check_inputs)
+        list(emissions), list(targets), blanks, code, emission_validity, check_inputs, fmt)
     return AlignmentBatch(tuple(lengths), *tensors)
 
 
@@ -296,6 +365,7 @@ def align_packed(
     emissions: Tensor, frames, targets: Tensor, tokens, *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
     check_inputs: bool = True, emission_validity: Tensor | None = None,
+    from_logits: bool = False,
 ) -> AlignmentBatch:
     """Packed variable-length form of ``align`` (no per-record tensors).
 
@@ -305,9 +375,11 @@ def align_packed(
     vector.  ``frames``, ``tokens`` and a per-record ``blank_id`` may be
     Python sequences, NumPy integer arrays or integer tensors (arrays and
     tensors skip the per-record Python work).  Results and errors are those
-    of ``align`` on the same records.
+    of ``align`` on the same records; ``from_logits`` takes a float32 or
+    bfloat16 logits matrix.
     """
-    code = _mode(mode, check_inputs)
+    code = _mode(mode, check_inputs, from_logits)
+    fmt = _input_format(emissions, from_logits)
     frames_t = _host_counts(frames, "frames")
     tokens_t = _host_counts(tokens, "tokens")
     count = frames_t.numel()
@@ -327,7 +399,7 @@ def align_packed(
     load_extension()
     # The op runs under a device guard for the inputs' device.
     tensors = torch.ops.ffa_b200.align_packed(
-        emissions, frames_t, targets, tokens_t, blanks_t, code, emission_validity, check_inputs)
+        emissions, frames_t, targets, tokens_t, blanks_t, code, emission_validity, check_inputs, fmt)
     return AlignmentBatch(tuple(frames_t.tolist()), *tensors)
 
 

@@ -6,6 +6,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "ffa_internal.h"
 
@@ -20,6 +21,10 @@ __device__ __forceinline__ unsigned smem_u32(const void* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
 }
 __device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
                : "memory");
 }
@@ -117,6 +122,70 @@ __device__ __forceinline__ unsigned long long ld_cluster_u64(const unsigned long
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+
+// How the kernels read an emission (ffa_input_format).  Format 0: fp32
+// log-probabilities, used as stored.  Formats 1 (fp32) and 2 (bf16): logits,
+// used as their log_softmax -- the emission of (t, v) is x[t, v] - z[t] in
+// one fp32 round-to-nearest subtraction, z[t] being row t's log-sum-exp that
+// ffa_row_lse wrote.  Every kernel forms it the same way, so every kernel
+// sees the same emission matrix.
+template <int kFmt>
+struct Input {
+  static_assert(kFmt >= 0 && kFmt <= 2, "input format");
+  using Elem = typename std::conditional<kFmt == 2, uint16_t, float>::type;
+  static constexpr bool kLogits = kFmt != 0;
+  static constexpr bool kHalf = kFmt == 2;
+};
+// A bf16 value (its 16 bits) as fp32: exact.
+__device__ __forceinline__ float bf16_to_float(uint32_t bits) { return __uint_as_float(bits << 16); }
+__device__ __forceinline__ float elem_to_float(float v) { return v; }
+__device__ __forceinline__ float elem_to_float(uint16_t v) { return bf16_to_float(v); }
+// The bf16 half of a 4-byte word at element parity `odd` (little endian).
+__device__ __forceinline__ float bf16_of_word(uint32_t word, bool odd) {
+  return __uint_as_float(odd ? (word & 0xffff0000u) : (word << 16));
+}
+
+// Row log-sum-exps of a run of frames from t0 (logits input): lane l holds
+// z[t0 + 32 b + l] of the run's current 32-frame block b and of the next one,
+// so a frame's value is one shuffle away and the next block's loads are in
+// flight a block ahead.  Every lane of the warp calls at().
+struct LseStream {
+  const float* z;  // the record's z[0 .. T)
+  int T;
+  float cur, nxt;
+  __device__ __forceinline__ float get(int t) const { return t < T ? __ldg(z + t) : 0.0f; }
+  __device__ __forceinline__ void start(const float* zr, int frames, int t0, int lane) {
+    z = zr;
+    T = frames;
+    cur = get(t0 + lane);
+    nxt = get(t0 + 32 + lane);
+  }
+  // Enter the block that starts at frame `first` (the previous next block).
+  __device__ __forceinline__ void advance(int first, int lane) {
+    cur = nxt;
+    nxt = get(first + 32 + lane);
+  }
+  // z of the frame at offset f from the run's start (f in the current block).
+  __device__ __forceinline__ float at(int f) const { return __shfl_sync(0xffffffffu, cur, f & 31); }
+};
+
+// A record's bf16 elements as 4-byte words (per-thread column gathers copy
+// whole aligned words): element i of the record -- i = t V + v -- lies in
+// word (i + odd) / 2 counted from `words`, in its upper half when i + odd is
+// odd.  That word is the 4-byte aligned granule holding the element, which
+// no device allocation splits.
+struct HalfWords {
+  const uint32_t* words;  // the 4-byte word holding the record's first element
+  int odd;                // 1 when that element is the word's upper half
+  __device__ __forceinline__ void set(const void* base) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(base);
+    words = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
+    odd = static_cast<int>((a >> 1) & 1);
+  }
+  __device__ __forceinline__ const uint32_t* word(int64_t i) const { return words + ((i + odd) >> 1); }
+  // Parity of element t V + v from the parities of frame t's first element and of v.
+  __device__ __forceinline__ bool row_odd(int64_t t, int V) const { return ((odd + (t & V)) & 1) != 0; }
+};
 
 // An emission that turns an unreachable state (-inf) into NaN: -inf + NaN and
 // -inf + inf are both NaN.

@@ -128,11 +128,17 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   return g;
 }
 
+// Bytes per stored element of an input format (ffa_input_format).
+size_t element_bytes(int format) { return format == FFA_INPUT_LOGITS_BF16 ? 2 : 4; }
+
 int check_record(const ffa_record& r, int64_t i, bool need_targets) {
-  if (r.emissions == nullptr || (reinterpret_cast<uintptr_t>(r.emissions) & 3) != 0 ||
-      r.reserved != 0)
+  if (r.format < FFA_INPUT_LOG_PROBS || r.format > FFA_INPUT_LOGITS_BF16)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "record " + std::to_string(i) + ": unknown input format");
+  if (r.emissions == nullptr ||
+      (reinterpret_cast<uintptr_t>(r.emissions) & (element_bytes(r.format) - 1)) != 0)
     return fail(FFA_ERR_INVALID_ARGUMENT,
-                "record " + std::to_string(i) + ": emissions must be a 4-byte aligned device pointer");
+                "record " + std::to_string(i) + ": emissions must be a " +
+                    std::to_string(element_bytes(r.format)) + "-byte aligned device pointer");
   if (r.frames < 1 || r.frames > FFA_MAX_FRAMES || r.vocab < 1 || r.vocab > FFA_MAX_VOCAB)
     return fail(FFA_ERR_UNSUPPORTED, "record " + std::to_string(i) +
                                          ": unsupported frame count or vocabulary");
@@ -167,9 +173,20 @@ int device_sms() {
 // at their end.
 struct AlignLayout {
   size_t recs, chunked, longs, fill, counters, slots, keys, classes, staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, workspace_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, lse, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
+  int format;  // the call's input format
 };
+
+// Every record of a call has one input format (the kernels are specialised
+// on it).
+int common_format(const ffa_record* records, int64_t count, int* format) {
+  for (int64_t i = 1; i < count; ++i)
+    if (records[i].format != records[0].format)
+      return fail(FFA_ERR_INVALID_ARGUMENT, "every record of a call must have the same input format");
+  *format = records[0].format;
+  return FFA_OK;
+}
 
 bool latency_bound(int64_t slots) { return slots <= device_sms(); }
 
@@ -196,6 +213,8 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
+  const int rc = common_format(records, count, &L->format);
+  if (rc) return rc;
   L->total_frames = frames;
   L->num_pieces = pieces;
   L->num_chunked = chunked;
@@ -223,6 +242,8 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->finish_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  // Logits: each frame's row log-sum-exp.
+  L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
   L->workspace_bytes = off;
   return FFA_OK;
 }
@@ -343,7 +364,7 @@ struct ScanLayout {
 };
 
 int64_t scan_chunks(const ffa_record& r) {
-  const uintptr_t base = reinterpret_cast<uintptr_t>(r.emissions);
+  const uintptr_t base = reinterpret_cast<uintptr_t>(r.emissions);  // fp32 (checked by plan_scan)
   const uintptr_t end = base + static_cast<uintptr_t>(r.frames) * r.vocab * 4;
   const uintptr_t aligned = base & ~static_cast<uintptr_t>(15);
   return static_cast<int64_t>((end - aligned + ffa::kScanChunkBytes - 1) / ffa::kScanChunkBytes);
@@ -356,6 +377,8 @@ int plan_scan(const ffa_record* records, int64_t count, ScanLayout* L) {
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, false);
     if (rc) return rc;
+    if (records[i].format == FFA_INPUT_LOGITS_BF16)
+      return fail(FFA_ERR_UNSUPPORTED, "the emission-validity scan reads fp32 records only");
     const int64_t chunks = scan_chunks(records[i]);
     if (chunks > INT32_MAX) return fail(FFA_ERR_UNSUPPORTED, "record too large to scan");
     items += chunks;
@@ -489,6 +512,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   int64_t out_off = 0, bp_off = 0, map_off = 0, seg_off = 0, nfill = 0, frontier_off = 0;
   int64_t np = 0, nchunked = 0;
   const bool lat = latency_bound(P);
+  const int fmt = L.format;
+  const size_t esize = element_bytes(fmt);  // bytes per stored element
   unsigned max_row_vocab = 0;
   int row_vocab = -1;  // common vocabulary of the row-staged records, 0 if mixed
   thread_local RunLengthModel runs_model;
@@ -501,7 +526,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, lat);
     ffa::RecordDev d{};
-    d.emissions = r.emissions;
+    d.emissions = static_cast<const float*>(r.emissions);  // bf16 bits for format 2
     d.targets = r.targets;
     d.out_off = out_off;
     d.bp_off = bp_off;
@@ -515,7 +540,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     d.kst = static_cast<uint8_t>(g.K);
     d.seg_log2 = static_cast<uint8_t>(g.seg_log2);
     // TMA row staging needs 16-byte aligned rows and a small row.
-    d.row_mode = (r.vocab % 4 == 0 && r.vocab <= ffa::kRowModeMaxVocab &&
+    d.row_mode = (r.vocab * esize % 16 == 0 && r.vocab <= ffa::kRowModeMaxVocab &&
                   (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0)
                      ? 1
                      : 0;
@@ -550,7 +575,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups));
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
-      align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4, 128));
+      align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * esize, 128));
   const int64_t row_slots =
       row_slot_bytes ? std::max<int64_t>(1, static_cast<int64_t>((ffa::kSmemBudget - header) / row_slot_bytes))
                      : ffa::kMaxWarps;
@@ -662,7 +687,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   const size_t long_header = ffa::long_header_bytes();
   auto long_smem = [&](int k, bool row) {
     return static_cast<unsigned>(
-        long_header + (row ? static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * 4
+        long_header + (row ? static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * esize
                            : ffa::gather_ring_bytes(k)));
   };
   const int rv_long = row_vocab > 0 ? row_vocab : 0;
@@ -676,8 +701,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     const int c8 = static_cast<int>((S + 8 * ffa::kCtaThreads - 1) / (8 * ffa::kCtaThreads));
     const int c16 = static_cast<int>((S + 16 * ffa::kCtaThreads - 1) / (16 * ffa::kCtaThreads));
     int k = 8, c = c8;
-    const int cap8 = ffa::long_capacity(8, c8, row, rv_long, long_smem(8, row));
-    if (cap8 < n && ffa::long_capacity(16, c16, row, rv_long, long_smem(16, row)) > cap8) {
+    const int cap8 = ffa::long_capacity(8, c8, row, rv_long, fmt, long_smem(8, row));
+    if (cap8 < n && ffa::long_capacity(16, c16, row, rv_long, fmt, long_smem(16, row)) > cap8) {
       k = 16;
       c = c16;
     }
@@ -727,9 +752,19 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                            outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
   fp.row_slot_bytes = row_slot_bytes;
   fp.run_pieces = run_pieces;
+  fp.lse = fmt != FFA_INPUT_LOG_PROBS ? reinterpret_cast<const float*>(dev + L.lse) : nullptr;
   const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + bundles_off);
   const int rv = row_vocab > 0 ? row_vocab : 0;
 
+  // Logits: every row's log-sum-exp, which each kernel below subtracts from
+  // the logits it reads.
+  if (fmt != FFA_INPUT_LOG_PROBS) {
+    int max_vocab = 1;
+    for (int64_t i = 0; i < count; ++i) max_vocab = std::max(max_vocab, records[i].vocab);
+    err = ffa::launch_lse(fp.recs, static_cast<int>(count), L.total_frames, max_vocab, fmt,
+                          reinterpret_cast<float*>(dev + L.lse), s);
+    if (err != cudaSuccess) return cuda_fail(err, "log-sum-exp launch");
+  }
   if (g_profile_before != nullptr) {
     err = cudaEventRecord(g_profile_before, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
@@ -750,6 +785,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     lp.maps = fp.maps;
     lp.anchors = fp.anchors;
     lp.out = fp.out;
+    lp.lse = fp.lse;
     const auto* dlongs = reinterpret_cast<const int32_t*>(dev + L.longs);
     for (size_t k = 0; k < long_keys.size();) {
       const uint64_t group = long_keys[k] >> 32;
@@ -759,7 +795,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       const int kst = ((group >> 8) & 1) ? 16 : 8;
       const int cluster = static_cast<int>(group & 0xff);
       lp.records = dlongs + k;
-      err = ffa::launch_long(lp, static_cast<int>(m), cluster, kst, row, rv, long_smem(kst, row), s);
+      err = ffa::launch_long(lp, static_cast<int>(m), cluster, kst, row, rv, fmt, long_smem(kst, row), s);
       if (err == cudaErrorInvalidClusterSize)
         return fail(FFA_ERR_UNSUPPORTED, "this GPU cannot co-schedule a cluster of " + std::to_string(cluster) +
                                              " CTAs, which records of up to " +
@@ -771,10 +807,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // First pass: every piece of every record (a one-piece record is the
   // conventional DP).
   fp.bundles = dbundles;
-  err = ffa::launch_forward(fp, static_cast<int>(nb_row), true, rv, row_smem, s);
+  err = ffa::launch_forward(fp, static_cast<int>(nb_row), true, rv, fmt, row_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   fp.bundles = dbundles + nb_row;
-  err = ffa::launch_forward(fp, static_cast<int>(nb - nb_row), false, 0, gather_smem, s);
+  err = ffa::launch_forward(fp, static_cast<int>(nb - nb_row), false, 0, fmt, gather_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
   if (g_profile_after != nullptr) {
     err = cudaEventRecord(g_profile_after, s);
@@ -804,12 +840,13 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       smem = static_cast<unsigned>(header + slots * row_slot_bytes);
     }
     err = ffa::launch_finish(fp, dchunked + first, static_cast<int>(n), fp.plan_first ? fp.finish_count + grp : nullptr,
-                             spread, threads, row, row ? rv : 0, smem, s);
+                             spread, threads, row, row ? rv : 0, fmt, smem, s);
     if (err != cudaSuccess) return cuda_fail(err, "finish launch");
   }
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
   err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
-                         static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, s);
+                         static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, fp.lse,
+                         fmt, s);
   if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
   if ((rc = mark(FFA_PROFILE_FILL))) return rc;
   return FFA_OK;
@@ -844,7 +881,7 @@ int ffa_emission_validity(const ffa_record* records, int64_t count, uint8_t* val
   auto* items = reinterpret_cast<ffa::ScanItem*>(host + L.items);
   int64_t n = 0;
   for (int64_t i = 0; i < count; ++i) {
-    recs[i] = ffa::ScanRecord{records[i].emissions, records[i].frames * records[i].vocab};
+    recs[i] = ffa::ScanRecord{static_cast<const float*>(records[i].emissions), records[i].frames * records[i].vocab};
     const int64_t chunks = scan_chunks(records[i]);
     for (int64_t c = 0; c < chunks; ++c)
       items[n++] = ffa::ScanItem{static_cast<int32_t>(i), static_cast<int32_t>(c)};
@@ -889,7 +926,7 @@ int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
   auto* recs = static_cast<ffa::RecordDev*>(staging);
   for (int64_t i = 0; i < count; ++i) {
     ffa::RecordDev d{};
-    d.emissions = records[i].emissions;
+    d.emissions = static_cast<const float*>(records[i].emissions);
     d.targets = records[i].targets;
     d.T = static_cast<int32_t>(records[i].frames);
     d.V = records[i].vocab;
@@ -905,6 +942,59 @@ int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
   return FFA_OK;
 }
 
+int ffa_row_logsumexp_query(const ffa_record* records, int64_t count, ffa_sizes* sizes) {
+  if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be NULL");
+  if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
+  int format = 0;
+  int rc = common_format(records, count, &format);
+  if (rc) return rc;
+  if (format == FFA_INPUT_LOG_PROBS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "the row log-sum-exp takes logits (input format 1 or 2)");
+  sizes->total_frames = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    if ((rc = check_record(records[i], i, false))) return rc;
+    sizes->total_frames += records[i].frames;
+  }
+  sizes->staging_bytes = align_up(sizeof(ffa::RecordDev) * count, 256);
+  sizes->workspace_bytes = sizes->staging_bytes;
+  return FFA_OK;
+}
+
+int ffa_row_logsumexp(const ffa_record* records, int64_t count, float* z,
+                      void* staging, size_t staging_bytes,
+                      void* workspace, size_t workspace_bytes, ffa_stream_t stream) {
+  if (z == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "z must not be NULL");
+  ffa_sizes sizes{};
+  int rc = ffa_row_logsumexp_query(records, count, &sizes);
+  if (rc) return rc;
+  if (staging == nullptr || staging_bytes < sizes.staging_bytes)
+    return fail(FFA_ERR_BUFFER_TOO_SMALL, "staging buffer smaller than the query reports");
+  if (workspace == nullptr || workspace_bytes < sizes.workspace_bytes ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(FFA_ERR_BUFFER_TOO_SMALL, "workspace missing, too small or not 256-byte aligned");
+  // The kernel reads a record's emissions, out_off, T and V.
+  auto* recs = static_cast<ffa::RecordDev*>(staging);
+  int64_t off = 0;
+  int max_vocab = 1;
+  for (int64_t i = 0; i < count; ++i) {
+    max_vocab = std::max(max_vocab, records[i].vocab);
+    ffa::RecordDev d{};
+    d.emissions = static_cast<const float*>(records[i].emissions);
+    d.out_off = off;
+    d.T = static_cast<int32_t>(records[i].frames);
+    d.V = records[i].vocab;
+    recs[i] = d;
+    off += records[i].frames;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t err = upload_descriptors(workspace, staging, sizes.staging_bytes, s);
+  if (err != cudaSuccess) return cuda_fail(err, "descriptor upload");
+  err = ffa::launch_lse(static_cast<const ffa::RecordDev*>(workspace), static_cast<int>(count), off, max_vocab,
+                        records[0].format, z, s);
+  if (err != cudaSuccess) return cuda_fail(err, "log-sum-exp launch");
+  return FFA_OK;
+}
 
 int ffa_token_spans_query(const int64_t* frames, const int32_t* tokens, int64_t count, ffa_sizes* sizes) {
   if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be null");

@@ -57,7 +57,7 @@ constexpr int kFillWarps = 8;
 
 // Device-side descriptor of one record (80 bytes).
 struct RecordDev {
-  const float* emissions;   // [T, V] fp32, caller memory
+  const float* emissions;   // [T, V], caller memory: fp32 (formats 0, 1) or bf16 bits (format 2)
   const int64_t* targets;   // [U] int64, caller memory (may be null if U == 0)
   int64_t out_off;          // first frame of this record in labels/scores
   int64_t bp_off;           // first uint32 word of the record's backpointer rows
@@ -208,12 +208,16 @@ struct ForwardParams {
   int32_t* finish_list;
   int32_t* finish_count;     // [kFinishGroups]
   int32_t finish_base[kFinishGroups];
+  // Logits input (formats 1, 2): row log-sum-exps, z of record r's frame t
+  // at lse[recs[r].out_off + t]; null for log-probabilities.
+  const float* lse;
 };
 
 // row_vocab: the vocabulary shared by every row-staged record of the
-// launch, or 0 when they differ.
+// launch, or 0 when they differ.  fmt: the call's input format
+// (ffa_input_format; the same for every record).
 cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
-                           int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+                           int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream);
 // Everything after the first pass of the optimized route -- seam plans,
 // repair rounds, conventional fallback -- in one launch: round 0's repairs on
 // ctas_per_record CTAs per listed record, the rest on the last of them.
@@ -223,12 +227,20 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 // first pass; CTAs past it exit at once (`count` is then the list's room).
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
                           const int32_t* device_count, int ctas_per_record, int threads, bool row_mode,
-                          int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+                          int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream);
 // Traceback fill of every segment; for records of the optimized route the
 // last fill CTA of the record also folds the objective of a joined path.
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        const int32_t* route, int32_t* fill_done, cudaStream_t stream);
+                        const int32_t* route, int32_t* fill_done, const float* lse, int fmt,
+                        cudaStream_t stream);
+// Row log-sum-exps of a logits batch (fmt 1 or 2): z[i] for each of the
+// `rows` frames in packed record order (records' out_off, T, V, emissions);
+// max_vocab: the largest V among the records.
+constexpr int kLseThreads = 256;
+constexpr int kLseRowsPerWarp = 8;
+cudaError_t launch_lse(const RecordDev* recs, int count, int64_t rows, int max_vocab, int fmt, float* z,
+                       cudaStream_t stream);
 cudaError_t launch_validity(const ScanRecord* recs, int64_t count, const ScanItem* items,
                             int64_t num_items, uint8_t* valid, cudaStream_t stream);
 
@@ -243,14 +255,15 @@ struct LongParams {
   uint16_t* maps;
   int32_t* anchors;
   OutputsDev out;
+  const float* lse;          // as ForwardParams::lse
 };
 // Conventional DP of long records (ffa_long.cu), K states per thread (8 or
 // 16).  Returns cudaErrorInvalidClusterSize when the device cannot run one
 // cluster of that many CTAs.
 cudaError_t launch_long(const LongParams& params, int count, int cluster, int k, bool row_mode,
-                        int row_vocab, unsigned smem_bytes, cudaStream_t stream);
+                        int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream);
 // How many such clusters the current device runs at once (0: none fit).
-int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned smem_bytes);
+int long_capacity(int k, int cluster, bool row_mode, int row_vocab, int fmt, unsigned smem_bytes);
 // Dynamic shared memory a long-record CTA needs besides its emission ring.
 size_t long_header_bytes();
 

@@ -84,11 +84,15 @@ struct PieceRun {
 // anchors come from warp traces over the backpointers after the DP (pieces,
 // one or two segments each, and repaired regions).  Thread tl owns states
 // K*tl .. K*tl+K-1 (odd offsets are tokens K/2*tl + k/2).
+// kFmt: the input format (Input<kFmt>); logits rows are staged and gathered
+// as stored and normalised as they are read.
 // Returns the number of emission chunks the run staged (row staging).
-template <int K, bool kRow, int kV, bool kMaps>
+template <int K, bool kRow, int kV, bool kMaps, int kFmt>
 __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, const PieceRun& run,
                                         ForwardShared& sh, unsigned char* smem_raw,
                                         const ForwardParams& P) {
+  using In = Input<kFmt>;
+  using Elem = typename In::Elem;
   constexpr int KT = K / 2;
   constexpr int kGroupsPerPiece = kPieceFrames / kGroup;
   const int tl = x.tl, lane = x.lane, warp = x.warp, NT = x.NT, slot = x.slot;
@@ -115,13 +119,20 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   }
 
   // Emission rows of this run, frame t0 first.
-  const float* e = rec.emissions + static_cast<int64_t>(t0) * V;
+  const Elem* e = reinterpret_cast<const Elem*>(rec.emissions) + static_cast<int64_t>(t0) * V;
   const int ngroups = (nfr + kGroup - 1) / kGroup;
-  float* ring = reinterpret_cast<float*>(smem_raw + kForwardHeader) +
-                static_cast<size_t>(slot) * (P.row_slot_bytes / 4);
+  Elem* ring = reinterpret_cast<Elem*>(smem_raw + kForwardHeader) +
+               static_cast<size_t>(slot) * (P.row_slot_bytes / sizeof(Elem));
   float* gring = reinterpret_cast<float*>(smem_raw + kForwardHeader) + x.tid;
   unsigned long long* full = sh.full[slot];
   bool fault = false;
+  HalfWords hw{};
+  if constexpr (In::kHalf && !kRow) hw.set(rec.emissions);
+  // z of the run's frames, a 32-frame block at a time (blocks follow the
+  // emission chunks).
+  static_assert(kChunkGroups * kGroup == 32, "log-sum-exp blocks");
+  LseStream lse{};
+  if constexpr (In::kLogits) lse.start(P.lse + rec.out_off, T, t0, lane);
 
   const int nchunks = (nfr + kChunkFrames - 1) / kChunkFrames;
   const int cb = run.chunk_base;
@@ -130,7 +141,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   auto issue_chunk = [&](int c) {  // kRow: by the slot's thread 0
     const int first = c * kChunkFrames;
     const int rows = min(kChunkFrames, nfr - first);
-    const unsigned bytes = static_cast<unsigned>(rows) * V * 4u;
+    const unsigned bytes = static_cast<unsigned>(rows) * V * static_cast<unsigned>(sizeof(Elem));
     unsigned long long* bar = &full[(cb + c) % kRowRing];
     mbar_expect_tx(bar, bytes);
     tma_bulk_load(ring + ((cb + c) % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(first) * V,
@@ -138,11 +149,18 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   };
   auto gather = [&](int f) {  // !kRow: KT + 1 private 4-byte copies of run frame f
     if (f < nfr) {
-      const float* row = e + static_cast<int64_t>(f) * V;
       float* dst = gring + (f % kGroup) * (KT + 1) * kCtaThreads;
-      cp_async4(dst, row + blank);
+      if constexpr (In::kHalf) {
+        const int64_t i = static_cast<int64_t>(t0 + f) * V;
+        cp_async4(dst, hw.word(i + blank));
 #pragma unroll
-      for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
+        for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, hw.word(i + col[q]));
+      } else {
+        const float* row = e + static_cast<int64_t>(f) * V;
+        cp_async4(dst, row + blank);
+#pragma unroll
+        for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
+      }
     }
     cp_async_commit();
   };
@@ -202,19 +220,35 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   const int64_t hi64 = static_cast<int64_t>(w_hi) - S + 2 * static_cast<int64_t>(T);
   const bool never = hi64 < 0;
   const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
-  auto load = [&](int f, int j, const float* rows, float& eb, float (&et)[KT]) {
+  // Frame t0 + f's emissions of this thread's states (row j of the staged
+  // group `rows`); logits become x - z.  Called by whole warps.
+  auto load = [&](int f, int j, const Elem* rows, float& eb, float (&et)[KT]) {
     if constexpr (kRow) {
-      const float* row = rows + j * V;
-      eb = row[blank];
+      const Elem* row = rows + j * V;
+      eb = elem_to_float(row[blank]);
 #pragma unroll
-      for (int q = 0; q < KT; ++q) et[q] = row[col[q]];
+      for (int q = 0; q < KT; ++q) et[q] = elem_to_float(row[col[q]]);
     } else {
       gather(f + kGroup - 1);
       cp_async_wait<kGroup - 1>();
       const float* cur = gring + (f & (kGroup - 1)) * (KT + 1) * kCtaThreads;
-      eb = cur[0];
+      if constexpr (In::kHalf) {
+        const bool odd = hw.row_odd(t0 + f, V);
+        eb = bf16_of_word(__float_as_uint(cur[0]), odd ^ (blank & 1));
 #pragma unroll
-      for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+        for (int q = 0; q < KT; ++q)
+          et[q] = bf16_of_word(__float_as_uint(cur[(q + 1) * kCtaThreads]), odd ^ (col[q] & 1));
+      } else {
+        eb = cur[0];
+#pragma unroll
+        for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+      }
+    }
+    if constexpr (In::kLogits) {
+      const float z = lse.at(f);
+      eb = __fsub_rn(eb, z);
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = __fsub_rn(et[q], z);
     }
   };
   auto store_map = [&](int t) {
@@ -228,7 +262,7 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
   auto store_codes_at = [&](int t, unsigned bits) {
     if (stores_codes) store_codes<K>(bp_rows + static_cast<int64_t>(t) * row_words * 4, tl, bits);
   };
-  auto frame = [&](int t, int j, const float* rows) {
+  auto frame = [&](int t, int j, const Elem* rows) {
     float eb, et[KT];
     load(t - t0, j, rows, eb, et);
     // Left neighbour's last state at t-1 (s-1 for k=0, s-2 for k=1): from
@@ -299,7 +333,9 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
 
   int piece = 0;  // current piece of the run
   for (int g = 0; g < ngroups; ++g) {
-    const float* rows = nullptr;
+    const Elem* rows = nullptr;
+    if constexpr (In::kLogits)
+      if (g > 0 && g % kChunkGroups == 0) lse.advance(t0 + g * kGroup, lane);
     if constexpr (kRow) {
       const int c = cb + g / kChunkGroups;
       if (g % kChunkGroups == 0 && !fault && !mbar_wait(&full[c % kRowRing], (c / kRowRing) & 1))
@@ -661,7 +697,7 @@ __device__ void plan_round0(const SlotCtx& x, const RecordDev& rec, ForwardShare
 // emission rows arrive kChunkFrames frames at a time by one TMA bulk copy
 // into a kRowRing-deep ring per slot; otherwise each thread gathers its
 // columns with cp.async into a private ring (large vocabularies).
-template <bool kRow, int kV>
+template <bool kRow, int kV, int kFmt>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -761,13 +797,13 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
   // Pieces of the optimized route (K = 8 or 16) find their anchors by
   // tracing; whole records walk segment maps.
   if (chunked && rec.kst == 16)
-    piece_dp<16, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+    piece_dp<16, kRow, kV, false, kFmt>(x, rec, run, sh, smem_raw, P);
   else if (chunked)
-    piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+    piece_dp<8, kRow, kV, false, kFmt>(x, rec, run, sh, smem_raw, P);
   else if (rec.kst == 4)
-    piece_dp<4, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+    piece_dp<4, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
   else
-    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+    piece_dp<8, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
   if (chunked && P.plan_first) plan_round0(x, rec, sh, P);
 }
 
@@ -786,7 +822,7 @@ static_assert(sizeof(JobList) + 64 <= 2048, "finisher static shared memory");
 // the record, and the record's route and diagnostics.  A record that round 0
 // already routes is finished by its CTA 0.  Data other CTAs of this launch
 // wrote (piece states, frontiers, backpointer rows) is read through L2.
-template <bool kRow, int kV>
+template <bool kRow, int kV, int kFmt>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ records,
                  const int32_t* __restrict__ device_count, int ctas_per_record, unsigned dynamic_smem) {
@@ -863,7 +899,7 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
         run.new_region = false;
         run.chunk_base = chunk_base;
         if (x.tl == 0) sh.slot_fault[x.slot] = 0;
-        chunk_base += piece_dp<8, kRow, kV, false>(x, rec, run, sh, smem_raw, P);
+        chunk_base += piece_dp<8, kRow, kV, false, kFmt>(x, rec, run, sh, smem_raw, P);
       }
     }
     if (parts > 1) {
@@ -904,20 +940,23 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   if (route_s == kRouteFallback && x.slot == 0) {
     PieceRun run{0, 0, rec.T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, chunk_base};
     if (x.tl == 0) sh.slot_fault[0] = 0;
-    piece_dp<8, kRow, kV, true>(x, rec, run, sh, smem_raw, P);
+    piece_dp<8, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
   }
 }
 
 // One warp per traceback segment: the warp walks the backpointers from the
 // segment's anchor (path[t-1] = path[t] - bp[t, path[t]], alignment.cu:656-659),
 // then maps states to labels and gathers the selected scores
-// (alignment.cu:662-666).  Failed records get -1 / -inf (alignment.cu:650-652).
+// (alignment.cu:662-666); a logits input's score is the same x - z the DPs
+// used (fmt, lse: as in ForwardParams).  Failed records get -1 / -inf
+// (alignment.cu:650-652).
 // For a record of the optimized route, the record's last fill CTA to finish
 // (a counter per record) then folds the objective of a joined path.
 __global__ void __launch_bounds__(32 * kFillWarps)
 ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ items,
                const uint32_t* __restrict__ bp_arena, const int32_t* __restrict__ anchors,
-               OutputsDev out, const int32_t* __restrict__ route, int32_t* __restrict__ fill_done) {
+               OutputsDev out, const int32_t* __restrict__ route, int32_t* __restrict__ fill_done,
+               const float* __restrict__ lse, int fmt) {
   __shared__ int32_t path[kFillWarps][1 << kMaxSegLog2];
   __shared__ int fold_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -941,12 +980,15 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
       warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
                       [&](int t, int s) { if (lane == 0) p[t - a] = s; });
       __syncwarp();
-      const float* e = rec.emissions;
       for (int t = a + lane; t < b; t += 32) {
         const int s = p[t - a];
         const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
+        const int64_t i = static_cast<int64_t>(t) * rec.V + label;
+        float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
+                               : rec.emissions[i];
+        if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
         labels[t] = label;
-        scores[t] = e[static_cast<int64_t>(t) * rec.V + label];
+        scores[t] = score;
       }
     }
   }
@@ -1099,6 +1141,110 @@ ffa_token_spans_kernel(const SpanRecord* __restrict__ recs, int64_t count) {
   for (int k = lane; k < 2 * rec.U; k += 32) spans[k] = -1;
 }
 
+// Row log-sum-exp of logits (input formats 1 and 2), the z that turns them
+// into the log_softmax emissions x - z:
+//   z[t] = m + log(sum_v exp(x[t, v] - m)),  m = max_v x[t, v],
+// in fp32 with CUDA's expf and logf.  Lane l of a row's warp takes columns
+// l, l + 32, l + 64, ... and sums their terms in that order; the warp then
+// adds the lanes' sums in a butterfly (so every lane holds the same sum).
+// That order depends on V alone, so a row's z is the same wherever the row
+// lies and whichever variant below computes it.  A row holding NaN or +inf,
+// or only -inf, gets NaN (its emissions are NaN, as torch.log_softmax's
+// are).  Rows are in packed frame order; record r's rows are out_off ..
+// out_off + T - 1, and each warp finds the record of its first row by a
+// search over the descriptors.
+//
+// Each warp takes kLseRowsPerWarp consecutive rows.  kN > 0 (every V of
+// the launch at most 32 kN, kN <= 2): the warp loads all of its rows' values
+// before it reduces any, and the rows' reductions interleave.  kN == 0: one
+// row at a time, each pass over the row's columns with 16 loads per lane in
+// flight (the second pass finds the row in L1).
+template <int kFmt, int kN>
+__global__ void __launch_bounds__(kLseThreads)
+ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* __restrict__ z) {
+  using Elem = typename Input<kFmt>::Elem;
+  constexpr int kRows = kLseRowsPerWarp;
+  const int lane = threadIdx.x & 31;
+  const int64_t first =
+      (static_cast<int64_t>(blockIdx.x) * (kLseThreads / 32) + (threadIdx.x >> 5)) * kRows;
+  if (first >= rows) return;
+  // The last record with out_off <= first, by a 32-way search: lane j tests
+  // the first record of the j-th of 32 blocks of the range (at most three
+  // rounds for 65535 records).  Record 0 starts at row 0.
+  int lo = 0, n = count;
+  while (n > 1) {
+    const int step = (n + 31) / 32;
+    const int cand = lo + lane * step;
+    const bool ok = cand < lo + n && recs[cand].out_off <= first;
+    const int j = 31 - __clz(static_cast<int>(__ballot_sync(0xffffffffu, ok)));
+    lo += j * step;
+    n = min(step, n - j * step);
+  }
+  int r = lo;
+  int64_t off = recs[r].out_off;
+  int64_t T = recs[r].T;
+  int V = recs[r].V;
+  // The row's data (records follow one another in row order).
+  auto locate = [&](int64_t row) {
+    while (row >= off + T && r + 1 < count) {
+      ++r;
+      off = recs[r].out_off;
+      T = recs[r].T;
+      V = recs[r].V;
+    }
+    return reinterpret_cast<const Elem*>(recs[r].emissions) + (row - off) * V;
+  };
+  if constexpr (kN == 0) {
+    const int64_t end = min(rows, first + kRows);
+    for (int64_t row = first; row < end; ++row) {
+      const Elem* x = locate(row);
+      float m = -INFINITY;
+#pragma unroll 16
+      for (int v = lane; v < V; v += 32) m = fmaxf(m, elem_to_float(x[v]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float s = 0.0f;
+#pragma unroll 16
+      for (int v = lane; v < V; v += 32) s = __fadd_rn(s, expf(__fsub_rn(elem_to_float(x[v]), m)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+      if (lane == 0) z[row] = __fadd_rn(m, logf(s));
+    }
+  } else {
+    static_assert(kN <= 2, "register-resident rows");
+    float val[kRows][kN];
+    int vocab[kRows];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      const int64_t row = first + q;
+      const Elem* x = row < rows ? locate(row) : nullptr;
+      vocab[q] = row < rows ? V : 0;
+#pragma unroll
+      for (int k = 0; k < kN; ++k) {
+        const int v = lane + 32 * k;
+        val[q][k] = v < vocab[q] ? elem_to_float(x[v]) : -INFINITY;
+      }
+    }
+    float mine = 0.0f;  // lane q < kRows keeps row first + q's z
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kN; ++k) m = fmaxf(m, val[q][k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float s = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kN; ++k)
+        if (lane + 32 * k < vocab[q]) s = __fadd_rn(s, expf(__fsub_rn(val[q][k], m)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+      if (lane == q) mine = __fadd_rn(m, logf(s));
+    }
+    if (lane < kRows && first + lane < rows) z[first + lane] = mine;
+  }
+}
+
 // One warp per record: the target checks of the forward kernel without the DP.
 __global__ void __launch_bounds__(256)
 ffa_check_targets_kernel(const RecordDev* __restrict__ recs, int64_t count,
@@ -1159,25 +1305,68 @@ cudaError_t launch_spans(const SpanRecord* recs, int64_t count, cudaStream_t str
 }
 void count_launch() { ++g_launches; }
 
-cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
-                           int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
-  if (num_bundles <= 0) return cudaSuccess;
-  auto kernel = !row_mode ? ffa_viterbi_forward<false, 0>
-                         : (row_vocab == 32 ? ffa_viterbi_forward<true, 32> : ffa_viterbi_forward<true, 0>);
-  // Opting in to >48 KiB of dynamic shared memory is per device and kernel:
-  // done once, to the whole budget, then every launch fits under it.
-  static std::atomic<uint64_t> opted[3];  // bit d: device d done
-  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
+namespace {
+// Kernel variants per (staging, vocabulary specialisation, input format):
+// log-probabilities have a V = 32 row-staged variant besides the generic
+// ones; logits inputs use the generic row-staged and gathered kernels.
+constexpr int kVariants = 7;
+int variant_of(bool row_mode, int row_vocab, int fmt) {
+  if (fmt == 0) return !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
+  return 3 + 2 * (fmt - 1) + (row_mode ? 1 : 0);
+}
+using ForwardKernel = void (*)(ForwardParams);
+using FinishKernel = void (*)(ForwardParams, const int32_t*, const int32_t*, int, unsigned);
+const ForwardKernel kForwardKernels[kVariants] = {
+    ffa_viterbi_forward<false, 0, 0>, ffa_viterbi_forward<true, 0, 0>, ffa_viterbi_forward<true, 32, 0>,
+    ffa_viterbi_forward<false, 0, 1>, ffa_viterbi_forward<true, 0, 1>,
+    ffa_viterbi_forward<false, 0, 2>, ffa_viterbi_forward<true, 0, 2>};
+const FinishKernel kFinishKernels[kVariants] = {
+    ffa_finish_route<false, 0, 0>, ffa_finish_route<true, 0, 0>, ffa_finish_route<true, 32, 0>,
+    ffa_finish_route<false, 0, 1>, ffa_finish_route<true, 0, 1>,
+    ffa_finish_route<false, 0, 2>, ffa_finish_route<true, 0, 2>};
+
+// Opting in to >48 KiB of dynamic shared memory is per device and kernel:
+// done once, to `bytes`, then every launch fits under it.
+template <typename Kernel>
+cudaError_t opt_in(Kernel kernel, std::atomic<uint64_t>& opted, size_t bytes) {
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
   const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
-  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kSmemBudget));
-    if (err != cudaSuccess) return err;
-    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
-  }
+  if (bit != 0 && (opted.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (err != cudaSuccess) return err;
+  if (bit) opted.fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
+
+template <int kFmt, int kN>
+cudaError_t lse_launch(const RecordDev* recs, int count, int64_t rows, float* z, cudaStream_t stream) {
+  const int64_t per_cta = static_cast<int64_t>(kLseThreads / 32) * kLseRowsPerWarp;
+  const int64_t blocks = (rows + per_cta - 1) / per_cta;
+  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+  ++g_launches;
+  ffa_row_lse<kFmt, kN><<<static_cast<unsigned>(blocks), kLseThreads, 0, stream>>>(recs, count, rows, z);
+  return cudaGetLastError();
+}
+template <int kFmt>
+cudaError_t lse_dispatch(const RecordDev* recs, int count, int64_t rows, int max_vocab, float* z,
+                         cudaStream_t stream) {
+  if (max_vocab <= 32) return lse_launch<kFmt, 1>(recs, count, rows, z, stream);
+  if (max_vocab <= 64) return lse_launch<kFmt, 2>(recs, count, rows, z, stream);
+  return lse_launch<kFmt, 0>(recs, count, rows, z, stream);
+}
+}  // namespace
+
+cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool row_mode,
+                           int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream) {
+  if (num_bundles <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted[kVariants];
+  const int variant = variant_of(row_mode, row_vocab, fmt);
+  const ForwardKernel kernel = kForwardKernels[variant];
+  cudaError_t err = opt_in(kernel, opted[variant], kSmemBudget);
+  if (err != cudaSuccess) return err;
   if (smem_bytes > kSmemBudget) return cudaErrorInvalidValue;
   ++g_launches;
   kernel<<<num_bundles, kCtaThreads, smem_bytes, stream>>>(params);
@@ -1186,38 +1375,39 @@ cudaError_t launch_forward(const ForwardParams& params, int num_bundles, bool ro
 
 cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, int count,
                           const int32_t* device_count, int ctas_per_record, int threads, bool row_mode,
-                          int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+                          int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
-  auto kernel = !row_mode ? ffa_finish_route<false, 0>
-                         : (row_vocab == 32 ? ffa_finish_route<true, 32> : ffa_finish_route<true, 0>);
-  static std::atomic<uint64_t> opted[3];  // bit d: device d opted in
-  const int variant = !row_mode ? 0 : (row_vocab == 32 ? 2 : 1);
-  int device = 0;
-  cudaError_t err = cudaGetDevice(&device);
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted[kVariants];
+  const int variant = variant_of(row_mode, row_vocab, fmt);
+  const FinishKernel kernel = kFinishKernels[variant];
+  cudaError_t err = opt_in(kernel, opted[variant], kFinishDynamicSmem);
   if (err != cudaSuccess) return err;
-  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
-  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kFinishDynamicSmem));
-    if (err != cudaSuccess) return err;
-    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
-  }
   if (smem_bytes > kFinishDynamicSmem) return cudaErrorInvalidValue;
-  ++g_launches;
   if (threads != kCtaThreads && threads != kCtaThreads / 2 && threads != kCtaThreads / 4)
     return cudaErrorInvalidValue;
+  ++g_launches;
   kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, device_count, ctas_per_record,
                                                                   smem_bytes);
   return cudaGetLastError();
 }
 
+cudaError_t launch_lse(const RecordDev* recs, int count, int64_t rows, int max_vocab, int fmt, float* z,
+                       cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  if (fmt == 1) return lse_dispatch<1>(recs, count, rows, max_vocab, z, stream);
+  if (fmt == 2) return lse_dispatch<2>(recs, count, rows, max_vocab, z, stream);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        const int32_t* route, int32_t* fill_done, cudaStream_t stream) {
+                        const int32_t* route, int32_t* fill_done, const float* lse, int fmt,
+                        cudaStream_t stream) {
   if (num_items <= 0) return cudaSuccess;
   ++g_launches;
   ffa_trace_fill<<<num_items, 32 * kFillWarps, 0, stream>>>(recs, items, bp, anchors, out, route,
-                                                             fill_done);
+                                                             fill_done, lse, fmt);
   return cudaGetLastError();
 }
 

@@ -65,9 +65,11 @@ __device__ __forceinline__ unsigned long long pack_link(int t, float alpha, int 
          (static_cast<unsigned>(t) & kFrameMask);
 }
 
-template <int K, bool kRow, int kV>
+template <int K, bool kRow, int kV, int kFmt>
 __global__ void __launch_bounds__(kCtaThreads, 1)
 ffa_long_forward(const __grid_constant__ LongParams P) {
+  using In = Input<kFmt>;
+  using Elem = typename In::Elem;
   constexpr int KT = K / 2;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   LongShared& sh = *reinterpret_cast<LongShared*>(smem_raw);
@@ -134,14 +136,20 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
   }
 
   // Emission rows: TMA bulk copies of kChunkFrames rows into a kRowRing ring
-  // (row staging), or per-thread cp.async gathers of the thread's columns.
-  const float* e = rec.emissions;
-  float* ring = reinterpret_cast<float*>(smem_raw + kLongHeader);
-  float* gring = ring + tid;
+  // (row staging), or per-thread cp.async gathers of the thread's columns;
+  // logits are normalised as they are read (x - z, Input<kFmt>).
+  const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
+  Elem* ring = reinterpret_cast<Elem*>(smem_raw + kLongHeader);
+  float* gring = reinterpret_cast<float*>(smem_raw + kLongHeader) + tid;
+  HalfWords hw{};
+  if constexpr (In::kHalf && !kRow) hw.set(rec.emissions);
+  static_assert(kChunkGroups * kGroup == 32, "log-sum-exp blocks");
+  LseStream lse{};
+  if constexpr (In::kLogits) lse.start(P.lse + rec.out_off, T, 0, lane);
   const int nchunks = (T + kChunkFrames - 1) / kChunkFrames;
   auto issue_chunk = [&](int c) {  // kRow: by thread 0
     const int rows = min(kChunkFrames, T - c * kChunkFrames);
-    const unsigned bytes = static_cast<unsigned>(rows) * V * 4u;
+    const unsigned bytes = static_cast<unsigned>(rows) * V * static_cast<unsigned>(sizeof(Elem));
     unsigned long long* bar = &sh.full[c % kRowRing];
     mbar_expect_tx(bar, bytes);
     tma_bulk_load(ring + (c % kRowRing) * kChunkFrames * V, e + static_cast<int64_t>(c) * kChunkFrames * V,
@@ -149,11 +157,18 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
   };
   auto gather = [&](int f) {  // !kRow: KT + 1 private 4-byte copies of frame f
     if (f < T) {
-      const float* row = e + static_cast<int64_t>(f) * V;
       float* dst = gring + (f % kGroup) * (KT + 1) * kCtaThreads;
-      cp_async4(dst, row + blank);
+      if constexpr (In::kHalf) {
+        const int64_t i = static_cast<int64_t>(f) * V;
+        cp_async4(dst, hw.word(i + blank));
 #pragma unroll
-      for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
+        for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, hw.word(i + col[q]));
+      } else {
+        const float* row = e + static_cast<int64_t>(f) * V;
+        cp_async4(dst, row + blank);
+#pragma unroll
+        for (int q = 0; q < KT; ++q) cp_async4(dst + (q + 1) * kCtaThreads, row + col[q]);
+      }
     }
     cp_async_commit();
   };
@@ -245,19 +260,35 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
   const bool never = hi64 < 0 || w_lo >= S;
   const unsigned band_hi = never ? 0u : (hi64 > 0xffffffffLL ? 0xffffffffu : static_cast<unsigned>(hi64));
 
-  auto load = [&](int f, int j, const float* rows, float& eb, float (&et)[KT]) {
+  // Frame f's emissions of this thread's states (row j of the staged group
+  // `rows`); logits become x - z.  Called by whole warps.
+  auto load = [&](int f, int j, const Elem* rows, float& eb, float (&et)[KT]) {
     if constexpr (kRow) {
-      const float* row = rows + j * V;
-      eb = row[blank];
+      const Elem* row = rows + j * V;
+      eb = elem_to_float(row[blank]);
 #pragma unroll
-      for (int q = 0; q < KT; ++q) et[q] = row[col[q]];
+      for (int q = 0; q < KT; ++q) et[q] = elem_to_float(row[col[q]]);
     } else {
       gather(f + kGroup - 1);
       cp_async_wait<kGroup - 1>();
       const float* cur = gring + (f & (kGroup - 1)) * (KT + 1) * kCtaThreads;
-      eb = cur[0];
+      if constexpr (In::kHalf) {
+        const bool odd = hw.row_odd(f, V);
+        eb = bf16_of_word(__float_as_uint(cur[0]), odd ^ (blank & 1));
 #pragma unroll
-      for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+        for (int q = 0; q < KT; ++q)
+          et[q] = bf16_of_word(__float_as_uint(cur[(q + 1) * kCtaThreads]), odd ^ (col[q] & 1));
+      } else {
+        eb = cur[0];
+#pragma unroll
+        for (int q = 0; q < KT; ++q) et[q] = cur[(q + 1) * kCtaThreads];
+      }
+    }
+    if constexpr (In::kLogits) {
+      const float z = lse.at(f);
+      eb = __fsub_rn(eb, z);
+#pragma unroll
+      for (int q = 0; q < KT; ++q) et[q] = __fsub_rn(et[q], z);
     }
   };
   auto store_map = [&](int t) {
@@ -267,7 +298,7 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
     for (int q = 0; q < KT; ++q)
       dst[q] = static_cast<uint32_t>(d[2 * q]) | (static_cast<uint32_t>(d[2 * q + 1]) << 16);
   };
-  auto frame = [&](int t, int j, const float* rows) {
+  auto frame = [&](int t, int j, const Elem* rows) {
     float eb, et[KT];
     load(t, j, rows, eb, et);
     float p1 = __shfl_up_sync(kFull, a[K - 1], 1);
@@ -305,7 +336,9 @@ ffa_long_forward(const __grid_constant__ LongParams P) {
 
   const int ngroups = (T + kGroup - 1) / kGroup;
   for (int gi = 0; gi < ngroups; ++gi) {
-    const float* rows = nullptr;
+    const Elem* rows = nullptr;
+    if constexpr (In::kLogits)
+      if (gi > 0 && gi % kChunkGroups == 0) lse.advance(gi * kGroup, lane);
     if constexpr (kRow) {
       const int c = gi / kChunkGroups;
       if (gi % kChunkGroups == 0 && !tma_fault && !mbar_wait(&sh.full[c % kRowRing], (c / kRowRing) & 1))
@@ -418,13 +451,21 @@ size_t long_header_bytes() { return kLongHeader; }
 
 namespace {
 using LongKernel = void (*)(LongParams);
-// Kernel variant and its index among the six (K, staging) instantiations.
-LongKernel long_kernel(int k, bool row_mode, int row_vocab, int* variant) {
-  const int v = (k == 16 ? 3 : 0) + (!row_mode ? 0 : (row_vocab == 32 ? 2 : 1));
+// Kernel variant and its index among the (K, staging, input format)
+// instantiations: per K, log-probabilities gathered / row-staged / row-staged
+// at V = 32, then fp32 and bf16 logits gathered / row-staged.
+constexpr int kLongVariants = 14;
+LongKernel long_kernel(int k, bool row_mode, int row_vocab, int fmt, int* variant) {
+  const int per_k = fmt == 0 ? (!row_mode ? 0 : (row_vocab == 32 ? 2 : 1)) : 3 + 2 * (fmt - 1) + (row_mode ? 1 : 0);
+  const int v = (k == 16 ? 7 : 0) + per_k;
   *variant = v;
-  static const LongKernel table[6] = {
-      ffa_long_forward<8, false, 0>,  ffa_long_forward<8, true, 0>,  ffa_long_forward<8, true, 32>,
-      ffa_long_forward<16, false, 0>, ffa_long_forward<16, true, 0>, ffa_long_forward<16, true, 32>};
+  static const LongKernel table[kLongVariants] = {
+      ffa_long_forward<8, false, 0, 0>,  ffa_long_forward<8, true, 0, 0>,  ffa_long_forward<8, true, 32, 0>,
+      ffa_long_forward<8, false, 0, 1>,  ffa_long_forward<8, true, 0, 1>,
+      ffa_long_forward<8, false, 0, 2>,  ffa_long_forward<8, true, 0, 2>,
+      ffa_long_forward<16, false, 0, 0>, ffa_long_forward<16, true, 0, 0>, ffa_long_forward<16, true, 32, 0>,
+      ffa_long_forward<16, false, 0, 1>, ffa_long_forward<16, true, 0, 1>,
+      ffa_long_forward<16, false, 0, 2>, ffa_long_forward<16, true, 0, 2>};
   return table[v];
 }
 cudaLaunchConfig_t long_config(int count, int cluster, unsigned smem, cudaStream_t stream,
@@ -445,7 +486,7 @@ cudaLaunchConfig_t long_config(int count, int cluster, unsigned smem, cudaStream
 // Per device and variant, once: the shared-memory budget and clusters beyond
 // the portable 8 CTAs.
 cudaError_t prepare_long(LongKernel kernel, int variant, int device) {
-  static std::atomic<uint64_t> opted[6];
+  static std::atomic<uint64_t> opted[kLongVariants];
   const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
   if (bit != 0 && (opted[variant].load(std::memory_order_acquire) & bit)) return cudaSuccess;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -458,14 +499,16 @@ cudaError_t prepare_long(LongKernel kernel, int variant, int device) {
 }
 }  // namespace
 
-int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned smem_bytes) {
-  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget) return 0;
+int long_capacity(int k, int cluster, bool row_mode, int row_vocab, int fmt, unsigned smem_bytes) {
+  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget ||
+      fmt < 0 || fmt > 2)
+    return 0;
   int variant = 0;
-  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, &variant);
+  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, fmt, &variant);
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return 0;
   // Cached per (device, variant, cluster size): the count + 1 (0 = unknown).
-  static std::atomic<int> known[6][64][kMaxClusterCtas + 1];
+  static std::atomic<int> known[kLongVariants][64][kMaxClusterCtas + 1];
   const int slot = device < 64 ? device : 63;
   const int cached = known[variant][slot][cluster].load(std::memory_order_acquire);
   if (cached > 0 && device < 64) return cached - 1;
@@ -482,13 +525,14 @@ int long_capacity(int k, int cluster, bool row_mode, int row_vocab, unsigned sme
 }
 
 cudaError_t launch_long(const LongParams& params, int count, int cluster, int k, bool row_mode,
-                        int row_vocab, unsigned smem_bytes, cudaStream_t stream) {
+                        int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
-  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget)
+  if ((k != 8 && k != 16) || cluster < 1 || cluster > kMaxClusterCtas || smem_bytes > kSmemBudget ||
+      fmt < 0 || fmt > 2)
     return cudaErrorInvalidValue;
-  if (long_capacity(k, cluster, row_mode, row_vocab, smem_bytes) < 1) return cudaErrorInvalidClusterSize;
+  if (long_capacity(k, cluster, row_mode, row_vocab, fmt, smem_bytes) < 1) return cudaErrorInvalidClusterSize;
   int variant = 0;
-  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, &variant);
+  const LongKernel kernel = long_kernel(k, row_mode, row_vocab, fmt, &variant);
   cudaLaunchAttribute attr;
   cudaLaunchConfig_t cfg = long_config(count, cluster, smem_bytes, stream, &attr);
   count_launch();

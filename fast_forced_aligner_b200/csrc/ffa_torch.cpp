@@ -1,10 +1,10 @@
 // ffa_torch.cpp -- thin PyTorch operator layer over the C ABI (libffa_b200.so).
 //
 // Registers torch.ops.ffa_b200.{align, align_packed, emission_validity,
-// check_targets}.  It mirrors the reference's op layer (alignment.cu:893-1061,
-// TORCH_LIBRARY at alignment.cu:1064-1070): tensor metadata checks, stream
-// lifetime protection (recordStream on borrowed inputs) and output allocation
-// from the caching allocator.  Everything below the ffa_* calls is plain
+// check_targets, token_spans, row_logsumexp}.  It mirrors the reference's op
+// layer (alignment.cu:893-1061, TORCH_LIBRARY at alignment.cu:1064-1070):
+// tensor metadata checks, stream lifetime protection (recordStream on
+// borrowed inputs) and output allocation from the caching allocator.  Everything below the ffa_* calls is plain
 // pointers and sizes.  Per call it makes two caching-allocator requests (one
 // block holds every output tensor, one the workspace) and stages descriptors
 // in a reused pinned host buffer, so the host cost stays a few microseconds.
@@ -216,19 +216,37 @@ void check_mode(int64_t mode) {
   TORCH_CHECK_VALUE(mode == 0 || mode == 1, "mode must be 'optimized' or 'conventional'");
 }
 
+// Input format (ffa_input_format) and the dtype it stores: fp32
+// log-probabilities, fp32 logits, bf16 logits.
+at::ScalarType format_dtype(int64_t fmt) {
+  TORCH_CHECK_VALUE(fmt >= FFA_INPUT_LOG_PROBS && fmt <= FFA_INPUT_LOGITS_BF16, "unknown input format");
+  return fmt == FFA_INPUT_LOGITS_BF16 ? at::kBFloat16 : at::kFloat;
+}
+const char* format_message(int64_t fmt, bool packed) {
+  if (fmt == FFA_INPUT_LOGITS_BF16)
+    return packed ? "inputs must be contiguous CUDA bfloat16 [N,V] and int64 [M] on one device"
+                  : "inputs must be contiguous CUDA bfloat16 [T,V] and int64 [U] on one device";
+  return packed ? "inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device"
+                : "inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device";
+}
+
 // align(Tensor[] emissions, Tensor[] targets, int[] blanks, int mode,
-//       Tensor? emission_validity, bool check_inputs) -> (Tensor[], int[])
+//       Tensor? emission_validity, bool check_inputs, int fmt) -> (Tensor[], int[])
+// fmt: ffa_input_format (1, 2: the emissions are logits, aligned as their
+// log_softmax).
 std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align(
     at::TensorList emissions, at::TensorList targets, at::IntArrayRef blanks, int64_t mode,
-    const std::optional<at::Tensor>& emission_validity, bool check_inputs) {
+    const std::optional<at::Tensor>& emission_validity, bool check_inputs, int64_t fmt) {
   check_mode(mode);
+  const at::ScalarType dtype = format_dtype(fmt);
+  const char* msg = format_message(fmt, false);
   const int64_t count = static_cast<int64_t>(emissions.size());
   TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS &&
                         static_cast<int64_t>(targets.size()) == count &&
                         static_cast<int64_t>(blanks.size()) == count,
                     "provide 1..65535 matching emissions and targets");
   const auto device = emissions[0].device();
-  TORCH_CHECK_VALUE(device.is_cuda(), "inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device");
+  TORCH_CHECK_VALUE(device.is_cuda(), msg);
   c10::cuda::CUDAGuard guard(device);
   const auto stream = c10::cuda::getCurrentCUDAStream();
   StreamRecorder rec{stream};
@@ -238,16 +256,17 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> align(
     const auto& e = emissions[i];
     const auto& t = targets[i];
     TORCH_CHECK_VALUE(e.device() == device && t.device() == device &&
-                          e.scalar_type() == at::kFloat && t.scalar_type() == at::kLong &&
+                          e.scalar_type() == dtype && t.scalar_type() == at::kLong &&
                           e.dim() == 2 && t.dim() == 1 && e.is_contiguous() && t.is_contiguous(),
-                      "inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device");
+                      msg);
     TORCH_CHECK_VALUE(e.size(0) > 0 && e.size(0) <= INT_MAX && e.size(1) > 0 &&
                           e.size(1) <= FFA_MAX_VOCAB && t.numel() <= FFA_MAX_TOKENS && blanks[i] >= 0 &&
                           blanks[i] < e.size(1),
                       "unsupported frame count, vocabulary, target length, or blank ID");
-    recs[i] = ffa_record{e.data_ptr<float>(), t.numel() ? t.data_ptr<int64_t>() : nullptr,
+    recs[i] = ffa_record{e.data_ptr(), t.numel() ? t.data_ptr<int64_t>() : nullptr,
                          e.size(0), static_cast<int32_t>(e.size(1)),
-                         static_cast<int32_t>(t.numel()), static_cast<int32_t>(blanks[i]), 0};
+                         static_cast<int32_t>(t.numel()), static_cast<int32_t>(blanks[i]),
+                         static_cast<int32_t>(fmt)};
     lengths[i] = e.size(0);
     rec(e);
     rec(t);
@@ -266,7 +285,7 @@ const int64_t* host_counts(const at::Tensor& t, int64_t n, const char* what) {
 
 // align_packed(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens,
 //              Tensor blanks, int mode, Tensor? emission_validity,
-//              bool check_inputs) -> Tensor[]
+//              bool check_inputs, int fmt) -> Tensor[]
 // Packed varlen form: record i is rows [sum frames[:i], +frames[i]) of a
 // contiguous fp32 [N, V] matrix and tokens [sum tokens[:i], +tokens[i]) of a
 // contiguous int64 vector.  One storage each, so no per-record tensors; the
@@ -275,8 +294,9 @@ const int64_t* host_counts(const at::Tensor& t, int64_t n, const char* what) {
 std::vector<at::Tensor> align_packed(
     const at::Tensor& emissions, const at::Tensor& frames_t, const at::Tensor& targets,
     const at::Tensor& tokens_t, const at::Tensor& blanks_t, int64_t mode,
-    const std::optional<at::Tensor>& emission_validity, bool check_inputs) {
+    const std::optional<at::Tensor>& emission_validity, bool check_inputs, int64_t fmt) {
   check_mode(mode);
+  const at::ScalarType dtype = format_dtype(fmt);
   const int64_t count = frames_t.numel();
   TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS && tokens_t.numel() == count &&
                         (blanks_t.numel() == count || blanks_t.numel() == 1),
@@ -288,10 +308,10 @@ std::vector<at::Tensor> align_packed(
   const int64_t blank_step = blanks_t.numel() == 1 ? 0 : 1;
   const auto device = emissions.device();
   TORCH_CHECK_VALUE(device.is_cuda() && targets.device() == device &&
-                        emissions.scalar_type() == at::kFloat && targets.scalar_type() == at::kLong &&
+                        emissions.scalar_type() == dtype && targets.scalar_type() == at::kLong &&
                         emissions.dim() == 2 && targets.dim() == 1 && emissions.is_contiguous() &&
                         targets.is_contiguous(),
-                    "inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device");
+                    format_message(fmt, true));
   const int64_t V = emissions.size(1);
   TORCH_CHECK_VALUE(V > 0 && V <= FFA_MAX_VOCAB, "unsupported vocabulary");
   c10::cuda::CUDAGuard guard(device);
@@ -302,7 +322,8 @@ std::vector<at::Tensor> align_packed(
   thread_local std::vector<ffa_record> recs;
   recs.resize(count);
   int64_t row = 0, tok = 0;
-  const float* ebase = emissions.numel() ? emissions.data_ptr<float>() : nullptr;
+  const auto* ebase = static_cast<const char*>(emissions.numel() ? emissions.data_ptr() : nullptr);
+  const int64_t row_bytes = V * static_cast<int64_t>(emissions.element_size());
   const int64_t* tbase = targets.numel() ? targets.data_ptr<int64_t>() : nullptr;
   const int64_t rows = emissions.size(0), ntok = targets.numel();
   for (int64_t i = 0; i < count; ++i) {
@@ -311,8 +332,8 @@ std::vector<at::Tensor> align_packed(
                       "unsupported frame count, target length, or blank ID");
     TORCH_CHECK_VALUE(row + T <= rows && tok + U <= ntok,
                       "frame or token counts exceed the packed tensors");
-    recs[i] = ffa_record{ebase + row * V, U ? tbase + tok : nullptr, T, static_cast<int32_t>(V),
-                         static_cast<int32_t>(U), static_cast<int32_t>(blank), 0};
+    recs[i] = ffa_record{ebase + row * row_bytes, U ? tbase + tok : nullptr, T, static_cast<int32_t>(V),
+                         static_cast<int32_t>(U), static_cast<int32_t>(blank), static_cast<int32_t>(fmt)};
     row += T;
     tok += U;
   }
@@ -337,7 +358,8 @@ at::Tensor emission_validity(at::TensorList emissions) {
                           e.is_contiguous() && e.size(0) > 0 && e.size(0) <= INT_MAX &&
                           e.size(1) > 0 && e.size(1) <= FFA_MAX_VOCAB,
                       msg);
-    recs[i] = ffa_record{e.data_ptr<float>(), nullptr, e.size(0), static_cast<int32_t>(e.size(1)), 0, 0, 0};
+    recs[i] = ffa_record{e.data_ptr<float>(), nullptr, e.size(0), static_cast<int32_t>(e.size(1)), 0, 0,
+                         FFA_INPUT_LOG_PROBS};
     rec(e);
   }
   ffa_sizes sizes{};
@@ -364,7 +386,7 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
                         static_cast<int64_t>(blanks.size()) == count,
                     "provide 1..65535 matching emissions and targets");
   const auto device = emissions[0].device();
-  const char* msg = "inputs must be contiguous CUDA float32 [T,V] and int64 [U] on one device";
+  const char* msg = "inputs must be contiguous CUDA float32 or bfloat16 [T,V] and int64 [U] on one device";
   TORCH_CHECK_VALUE(device.is_cuda(), msg);
   c10::cuda::CUDAGuard guard(device);
   const auto stream = c10::cuda::getCurrentCUDAStream();
@@ -374,16 +396,19 @@ at::Tensor check_targets(at::TensorList emissions, at::TensorList targets, at::I
     const auto& e = emissions[i];
     const auto& t = targets[i];
     TORCH_CHECK_VALUE(e.device() == device && t.device() == device &&
-                          e.scalar_type() == at::kFloat && t.scalar_type() == at::kLong &&
-                          e.dim() == 2 && t.dim() == 1 && e.is_contiguous() && t.is_contiguous(),
+                          (e.scalar_type() == at::kFloat || e.scalar_type() == at::kBFloat16) &&
+                          t.scalar_type() == at::kLong && e.dim() == 2 && t.dim() == 1 && e.is_contiguous() &&
+                          t.is_contiguous(),
                       msg);
     TORCH_CHECK_VALUE(e.size(0) > 0 && e.size(0) <= INT_MAX && e.size(1) > 0 &&
                           e.size(1) <= FFA_MAX_VOCAB && t.numel() <= FFA_MAX_TOKENS && blanks[i] >= 0 &&
                           blanks[i] < e.size(1),
                       "unsupported frame count, vocabulary, target length, or blank ID");
-    recs[i] = ffa_record{e.data_ptr<float>(), t.numel() ? t.data_ptr<int64_t>() : nullptr,
+    // Only the shapes and targets are read: logits check as log-probabilities do.
+    recs[i] = ffa_record{e.data_ptr(), t.numel() ? t.data_ptr<int64_t>() : nullptr,
                          e.size(0), static_cast<int32_t>(e.size(1)),
-                         static_cast<int32_t>(t.numel()), static_cast<int32_t>(blanks[i]), 0};
+                         static_cast<int32_t>(t.numel()), static_cast<int32_t>(blanks[i]),
+                         e.scalar_type() == at::kBFloat16 ? FFA_INPUT_LOGITS_BF16 : FFA_INPUT_LOG_PROBS};
     rec(t);
   }
   ffa_sizes sizes{};
@@ -448,13 +473,52 @@ at::Tensor token_spans(const at::Tensor& labels, const at::Tensor& frames_t, con
   return spans;
 }
 
+// row_logsumexp(Tensor[] logits) -> Tensor
+// CUDA float32 [sum T]: each row's log-sum-exp as ffa_align subtracts it
+// from logits (fp32 or bf16, one dtype for the list).
+at::Tensor row_logsumexp(at::TensorList logits) {
+  const int64_t count = static_cast<int64_t>(logits.size());
+  TORCH_CHECK_VALUE(count > 0 && count <= FFA_MAX_RECORDS, "provide 1..65535 logits tensors");
+  const auto device = logits[0].device();
+  const at::ScalarType dtype = logits[0].scalar_type();
+  const char* msg = "logits must be contiguous CUDA float32 or bfloat16 [T,V] tensors of one dtype on one device";
+  TORCH_CHECK_VALUE(device.is_cuda() && (dtype == at::kFloat || dtype == at::kBFloat16), msg);
+  const int32_t fmt = dtype == at::kBFloat16 ? FFA_INPUT_LOGITS_BF16 : FFA_INPUT_LOGITS_F32;
+  c10::cuda::CUDAGuard guard(device);
+  const auto stream = c10::cuda::getCurrentCUDAStream();
+  StreamRecorder rec{stream};
+  std::vector<ffa_record> recs(count);
+  int64_t rows = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    const auto& e = logits[i];
+    TORCH_CHECK_VALUE(e.device() == device && e.scalar_type() == dtype && e.dim() == 2 && e.is_contiguous() &&
+                          e.size(0) > 0 && e.size(0) <= INT_MAX && e.size(1) > 0 && e.size(1) <= FFA_MAX_VOCAB,
+                      msg);
+    recs[i] = ffa_record{e.data_ptr(), nullptr, e.size(0), static_cast<int32_t>(e.size(1)), 0, 0, fmt};
+    rows += e.size(0);
+    rec(e);
+  }
+  ffa_sizes sizes{};
+  check_status(ffa_row_logsumexp_query(recs.data(), count, &sizes));
+  auto z = at::empty({rows}, logits[0].options().dtype(at::kFloat));
+  auto workspace = device_scratch(sizes.workspace_bytes);
+  PinnedStaging& staging = staging_for(device.index());
+  const int rc = ffa_row_logsumexp(recs.data(), count, z.data_ptr<float>(), staging.acquire(sizes.staging_bytes),
+                                   sizes.staging_bytes, workspace.get(), std::max<size_t>(sizes.workspace_bytes, 256),
+                                   reinterpret_cast<ffa_stream_t>(stream.stream()));
+  if (rc == FFA_OK) staging.release(stream.stream());
+  check_status(rc);
+  return z;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(ffa_b200, m) {
   m.def("align(Tensor[] emissions, Tensor[] targets, int[] blanks, int mode, "
-        "Tensor? emission_validity=None, bool check_inputs=True) -> (Tensor[], int[])");
+        "Tensor? emission_validity=None, bool check_inputs=True, int fmt=0) -> (Tensor[], int[])");
   m.def("align_packed(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens, Tensor blanks, "
-        "int mode, Tensor? emission_validity=None, bool check_inputs=True) -> Tensor[]");
+        "int mode, Tensor? emission_validity=None, bool check_inputs=True, int fmt=0) -> Tensor[]");
+  m.def("row_logsumexp(Tensor[] logits) -> Tensor");
   m.def("emission_validity(Tensor[] emissions) -> Tensor");
   m.def("check_targets(Tensor[] emissions, Tensor[] targets, int[] blanks) -> Tensor");
   m.def("token_spans(Tensor labels, Tensor frames, Tensor tokens, Tensor blanks) -> Tensor");
@@ -466,4 +530,5 @@ TORCH_LIBRARY_IMPL(ffa_b200, CUDA, m) {
   m.impl("emission_validity", &emission_validity);
   m.impl("check_targets", &check_targets);
   m.impl("token_spans", &token_spans);
+  m.impl("row_logsumexp", &row_logsumexp);
 }

@@ -77,9 +77,11 @@ class AlignStream:
     @torch.inference_mode()
     def submit(self, emissions: Tensor, frames, targets: Tensor, tokens, *,
                blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
-               check_inputs: bool = True) -> PendingAlignment:
+               check_inputs: bool = True, from_logits: bool = False) -> PendingAlignment:
         """Enqueue host emissions ``[N, V]`` fp32 and targets ``[M]`` int64
-        (packed as for ``align_packed``); returns a PendingAlignment."""
+        (packed as for ``align_packed``; with ``from_logits``, fp32 or bf16
+        logits, which halves the host->device bytes in bf16); returns a
+        PendingAlignment."""
         for t, what in ((emissions, "emissions"), (targets, "targets")):
             if not isinstance(t, Tensor) or t.device.type != "cpu":
                 raise ValueError(f"{what} must be a host tensor")
@@ -93,7 +95,7 @@ class AlignStream:
             self.compute.wait_event(inputs_ready)
             with torch.cuda.stream(self.compute):
                 batch = align_packed(e, frames, t, tokens, blank_id=blank_id, mode=mode,
-                                     check_inputs=check_inputs)
+                                     check_inputs=check_inputs, from_logits=from_logits)
                 e.record_stream(self.compute)
                 t.record_stream(self.compute)
                 aligned = torch.cuda.Event()

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define FFA_ABI_VERSION 1
+#define FFA_ABI_VERSION 2 /* 2: input formats (ffa_record.format), ffa_row_logsumexp */
 
 #if defined(__GNUC__)
 #define FFA_API __attribute__((visibility("default")))
@@ -73,17 +73,31 @@ enum {
 #define FFA_MAX_FRAMES 2147483647LL
 #define FFA_MAX_TOKENS 32767
 
-/* One record: a device-resident fp32 [frames, vocab] row-major emission
- * matrix and an int64 [tokens] transcript (reference: one entry of the
- * `emissions` / `targets` tensor lists, alignment.cu:961-988). */
+/* What a record's [frames, vocab] matrix holds.  The reference aligns fp32
+ * log-probabilities (format 0); its example pipelines get them from a
+ * model's logits with torch.log_softmax (examples/transformers_ctc/
+ * align.py:55-56).  Formats 1 and 2 take the logits themselves and align
+ * their log_softmax without writing it out: the emission of (t, v) is
+ * x[t, v] - z[t], one fp32 round-to-nearest subtraction, where z[t] is row
+ * t's log-sum-exp as ffa_row_logsumexp computes it.  Every record of one
+ * call has the same format. */
+typedef enum ffa_input_format {
+  FFA_INPUT_LOG_PROBS = 0,   /* fp32 log-probabilities, used as stored */
+  FFA_INPUT_LOGITS_F32 = 1,  /* fp32 logits */
+  FFA_INPUT_LOGITS_BF16 = 2  /* bf16 logits (uint16 bit patterns) */
+} ffa_input_format;
+
+/* One record: a device-resident [frames, vocab] row-major emission (or
+ * logits) matrix and an int64 [tokens] transcript (reference: one entry of
+ * the `emissions` / `targets` tensor lists, alignment.cu:961-988). */
 typedef struct ffa_record {
-  const float* emissions;  /* device pointer, 4-byte aligned */
+  const void* emissions;   /* device pointer: fp32 (formats 0, 1; 4-byte aligned) or bf16 (2-byte aligned) */
   const int64_t* targets;  /* device pointer; may be NULL when tokens == 0 */
   int64_t frames;          /* T, 1 .. FFA_MAX_FRAMES */
   int32_t vocab;           /* V, 1 .. FFA_MAX_VOCAB */
   int32_t tokens;          /* U >= 0; states S = 2U + 1 */
   int32_t blank;           /* 0 .. V-1 */
-  int32_t reserved;        /* must be 0 */
+  int32_t format;          /* ffa_input_format (version 1 named it `reserved`, always 0) */
 } ffa_record;
 
 /* Caller-allocated device outputs, packed in record order without padding
@@ -143,7 +157,9 @@ FFA_API int ffa_align(const ffa_record* records, int64_t count, int mode, int fl
 FFA_API int ffa_emission_validity_query(const ffa_record* records, int64_t count, ffa_sizes* sizes);
 
 /* valid[i] = 1 unless record i holds a NaN or +inf (-inf is allowed).
- * Same staging/workspace contract as ffa_align. */
+ * Scans the stored fp32 values (formats 0 and 1; bf16 records are
+ * rejected with FFA_ERR_UNSUPPORTED).  Same staging/workspace contract as
+ * ffa_align. */
 FFA_API int ffa_emission_validity(const ffa_record* records, int64_t count, uint8_t* valid,
                           void* staging, size_t staging_bytes,
                           void* workspace, size_t workspace_bytes, ffa_stream_t stream);
@@ -191,7 +207,7 @@ FFA_API int64_t ffa_launch_count(void);
  * call has no finishing launch; its point is recorded where it would be, so
  * that phase measures zero. */
 enum {
-  FFA_PROFILE_START = 0,   /* after the descriptor upload */
+  FFA_PROFILE_START = 0,   /* after the descriptor upload (and a logits call's row log-sum-exps) */
   FFA_PROFILE_FIRST,       /* after the first forward pass (every piece / record) */
   FFA_PROFILE_FINISH,      /* after the optimized route's seam plans, repairs and fallback */
   FFA_PROFILE_FILL,        /* after the traceback fill (and objective fold) */
@@ -215,6 +231,22 @@ FFA_API int ffa_check_targets_query(const ffa_record* records, int64_t count, ff
  * codes and precedence ffa_align writes with FFA_FLAG_CHECK_INPUTS
  * (alignment.cu:852-874).  Same staging/workspace contract as ffa_align. */
 FFA_API int ffa_check_targets(const ffa_record* records, int64_t count, int32_t* status,
+                              void* staging, size_t staging_bytes,
+                              void* workspace, size_t workspace_bytes, ffa_stream_t stream);
+
+/* ---- row log-sum-exp of logits (no op in the reference, whose examples
+ *      apply torch.log_softmax before aligning) ---------------------------- */
+
+/* Host only: sizes for ffa_row_logsumexp (records of format 1 or 2; targets,
+ * tokens and blank are ignored). */
+FFA_API int ffa_row_logsumexp_query(const ffa_record* records, int64_t count, ffa_sizes* sizes);
+
+/* z (device float [sum frames], record i's frames in record order) = each
+ * row's log-sum-exp, m + logf(sum_v expf(x - m)) with m the row's maximum,
+ * exactly the values ffa_align subtracts from logits: x - z[t] in fp32 is
+ * the emission matrix it aligns.  A row holding NaN or +inf, or only -inf,
+ * gets NaN.  Same staging/workspace contract as ffa_align. */
+FFA_API int ffa_row_logsumexp(const ffa_record* records, int64_t count, float* z,
                               void* staging, size_t staging_bytes,
                               void* workspace, size_t workspace_bytes, ffa_stream_t stream);
 

@@ -20,7 +20,7 @@ SHIM = ROOT / "fast_forced_aligner_b200" / "_ffa_torch.so"
 class Record(ctypes.Structure):
     _fields_ = [("emissions", ctypes.c_void_p), ("targets", ctypes.c_void_p),
                 ("frames", ctypes.c_int64), ("vocab", ctypes.c_int32), ("tokens", ctypes.c_int32),
-                ("blank", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("blank", ctypes.c_int32), ("format", ctypes.c_int32)]
 
 
 class Sizes(ctypes.Structure):
@@ -50,14 +50,14 @@ def test_library_exports_every_declared_symbol(lib):
     assert {"ffa_align", "ffa_align_query", "ffa_emission_validity"} <= set(names)
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.ffa_abi_version() == 1
+    assert lib.ffa_abi_version() == 2
 
 
-def records(*specs):
+def records(*specs, fmt=0):
     arr = (Record * len(specs))()
     for i, (T, V, U, blank) in enumerate(specs):
         # Planning never dereferences device pointers: fake aligned addresses.
-        arr[i] = Record(0x10000 * (i + 1), 0x900000 * (i + 1) if U else None, T, V, U, blank, 0)
+        arr[i] = Record(0x10000 * (i + 1), 0x900000 * (i + 1) if U else None, T, V, U, blank, fmt)
     return arr
 
 
@@ -124,10 +124,59 @@ def test_validity_and_target_queries(lib):
     assert lib.ffa_check_targets_query(records((100, 32, 5, 0)), 1, ctypes.byref(sizes)) == 0
 
 
+def test_logits_formats_plan_like_log_probabilities(lib):
+    # Formats 1 (fp32 logits) and 2 (bf16 logits) plan the same DP; the
+    # workspace also holds one fp32 log-sum-exp per frame.
+    specs = ((600, 32, 100, 0), (7, 6, 0, 5), (2305, 1025, 2047, 1024))
+    base, f32, bf16 = Sizes(), Sizes(), Sizes()
+    assert lib.ffa_align_query(records(*specs), 3, 1, 1, ctypes.byref(base)) == 0
+    assert lib.ffa_align_query(records(*specs, fmt=1), 3, 1, 1, ctypes.byref(f32)) == 0
+    assert lib.ffa_align_query(records(*specs, fmt=2), 3, 1, 1, ctypes.byref(bf16)) == 0
+    assert f32.total_frames == bf16.total_frames == base.total_frames
+    assert f32.workspace_bytes == bf16.workspace_bytes >= base.workspace_bytes + 4 * base.total_frames
+    assert f32.staging_bytes == base.staging_bytes
+
+
+def test_input_format_rules(lib):
+    sizes = Sizes()
+    # A bf16 record needs 2-byte alignment only; fp32 ones need 4.
+    half = records((10, 33, 1, 0), fmt=2)
+    half[0].emissions = 0x10002
+    assert lib.ffa_align_query(half, 1, 1, 1, ctypes.byref(sizes)) == 0
+    single = records((10, 33, 1, 0), fmt=1)
+    single[0].emissions = 0x10002
+    assert lib.ffa_align_query(single, 1, 1, 1, ctypes.byref(sizes)) == -1
+    odd = records((10, 33, 1, 0), fmt=2)
+    odd[0].emissions = 0x10001
+    assert lib.ffa_align_query(odd, 1, 1, 1, ctypes.byref(sizes)) == -1
+    # Unknown formats, and formats mixed in one call, are rejected.
+    assert lib.ffa_align_query(records((10, 32, 1, 0), fmt=3), 1, 1, 1, ctypes.byref(sizes)) == -1
+    assert b"format" in lib.ffa_last_error()
+    mixed = records((10, 32, 1, 0), (12, 32, 1, 0), fmt=1)
+    mixed[1].format = 2
+    assert lib.ffa_align_query(mixed, 2, 1, 1, ctypes.byref(sizes)) == -1
+    assert b"same input format" in lib.ffa_last_error()
+    # The emission-validity scan reads fp32 only.
+    assert lib.ffa_emission_validity_query(records((10, 32, 0, 0), fmt=1), 1, ctypes.byref(sizes)) == 0
+    assert lib.ffa_emission_validity_query(records((10, 32, 0, 0), fmt=2), 1, ctypes.byref(sizes)) == -2
+
+
+def test_row_logsumexp_query(lib):
+    sizes = Sizes()
+    assert lib.ffa_row_logsumexp_query(records((100, 32, 0, 0), (5, 1025, 0, 0), fmt=2), 2,
+                                       ctypes.byref(sizes)) == 0
+    assert sizes.total_frames == 105 and sizes.workspace_bytes >= sizes.staging_bytes > 0
+    assert lib.ffa_row_logsumexp_query(records((100, 32, 0, 0)), 1, ctypes.byref(sizes)) == -1
+    assert b"logits" in lib.ffa_last_error()
+
+
 def test_torch_ops_register_without_a_gpu():
     torch.ops.load_library(str(SHIM))
-    for name in ("align", "align_packed", "emission_validity", "check_targets", "token_spans"):
+    for name in ("align", "align_packed", "emission_validity", "check_targets", "token_spans",
+                 "row_logsumexp"):
         assert hasattr(torch.ops.ffa_b200, name)
+    schema = str(torch.ops.ffa_b200.align.default._schema)
+    assert "int fmt=0" in schema
 
 
 # ---- Python surface (reference tests/test_extension.py, test_core.py:85-93) ----
@@ -181,6 +230,12 @@ def test_argument_contract_without_gpu():
         ffa.align([e], [t], blank_id=[True])
     with pytest.raises(ValueError, match="CUDA"):
         ffa.align([e], [t])  # CPU tensors
+    with pytest.raises(TypeError, match="from_logits"):
+        ffa.align([e], [t], from_logits=1)
+    with pytest.raises(TypeError, match="from_logits"):
+        ffa.align_packed(e, [12], t, [1], from_logits="yes")
+    with pytest.raises(ValueError, match="CUDA"):
+        ffa.row_logsumexp(e)
     with pytest.raises(ValueError):
         ffa.emission_validity([])
     with pytest.raises(ValueError):
