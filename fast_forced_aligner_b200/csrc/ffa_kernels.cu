@@ -1144,7 +1144,9 @@ ffa_token_spans_kernel(const SpanRecord* __restrict__ recs, int64_t count) {
 // Row log-sum-exp of logits (input formats 1 and 2), the z that turns them
 // into the log_softmax emissions x - z:
 //   z[t] = m + log(sum_v exp(x[t, v] - m)),  m = max_v x[t, v],
-// in fp32 with CUDA's expf and logf.  Lane l of a row's warp takes columns
+// in fp32: the terms with CUDA's __expf intrinsic (its relative error, a
+// few 1e-7 on terms in (0, 1], stays below the additions' rounding of the
+// sum), the log with logf.  Lane l of a row's warp takes columns
 // l, l + 32, l + 64, ... and sums their terms in that order; the warp then
 // adds the lanes' sums in a butterfly (so every lane holds the same sum).
 // That order depends on V alone, so a row's z is the same wherever the row
@@ -1205,7 +1207,7 @@ ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* 
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       float s = 0.0f;
 #pragma unroll 16
-      for (int v = lane; v < V; v += 32) s = __fadd_rn(s, expf(__fsub_rn(elem_to_float(x[v]), m)));
+      for (int v = lane; v < V; v += 32) s = __fadd_rn(s, __expf(__fsub_rn(elem_to_float(x[v]), m)));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
       if (lane == 0) z[row] = __fadd_rn(m, logf(s));
@@ -1236,7 +1238,7 @@ ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* 
       float s = 0.0f;
 #pragma unroll
       for (int k = 0; k < kN; ++k)
-        if (lane + 32 * k < vocab[q]) s = __fadd_rn(s, expf(__fsub_rn(val[q][k], m)));
+        if (lane + 32 * k < vocab[q]) s = __fadd_rn(s, __expf(__fsub_rn(val[q][k], m)));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
       if (lane == q) mine = __fadd_rn(m, logf(s));

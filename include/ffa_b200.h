@@ -242,7 +242,7 @@ FFA_API int ffa_check_targets(const ffa_record* records, int64_t count, int32_t*
 FFA_API int ffa_row_logsumexp_query(const ffa_record* records, int64_t count, ffa_sizes* sizes);
 
 /* z (device float [sum frames], record i's frames in record order) = each
- * row's log-sum-exp, m + logf(sum_v expf(x - m)) with m the row's maximum,
+ * row's log-sum-exp, m + logf(sum_v __expf(x - m)) with m the row's maximum,
  * exactly the values ffa_align subtracts from logits: x - z[t] in fp32 is
  * the emission matrix it aligns.  A row holding NaN or +inf, or only -inf,
  * gets NaN.  Same staging/workspace contract as ffa_align. */

@@ -28,10 +28,10 @@ def lse64(x: np.ndarray) -> np.ndarray:
 def lse_tolerance(V: int, z: np.ndarray) -> np.ndarray:
     """Bound on |z - lse64| for the kernel's fp32 arithmetic.  In log space:
     each of the ceil(V/32) + 5 additions of terms in (0, 1] contributes at
-    most 2^-24 (6e-8); the rounded arguments x - m and expf's error a few
-    times that (the terms' weighted mean of 2^-24 |x - m| plus 2 ulps); logf
-    two ulps of log(s) < log(V) + 1; the final m + log(s) half an ulp of
-    |z|.  Any algorithmic slip (a lost column, a wrong maximum) is orders of
+    most 2^-24 (6e-8); the rounded arguments x - m and __expf's error a few
+    times that (the terms' weighted mean of 2^-24 |x - m|, and the
+    intrinsic's few 1e-7 relative on each term); logf two ulps of
+    log(s) < log(V) + 1; the final m + log(s) half an ulp of |z|.  Any algorithmic slip (a lost column, a wrong maximum) is orders of
     magnitude above this."""
     adds = -(-V // 32) + 5
     log_ulp = float(np.spacing(np.float32(np.log(V) + 1.0)))
