@@ -1161,15 +1161,12 @@ ffa_token_spans_kernel(const SpanRecord* __restrict__ recs, int64_t count) {
 // before it reduces any, and the rows' reductions interleave.  kN == 0: one
 // row at a time, each pass over the row's columns with 16 loads per lane in
 // flight (the second pass finds the row in L1).
+// Rows first .. first + kLseRowsPerWarp - 1 (those below `rows`), by one warp.
 template <int kFmt, int kN>
-__global__ void __launch_bounds__(kLseThreads)
-ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* __restrict__ z) {
+__device__ __forceinline__ void lse_rows(const RecordDev* __restrict__ recs, int count, int64_t rows,
+                                         float* __restrict__ z, int64_t first, int lane) {
   using Elem = typename Input<kFmt>::Elem;
   constexpr int kRows = kLseRowsPerWarp;
-  const int lane = threadIdx.x & 31;
-  const int64_t first =
-      (static_cast<int64_t>(blockIdx.x) * (kLseThreads / 32) + (threadIdx.x >> 5)) * kRows;
-  if (first >= rows) return;
   // The last record with out_off <= first, by a 32-way search: lane j tests
   // the first record of the j-th of 32 blocks of the range (at most three
   // rounds for 65535 records).  Record 0 starts at row 0.
@@ -1245,6 +1242,18 @@ ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* 
     }
     if (lane < kRows && first + lane < rows) z[first + lane] = mine;
   }
+}
+
+// The grid holds one wave of CTAs (or fewer); each warp takes row groups
+// warp, warp + all warps, ... so no tail wave runs at low occupancy.
+template <int kFmt, int kN>
+__global__ void __launch_bounds__(kLseThreads)
+ffa_row_lse(const RecordDev* __restrict__ recs, int count, int64_t rows, float* __restrict__ z) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kLseThreads / 32);
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * (kLseThreads / 32) + (threadIdx.x >> 5);
+       g * kLseRowsPerWarp < rows; g += warps)
+    lse_rows<kFmt, kN>(recs, count, rows, z, g * kLseRowsPerWarp, lane);
 }
 
 // One warp per record: the target checks of the forward kernel without the DP.
@@ -1344,9 +1353,24 @@ cudaError_t opt_in(Kernel kernel, std::atomic<uint64_t>& opted, size_t bytes) {
 
 template <int kFmt, int kN>
 cudaError_t lse_launch(const RecordDev* recs, int count, int64_t rows, float* z, cudaStream_t stream) {
+  // One wave: the SMs times the CTAs of this variant resident on one SM
+  // (cached per device).
+  static std::atomic<int> wave[64];
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  int ctas = device < 64 ? wave[device].load(std::memory_order_relaxed) : 0;
+  if (ctas <= 0) {
+    int sms = 0, per_sm = 0;
+    err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (err != cudaSuccess) return err;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ffa_row_lse<kFmt, kN>, kLseThreads, 0);
+    if (err != cudaSuccess) return err;
+    ctas = std::max(1, sms * per_sm);
+    if (device < 64) wave[device].store(ctas, std::memory_order_relaxed);
+  }
   const int64_t per_cta = static_cast<int64_t>(kLseThreads / 32) * kLseRowsPerWarp;
-  const int64_t blocks = (rows + per_cta - 1) / per_cta;
-  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+  const int64_t blocks = std::min<int64_t>((rows + per_cta - 1) / per_cta, ctas);
   ++g_launches;
   ffa_row_lse<kFmt, kN><<<static_cast<unsigned>(blocks), kLseThreads, 0, stream>>>(recs, count, rows, z);
   return cudaGetLastError();
