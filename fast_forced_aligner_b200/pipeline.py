@@ -103,10 +103,34 @@ class AlignStream:
             self.copy_out.wait_event(aligned)
             with torch.cuda.stream(self.copy_out):
                 fields = (batch.labels, batch.scores, batch.status, batch.objective)
-                host = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in fields]
-                for h, x in zip(host, fields):
-                    h.copy_(x, non_blocking=True)
-                    x.record_stream(self.copy_out)
+                host = _copy_to_host(fields, self.copy_out)
                 done = torch.cuda.Event()
                 done.record(self.copy_out)
         return PendingAlignment(done, HostAlignment(batch.lengths, *host))
+
+
+def _copy_to_host(fields, stream) -> list[Tensor]:
+    """Pinned host copies of device tensors, enqueued on `stream`.  The align
+    op carves its outputs from one allocation, so one copy of the span that
+    holds them (one pinned buffer, one transfer) replaces a copy per field;
+    fields that do not share an allocation are copied one by one."""
+    storage = fields[0].untyped_storage()
+    spans = []
+    for x in fields:
+        if x.untyped_storage().data_ptr() != storage.data_ptr() or not x.is_contiguous():
+            spans = None
+            break
+        start = x.storage_offset() * x.element_size()
+        spans.append((start, start + x.numel() * x.element_size()))
+    if spans is None or any(s % 8 for s, _ in spans):
+        host = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in fields]
+        for h, x in zip(host, fields):
+            h.copy_(x, non_blocking=True)
+            x.record_stream(stream)
+        return host
+    lo, hi = min(s for s, _ in spans), max(e for _, e in spans)
+    span = torch.empty(0, dtype=torch.uint8, device=fields[0].device).set_(storage, lo, (hi - lo,))
+    pinned = torch.empty(hi - lo, dtype=torch.uint8, pin_memory=True)
+    pinned.copy_(span, non_blocking=True)
+    span.record_stream(stream)
+    return [pinned[s - lo:e - lo].view(x.dtype).view(x.shape) for (s, e), x in zip(spans, fields)]

@@ -31,8 +31,9 @@ def lse_tolerance(V: int, z: np.ndarray) -> np.ndarray:
     most 2^-24 (6e-8); the rounded arguments x - m and __expf's error a few
     times that (the terms' weighted mean of 2^-24 |x - m|, and the
     intrinsic's few 1e-7 relative on each term); logf two ulps of
-    log(s) < log(V) + 1; the final m + log(s) half an ulp of |z|.  Any algorithmic slip (a lost column, a wrong maximum) is orders of
-    magnitude above this."""
+    log(s) < log(V) + 1; the final m + log(s) half an ulp of |z|.  Any
+    algorithmic slip (a lost column, a wrong maximum) is orders of magnitude
+    above this."""
     adds = -(-V // 32) + 5
     log_ulp = float(np.spacing(np.float32(np.log(V) + 1.0)))
     return 1e-7 * (adds + 16) + 2 * log_ulp + 2 * np.spacing(np.abs(z).astype(np.float32)).astype(np.float64)
@@ -112,6 +113,27 @@ def test_row_logsumexp_same_in_every_variant(cuda, dtype):
     sizes = [x.shape[0] for x in xs]
     parts = np.split(alone, np.cumsum(sizes)[:-1])
     assert_same_bits(shuffled, np.concatenate(parts[::-1]), "reversed order")
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES))
+@pytest.mark.parametrize("V", [65, 100, 1025, 2049])
+def test_row_logsumexp_independent_of_address(cuda, dtype, V):
+    # The same rows copied to every element offset within a 16-byte block
+    # must give the same z bit for bit (and each within the fp64 bound): the
+    # summation order is a function of V, not of where a row lies.
+    rng = np.random.default_rng(V)
+    x = to_device((rng.standard_normal((40, V)) * 4).astype(np.float32), DTYPES[dtype])
+    per_block = 16 // x.element_size()
+    results = []
+    for shift in range(per_block):
+        buf = torch.empty(x.numel() + per_block, dtype=x.dtype, device="cuda")
+        view = buf[shift:shift + x.numel()].view(x.shape)
+        view.copy_(x)
+        results.append(ffa.row_logsumexp(view).cpu().numpy())
+    for shift, z in enumerate(results[1:], 1):
+        assert_same_bits(z, results[0], f"element offset {shift}")
+    ref = lse64(exact_values(x))
+    assert (np.abs(results[0] - ref) <= lse_tolerance(V, ref)).all()
 
 
 @pytest.mark.parametrize("dtype", list(DTYPES))
