@@ -5,10 +5,11 @@
                     [--mode optimized|conventional]
                     [--impl ours|reference|reference-cuda]
 
-One step = one ``align`` call over one synthetic batch of BASELINE.json's
-configs[C] (default cfg1, the config the 1-GPU metric is quoted on).  Under
-torchrun each rank aligns its own independent batch of that shape on its own
-GPU (records are independent: no collective on the data path; weak scaling).
+One step = one ``align`` call over one synthetic batch of benchmark
+configuration C (default cfg1, the configuration the 1-GPU metric is quoted
+on).  Under torchrun each rank aligns its own independent batch of that shape
+on its own GPU (records are independent: no collective on the data path;
+weak scaling).
 With --split every rank draws the same batch and aligns its share of a
 length-balanced partition of its records instead (strong scaling: the
 multi-GPU configuration's whole-box measurement).

@@ -1,4 +1,4 @@
-"""Seeded synthetic CTC alignment workloads with BASELINE.json's config shapes.
+"""Seeded synthetic CTC alignment workloads with the benchmark configurations' shapes.
 
 The reference measures on a speech-emission suite that is not shipped; these
 generators stand in for it with the shapes, lengths and value distributions

@@ -71,7 +71,7 @@ def test_gathered_long_record_matches_oracle(cuda):
 
 
 def test_full_size_cfg2_matches_oracle(cuda):
-    # BASELINE.json's configs[2] at full size: 8 recordings of 90000 frames,
+    # Benchmark configuration 2 at full size: 8 recordings of 90000 frames,
     # U = 27000 (S = 54001: 14-CTA clusters), 3.9e10 trellis cells.
     wl = workloads.config(2)
     es, ts = wl.records()

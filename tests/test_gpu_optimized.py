@@ -2,7 +2,7 @@
 resumed from saved frontiers, conventional fallback.
 
 Its contract is the conventional DP's exact outputs on every input without
-ties, so every test here compares against the CPU
+ties (the optimized route's contract), so every test here compares against the CPU
 oracle bit for bit, on inputs built to drive each branch of the route:
 confident and weak emissions (joins, repairs, chains of failing seams,
 fallback), piece-boundary lengths, NaN and +inf emissions (fallback, and the

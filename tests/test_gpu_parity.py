@@ -1,7 +1,7 @@
 """Bit-exact parity of the CUDA path with the CPU oracle, the reference's
 own CPU comparator (golden fixtures) and the reference's own CUDA extension.
 
-Configs follow BASELINE.json (fast_forced_aligner_b200.workloads); cfg4 runs
+Configs follow the benchmark configurations (fast_forced_aligner_b200.workloads); cfg4 runs
 at full size.  Both modes must return the conventional DP's exact outputs on
 every record without a constructed tie; on cfg4's 64 tie records the
 optimized route must return the same optimum (a path of equal score), and the
@@ -97,7 +97,7 @@ def test_tie_records_are_exact_in_conventional_mode(cuda):
 
 
 def test_full_size_properties_cfg4(cuda):
-    # Size-independent properties at BASELINE.json's full cfg4 size: the path
+    # Size-independent properties at cfg4's full size: the path
     # collapses to the transcript, scores are the selected emissions and the
     # objective is the sequential fp32 sum along the path.
     wl, _ = config(4)
