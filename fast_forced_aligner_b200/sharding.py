@@ -175,7 +175,7 @@ class ShardedAlignment:
 def align_sharded(
     emissions: Sequence[Tensor], targets: Sequence[Tensor], *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized", check_inputs: bool = True,
-    devices: Sequence[torch.device | str | int] | None = None,
+    devices: Sequence[torch.device | str | int] | None = None, from_logits: bool = False,
 ) -> ShardedAlignment:
     """Align a batch over several GPUs of this process, no collective involved.
 
@@ -184,8 +184,8 @@ def align_sharded(
     ``devices`` by ``partition_records`` and each record is copied to its
     device (inputs may be CPU tensors; pinned ones copy asynchronously).
     Every device's shard is aligned from its own host thread on that device's
-    current stream.  Arguments and per-record results are those of ``align``;
-    errors of any shard are raised here.
+    current stream.  Arguments (``from_logits`` included) and per-record
+    results are those of ``align``; errors of any shard are raised here.
     """
     count = len(emissions)
     if count == 0 or len(targets) != count:
@@ -217,7 +217,7 @@ def align_sharded(
                 es = [emissions[i].to(device, non_blocking=True) for i in ix.tolist()]
                 ts = [targets[i].to(device, non_blocking=True) for i in ix.tolist()]
                 results[k] = align(es, ts, blank_id=[blanks[i] for i in ix.tolist()], mode=mode,
-                                   check_inputs=check_inputs)
+                                   check_inputs=check_inputs, from_logits=from_logits)
         except BaseException as error:  # re-raised on the calling thread
             errors[k] = error
 

@@ -45,6 +45,21 @@ def test_threads_on_one_device_match_one_call(cuda, mode):
     assert sharded.status().tolist() == whole.status.cpu().tolist()
 
 
+def test_sharded_logits_match_one_call(cuda):
+    # bf16 logits over three shards on one device: each shard computes its
+    # rows' log-sum-exps, and a row's value does not depend on its batch.
+    wl = workloads.config(4, scale=1 / 32)
+    es, ts = wl.records()
+    rng = np.random.default_rng(9)
+    logits = [torch.from_numpy(e + rng.uniform(-5, 5, (e.shape[0], 1)).astype(np.float32)).to(torch.bfloat16)
+              for e in es]
+    targets = [torch.from_numpy(t) for t in ts]
+    whole = ffa.align([x.to(cuda) for x in logits], [t.to(cuda) for t in targets], blank_id=wl.blank,
+                      from_logits=True)
+    sharded = ffa.align_sharded(logits, targets, blank_id=wl.blank, devices=[0, 0, 0], from_logits=True)
+    _same(sharded.gather(cuda), whole)
+
+
 def test_records_stay_on_their_device(cuda):
     wl = workloads.config(0, scale=0.5)
     es, ts = wl.records()
