@@ -41,3 +41,21 @@ def test_stream_rejects_device_inputs(cuda):
     e = torch.zeros(10, 6, device=cuda)
     with pytest.raises(ValueError, match="host"):
         stream.submit(e, [10], torch.tensor([1]), [1])
+
+
+def test_stream_of_bf16_logits_matches_device_call(cuda):
+    # Host bf16 logits (half the bytes to copy), aligned as their log_softmax.
+    wl = workloads.config(1, scale=0.25)
+    rng = np.random.default_rng(4)
+    x = torch.from_numpy(wl.emissions + rng.uniform(-6, 6, (wl.emissions.shape[0], 1)).astype(np.float32))
+    x = x.to(torch.bfloat16).pin_memory()
+    t = torch.from_numpy(wl.targets).pin_memory()
+    got = AlignStream(cuda).submit(x, wl.lengths, t, wl.target_lengths, blank_id=wl.blank,
+                                   from_logits=True).result()
+    ref = ffa.align_packed(x.to(cuda), wl.lengths, t.to(cuda), wl.target_lengths, blank_id=wl.blank,
+                           from_logits=True)
+    assert got.lengths == ref.lengths
+    assert torch.equal(got.labels, ref.labels.cpu())
+    assert torch.equal(got.scores.view(torch.int32), ref.scores.cpu().view(torch.int32))
+    assert torch.equal(got.status, ref.status.cpu())
+    assert torch.equal(got.objective.view(torch.int32), ref.objective.cpu().view(torch.int32))
