@@ -385,7 +385,10 @@ def run_ours(args):
         def e2e_step():
             return astream.submit(e_host, wl.lengths, t_host, wl.target_lengths, blank_id=wl.blank,
                                   mode=args.mode, from_logits=from_logits)
-        for _ in range(args.warmup):
+        # Warm-up with as many batches in flight as the timed loop has, so
+        # that the pinned result blocks the timed loop cycles through are
+        # allocated (page-locked) before it starts.
+        for _ in range(max(args.warmup, args.steps)):
             pending = e2e_step()
         pending.result()
         torch.cuda.synchronize()

@@ -360,6 +360,25 @@ def _host_counts(values, what: str) -> Tensor:
     return torch.from_numpy(np.ascontiguousarray(array, dtype=np.int64))
 
 
+def _packed_counts(frames, tokens, blank_id) -> tuple[Tensor, Tensor, Tensor]:
+    """CPU int64 frame counts, token counts and blanks (one, or one per
+    record) of a packed batch, with align_packed's checks and messages."""
+    frames_t = _host_counts(frames, "frames")
+    tokens_t = _host_counts(tokens, "tokens")
+    count = frames_t.numel()
+    if not 0 < count <= 65535 or tokens_t.numel() != count:
+        raise ValueError("provide 1..65535 matching frame counts, token counts and blanks")
+    if type(blank_id) is int:
+        blanks_t = torch.tensor([blank_id], dtype=torch.int64)
+    elif not isinstance(blank_id, (Sequence, np.ndarray, Tensor)):
+        raise TypeError("blank_id must be an int or a sequence of ints")  # as align's list(blank_id)
+    else:
+        blanks_t = _host_counts(blank_id, "blank_id")
+        if blanks_t.numel() != count:
+            raise ValueError("provide one blank ID per record")
+    return frames_t, tokens_t, blanks_t
+
+
 @torch.inference_mode()
 def align_packed(
     emissions: Tensor, frames, targets: Tensor, tokens, *,
@@ -380,19 +399,8 @@ def align_packed(
     """
     code = _mode(mode, check_inputs, from_logits)
     fmt = _input_format(emissions, from_logits)
-    frames_t = _host_counts(frames, "frames")
-    tokens_t = _host_counts(tokens, "tokens")
+    frames_t, tokens_t, blanks_t = _packed_counts(frames, tokens, blank_id)
     count = frames_t.numel()
-    if not 0 < count <= 65535 or tokens_t.numel() != count:
-        raise ValueError("provide 1..65535 matching frame counts, token counts and blanks")
-    if type(blank_id) is int:
-        blanks_t = torch.tensor([blank_id], dtype=torch.int64)
-    elif not isinstance(blank_id, (Sequence, np.ndarray, Tensor)):
-        raise TypeError("blank_id must be an int or a sequence of ints")  # as align's list(blank_id)
-    else:
-        blanks_t = _host_counts(blank_id, "blank_id")
-        if blanks_t.numel() != count:
-            raise ValueError("provide one blank ID per record")
     if not isinstance(emissions, Tensor) or emissions.device.type != "cuda":
         raise ValueError("inputs must be contiguous CUDA float32 [N,V] and int64 [M] on one device")
     _check_mask(emission_validity, emissions.device, count)

@@ -10,6 +10,7 @@
 // in a reused pinned host buffer, so the host cost stays a few microseconds.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAEvent.h>
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
@@ -341,6 +342,79 @@ std::vector<at::Tensor> align_packed(
   return std::get<0>(run_align(recs, device, mode, mask, check_inputs, stream, {}));
 }
 
+// align_stream(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens,
+//              Tensor blanks, int mode, bool check_inputs, int fmt, int device,
+//              int copy_in, int compute, int copy_out) -> Tensor[]
+// One batch of host-resident packed inputs (pinned for the copies to be
+// asynchronous): host->device copies on stream `copy_in`; the align on
+// `compute` once they have landed; one device->host copy of the output
+// block's labels .. objective span on `copy_out` into a pinned block.
+// Returns labels, scores, status, objective as views of that block.  The
+// streams are torch stream ids of `device`; the caller records an event on
+// `copy_out` to learn when the results are in.  Doing the whole submission
+// here costs one dispatcher call instead of a dozen Python-level operations.
+std::vector<at::Tensor> align_stream(const at::Tensor& emissions, const at::Tensor& frames_t,
+                                     const at::Tensor& targets, const at::Tensor& tokens_t,
+                                     const at::Tensor& blanks_t, int64_t mode, bool check_inputs, int64_t fmt,
+                                     int64_t device_index, int64_t copy_in_id, int64_t compute_id,
+                                     int64_t copy_out_id) {
+  TORCH_CHECK_VALUE(emissions.device().is_cpu() && targets.device().is_cpu(),
+                    "emissions and targets must be host tensors");
+  TORCH_CHECK_VALUE(device_index >= 0 && device_index < 64, "device index out of range");
+  const c10::Device device(c10::DeviceType::CUDA, static_cast<c10::DeviceIndex>(device_index));
+  c10::cuda::CUDAGuard guard(device);
+  auto stream_of = [&](int64_t id) {
+    return c10::cuda::CUDAStream::unpack3(id, static_cast<c10::DeviceIndex>(device_index), c10::DeviceType::CUDA);
+  };
+  const c10::cuda::CUDAStream copy_in = stream_of(copy_in_id), compute = stream_of(compute_id),
+                              copy_out = stream_of(copy_out_id);
+  at::Tensor e, t;
+  {
+    c10::cuda::CUDAStreamGuard on(copy_in);
+    e = at::empty(emissions.sizes(), emissions.options().device(device));
+    t = at::empty(targets.sizes(), targets.options().device(device));
+    e.copy_(emissions, /*non_blocking=*/true);
+    t.copy_(targets, /*non_blocking=*/true);
+  }
+  at::cuda::CUDAEvent landed;
+  landed.record(copy_in);
+  landed.block(compute);
+  std::vector<at::Tensor> out;
+  {
+    c10::cuda::CUDAStreamGuard on(compute);
+    out = align_packed(e, frames_t, t, tokens_t, blanks_t, mode, std::nullopt, check_inputs, fmt);
+  }
+  // e and t were allocated on copy_in and are read on compute.
+  c10::cuda::CUDACachingAllocator::recordStream(e.storage().data_ptr(), compute);
+  c10::cuda::CUDACachingAllocator::recordStream(t.storage().data_ptr(), compute);
+  at::cuda::CUDAEvent aligned;
+  aligned.record(compute);
+  aligned.block(copy_out);
+  // labels, scores, status, objective: one allocation (OutputBlock), copied
+  // back as one span.
+  const at::Tensor* fields[4] = {&out[0], &out[1], &out[2], &out[3]};
+  int64_t lo = INT64_MAX, hi = 0;
+  for (const at::Tensor* f : fields) {
+    TORCH_CHECK(f->storage().is_alias_of(out[0].storage()), "align outputs must share one allocation");
+    const int64_t start = f->storage_offset() * static_cast<int64_t>(f->element_size());
+    lo = std::min(lo, start);
+    hi = std::max(hi, start + f->numel() * static_cast<int64_t>(f->element_size()));
+  }
+  c10::cuda::CUDAStreamGuard on(copy_out);
+  at::Tensor span = at::empty({0}, out[0].options().dtype(at::kByte));
+  span.set_(out[0].storage(), lo, {hi - lo}, {1});
+  at::Tensor host = at::empty({hi - lo}, at::TensorOptions().dtype(at::kByte).pinned_memory(true));
+  host.copy_(span, /*non_blocking=*/true);
+  c10::cuda::CUDACachingAllocator::recordStream(out[0].storage().data_ptr(), copy_out);
+  std::vector<at::Tensor> result;
+  for (const at::Tensor* f : fields) {
+    const int64_t start = f->storage_offset() * static_cast<int64_t>(f->element_size());
+    const int64_t bytes = f->numel() * static_cast<int64_t>(f->element_size());
+    result.push_back(host.narrow(0, start - lo, bytes).view(f->scalar_type()).view(f->sizes()));
+  }
+  return result;
+}
+
 // emission_validity(Tensor[] emissions) -> Tensor   (alignment.cu:893-917)
 at::Tensor emission_validity(at::TensorList emissions) {
   const int64_t count = static_cast<int64_t>(emissions.size());
@@ -519,6 +593,8 @@ TORCH_LIBRARY(ffa_b200, m) {
   m.def("align_packed(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens, Tensor blanks, "
         "int mode, Tensor? emission_validity=None, bool check_inputs=True, int fmt=0) -> Tensor[]");
   m.def("row_logsumexp(Tensor[] logits) -> Tensor");
+  m.def("align_stream(Tensor emissions, Tensor frames, Tensor targets, Tensor tokens, Tensor blanks, int mode, "
+        "bool check_inputs, int fmt, int device, int copy_in, int compute, int copy_out) -> Tensor[]");
   m.def("emission_validity(Tensor[] emissions) -> Tensor");
   m.def("check_targets(Tensor[] emissions, Tensor[] targets, int[] blanks) -> Tensor");
   m.def("token_spans(Tensor labels, Tensor frames, Tensor tokens, Tensor blanks) -> Tensor");
@@ -531,4 +607,10 @@ TORCH_LIBRARY_IMPL(ffa_b200, CUDA, m) {
   m.impl("check_targets", &check_targets);
   m.impl("token_spans", &token_spans);
   m.impl("row_logsumexp", &row_logsumexp);
+}
+
+// align_stream takes host tensors and stream ids: registered for the CPU
+// dispatch key (its inputs' device), it runs on the CUDA device it is given.
+TORCH_LIBRARY_IMPL(ffa_b200, CPU, m) {
+  m.impl("align_stream", &align_stream);
 }

@@ -19,7 +19,7 @@ from typing import Sequence
 import torch
 from torch import Tensor
 
-from .alignment import Mode, align_packed
+from .alignment import Mode, _input_format, _mode, _packed_counts, load_extension
 
 
 @dataclass(frozen=True)
@@ -81,56 +81,18 @@ class AlignStream:
         """Enqueue host emissions ``[N, V]`` fp32 and targets ``[M]`` int64
         (packed as for ``align_packed``; with ``from_logits``, fp32 or bf16
         logits, which halves the host->device bytes in bf16); returns a
-        PendingAlignment."""
+        PendingAlignment.  The copies, the align and the copy back are
+        enqueued by one native call (``torch.ops.ffa_b200.align_stream``)."""
         for t, what in ((emissions, "emissions"), (targets, "targets")):
             if not isinstance(t, Tensor) or t.device.type != "cpu":
                 raise ValueError(f"{what} must be a host tensor")
-        dev = self.device
-        with torch.cuda.device(dev):
-            with torch.cuda.stream(self.copy_in):
-                e = emissions.to(dev, non_blocking=True)
-                t = targets.to(dev, non_blocking=True)
-                inputs_ready = torch.cuda.Event()
-                inputs_ready.record(self.copy_in)
-            self.compute.wait_event(inputs_ready)
-            with torch.cuda.stream(self.compute):
-                batch = align_packed(e, frames, t, tokens, blank_id=blank_id, mode=mode,
-                                     check_inputs=check_inputs, from_logits=from_logits)
-                e.record_stream(self.compute)
-                t.record_stream(self.compute)
-                aligned = torch.cuda.Event()
-                aligned.record(self.compute)
-            self.copy_out.wait_event(aligned)
-            with torch.cuda.stream(self.copy_out):
-                fields = (batch.labels, batch.scores, batch.status, batch.objective)
-                host = _copy_to_host(fields, self.copy_out)
-                done = torch.cuda.Event()
-                done.record(self.copy_out)
-        return PendingAlignment(done, HostAlignment(batch.lengths, *host))
-
-
-def _copy_to_host(fields, stream) -> list[Tensor]:
-    """Pinned host copies of device tensors, enqueued on `stream`.  The align
-    op carves its outputs from one allocation, so one copy of the span that
-    holds them (one pinned buffer, one transfer) replaces a copy per field;
-    fields that do not share an allocation are copied one by one."""
-    storage = fields[0].untyped_storage()
-    spans = []
-    for x in fields:
-        if x.untyped_storage().data_ptr() != storage.data_ptr() or not x.is_contiguous():
-            spans = None
-            break
-        start = x.storage_offset() * x.element_size()
-        spans.append((start, start + x.numel() * x.element_size()))
-    if spans is None or any(s % 8 for s, _ in spans):
-        host = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in fields]
-        for h, x in zip(host, fields):
-            h.copy_(x, non_blocking=True)
-            x.record_stream(stream)
-        return host
-    lo, hi = min(s for s, _ in spans), max(e for _, e in spans)
-    span = torch.empty(0, dtype=torch.uint8, device=fields[0].device).set_(storage, lo, (hi - lo,))
-    pinned = torch.empty(hi - lo, dtype=torch.uint8, pin_memory=True)
-    pinned.copy_(span, non_blocking=True)
-    span.record_stream(stream)
-    return [pinned[s - lo:e - lo].view(x.dtype).view(x.shape) for (s, e), x in zip(spans, fields)]
+        code = _mode(mode, check_inputs, from_logits)
+        fmt = _input_format(emissions, from_logits)
+        frames_t, tokens_t, blanks_t = _packed_counts(frames, tokens, blank_id)
+        load_extension()
+        labels, scores, status, objective = torch.ops.ffa_b200.align_stream(
+            emissions, frames_t, targets, tokens_t, blanks_t, code, check_inputs, fmt, self.device.index,
+            self.copy_in.stream_id, self.compute.stream_id, self.copy_out.stream_id)
+        done = torch.cuda.Event()
+        done.record(self.copy_out)
+        return PendingAlignment(done, HostAlignment(tuple(frames_t.tolist()), labels, scores, status, objective))

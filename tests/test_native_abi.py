@@ -173,7 +173,7 @@ def test_row_logsumexp_query(lib):
 def test_torch_ops_register_without_a_gpu():
     torch.ops.load_library(str(SHIM))
     for name in ("align", "align_packed", "emission_validity", "check_targets", "token_spans",
-                 "row_logsumexp"):
+                 "row_logsumexp", "align_stream"):
         assert hasattr(torch.ops.ffa_b200, name)
     schema = str(torch.ops.ffa_b200.align.default._schema)
     assert "int fmt=0" in schema
