@@ -1,13 +1,14 @@
 // ffa_torch.cpp -- thin PyTorch operator layer over the C ABI (libffa_b200.so).
 //
 // Registers torch.ops.ffa_b200.{align, align_packed, emission_validity,
-// check_targets, token_spans, row_logsumexp}.  It mirrors the reference's op
-// layer (alignment.cu:893-1061, TORCH_LIBRARY at alignment.cu:1064-1070):
-// tensor metadata checks, stream lifetime protection (recordStream on
-// borrowed inputs) and output allocation from the caching allocator.  Everything below the ffa_* calls is plain
-// pointers and sizes.  Per call it makes two caching-allocator requests (one
-// block holds every output tensor, one the workspace) and stages descriptors
-// in a reused pinned host buffer, so the host cost stays a few microseconds.
+// check_targets, token_spans, row_logsumexp, align_stream}.  It mirrors the
+// reference's op layer (alignment.cu:893-1061, TORCH_LIBRARY at
+// alignment.cu:1064-1070): tensor metadata checks, stream lifetime
+// protection (recordStream on borrowed inputs) and output allocation from
+// the caching allocator.  Everything below the ffa_* calls is plain pointers
+// and sizes.  Per call it makes two caching-allocator requests (one block
+// holds every output tensor, one the workspace) and stages descriptors in a
+// reused pinned host buffer, so the host cost stays a few microseconds.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAEvent.h>
