@@ -69,6 +69,8 @@ class AlignStream:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("AlignStream needs a CUDA device")
+        if self.device.index is None:  # "cuda": the current device
+            self.device = torch.device("cuda", torch.cuda.current_device())
         with torch.cuda.device(self.device):
             self.copy_in = torch.cuda.Stream()
             self.compute = torch.cuda.Stream()

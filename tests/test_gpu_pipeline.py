@@ -50,8 +50,9 @@ def test_stream_of_bf16_logits_matches_device_call(cuda):
     x = torch.from_numpy(wl.emissions + rng.uniform(-6, 6, (wl.emissions.shape[0], 1)).astype(np.float32))
     x = x.to(torch.bfloat16).pin_memory()
     t = torch.from_numpy(wl.targets).pin_memory()
-    got = AlignStream(cuda).submit(x, wl.lengths, t, wl.target_lengths, blank_id=wl.blank,
-                                   from_logits=True).result()
+    stream = AlignStream("cuda")  # no index: the current device
+    assert stream.device == torch.device("cuda", torch.cuda.current_device())
+    got = stream.submit(x, wl.lengths, t, wl.target_lengths, blank_id=wl.blank, from_logits=True).result()
     ref = ffa.align_packed(x.to(cuda), wl.lengths, t.to(cuda), wl.target_lengths, blank_id=wl.blank,
                            from_logits=True)
     assert got.lengths == ref.lengths
