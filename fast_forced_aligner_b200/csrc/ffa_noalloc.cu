@@ -12,10 +12,12 @@
 //   - host staging: a static array of kNoAllocStagingBytes (2 MiB) from which
 //     the per-call descriptor table is uploaded (pageable memory: the upload
 //     is staged by the driver).
-// Because every call shares these buffers, calls whose work may overlap on a
-// GPU (concurrent streams, or host threads calling at the same time) race;
-// serialise them.  The scratch needs no clearing between calls: every byte a
-// kernel reads is written earlier in the same call.
+// Because every call shares these buffers -- and the host staging array
+// serves every GPU of the process -- calls must be serialised across the
+// whole process: one call in flight at a time, on any device, from any host
+// thread (concurrent streams or threads race, on different GPUs too).  The
+// scratch needs no clearing between calls: every byte a kernel reads is
+// written earlier in the same call.
 #include <cuda_runtime.h>
 
 #include <atomic>

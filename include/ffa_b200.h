@@ -24,8 +24,10 @@
  *     the device `status` array (0 ok, 1 no finite path, 2 masked by the
  *     emission-validity mask, 3 invalid target IDs, 4 too few frames),
  *     exactly as the reference's status contract (alignment.py:88-94).
- *   - Thread safety: every function is reentrant; concurrent calls on
- *     different streams or devices share no mutable state.
+ *   - Thread safety: every function except ffa_align_noalloc is reentrant;
+ *     concurrent calls on different streams or devices share no mutable
+ *     state.  ffa_align_noalloc uses one process-wide device scratch array
+ *     and one host staging array: see its own comment.
  */
 #ifndef FFA_B200_H
 #define FFA_B200_H
@@ -139,9 +141,12 @@ FFA_API int ffa_align_query(const ffa_record* records, int64_t count, int mode, 
  *       false entry gives status 2 unless target validation fails
  *       (alignment.cu:836, 870-874).
  *   staging: host memory of sizes.staging_bytes.  The call writes the device
- *       descriptor table into it and enqueues one cudaMemcpyAsync from it;
- *       pinned memory keeps the call asynchronous.  Keep it unchanged until
- *       the stream has passed this call.
+ *       descriptor table into it and enqueues its upload: from pinned (mapped)
+ *       memory, a small kernel that reads the table through the buffer's
+ *       device mapping in 16-byte loads -- so the buffer must be readable up
+ *       to sizes.staging_bytes rounded up to a multiple of 16; from any other
+ *       memory, one cudaMemcpyAsync.  Keep it unchanged until the stream has
+ *       passed this call.
  *   workspace: device scratch of sizes.workspace_bytes, 256-byte aligned,
  *       not shared with concurrent work on another stream.
  * No host synchronisation, no allocation, no device-to-host transfer. */
@@ -165,7 +170,8 @@ FFA_API int ffa_emission_validity(const ffa_record* records, int64_t count, uint
                           void* workspace, size_t workspace_bytes, ffa_stream_t stream);
 
 /* ---- allocation-free align (no counterpart in the reference, whose
- *      align always allocates its scratch with at::empty) ------------------- */
+ *      align always allocates its scratch with at::empty).  NOT reentrant:
+ *      the reentrancy convention at the top of this header excludes it. ---- */
 
 /* For callers that cannot allocate device memory when they align -- code
  * running inside a framework that owns every device allocation, pipelines
@@ -180,9 +186,11 @@ FFA_API int ffa_emission_validity(const ffa_record* records, int64_t count, uint
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
  *     before any stream capture.
- *   - All calls share the two buffers: calls that may overlap on a GPU (other
- *     streams, other host threads) race and must be serialised by the caller.
- *     Nothing in them needs clearing between calls. */
+ *   - All calls share the two buffers, and the host staging array serves
+ *     every device: calls must be serialised across the whole process -- one
+ *     call in flight at a time, on any GPU, from any host thread -- not only
+ *     per GPU.  Calls that overlap race.  Nothing in them needs clearing
+ *     between calls. */
 FFA_API int ffa_align_noalloc(const ffa_record* records, int64_t count, int mode, int flags,
                               const uint8_t* emission_validity, const ffa_outputs* outputs,
                               ffa_stream_t stream);

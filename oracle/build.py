@@ -31,7 +31,10 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("FFA_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: FFA_REFERENCE_ROOT, else a "reference" folder beside
+# this repository's root.  Where neither exists (the GPU box), only the
+# prebuilt checkers under oracle/_ref are used.
+REFERENCE = Path(os.environ.get("FFA_REFERENCE_ROOT") or HERE.parent.parent / "reference")
 ORACLE_SO = HERE / "libffa_oracle.so"
 CORRECTED_SO = REF_OUT / ("ffa_corrected_ctc_cpp" + sysconfig.get_config_var("EXT_SUFFIX"))
 REF_CUDA_SO = REF_OUT / "fast_forced_aligner_cuda.so"
@@ -111,6 +114,9 @@ def build_reference_cuda(force: bool = False) -> Path | None:
 
 def build_all(force: bool = False, reference_cuda: bool = True) -> None:
     build_oracle(force)
+    if not REFERENCE.is_dir():
+        print(f"oracle/build.py: no reference tree at {REFERENCE} (set FFA_REFERENCE_ROOT); "
+              "using the prebuilt checkers under oracle/_ref, if any", file=sys.stderr)
     build_corrected(force)
     if reference_cuda:
         build_reference_cuda(force)

@@ -163,3 +163,65 @@ def default_threads() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+def greedy_chunk_stats(emissions: np.ndarray, targets: np.ndarray, blank: int,
+                       chunk: int = 128) -> np.ndarray:
+    """The reference's greedy shortcut counts for one record (int64 [3]):
+    accepted greedy chunks, the frames in them, and chunks rejected because
+    the greedy label sequence had several legal placements
+    (src/fast_forced_aligner/csrc/alignment.cu:29-153, reported as
+    ``shortcut_stats``, alignment.py:116-121).
+
+    Per chunk of ``chunk`` frames: each frame's greedy label is the unique
+    finite maximum over the transcript alphabet, blank included (a NaN never
+    compares greater or equal there, so NaN columns drop out), else the chunk
+    is rejected (:60-91); the relative state offsets r advance by 0 on a
+    repeated label, 1 into or out of a blank, 2 between tokens (:112-117); a
+    start s is legal when l[s] is the chunk's first label (s <= 1 for the
+    first chunk), its terminal s + r[-1] is a state (>= S-2 for the last
+    chunk), and every label change lands on a state with that label
+    (:119-128).  Exactly one legal start accepts the chunk (if its fp32 sum of
+    maxima is finite); more count as rejected for several placements."""
+    e = np.asarray(emissions, np.float32)
+    T = e.shape[0]
+    tokens = np.asarray(targets, np.int64)
+    S = 2 * tokens.size + 1
+    labels = np.full(S, blank, np.int64)
+    labels[1::2] = tokens
+    alphabet = np.unique(labels)
+    sub = np.where(np.isnan(e[:, alphabet]), np.float32(-np.inf), e[:, alphabet])
+    best = sub.max(axis=1)
+    unique = (sub == best[:, None]).sum(axis=1) == 1
+    finite = np.isfinite(best)
+    greedy = alphabet[sub.argmax(axis=1)]
+    stats = np.zeros(3, np.int64)
+    for a in range(0, T, chunk):
+        b = min(T, a + chunk)
+        if not (unique[a:b].all() and finite[a:b].all()):
+            continue
+        g = greedy[a:b]
+        change = np.r_[False, g[1:] != g[:-1]]
+        prev = np.r_[g[0], g[:-1]]
+        step = np.where(change, np.where((g == blank) | (prev == blank), 1, 2), 0)
+        r = np.cumsum(step)
+        starts = np.flatnonzero(labels == g[0])
+        if a == 0:
+            starts = starts[starts <= 1]
+        term = starts + r[-1]
+        ok = term < S
+        if b == T:
+            ok &= term >= S - 2
+        starts = starts[ok]
+        idx = np.flatnonzero(change)
+        matches = sum(1 for s in starts if np.all(labels[s + r[idx]] == g[idx]))
+        if matches == 1:
+            total = np.float32(0)
+            for v in best[a:b]:
+                total = np.float32(total + v)
+            if np.isfinite(total):
+                stats[0] += 1
+                stats[1] += b - a
+        elif matches > 1:
+            stats[2] += 1
+    return stats

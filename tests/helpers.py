@@ -90,3 +90,79 @@ def assert_same_optimum(result, ref: oracle.OracleResult, emissions, targets, bl
         step = float(np.spacing(np.float32(abs(ref.objective[i]))))
         assert abs(mine - best) <= 4 * step, f"{what} record {i}: {mine} vs {best} (fp32 step {step})"
     return same_path
+
+
+def conventional_scores(e: np.ndarray, targets: np.ndarray, blank: int) -> np.ndarray:
+    """The conventional DP's fp32 scores alpha[t, s] of one record (the
+    recurrence of alignment.cu:407-429: one fp32 add per cell, stay > step >
+    skip by strict '>'), as a [T, S] array.  Small records only."""
+    T = e.shape[0]
+    S = 2 * len(targets) + 1
+    labels = np.full(S, blank, np.int64)
+    labels[1::2] = targets
+    skip = np.zeros(S, bool)
+    skip[3::2] = (labels[3::2] != blank) & (labels[3::2] != labels[1:-2:2])
+    alpha = np.full((T, S), -np.inf, np.float32)
+    alpha[0, :min(2, S)] = e[0, labels[:min(2, S)]]
+    ninf = np.float32(-np.inf)
+    for t in range(1, T):
+        a = alpha[t - 1]
+        step = np.r_[ninf, a[:-1]]
+        best = np.where(step > a, step, a)
+        if S > 2:
+            sk = np.r_[ninf, ninf, a[:-2]]
+            best = np.where(skip & (sk > best), sk, best)
+        alpha[t] = (best + e[t, labels]).astype(np.float32)
+    return alpha
+
+
+def state_path(labels: np.ndarray, targets: np.ndarray, blank: int) -> np.ndarray:
+    """The CTC state of every frame of a legal label path (a repeated label
+    stays, a new label steps to the next state that carries it)."""
+    S = 2 * len(targets) + 1
+    lab = np.full(S, blank, np.int64)
+    lab[1::2] = targets
+    cur = 0 if labels[0] == blank else 1
+    out = [cur]
+    for x in labels[1:]:
+        if x != lab[cur]:
+            cur += 1 if (cur + 1 < S and x == lab[cur + 1]) else 2
+        out.append(cur)
+    return np.array(out)
+
+
+def classify_divergence(e: np.ndarray, targets: np.ndarray, blank: int, mine_labels: np.ndarray,
+                        conv_labels: np.ndarray) -> str:
+    """Why an optimized-route path differs from the conventional one, decided
+    exactly, in the spirit of the reference's own accuracy audit
+    (benchmarks/accuracy.py:67-105):
+      "identical"     the label paths are equal;
+      "equal_fp32"    both paths' sequential fp32 sums are bitwise equal;
+      "tie_rule"      where the two paths meet, the conventional DP chose
+                      between equal fp32 scores (its stay > step > skip or
+                      terminal >= rule decided);
+      "equal_score"   equal exact (fp64) path sums;
+      "better"        the optimized path's exact sum is higher: the
+                      conventional choice was decided by fp32 rounding;
+      "worse"         a genuine divergence: the optimized path scores lower
+                      exactly.
+    Only "worse" is a parity failure."""
+    if np.array_equal(mine_labels, conv_labels):
+        return "identical"
+    rows = np.arange(e.shape[0])
+    mine = e[rows, mine_labels]
+    conv = e[rows, conv_labels]
+    if sequential_sum(mine).view(np.int32) == sequential_sum(conv).view(np.int32):
+        return "equal_fp32"
+    sm, sc = state_path(mine_labels, targets, blank), state_path(conv_labels, targets, blank)
+    alpha = conventional_scores(e, targets, blank)
+    T = e.shape[0]
+    last = int(np.flatnonzero(sm != sc)[-1])
+    # The last frame where the state paths differ: there the conventional DP
+    # compared both predecessors (or, at the last frame, both terminals).
+    if alpha[last, sm[last]] == alpha[last, sc[last]]:
+        return "tie_rule"
+    a, b = float(np.sum(mine.astype(np.float64))), float(np.sum(conv.astype(np.float64)))
+    if a == b:
+        return "equal_score"
+    return "better" if a > b else "worse"

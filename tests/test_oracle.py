@@ -174,3 +174,51 @@ def test_objective_is_sequential_fp32_path_sum():
     for k, v in enumerate(r.scores):
         acc = v if k == 0 else np.float32(acc + v)
     assert acc == r.objective[0]
+
+
+# ---- the reference's greedy chunk counts (alignment.cu:29-153), restated in
+#      oracle.greedy_chunk_stats: known answers on small hand-built records ----
+
+def _one_hot(labels, V=4, hi=-0.1, lo=-5.0):
+    e = np.full((len(labels), V), lo, np.float32)
+    e[np.arange(len(labels)), labels] = hi
+    return e
+
+
+def test_greedy_chunk_accepts_a_unique_placement():
+    # Frames follow blank 1 1 blank 2 exactly: one legal placement from state 0.
+    e = _one_hot([0, 1, 1, 0, 2])
+    assert oracle.greedy_chunk_stats(e, np.array([1, 2]), 0, chunk=5).tolist() == [1, 5, 0]
+
+
+def test_greedy_chunk_counts_several_placements():
+    # Transcript 1 2 1 2: the middle chunk "2 2" (frames 2-3) fits token
+    # states 3 and 7, so it has two placements.
+    e = _one_hot([1, 0, 2, 2, 0, 1, 0, 2])
+    stats = oracle.greedy_chunk_stats(e, np.array([1, 2, 1, 2]), 0, chunk=2)
+    assert stats[2] >= 1
+
+
+def test_greedy_chunk_rejects_ties_and_illegal_sequences():
+    e = _one_hot([0, 1, 1, 0, 2])
+    e[2, 3] = e[2, 1]  # label 3 is not in the alphabet: no effect
+    assert oracle.greedy_chunk_stats(e, np.array([1, 2]), 0, chunk=5).tolist() == [1, 5, 0]
+    e[2, 2] = e[2, 1]  # a tie inside the alphabet rejects the chunk
+    assert oracle.greedy_chunk_stats(e, np.array([1, 2]), 0, chunk=5).tolist() == [0, 0, 0]
+    # Greedy labels 2 then 1 cannot follow transcript 1 2 in order.
+    assert oracle.greedy_chunk_stats(_one_hot([2, 1]), np.array([1, 2]), 0, chunk=2).tolist() == [0, 0, 0]
+
+
+# ---- the exact divergence classes the parity tests use (tests/helpers.py) ----
+
+def test_divergence_classes():
+    from tests.helpers import classify_divergence
+    # Two frames, transcript [1]: paths 1,0 and 0,1 with equal emissions tie.
+    e = np.array([[-1.0, -1.0], [-1.0, -1.0]], np.float32)
+    t = np.array([1])
+    assert classify_divergence(e, t, 0, np.array([1, 0]), np.array([1, 0])) == "identical"
+    assert classify_divergence(e, t, 0, np.array([0, 1]), np.array([1, 1])) == "equal_fp32"
+    e2 = np.array([[-1.0, -0.5], [-1.0, -2.0]], np.float32)
+    # Path 1,0 scores -1.5 and path 0,1 scores -3: the second is worse.
+    assert classify_divergence(e2, t, 0, np.array([0, 1]), np.array([1, 0])) == "worse"
+    assert classify_divergence(e2, t, 0, np.array([1, 0]), np.array([0, 1])) == "better"
