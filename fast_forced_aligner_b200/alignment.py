@@ -219,14 +219,21 @@ def emission_validity(emissions: Sequence[Tensor]) -> Tensor:
         return torch.ops.ffa_b200.emission_validity(list(emissions))
 
 
-def _mode(mode, check_inputs, from_logits=False) -> int:
+_ROUTES = ("auto", "pieces")
+
+
+def _mode(mode, check_inputs, from_logits=False, route="auto") -> int:
+    """The torch op's mode code: 0 conventional, 1 optimized, 2 optimized on
+    the chunked route for every record (``route="pieces"``)."""
     if mode not in _MODES:
         raise ValueError("mode must be 'optimized' or 'conventional'")
     if type(check_inputs) is not bool:
         raise TypeError("check_inputs must be bool")
     if type(from_logits) is not bool:
         raise TypeError("from_logits must be bool")
-    return _MODES[mode]
+    if route not in _ROUTES:
+        raise ValueError("route must be 'auto' or 'pieces'")
+    return 2 if (_MODES[mode] == 1 and route == "pieces") else _MODES[mode]
 
 
 def _input_format(first, from_logits: bool) -> int:
@@ -292,7 +299,7 @@ def align(
     emissions: Sequence[Tensor], targets: Sequence[Tensor], *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
     check_inputs: bool = True, emission_validity: Tensor | None = None,
-    from_logits: bool = False,
+    from_logits: bool = False, route: str = "auto",
 ) -> AlignmentBatch:
     """Align known CTC targets to resident emissions; return CUDA frame paths.
 
@@ -309,12 +316,19 @@ def align(
         blank_id: one Python int or ``B`` Python ints (bools rejected).
         mode: ``"optimized"`` (default) or ``"conventional"``.  Conventional
             runs the exact max-plus Viterbi DP (stay > step > skip tie rule).
-            Optimized solves long records in 32-frame pieces joined at legal
-            seams (with repairs, and the conventional DP as fallback); it
-            returns the conventional outputs bit for bit unless the
-            conventional DP meets a tie on its path -- equal scores, or scores
-            closer than the fp32 rounding step of its running sum -- where it
-            returns a path of the same optimal score.
+            Optimized runs, for records of at most 64 labels (16-byte aligned
+            rows), 4096 states and 8192 frames, the window route: the same DP
+            restricted to 64 states that slide up the trellis, certified on
+            the GPU against each frame's greedy bound (the best emission over
+            the transcript alphabet) -- its outputs are then the conventional
+            ones bit for bit, ties included -- with the full DP where the
+            certificate fails.  Other records take the chunked route:
+            32-frame pieces joined at legal seams (with repairs, and the
+            conventional DP as fallback), which returns the conventional
+            outputs bit for bit unless the conventional DP meets a tie on its
+            path -- equal scores, or scores closer than the fp32 rounding
+            step of its running sum -- where it returns a path of at least
+            the same exact score.
         check_inputs: validate target IDs (status 3) and frame feasibility
             (status 4) on the GPU; must be a Python bool.
         emission_validity: optional CUDA bool ``[B]`` mask; False gives status
@@ -325,6 +339,10 @@ def align(
             subtracts the row's log-sum-exp (``log_softmax`` returns the same
             matrices, for inspection).  Not in the reference, whose examples
             call ``torch.log_softmax`` first.
+        route: ``"auto"`` (default) as described under ``mode``, or
+            ``"pieces"``: the chunked route for every record of the
+            optimized mode (the reference's optimized design).  Not in the
+            reference.
 
     Returns:
         AlignmentBatch with packed CUDA outputs.  Failures are recorded in
@@ -336,7 +354,7 @@ def align(
         TypeError: ``check_inputs`` or ``from_logits`` is not a bool.
         RuntimeError: the native library is unavailable or CUDA fails.
     """
-    code = _mode(mode, check_inputs, from_logits)
+    code = _mode(mode, check_inputs, from_logits, route)
     blanks = _metadata(emissions, targets, blank_id)
     fmt = _input_format(emissions[0], from_logits)
     _check_mask(emission_validity, emissions[0].device, len(emissions))
@@ -384,7 +402,7 @@ def align_packed(
     emissions: Tensor, frames, targets: Tensor, tokens, *,
     blank_id: int | Sequence[int] = 0, mode: Mode = "optimized",
     check_inputs: bool = True, emission_validity: Tensor | None = None,
-    from_logits: bool = False,
+    from_logits: bool = False, route: str = "auto",
 ) -> AlignmentBatch:
     """Packed variable-length form of ``align`` (no per-record tensors).
 
@@ -397,7 +415,7 @@ def align_packed(
     of ``align`` on the same records; ``from_logits`` takes a float32 or
     bfloat16 logits matrix.
     """
-    code = _mode(mode, check_inputs, from_logits)
+    code = _mode(mode, check_inputs, from_logits, route)
     fmt = _input_format(emissions, from_logits)
     frames_t, tokens_t, blanks_t = _packed_counts(frames, tokens, blank_id)
     count = frames_t.numel()

@@ -46,7 +46,8 @@ def _run(cmd: list[str], verbose: bool) -> str:
 
 
 def build_library(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    sources = [CSRC / "ffa_kernels.cu", CSRC / "ffa_long.cu", CSRC / "ffa_host.cpp", CSRC / "ffa_noalloc.cu"]
+    sources = [CSRC / "ffa_kernels.cu", CSRC / "ffa_long.cu", CSRC / "ffa_window.cu", CSRC / "ffa_host.cpp",
+               CSRC / "ffa_noalloc.cu"]
     headers = [CSRC / "ffa_internal.h", CSRC / "ffa_device.cuh", INCLUDE / "ffa_b200.h"]
     if not (force or _stale(LIB, sources + headers)):
         return LIB

@@ -49,7 +49,8 @@ int fail(int code, const std::string& message) {
 constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Geometry {
-  bool chunked;  // optimized route: solved in pieces
+  bool window;   // optimized mode: the window DP (ffa_window.cu), full DP as fallback
+  bool chunked;  // optimized mode: solved in pieces
   int cluster;   // > 0: a long record, solved by a cluster of this many CTAs
   int K;         // states per thread
   int nw;        // warps for the DP
@@ -80,8 +81,26 @@ int piece_k(int64_t S) {
   return cost16 <= cost8 ? 16 : 8;
 }
 
-bool chunked_record(const ffa_record& r, bool optimized) {
-  return optimized && r.frames >= ffa::kPieceMinFrames;
+// Bytes per stored element of an input format (ffa_input_format).
+size_t element_bytes(int format) { return format == FFA_INPUT_LOGITS_BF16 ? 2 : 4; }
+
+// TMA row staging needs 16-byte aligned rows and a small row.
+bool row_staged(const ffa_record& r) {
+  return r.vocab * element_bytes(r.format) % 16 == 0 && r.vocab <= ffa::kRowModeMaxVocab &&
+         (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0;
+}
+
+// Records the window DP takes (windows: optimized mode without
+// FFA_FLAG_PIECE_ROUTE): row-staged, at most kMaxStates states, and short
+// enough for their backpointers to stay in shared memory.
+bool window_record(const ffa_record& r, bool windows) {
+  return windows && 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates &&
+         r.frames <= ffa::kWinMaxFrames && row_staged(r);
+}
+
+// Records of the optimized mode solved in pieces: the rest, when long enough.
+bool chunked_record(const ffa_record& r, bool optimized, bool windows) {
+  return optimized && !window_record(r, windows) && r.frames >= ffa::kPieceMinFrames;
 }
 
 // Pieces of kPieceFrames frames; the last one also takes a remainder shorter
@@ -92,7 +111,7 @@ int64_t piece_count(int64_t T) {
   return std::max<int64_t>(C, 1);
 }
 
-Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
+Geometry geometry(const ffa_record& r, bool optimized, bool windows, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
   if (S > ffa::kMaxStates) {
@@ -103,8 +122,10 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
     g.K = 8;
     g.nw = ffa::kMaxWarps;
   } else {
-    g.chunked = chunked_record(r, optimized);
-    g.K = g.chunked ? piece_k(S) : choose_k(S, latency_bound);
+    g.window = window_record(r, windows);
+    g.chunked = chunked_record(r, optimized, windows);
+    // A window record's fallback is a whole-record DP at 8 states per thread.
+    g.K = g.chunked ? piece_k(S) : (g.window ? 8 : choose_k(S, latency_bound));
     const int slot_log2 = g.K == 4 ? 7 : g.K == 8 ? 8 : 9;  // log2(32 K): states per warp
     g.nw = static_cast<int>((S + (int64_t{1} << slot_log2) - 1) >> slot_log2);
   }
@@ -127,9 +148,6 @@ Geometry geometry(const ffa_record& r, bool optimized, bool latency_bound) {
   g.frontier_elems = g.chunked ? g.pieces * ffa::state_stride(S32) : 0;
   return g;
 }
-
-// Bytes per stored element of an input format (ffa_input_format).
-size_t element_bytes(int format) { return format == FFA_INPUT_LOGITS_BF16 ? 2 : 4; }
 
 int check_record(const ffa_record& r, int64_t i, bool need_targets) {
   if (r.format < FFA_INPUT_LOG_PROBS || r.format > FFA_INPUT_LOGITS_BF16)
@@ -172,8 +190,8 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, longs, fill, counters, slots, keys, classes, staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, lse, workspace_bytes;
+  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, slots, keys, classes, staging_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, lse, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
   int format;  // the call's input format
 };
@@ -192,7 +210,7 @@ bool latency_bound(int64_t slots) { return slots <= device_sms(); }
 
 // Sizes of one call.  Everything here is independent of the thread layout
 // (states per thread), so one pass over the records suffices.
-int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLayout* L) {
+int plan_align(const ffa_record* records, int64_t count, bool optimized, bool windows, AlignLayout* L) {
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
@@ -200,12 +218,12 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
-    const Geometry g = geometry(records[i], optimized, false);
+    const Geometry g = geometry(records[i], optimized, windows, false);
     frames += records[i].frames;
     bp_words += g.bp_words;
     map_elems += align_up(static_cast<size_t>(g.map_elems), 8);
     segments += g.segments;
-    fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
+    if (!g.window) fill += (g.segments + ffa::kFillWarps - 1) / ffa::kFillWarps;
     frontier += g.frontier_elems;
     chunked += g.chunked ? 1 : 0;
     longs += g.cluster > 0 ? 1 : 0;
@@ -227,7 +245,11 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 16);
   // Zeroed counters of round 0's plan in the first pass (per record, then
   // per finisher group), uploaded with the descriptors.
-  L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups), 16);
+  // (and the window fallback's list length).
+  L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups + 1), 16);
+  // Window route: one slot per record, at most one CTA per record.
+  L->win_slots = off; off = align_up(off + sizeof(ffa::WinSlot) * count, 16);
+  L->win_ctas = off; off = align_up(off + sizeof(ffa::WinCta) * count, 16);
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
@@ -242,6 +264,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, AlignLa
   L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->finish_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  L->fallback = off; off = align_up(off + sizeof(int32_t) * count, 256);
   // Logits: each frame's row log-sum-exp.
   L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
   L->workspace_bytes = off;
@@ -468,9 +491,10 @@ int ffa_align_query(const ffa_record* records, int64_t count, int mode, int flag
   if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be NULL");
   if (mode != FFA_MODE_CONVENTIONAL && mode != FFA_MODE_OPTIMIZED)
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
-  if (flags & ~FFA_FLAG_CHECK_INPUTS) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  if (flags & ~(FFA_FLAG_CHECK_INPUTS | FFA_FLAG_PIECE_ROUTE)) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
   AlignLayout L{};
-  const int rc = plan_align(records, count, mode == FFA_MODE_OPTIMIZED, &L);
+  const bool optimized = mode == FFA_MODE_OPTIMIZED;
+  const int rc = plan_align(records, count, optimized, optimized && !(flags & FFA_FLAG_PIECE_ROUTE), &L);
   if (rc) return rc;
   sizes->staging_bytes = L.staging_bytes;
   sizes->workspace_bytes = L.workspace_bytes;
@@ -489,10 +513,11 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return fail(FFA_ERR_INVALID_ARGUMENT, "every output buffer except reuse_stats is required");
   if (mode != FFA_MODE_CONVENTIONAL && mode != FFA_MODE_OPTIMIZED)
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
-  if (flags & ~FFA_FLAG_CHECK_INPUTS) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  if (flags & ~(FFA_FLAG_CHECK_INPUTS | FFA_FLAG_PIECE_ROUTE)) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
   const bool optimized = mode == FFA_MODE_OPTIMIZED;
+  const bool windows = optimized && !(flags & FFA_FLAG_PIECE_ROUTE);
   AlignLayout L{};
-  int rc = plan_align(records, count, optimized, &L);
+  int rc = plan_align(records, count, optimized, windows, &L);
   if (rc) return rc;
   if (staging == nullptr || staging_bytes < L.staging_bytes)
     return fail(FFA_ERR_BUFFER_TOO_SMALL, "staging buffer smaller than ffa_align_query reports");
@@ -522,9 +547,11 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // index).
   thread_local std::vector<uint64_t> long_keys;
   long_keys.clear();
+  thread_local std::vector<int32_t> win_records;
+  win_records.clear();
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
-    const Geometry g = geometry(r, optimized, lat);
+    const Geometry g = geometry(r, optimized, windows, lat);
     ffa::RecordDev d{};
     d.emissions = static_cast<const float*>(r.emissions);  // bf16 bits for format 2
     d.targets = r.targets;
@@ -539,11 +566,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     d.nw = static_cast<uint8_t>(g.nw);
     d.kst = static_cast<uint8_t>(g.K);
     d.seg_log2 = static_cast<uint8_t>(g.seg_log2);
-    // TMA row staging needs 16-byte aligned rows and a small row.
-    d.row_mode = (r.vocab * esize % 16 == 0 && r.vocab <= ffa::kRowModeMaxVocab &&
-                  (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0)
-                     ? 1
-                     : 0;
+    d.row_mode = row_staged(r) ? 1 : 0;
     d.frontier_off = frontier_off;
     d.first_piece = static_cast<int32_t>(np);
     d.num_pieces = static_cast<int32_t>(g.pieces);
@@ -556,6 +579,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     }
     if (g.cluster > 0) {
       long_keys.push_back(static_cast<uint64_t>(i));  // keyed below, once the batch is known
+    } else if (g.window) {
+      win_records.push_back(static_cast<int32_t>(i));
     } else if (g.chunked) {
       ++nchunked;
       runs_model.add(cls, g.pieces);
@@ -563,8 +588,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       runs_model.add_whole(cls);
     }
     np += g.pieces;
-    for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
-      fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
+    if (!g.window)
+      for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
+        fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
     out_off += r.frames;
     bp_off += g.bp_words;
     map_off += static_cast<int64_t>(align_up(static_cast<size_t>(g.map_elems), 8));
@@ -572,7 +598,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     frontier_off += g.frontier_elems;
   }
 
-  std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups));
+  std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups + 1));
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
       align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * esize, 128));
@@ -609,6 +635,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     const int32_t i = sorted[k];
     const ffa::RecordDev& d = recs[i];
     if (2 * d.U + 1 > ffa::kMaxStates) continue;  // long records run on clusters
+    if (window_record(records[i], windows)) continue;  // the window route
     const int64_t before = n_first;
     const int32_t step = d.num_pieces > 1 ? run_pieces : 1;
     for (int32_t j = 0; j < d.num_pieces; j += step) order[n_first++] = ffa::SlotRef{i, j};
@@ -713,6 +740,43 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // By launch: row-staged first, then by states per thread and cluster size.
   std::sort(long_keys.begin(), long_keys.end());
   for (size_t k = 0; k < long_keys.size(); ++k) longs[k] = static_cast<int32_t>(long_keys[k] & 0xffffffffu);
+  // Window route: records longest first (by length bucket), packed into CTAs
+  // of at most kWinWarps records -- one record per CTA while the records do
+  // not outnumber the SMs (each then has an SM to itself), else as many as
+  // spread them evenly over the SMs -- with each record's shared-memory slice
+  // (win_layout) side by side, and the launch sized for the largest CTA.
+  auto* wslots = reinterpret_cast<ffa::WinSlot*>(host + L.win_slots);
+  auto* wctas = reinterpret_cast<ffa::WinCta*>(host + L.win_ctas);
+  int64_t n_wcta = 0;
+  uint32_t win_smem = 0;
+  int win_vocab = -1;
+  if (!win_records.empty()) {
+    const int64_t nwin = static_cast<int64_t>(win_records.size());
+    thread_local std::vector<int32_t> bucket_start;
+    bucket_start.assign(kLengthBuckets + 1, 0);
+    auto bucket = [&](int32_t i) { return kLengthBuckets - 1 - length_bucket(static_cast<uint32_t>(recs[i].T)); };
+    for (int32_t i : win_records) ++bucket_start[bucket(i) + 1];
+    for (int b = 0; b < kLengthBuckets; ++b) bucket_start[b + 1] += bucket_start[b];
+    auto* sorted_win = reinterpret_cast<int32_t*>(host + L.keys);  // the first pass is done with the keys
+    for (int32_t i : win_records) sorted_win[bucket_start[bucket(i)]++] = i;
+    const int64_t per_cta = std::clamp<int64_t>((nwin + sms - 1) / sms, 1, ffa::kWinWarps);
+    const uint32_t budget = static_cast<uint32_t>(ffa::kSmemBudget - 1024);
+    uint32_t cur = 0;
+    for (int64_t k = 0; k < nwin; ++k) {
+      const int32_t i = sorted_win[k];
+      const ffa::RecordDev& d = recs[i];
+      win_vocab = (win_vocab < 0 || win_vocab == d.V) ? d.V : 0;
+      const uint32_t need = ffa::win_layout(d.T, d.U, d.V, static_cast<int>(esize)).bytes;
+      if (n_wcta == 0 || wctas[n_wcta - 1].count == per_cta || cur + need > budget) {
+        wctas[n_wcta++] = ffa::WinCta{static_cast<int32_t>(k), 0};
+        cur = 0;
+      }
+      wslots[k] = ffa::WinSlot{i, cur};
+      cur += need;
+      ++wctas[n_wcta - 1].count;
+      win_smem = std::max(win_smem, cur);
+    }
+  }
   const size_t upload_bytes = bundles_off + sizeof(ffa::Bundle) * nb;
   const unsigned row_smem = static_cast<unsigned>(header + max_row_slots * row_slot_bytes);
   const unsigned gather_smem = static_cast<unsigned>(header + ffa::gather_ring_bytes(max_gather_k));
@@ -774,6 +838,26 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return e == cudaSuccess ? FFA_OK : cuda_fail(e, "profiling event");
   };
   if ((rc = mark(FFA_PROFILE_START))) return rc;
+  // Window route: the window DP of every such record, then the full DP of
+  // those whose window was not certified (a device-written list).
+  if (n_wcta > 0) {
+    ffa::WindowParams wp{};
+    wp.recs = fp.recs;
+    wp.slots = reinterpret_cast<const ffa::WinSlot*>(dev + L.win_slots);
+    wp.ctas = reinterpret_cast<const ffa::WinCta*>(dev + L.win_ctas);
+    wp.mask = fp.mask;
+    wp.check_inputs = fp.check_inputs;
+    wp.out = fp.out;
+    wp.lse = fp.lse;
+    wp.fallback_list = reinterpret_cast<int32_t*>(dev + L.fallback);
+    wp.fallback_count = fp.slot_done + count + ffa::kFinishGroups;
+    const int wv = win_vocab > 0 ? win_vocab : 0;
+    err = ffa::launch_window(wp, static_cast<int>(n_wcta), wv, fmt, win_smem, s);
+    if (err != cudaSuccess) return cuda_fail(err, "window launch");
+    err = ffa::launch_window_fallback(fp, wp.fallback_list, wp.fallback_count, static_cast<int>(win_records.size()),
+                                      wv, fmt, static_cast<unsigned>(header + row_slot_bytes), s);
+    if (err != cudaSuccess) return cuda_fail(err, "window fallback launch");
+  }
   // Long records: the conventional DP on one cluster each, one launch per
   // (staging kind, states per thread, cluster size).
   if (!long_keys.empty()) {

@@ -944,14 +944,48 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
   }
 }
 
-// One warp per traceback segment: the warp walks the backpointers from the
-// segment's anchor (path[t-1] = path[t] - bp[t, path[t]], alignment.cu:656-659),
-// then maps states to labels and gathers the selected scores
-// (alignment.cu:662-666); a logits input's score is the same x - z the DPs
-// used (fmt, lse: as in ForwardParams).  Failed records get -1 / -inf
-// (alignment.cu:650-652).
-// For a record of the optimized route, the record's last fill CTA to finish
-// (a counter per record) then folds the objective of a joined path.
+// Traceback segment c of a record by one warp: the warp walks the
+// backpointers from the segment's anchor (path[t-1] = path[t] - bp[t, path[t]],
+// alignment.cu:656-659), then maps states to labels and gathers the selected
+// scores (alignment.cu:662-666); a logits input's score is the same x - z the
+// DPs used (fmt, lse: as in ForwardParams).  A failed record gets -1 / -inf
+// (alignment.cu:650-652).  p: this warp's path scratch (1 << kMaxSegLog2).
+__device__ __forceinline__ void fill_segment(const RecordDev& rec, int record, int c, const uint32_t* bp_arena,
+                                             const int32_t* anchors, const OutputsDev& out, const float* lse,
+                                             int fmt, int32_t* p, int lane) {
+  const int T = rec.T;
+  const int H = 1 << rec.seg_log2;
+  const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
+  if (c >= C) return;
+  int64_t* labels = out.labels + rec.out_off;
+  float* scores = out.scores + rec.out_off;
+  const int a = c * H;
+  const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
+  if (out.status[record] != 0) {
+    for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
+    return;
+  }
+  const int s_end = anchors[rec.seg_off + c];
+  if (lane == 0) p[b - 1 - a] = s_end;
+  warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
+                  [&](int t, int s) { if (lane == 0) p[t - a] = s; });
+  __syncwarp();
+  for (int t = a + lane; t < b; t += 32) {
+    const int s = p[t - a];
+    const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
+    const int64_t i = static_cast<int64_t>(t) * rec.V + label;
+    float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
+                           : rec.emissions[i];
+    if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
+    labels[t] = label;
+    scores[t] = score;
+  }
+  __syncwarp();
+}
+
+// One warp per traceback segment (fill_segment); for a record of the
+// chunked route, the record's last fill CTA to finish (a counter per
+// record) then folds the objective of a joined path.
 __global__ void __launch_bounds__(32 * kFillWarps)
 ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ items,
                const uint32_t* __restrict__ bp_arena, const int32_t* __restrict__ anchors,
@@ -962,36 +996,12 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const FillItem item = items[blockIdx.x];
   const RecordDev rec = recs[item.record];
-  const int c = item.first_seg + warp;
   const int T = rec.T;
   const int H = 1 << rec.seg_log2;
   const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
   int64_t* labels = out.labels + rec.out_off;
   float* scores = out.scores + rec.out_off;
-  if (c < C) {
-    const int a = c * H;
-    const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
-    if (out.status[item.record] != 0) {
-      for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
-    } else {
-      int32_t* p = path[warp];
-      const int s_end = anchors[rec.seg_off + c];
-      if (lane == 0) p[b - 1 - a] = s_end;
-      warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
-                      [&](int t, int s) { if (lane == 0) p[t - a] = s; });
-      __syncwarp();
-      for (int t = a + lane; t < b; t += 32) {
-        const int s = p[t - a];
-        const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
-        const int64_t i = static_cast<int64_t>(t) * rec.V + label;
-        float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
-                               : rec.emissions[i];
-        if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
-        labels[t] = label;
-        scores[t] = score;
-      }
-    }
-  }
+  fill_segment(rec, item.record, item.first_seg + warp, bp_arena, anchors, out, lse, fmt, path[warp], lane);
   if (rec.num_pieces <= 1) return;  // uniform over the CTA
 
   // Objective of a joined record: the path's selected emissions summed in
@@ -1047,6 +1057,55 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
   __syncthreads();
   if (fold_flag) return;
   for (int t = threadIdx.x; t < T; t += 32 * kFillWarps) { labels[t] = -1; scores[t] = -INFINITY; }
+}
+
+// Records of the window route (ffa_window.cu) whose window was not
+// certified: the full conventional DP (alignment.cu:354-523), 4 or 8 states
+// per thread with segment maps, then the traceback and outputs of its
+// segments by the CTA's first kFillWarps warps.  The list and its count are
+// written by the window kernel; CTAs stride over it.
+template <bool kRow, int kV, int kFmt>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+ffa_window_fallback(const __grid_constant__ ForwardParams P, const int32_t* __restrict__ list,
+                    const int32_t* __restrict__ count) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  ForwardShared& sh = *reinterpret_cast<ForwardShared*>(smem_raw);
+  __shared__ int32_t path[kFillWarps][1 << kMaxSegLog2];
+  const int n = *count;
+  int chunk_base = 0;  // emission chunks the slot's ring has carried (row staging)
+  for (int i = static_cast<int>(blockIdx.x); i < n; i += static_cast<int>(gridDim.x)) {
+    const int r = list[i];
+    const RecordDev rec = P.recs[r];
+    SlotCtx x;
+    x.tid = threadIdx.x;
+    x.warp = x.tid >> 5;
+    x.lane = x.tid & 31;
+    x.r = r;
+    x.slot = 0;
+    x.first_warp = 0;
+    x.bar = 1;
+    x.lw = x.warp;
+    x.NT = rec.nw * 32;
+    x.tl = x.tid;
+    __syncthreads();  // the previous record's fill is done with the shared state
+    if (x.tid == 0) {
+      sh.edge = Boundary{-INFINITY, 0};
+      sh.slot_fault[0] = 0;
+    }
+    __syncthreads();
+    if (x.warp < rec.nw) {
+      PieceRun run{0, 0, rec.T, kInitRecord, 1, nullptr, nullptr, -1, -1, false, chunk_base};
+      if (rec.kst == 4) piece_dp<4, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
+      else piece_dp<8, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
+    }
+    chunk_base += (rec.T + kChunkFrames - 1) / kChunkFrames;
+    __syncthreads();  // objective, status, anchors and backpointers are written
+    if (x.warp < kFillWarps) {
+      const int C = static_cast<int>((static_cast<int64_t>(rec.T) + (1 << rec.seg_log2) - 1) >> rec.seg_log2);
+      for (int c = x.warp; c < C; c += kFillWarps)
+        fill_segment(rec, r, c, P.bp, P.anchors, P.out, P.lse, kFmt, path[x.warp], x.lane);
+    }
+  }
 }
 
 // valid[r] was set to 1; any CTA finding NaN or +inf in its chunk clears it.
@@ -1336,6 +1395,12 @@ const FinishKernel kFinishKernels[kVariants] = {
     ffa_finish_route<false, 0, 1>, ffa_finish_route<true, 0, 1>,
     ffa_finish_route<false, 0, 2>, ffa_finish_route<true, 0, 2>};
 
+using FallbackKernel = void (*)(ForwardParams, const int32_t*, const int32_t*);
+const FallbackKernel kFallbackKernels[kVariants] = {
+    ffa_window_fallback<false, 0, 0>, ffa_window_fallback<true, 0, 0>, ffa_window_fallback<true, 32, 0>,
+    ffa_window_fallback<false, 0, 1>, ffa_window_fallback<true, 0, 1>,
+    ffa_window_fallback<false, 0, 2>, ffa_window_fallback<true, 0, 2>};
+
 // Opting in to >48 KiB of dynamic shared memory is per device and kernel:
 // done once, to `bytes`, then every launch fits under it.
 template <typename Kernel>
@@ -1349,6 +1414,18 @@ cudaError_t opt_in(Kernel kernel, std::atomic<uint64_t>& opted, size_t bytes) {
   if (err != cudaSuccess) return err;
   if (bit) opted.fetch_or(bit, std::memory_order_acq_rel);
   return cudaSuccess;
+}
+
+// The current device's SM count (cached per device).
+int device_sm_count() {
+  static std::atomic<int> cache[64];
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 148;
+  int v = device < 64 ? cache[device].load(std::memory_order_relaxed) : 0;
+  if (v > 0) return v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+  if (device < 64) cache[device].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 template <int kFmt, int kN>
@@ -1415,6 +1492,24 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
   ++g_launches;
   kernel<<<count * ctas_per_record, threads, smem_bytes, stream>>>(params, records, device_count, ctas_per_record,
                                                                   smem_bytes);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_window_fallback(const ForwardParams& params, const int32_t* list, const int32_t* count,
+                                   int max_count, int row_vocab, int fmt, unsigned smem_bytes, cudaStream_t stream) {
+  if (max_count <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted[kVariants];
+  const int variant = variant_of(true, row_vocab, fmt);
+  const FallbackKernel kernel = kFallbackKernels[variant];
+  // Static shared memory: the fill warps' path scratch.
+  constexpr size_t kDynamic = kSmemBudget - sizeof(int32_t) * kFillWarps * (1 << kMaxSegLog2);
+  cudaError_t err = opt_in(kernel, opted[variant], kDynamic);
+  if (err != cudaSuccess) return err;
+  if (smem_bytes > kDynamic) return cudaErrorInvalidValue;
+  const int ctas = std::min(max_count, std::max(device_sm_count(), 1));
+  ++g_launches;
+  kernel<<<ctas, kCtaThreads, smem_bytes, stream>>>(params, list, count);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,674 @@
+// ffa_window.cu -- the window route of the optimized mode (sm_100a).
+//
+//   ffa_window_viterbi   one warp per record: the conventional max-plus
+//                        Viterbi DP (alignment.cu:354-523) restricted to a
+//                        64-state window that slides up the trellis, with
+//                        the greedy bound of every frame (the largest
+//                        emission over the transcript alphabet, the maximum
+//                        the reference's greedy_shortcuts finds,
+//                        alignment.cu:29-153) certifying that no state left
+//                        outside the window could have been on the full DP's
+//                        path.  Emission rows arrive by TMA bulk copies;
+//                        backpointers, segment maps and the traceback stay in
+//                        shared memory, and the warp writes the record's
+//                        labels, scores, objective, status and diagnostics.
+//
+// Why the window result is the conventional result.  Let m[t] be the largest
+// emission of frame t over the record's alphabet (every state's label is in
+// it), all m[t] <= 0 (log-probabilities), and M(t) = m[0] + ... + m[t].  Any
+// path's score after frame t is at most its score at t plus m[t+1] + ... +
+// m[T-1]; so a path through state s at frame t scores at most
+// M(T-1) - lambda(t, s), with lambda(t, s) = M(t) - alpha(t, s) >= 0 the
+// "prefix loss".  The window DP runs the reference recurrence (one fp32
+// round-to-nearest add per cell, stay > step > skip by strict '>') on the
+// states inside the window, with -inf for every state outside it, so its
+// values never exceed the full DP's.  A state leaves the window in two ways:
+// slid out below (its prefix loss at that frame is recorded), or reached above
+// the top from the window's top state (that state's prefix loss is recorded:
+// an exit one frame later has at least that loss, less one rounding step).
+// Suppose the full DP's path P leaves the window for the first time at frame
+// t; up to t the window DP made P's decisions with P's exact values (an
+// alternative the window lacks is -inf, no more than its full value, and a
+// full-DP loser stays a loser), so the recorded loss bounds P's prefix loss
+// there.  The full DP's objective is the fp32 sequential sum of P's
+// emissions: at most M(T-1) - lambda_exit plus the rounding of the remaining
+// additions, each below 2^-24 of a partial sum's magnitude -- and with all
+// emissions <= 0 those partial sums lie between 0 and the objective, which
+// is at least the window's own (OPT).  So if every recorded loss exceeds
+// L = M(T-1) - OPT by more than those rounding terms, P never left the
+// window: the window DP returned the full DP's path, scores and objective bit
+// for bit, ties included.  A record that is not so certified -- or holds NaN
+// or +inf in an alphabet column, or a positive emission -- runs the full
+// conventional DP (ffa_window_fallback in ffa_kernels.cu).
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+
+#include "ffa_device.cuh"
+#include "ffa_internal.h"
+
+namespace ffa {
+using namespace dev;
+namespace {
+
+static_assert(kWinStates == 64 && kWinChunk == 32, "window geometry: 32 lanes x 2 states, 32-frame segments");
+static_assert(kWinGreedyChunk % kWinChunk == 0, "greedy chunks are whole segments");
+constexpr unsigned kFull = 0xffffffffu;
+
+// An order-preserving key of a float for an unsigned max (NaN never occurs
+// in a certified record; it only steers the window's position).
+__device__ __forceinline__ unsigned order_key(float v) {
+  const unsigned u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ double warp_min(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmin(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// The reference's greedy chunk test (alignment.cu:93-153) on one chunk of
+// frames [a, b): every frame's greedy label g[t] (the unique finite maximum
+// over the alphabet; 0xff when there is none) must exist, and the label
+// sequence must match exactly one placement s .. s + r[b-1] among the
+// record's states (a legal CTC walk: the state advances by 0 on a repeated
+// label, by 1 into or out of a blank, by 2 between tokens).  Returns 1 for an
+// accepted chunk, 2 for a chunk with several placements, 0 otherwise.  By the
+// whole warp; g, tok and the label position lists (lpos[lstart[c] ..
+// lstart[c+1]): the token positions u with tok[u] == c) in shared memory.
+__device__ int greedy_chunk(const uint8_t* g, const uint8_t* tok, const uint16_t* lpos, const uint16_t* lstart,
+                            int a, int b, int T, int S, int blank, int lane) {
+  bool bad = false;
+  for (int t = a + lane; t < b; t += 32) bad |= g[t] == 0xff;
+  if (__any_sync(kFull, bad)) return 0;
+  // r[t] - r[a] by a warp scan: lane j takes frames a + 4j .. a + 4j + 3.
+  int inc[4], own = 0;
+  bool change = false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int t = a + 4 * lane + q;
+    int d = 0;
+    if (t > a && t < b) {
+      const int x = g[t], y = g[t - 1];
+      d = x == y ? 0 : ((x == blank || y == blank) ? 1 : 2);
+    }
+    change |= d != 0;
+    own += d;
+    inc[q] = own;
+  }
+  int scan = own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kFull, scan, o);
+    if (lane >= o) scan += v;
+  }
+  const int before = scan - own;                 // increments of the frames before this lane's four
+  const int R = __shfl_sync(kFull, scan, 31);    // r[b-1]
+  auto label_of = [&](int s) { return (s & 1) ? static_cast<int>(tok[s >> 1]) : blank; };
+  const int ga = g[a];
+  const int hi_start = a == 0 ? 1 : S - 1;  // the first chunk starts at state 0 or 1 (alignment.cu:119)
+  auto in_range = [&](int s) {
+    const int term = s + R;
+    return s >= 0 && s <= hi_start && term < S && !(b == T && term < S - 2);
+  };
+  int matches = 0;
+  if (!__any_sync(kFull, change)) {
+    // One label throughout: every state holding it in range is a placement.
+    if (ga == blank) {
+      const int lo = b == T ? max(0, S - 2) : 0, hi = min(hi_start, S - 1);
+      matches = hi < lo ? 0 : (hi / 2 - (lo + 1) / 2 + 1);  // even states in [lo, hi]
+    } else {
+      for (int j = lstart[ga] + lane; j < lstart[ga + 1]; j += 32) matches += in_range(2 * lpos[j] + 1) ? 1 : 0;
+      matches = __reduce_add_sync(kFull, matches);
+    }
+    return matches == 1 ? 1 : (matches > 1 ? 2 : 0);
+  }
+  // The start is a token state of label g[a] when g[a] is a token, else the
+  // blank just below a token state of the label of the first change.
+  int first = 1 << 30;
+  for (int k = lane; k < b - a; k += 32)
+    if (k > 0 && g[a + k] != g[a + k - 1]) first = min(first, k);
+  first = __reduce_min_sync(kFull, first);
+  const int lab = ga != blank ? ga : g[a + first];
+  const int shift = ga != blank ? 1 : 0;  // start = 2u + shift for token position u of `lab`
+  const int n1 = lstart[lab + 1];
+  for (int j0 = lstart[lab]; j0 < n1; j0 += 32) {
+    const int j = j0 + lane;
+    unsigned cands = __ballot_sync(kFull, j < n1 && in_range(2 * lpos[j] + shift));
+    while (cands) {
+      const int q = __ffs(cands) - 1;
+      cands &= cands - 1;
+      const int s0 = 2 * lpos[j0 + q] + shift;
+      bool ok = true;  // every label change lands on a state holding the new label
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int t = a + 4 * lane + k;
+        if (t > a && t < b && g[t] != g[t - 1]) {
+          const int st = s0 + before + inc[k];
+          ok &= st < S && label_of(st) == g[t];
+        }
+      }
+      if (__all_sync(kFull, ok)) ++matches;
+    }
+  }
+  return matches == 1 ? 1 : (matches > 1 ? 2 : 0);
+}
+
+// A lane's two states: base + 2 lane (a blank) and base + 2 lane + 1, their
+// scores and their ancestors (each state's path state at the frame before
+// the current traceback segment).
+struct WinState {
+  float a0, a1;
+  int anc0, anc1;
+};
+
+// One frame of the recurrence (alignment.cu:414-429): stay, then step if
+// strictly greater, then skip if strictly greater and legal; one fp32
+// round-to-nearest add per cell.  seg: the frame starts a traceback segment
+// (ancestors restart from the predecessors).  s0: the lane's blank state.
+// Returns the frame's 4 code bits shifted to slot j of the group's word.
+__device__ __forceinline__ uint32_t win_frame(WinState& x, float eb, float et, bool sk1, bool first_lane, int s0,
+                                              bool seg, int j) {
+  float p1 = __shfl_up_sync(kFull, x.a1, 1);  // s-1 for the blank, s-2 for the token
+  int pa = __shfl_up_sync(kFull, x.anc1, 1);
+  if (seg) { x.anc0 = s0; x.anc1 = s0 + 1; pa = s0 - 1; }
+  p1 = first_lane ? -INFINITY : p1;           // below the window: -inf
+  const bool c0 = p1 > x.a0;
+  const bool c1 = x.a0 > x.a1;
+  float b1 = c1 ? x.a0 : x.a1;
+  int n1 = c1 ? x.anc0 : x.anc1;
+  const bool j2 = sk1 && p1 > b1;
+  b1 = j2 ? p1 : b1;
+  n1 = j2 ? pa : n1;
+  const float b0 = c0 ? p1 : x.a0;
+  x.anc0 = c0 ? pa : x.anc0;
+  x.anc1 = n1;
+  x.a0 = __fadd_rn(b0, eb);
+  x.a1 = __fadd_rn(b1, et);
+  return ((c0 ? 1u : 0u) | (j2 ? 8u : (c1 ? 4u : 0u))) << (4 * j);
+}
+
+// The window DP of one record by one warp.  sm: the record's slice of the
+// CTA's dynamic shared memory (WinLayout); full: its kWinRing mbarriers.
+template <int kFmt, int kV>
+__device__ __forceinline__ void window_record(const WindowParams& P, int r, unsigned char* sm,
+                                              unsigned long long* full, int lane) {
+  using In = Input<kFmt>;
+  using Elem = typename In::Elem;
+  const RecordDev rec = P.recs[r];
+  const int T = rec.T, U = rec.U, blank = rec.blank;
+  const int V = kV > 0 ? kV : rec.V;
+  const int S = 2 * U + 1;
+  const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)));
+  Elem* ring = reinterpret_cast<Elem*>(sm + L.ring);
+  uint8_t* tok = sm + L.tok;
+  uint16_t* lpos = reinterpret_cast<uint16_t*>(sm + L.lpos);
+  uint16_t* lstart = reinterpret_cast<uint16_t*>(sm + L.lstart);
+  uint32_t* bp = reinterpret_cast<uint32_t*>(sm + L.bp);
+  uint16_t* gb = reinterpret_cast<uint16_t*>(sm + L.gb);
+  uint16_t* map = reinterpret_cast<uint16_t*>(sm + L.map);
+  int16_t* anc = reinterpret_cast<int16_t*>(sm + L.anc);
+  float* stash = reinterpret_cast<float*>(sm + L.stash);
+  uint16_t* path = reinterpret_cast<uint16_t*>(sm + L.path);
+  uint8_t* greedy = sm + L.greedy;
+  int64_t* labels = P.out.labels + rec.out_off;
+  float* scores = P.out.scores + rec.out_off;
+  const float kNegInf = -INFINITY;
+
+  // ---- status: mask, then target validation (alignment.cu:836, 852-874);
+  //      the transcript's label columns into shared memory, its alphabet ----
+  int status = (P.mask != nullptr && !P.mask[r]) ? 2 : 0;
+  int bad = 0, rep = 0;
+  unsigned alo = 0, ahi = 0;  // the transcript alphabet as a bit mask (V <= 64)
+  int64_t carry = 0;          // the token before this 32-token block
+#pragma unroll 4
+  for (int base = 0; base < U; base += 32) {
+    const int k = base + lane;
+    const int64_t token = k < U ? rec.targets[k] : 0;
+    int64_t prev = __shfl_up_sync(kFull, token, 1);
+    if (lane == 0) prev = carry;
+    carry = __shfl_sync(kFull, token, 31);
+    if (k < U) {
+      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
+      if (k > 0) rep += token == prev ? 1 : 0;
+      const int c = clamp_label(token, V);
+      tok[k] = static_cast<uint8_t>(c);
+      if (c < 32) alo |= 1u << c; else ahi |= 1u << (c - 32);
+    }
+  }
+  if (P.check_inputs) {
+    bad = __reduce_or_sync(kFull, bad);
+    rep = __reduce_add_sync(kFull, rep);
+    if (bad) status = 3;
+    else if (static_cast<int64_t>(U) + rep > T) status = 4;
+  }
+  alo = __reduce_or_sync(kFull, alo);
+  ahi = __reduce_or_sync(kFull, ahi);
+  if (blank < 32) alo |= 1u << blank; else ahi |= 1u << (blank - 32);
+  if (lane == 0) {
+    // Diagnostics start at zero (alignment.py:101-129).
+    P.out.stitched[r] = 0;
+    P.out.repair_passes[r] = 0;
+    P.out.repaired_frames[r] = 0;
+    for (int j = 0; j < 3; ++j) { P.out.shortcut_stats[3 * r + j] = 0; P.out.routing_stats[3 * r + j] = 0; }
+    if (P.out.reuse_stats) for (int j = 0; j < 4; ++j) P.out.reuse_stats[4 * r + j] = 0;
+  }
+  if (status >= 2) {
+    if (lane == 0) { P.out.status[r] = status; P.out.objective[r] = -INFINITY; }
+    for (int t = lane; t < T; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
+    return;
+  }
+  __syncwarp();
+
+  // ---- emission rows: kWinChunk-row TMA copies into a kWinRing ring ----
+  const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
+  const int nchunks = (T + kWinChunk - 1) / kWinChunk;
+  auto issue = [&](int c) {  // by lane 0
+    const int rows = min(kWinChunk, T - c * kWinChunk);
+    const unsigned bytes = static_cast<unsigned>(rows) * V * static_cast<unsigned>(sizeof(Elem));
+    unsigned long long* bar = &full[c % kWinRing];
+    mbar_expect_tx(bar, bytes);
+    tma_bulk_load(ring + (c % kWinRing) * kWinChunk * V, e + static_cast<int64_t>(c) * kWinChunk * V, bytes, bar);
+  };
+  if (lane == 0) {
+    for (int k = 0; k < kWinRing; ++k) mbar_init(&full[k], 1);
+    fence_mbar_init();
+    for (int c = 0; c < kWinRing && c < nchunks; ++c) issue(c);
+  }
+  {
+    // Token positions grouped by label (a counting sort by the warp) for the
+    // greedy chunks' placement search.  Lanes holding equal labels form a
+    // group (match_any); the group's first lane updates the label's count.
+    uint16_t* cursor = lstart + (V + 1);
+    for (int c = lane; c <= V; c += 32) cursor[c] = 0;
+    __syncwarp();
+    for (int base = 0; base < U; base += 32) {
+      const int k = base + lane;
+      const int c = k < U ? tok[k] : 0x100 + lane;
+      const unsigned grp = __match_any_sync(kFull, c);
+      if (k < U && lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
+      __syncwarp();
+    }
+    // Exclusive prefix over labels (V <= 64: two per lane).
+    const int c0 = 2 * lane, c1 = c0 + 1;
+    const int n0 = c0 < V ? cursor[c0] : 0, n1 = c1 < V ? cursor[c1] : 0;
+    int incl = n0 + n1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - n0 - n1;
+    __syncwarp();
+    if (c0 <= V) { lstart[c0] = static_cast<uint16_t>(excl); cursor[c0] = static_cast<uint16_t>(excl); }
+    if (c1 <= V) { lstart[c1] = static_cast<uint16_t>(excl + n0); cursor[c1] = static_cast<uint16_t>(excl + n0); }
+    if (lane == 0) lstart[V] = static_cast<uint16_t>(U);  // (V = 64 lies past the lanes' pairs)
+    __syncwarp();
+    for (int base = 0; base < U; base += 32) {
+      const int k = base + lane;
+      const int c = k < U ? tok[k] : 0x100 + lane;
+      const unsigned grp = __match_any_sync(kFull, c);
+      const int at = k < U ? cursor[c] + __popc(grp & ((1u << lane) - 1u)) : 0;
+      __syncwarp();
+      if (k < U) {
+        lpos[at] = static_cast<uint16_t>(k);
+        if (lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
+      }
+      __syncwarp();
+    }
+  }
+  LseStream lse{};
+  if constexpr (In::kLogits) lse.start(P.lse + rec.out_off, T, 0, lane);
+  const int rot = lane % V;
+  const bool full_alphabet = V == 32 && alo == kFull;
+
+  // ---- the window: lane l owns states base + 2l (a blank) and base + 2l + 1 ----
+  int base = 0;
+  WinState x{kNegInf, kNegInf, 0, 0};
+  int col1 = blank;  // label column of state base + 2l + 1
+  bool v0 = false, v1 = false, sk1 = false;
+  auto label_of = [&](int s) { return (s & 1) ? static_cast<int>(tok[s >> 1]) : blank; };
+  auto lane_states = [&]() {
+    const int s1 = base + 2 * lane + 1;
+    v0 = s1 - 1 < S;
+    v1 = s1 < S;
+    col1 = v1 ? label_of(s1) : blank;
+    const int u = s1 >> 1;  // skip s1-2 -> s1: a token unlike the blank and its predecessor (alignment.cu:407)
+    sk1 = v1 && u >= 1 && tok[u] != blank && tok[u] != tok[u - 1];
+  };
+  lane_states();
+  const bool first_lane = lane == 0, top_lane = lane == 31;
+
+  double Mbase = 0.0;     // sum of the greedy bounds m of the frames before this chunk
+  double esc = INFINITY;  // smallest recorded prefix loss of a state that left the window (this lane's)
+  bool poison = false, positive = false, fault = false;
+  // A state s at frame t can still reach a terminal state (S-2 or S-1).
+  auto reaches_end = [&](int s, int t) { return s + 2 * (T - 1 - t) >= S - 2; };
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * kWinChunk;
+    const int rows = min(kWinChunk, T - t0);
+    if (!fault && !mbar_wait(&full[c % kWinRing], (c / kWinRing) & 1)) fault = true;
+    fault = __any_sync(kFull, fault);
+    if (fault) break;
+    const Elem* chunk = ring + (c % kWinRing) * kWinChunk * V;
+    if constexpr (In::kLogits)
+      if (c > 0) lse.advance(t0, lane);
+    // Greedy bound of frame t0 + lane: the largest emission over the
+    // alphabet, whether it is the unique maximum (and its column), and
+    // whether an alphabet column holds NaN or +inf.  Columns are read in an
+    // order rotated by the lane, against bank conflicts.
+    float m = 0.0f;
+    if (lane < rows) {
+      const Elem* row = chunk + lane * V;
+      float best = -INFINITY;
+      bool nonfinite = false;
+      int arg = 0, ties = 0;
+      if constexpr (kV == 32 && kFmt == 0) {
+        float xs[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int quad = (q + lane) & 7;
+          const float4 v4 = reinterpret_cast<const float4*>(row)[quad];
+          xs[4 * q] = v4.x; xs[4 * q + 1] = v4.y; xs[4 * q + 2] = v4.z; xs[4 * q + 3] = v4.w;
+        }
+        const unsigned amask = (alo >> (4 * (lane & 7))) | (alo << ((32 - 4 * (lane & 7)) & 31));
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          // xs[k] is column (k + 4 lane) mod 32; amask bit k says whether it is in the alphabet.
+          const bool in = full_alphabet || ((amask >> k) & 1u);
+          nonfinite |= in && !(xs[k] < INFINITY);
+          best = fmaxf(best, in ? xs[k] : -INFINITY);
+        }
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const bool in = full_alphabet || ((amask >> k) & 1u);
+          const bool hit = in && xs[k] == best;
+          ties += hit ? 1 : 0;
+          arg = hit ? ((k + 4 * lane) & 31) : arg;
+        }
+      } else {
+        for (int k = 0; k < V; ++k) {
+          int col = k + rot;
+          if (col >= V) col -= V;
+          const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
+          if (!in) continue;
+          const float v = elem_to_float(row[col]);
+          nonfinite |= !(v < INFINITY);
+          if (v > best) { best = v; arg = col; ties = 1; }
+          else if (v == best) ++ties;
+        }
+      }
+      m = best;
+      if constexpr (In::kLogits) {
+        m = __fsub_rn(best, lse.cur);
+        nonfinite |= !isfinite(lse.cur);
+      }
+      poison |= nonfinite;
+      positive |= m > 0.0f;
+      // The greedy label (alignment.cu:60-91): the unique finite maximum (a
+      // NaN column never compares greater or equal, so it drops out there).
+      greedy[t0 + lane] = (ties == 1 && isfinite(m)) ? static_cast<uint8_t>(arg) : 0xff;
+    }
+    // M of each frame of the chunk: lane f holds m[t0] + ... + m[t0 + f] (fp64).
+    double Mpre = static_cast<double>(m);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(kFull, Mpre, o);
+      if (lane >= o) Mpre += v;
+    }
+    for (int g = 0; g < kWinChunk / 8 && 8 * g < rows; ++g) {
+      const int tg = t0 + 8 * g;
+      if (tg > 0 && base + kWinStates < S) {
+        // Slide: while the best state that can still reach the end sits at or
+        // above base + kWinHigh, drop the bottom kWinSlide states (recording
+        // their prefix losses at frame tg-1) and take kWinSlide new ones.
+        const double Mprev = tg > t0 ? Mbase + __shfl_sync(kFull, Mpre, tg - 1 - t0) : Mbase;
+        for (int it = 0; it < 2 && base + kWinStates < S; ++it) {
+          const int s0 = base + 2 * lane;
+          unsigned key = 0;
+          if (v0 && reaches_end(s0, tg - 1)) key = max(key, order_key(x.a0));
+          if (v1 && reaches_end(s0 + 1, tg - 1)) key = max(key, order_key(x.a1));
+          const unsigned kmax = __reduce_max_sync(kFull, key);
+          if (kmax <= order_key(kNegInf)) break;
+          const int best_lane = __ffs(__ballot_sync(kFull, key == kmax)) - 1;
+          if (2 * best_lane < kWinHigh) break;
+          if (lane < kWinSlide / 2) {
+            if (v0 && reaches_end(s0, tg - 1)) esc = fmin(esc, Mprev - static_cast<double>(x.a0));
+            if (v1 && reaches_end(s0 + 1, tg - 1)) esc = fmin(esc, Mprev - static_cast<double>(x.a1));
+          }
+          constexpr int kShift = kWinSlide / 2;
+          x.a0 = __shfl_down_sync(kFull, x.a0, kShift);
+          x.a1 = __shfl_down_sync(kFull, x.a1, kShift);
+          x.anc0 = __shfl_down_sync(kFull, x.anc0, kShift);
+          x.anc1 = __shfl_down_sync(kFull, x.anc1, kShift);
+          if (lane >= 32 - kShift) { x.a0 = kNegInf; x.a1 = kNegInf; }
+          base += kWinSlide;
+          lane_states();
+        }
+      }
+      if (lane == 0) gb[tg >> 3] = static_cast<uint16_t>(base);
+      // While states lie above the window, the top state's score is kept at
+      // every frame (an exit above the window at the next frame scores at
+      // most that plus the next frame's bound); otherwise -inf.
+      const bool open = base + kWinStates < S;
+      const bool keep_top = top_lane && open;
+      if (top_lane && !open)
+        for (int j = 0; j < 8; ++j) stash[8 * g + j] = kNegInf;
+      const int s0 = base + 2 * lane;
+      const bool seg0 = g == 0;  // the chunk's first frame starts a traceback segment
+      const Elem* grow = chunk + 8 * g * V;
+      uint32_t w = 0;  // this lane's jump codes of the group: 4 bits a frame
+      auto emissions_of = [&](int j, float& eb, float& et) {
+        const Elem* row = grow + j * V;
+        eb = elem_to_float(row[blank]);
+        et = elem_to_float(row[col1]);
+        if constexpr (In::kLogits) {
+          const float z = lse.at(8 * g + j);
+          eb = __fsub_rn(eb, z);
+          et = __fsub_rn(et, z);
+        }
+      };
+      if (tg > 0 && tg + 8 <= T) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float eb, et;
+          emissions_of(j, eb, et);
+          w |= win_frame(x, eb, et, sk1, first_lane, s0, seg0 && j == 0, j);
+          if (keep_top) stash[8 * g + j] = x.a1;
+        }
+      } else {
+        for (int j = 0; j < 8 && tg + j < T; ++j) {
+          float eb, et;
+          emissions_of(j, eb, et);
+          if (tg + j == 0) {
+            // Frame 0: alpha[s] = e[0, l[s]] for s < 2 (alignment.cu:409).
+            x.a0 = first_lane ? eb : kNegInf;
+            x.a1 = (first_lane && S > 1) ? et : kNegInf;
+            x.anc0 = s0;
+            x.anc1 = s0 + 1;
+          } else {
+            w |= win_frame(x, eb, et, sk1, first_lane, s0, seg0 && j == 0, j);
+          }
+          if (keep_top) stash[8 * g + j] = x.a1;
+        }
+      }
+      bp[(tg >> 3) * 32 + lane] = w;
+      const int tl = min(tg + 8, T) - 1;
+      if ((tl & (kWinChunk - 1)) == kWinChunk - 1 || tl == T - 1) {
+        // Segment map: each window state's path state at the frame before
+        // the segment.
+        uint16_t* mp = map + (tl / kWinChunk) * kWinStates + 2 * lane;
+        mp[0] = static_cast<uint16_t>(x.anc0);
+        mp[1] = static_cast<uint16_t>(x.anc1);
+      }
+    }
+    __syncwarp();  // the top state's scores are in the stash; every lane has read the ring entry
+    if (lane < rows) esc = fmin(esc, (Mbase + Mpre) - static_cast<double>(stash[lane]));
+    Mbase += __shfl_sync(kFull, Mpre, 31);
+    __syncwarp();
+    if (lane == 0 && c + kWinRing < nchunks) {
+      fence_proxy_async();
+      issue(c + kWinRing);
+    }
+  }
+  if (fault) {
+    // A bounded wait gave up: status 5; give the copies still in flight a
+    // short, bounded chance to land before the shared memory goes away.
+    if (lane == 0) {
+      for (int c = max(0, nchunks - kWinRing); c < nchunks; ++c)
+        mbar_wait(&full[c % kWinRing], (c / kWinRing) & 1, kDrainNs);
+      P.out.status[r] = kStatusDeviceFault;
+      P.out.objective[r] = -INFINITY;
+    }
+    for (int t = lane; t < T; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
+    return;
+  }
+
+  // ---- terminal rule (alignment.cu:496-510) and the certificate ----
+  const double M = Mbase;
+  const bool covers = base + kWinStates >= S;  // S-1 and S-2 inside the window
+  const int l_last = min(max((S - 1 - base) >> 1, 0), 31);
+  const int l_prev = min(max((S - 3 - base) >> 1, 0), 31);
+  const float vlast = __shfl_sync(kFull, x.a0, l_last);
+  const float vprev = S > 1 ? __shfl_sync(kFull, x.a1, l_prev) : kNegInf;
+  const bool take_prev = S > 1 && vprev >= vlast;
+  const float opt = take_prev ? vprev : vlast;
+  const int term = take_prev ? S - 2 : S - 1;
+  poison = __any_sync(kFull, poison);
+  positive = __any_sync(kFull, positive);
+  const double exit_loss = warp_min(esc);
+  const double loss = M - static_cast<double>(opt);
+  // Rounding: T additions along the full DP's path, each within 2^-24 of
+  // |OPT|; one more for an exit above the window bounded through the top
+  // state; the fp64 sums of m.
+  const double aopt = fabs(static_cast<double>(opt)), am = fabs(M);
+  const double margin =
+      static_cast<double>(T) * (ldexp(aopt, -23) + ldexp(am, -50)) + ldexp(aopt + am, -21) + 1e-9;
+  const bool certified =
+      covers && !poison && !positive && isfinite(opt) && isfinite(M) && exit_loss > loss + margin;
+
+  {
+    // Greedy chunk statistics (alignment.cu:130-153), whichever DP solves the
+    // record: accepted chunks, their frames, chunks with several placements.
+    __syncwarp();
+    int64_t accepted = 0, frames = 0, multiple = 0;
+    for (int a = 0; a < T; a += kWinGreedyChunk) {
+      const int b = min(T, a + kWinGreedyChunk);
+      const int verdict = greedy_chunk(greedy, tok, lpos, lstart, a, b, T, S, blank, lane);
+      if (verdict == 1) { ++accepted; frames += b - a; }
+      if (verdict == 2) ++multiple;
+    }
+    if (lane == 0) {
+      P.out.shortcut_stats[3 * r + 0] = accepted;
+      P.out.shortcut_stats[3 * r + 1] = frames;
+      P.out.shortcut_stats[3 * r + 2] = multiple;
+    }
+  }
+  if (!certified) {
+    // The full conventional DP takes the record (ffa_window_fallback); the
+    // reference's routing state 2 is its completed early fallback.
+    if (lane == 0) {
+      P.out.routing_stats[3 * r] = 2;
+      P.fallback_list[atomicAdd(P.fallback_count, 1)] = r;
+    }
+    return;
+  }
+
+  // ---- traceback in shared memory ----
+  const int nseg = nchunks;
+  if (lane == 0) {
+    // Anchors: the path's state at each segment's last frame, from the maps.
+    int s = term;
+    for (int g = nseg - 1; g >= 0; --g) {
+      anc[g] = static_cast<int16_t>(s);
+      if (g > 0) {
+        const int tl = min(T, (g + 1) * kWinChunk) - 1;
+        const int k = min(max(s - static_cast<int>(gb[tl >> 3]), 0), kWinStates - 1);
+        s = map[g * kWinStates + k];
+      }
+    }
+  }
+  __syncwarp();
+  // Lane j walks segments j, j + 32, ... back from their anchors
+  // (path[t-1] = path[t] - jump(t, path[t]), alignment.cu:656-659).
+  for (int g = lane; g < nseg; g += 32) {
+    const int t_lo = g * kWinChunk;
+    const int t_hi = min(T, t_lo + kWinChunk) - 1;
+    int s = anc[g];
+    path[t_hi] = static_cast<uint16_t>(s);
+    for (int t = t_hi; t > t_lo; --t) {
+      const int k = min(max(s - static_cast<int>(gb[t >> 3]), 0), kWinStates - 1);
+      const uint32_t word = bp[(t >> 3) * 32 + (k >> 1)];
+      s -= static_cast<int>((word >> (4 * (t & 7) + 2 * (k & 1))) & 3u);
+      path[t - 1] = static_cast<uint16_t>(s);
+    }
+  }
+  __syncwarp();
+  // Labels and the selected scores (alignment.cu:662-666), frame-coalesced.
+#pragma unroll 4
+  for (int t = lane; t < T; t += 32) {
+    const int label = label_of(min(static_cast<int>(path[t]), S - 1));
+    const int64_t i = static_cast<int64_t>(t) * V + label;
+    float score = elem_to_float(e[i]);
+    if constexpr (In::kLogits) score = __fsub_rn(score, P.lse[rec.out_off + t]);
+    labels[t] = label;
+    scores[t] = score;
+  }
+  if (lane == 0) {
+    P.out.objective[r] = opt;
+    P.out.status[r] = 0;
+  }
+}
+
+template <int kFmt, int kV>
+__global__ void __launch_bounds__(32 * kWinWarps)
+ffa_window_viterbi(const __grid_constant__ WindowParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ unsigned long long bars[kWinWarps][kWinRing];
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const WinCta cta = P.ctas[blockIdx.x];
+  if (warp >= cta.count) return;
+  const WinSlot slot = P.slots[cta.first + warp];
+  window_record<kFmt, kV>(P, slot.record, smem_raw + slot.smem_off, bars[warp], lane);
+}
+
+using WindowKernel = void (*)(WindowParams);
+// Variants: log-probabilities with V = 32 specialised, any row vocabulary,
+// fp32 and bf16 logits.
+constexpr int kWindowVariants = 4;
+const WindowKernel kWindowKernels[kWindowVariants] = {
+    ffa_window_viterbi<0, 32>, ffa_window_viterbi<0, 0>, ffa_window_viterbi<1, 0>, ffa_window_viterbi<2, 0>};
+
+}  // namespace
+
+cudaError_t launch_window(const WindowParams& params, int num_ctas, int row_vocab, int fmt, unsigned smem_bytes,
+                          cudaStream_t stream) {
+  if (num_ctas <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  const int variant = fmt == 0 ? (row_vocab == 32 ? 0 : 1) : 1 + fmt;
+  static std::atomic<uint64_t> opted[kWindowVariants];
+  const WindowKernel kernel = kWindowKernels[variant];
+  // The CTA's static shared memory (its mbarriers) stays under 1 KiB.
+  constexpr size_t kStatic = 1024;
+  static_assert(sizeof(unsigned long long) * kWinWarps * kWinRing <= kStatic, "window static shared memory");
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmemBudget - kStatic));
+    if (err != cudaSuccess) return err;
+    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
+  }
+  if (smem_bytes > kSmemBudget - kStatic) return cudaErrorInvalidValue;
+  count_launch();
+  kernel<<<num_ctas, 32 * kWinWarps, smem_bytes, stream>>>(params);
+  return cudaGetLastError();
+}
+
+}  // namespace ffa

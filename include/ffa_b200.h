@@ -60,11 +60,24 @@ typedef enum ffa_status {
 
 typedef enum ffa_mode {
   FFA_MODE_CONVENTIONAL = 0, /* full-record max-plus Viterbi DP */
-  FFA_MODE_OPTIMIZED = 1     /* greedy/chunked route with exact DP fallback */
+  FFA_MODE_OPTIMIZED = 1     /* greedy-bounded window DP / chunked route, exact DP fallback */
 } ffa_mode;
 
+/* Optimized mode solves a record whose rows can be TMA-staged (vocab <= 64,
+ * 16-byte aligned rows), with at most 4096 states and 8192 frames, by the
+ * window route: the conventional DP restricted to a 64-state window that
+ * slides up the trellis, certified on the device against the greedy bound of
+ * every frame (the largest emission over the transcript alphabet, the
+ * maximum the reference's greedy_shortcuts finds, alignment.cu:29-153) --
+ * its outputs are then the conventional DP's, bit for bit, ties included --
+ * and the full conventional DP where the certificate fails.  Every other
+ * record of the optimized mode (or every record, with FFA_FLAG_PIECE_ROUTE)
+ * takes the chunked route of the reference's optimized mode
+ * (alignment.cu:163-228, 525-592): relaxed 32-frame pieces joined at legal
+ * seams, repairs of merged regions, the full DP as fallback. */
 enum {
-  FFA_FLAG_CHECK_INPUTS = 1 /* validate target IDs and frame feasibility on the device */
+  FFA_FLAG_CHECK_INPUTS = 1, /* validate target IDs and frame feasibility on the device */
+  FFA_FLAG_PIECE_ROUTE = 2   /* optimized mode: the chunked route for every record */
 };
 
 /* Limits (alignment.py:237, 249-250).  The reference stops at 2047 tokens
@@ -103,13 +116,18 @@ typedef struct ffa_record {
 } ffa_record;
 
 /* Caller-allocated device outputs, packed in record order without padding
- * (reference AlignmentBatch fields, alignment.py:138-148). */
+ * (reference AlignmentBatch fields, alignment.py:138-148).  Diagnostics of
+ * the window route: stitched, repair_passes, repaired_frames and reuse_stats
+ * are 0; shortcut_stats holds the reference's greedy chunk counts (accepted
+ * 128-frame chunks, their frames, chunks with several placements); the
+ * routing state routing_stats[i, 0] is 2 when the record ran the full DP as
+ * fallback (the reference's completed early fallback), else 0. */
 typedef struct ffa_outputs {
   int64_t* labels;          /* [sum T] vocabulary id per frame; -1 for failed records */
   float* scores;            /* [sum T] selected emission per frame; -inf for failed */
   int32_t* status;          /* [B] */
   float* objective;         /* [B] native accumulated path score */
-  int32_t* stitched;        /* [B] 1 = optimized route joined chunk paths */
+  int32_t* stitched;        /* [B] 1 = the chunked route joined piece paths */
   int32_t* repair_passes;   /* [B] */
   int64_t* repaired_frames; /* [B] */
   int64_t* shortcut_stats;  /* [B, 3] */
