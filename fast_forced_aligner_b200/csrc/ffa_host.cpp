@@ -56,6 +56,7 @@ struct Geometry {
   int nw;        // warps for the DP
   int seg_log2;  // traceback segment length
   int64_t segments;
+  int64_t greedy_items;  // window records: greedy pass chunks
   int64_t bp_words;
   int64_t map_elems;
   int64_t pieces;
@@ -140,6 +141,7 @@ Geometry geometry(const ffa_record& r, bool optimized, bool windows, bool latenc
       ++g.seg_log2;
   }
   g.segments = (r.frames + (int64_t{1} << g.seg_log2) - 1) >> g.seg_log2;
+  g.greedy_items = g.window ? (r.frames + ffa::kGreedyChunk - 1) / ffa::kGreedyChunk : 0;
   // Backpointer rows, frontiers and maps do not depend on the thread layout.
   const int S32 = static_cast<int>(S);
   g.bp_words = r.frames * ffa::bp_row_words(S32);
@@ -190,9 +192,11 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, slots, keys, classes, staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, lse, workspace_bytes;
-  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items;
+  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, slots, keys, classes,
+      staging_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, lse,
+      workspace_bytes;
+  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy;
   int format;  // the call's input format
 };
 
@@ -214,7 +218,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0, longs = 0;
+          pieces = 0, longs = 0, greedy = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
@@ -228,6 +232,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
     chunked += g.chunked ? 1 : 0;
     longs += g.cluster > 0 ? 1 : 0;
     pieces += g.pieces;
+    greedy += g.greedy_items;
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
@@ -250,6 +255,10 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
   // Window route: one slot per record, at most one CTA per record.
   L->win_slots = off; off = align_up(off + sizeof(ffa::WinSlot) * count, 16);
   L->win_ctas = off; off = align_up(off + sizeof(ffa::WinCta) * count, 16);
+  // Greedy pass: its items, and each record's first item.
+  L->greedy_items = off; off = align_up(off + sizeof(ffa::GreedyItem) * greedy, 16);
+  L->greedy_first = off; off = align_up(off + sizeof(int32_t) * count, 16);
+  L->num_greedy = greedy;
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
@@ -265,6 +274,8 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
   L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->finish_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->fallback = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  L->bound = off; off = align_up(off + (greedy ? sizeof(float) * frames : 0), 256);
+  L->verdicts = off; off = align_up(off + greedy, 256);
   // Logits: each frame's row log-sum-exp.
   L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
   L->workspace_bytes = off;
@@ -549,6 +560,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   long_keys.clear();
   thread_local std::vector<int32_t> win_records;
   win_records.clear();
+  auto* gitems = reinterpret_cast<ffa::GreedyItem*>(host + L.greedy_items);
+  auto* gfirst = reinterpret_cast<int32_t*>(host + L.greedy_first);
+  int64_t ngreedy = 0;
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, windows, lat);
@@ -581,6 +595,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       long_keys.push_back(static_cast<uint64_t>(i));  // keyed below, once the batch is known
     } else if (g.window) {
       win_records.push_back(static_cast<int32_t>(i));
+      gfirst[i] = static_cast<int32_t>(ngreedy);
+      for (int64_t k = 0; k < g.greedy_items; ++k)
+        gitems[ngreedy++] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
     } else if (g.chunked) {
       ++nchunked;
       runs_model.add(cls, g.pieces);
@@ -841,6 +858,22 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // Window route: the window DP of every such record, then the full DP of
   // those whose window was not certified (a device-written list).
   if (n_wcta > 0) {
+    const int wv = win_vocab > 0 ? win_vocab : 0;
+    // The greedy pass streams every row of the window records once: it is
+    // the launch the forward profiling events bracket.
+    ffa::GreedyParams gp{};
+    gp.recs = fp.recs;
+    gp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items);
+    gp.count = ngreedy;
+    gp.lse = fp.lse;
+    gp.bound = reinterpret_cast<float*>(dev + L.bound);
+    gp.verdicts = reinterpret_cast<uint8_t*>(dev + L.verdicts);
+    if (g_profile_before != nullptr && (err = cudaEventRecord(g_profile_before, s)) != cudaSuccess)
+      return cuda_fail(err, "profiling event");
+    err = ffa::launch_greedy(gp, wv, fmt, s);
+    if (err != cudaSuccess) return cuda_fail(err, "greedy pass launch");
+    if (g_profile_after != nullptr && (err = cudaEventRecord(g_profile_after, s)) != cudaSuccess)
+      return cuda_fail(err, "profiling event");
     ffa::WindowParams wp{};
     wp.recs = fp.recs;
     wp.slots = reinterpret_cast<const ffa::WinSlot*>(dev + L.win_slots);
@@ -849,9 +882,11 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     wp.check_inputs = fp.check_inputs;
     wp.out = fp.out;
     wp.lse = fp.lse;
+    wp.bound = gp.bound;
+    wp.verdicts = gp.verdicts;
+    wp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
     wp.fallback_list = reinterpret_cast<int32_t*>(dev + L.fallback);
     wp.fallback_count = fp.slot_done + count + ffa::kFinishGroups;
-    const int wv = win_vocab > 0 ? win_vocab : 0;
     err = ffa::launch_window(wp, static_cast<int>(n_wcta), wv, fmt, win_smem, s);
     if (err != cudaSuccess) return cuda_fail(err, "window launch");
     err = ffa::launch_window_fallback(fp, wp.fallback_list, wp.fallback_count, static_cast<int>(win_records.size()),
@@ -896,7 +931,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   fp.bundles = dbundles + nb_row;
   err = ffa::launch_forward(fp, static_cast<int>(nb - nb_row), false, 0, fmt, gather_smem, s);
   if (err != cudaSuccess) return cuda_fail(err, "forward launch");
-  if (g_profile_after != nullptr) {
+  if (g_profile_after != nullptr && n_wcta == 0) {  // (with window records: around the greedy pass)
     err = cudaEventRecord(g_profile_after, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }

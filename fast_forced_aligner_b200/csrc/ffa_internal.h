@@ -272,31 +272,52 @@ size_t long_header_bytes();
 cudaError_t launch_upload(const void* mapped_src, void* dst, size_t bytes, cudaStream_t stream);
 
 // ---- Window route of the optimized mode (ffa_window.cu) -------------------
-// A record runs the conventional DP restricted to a window of kWinStates
-// consecutive states that slides up the trellis, one warp per record, 2
-// states per lane.  Each frame also takes the greedy bound m[t] -- the
-// largest emission over the record's transcript alphabet (the maximum the
-// reference's greedy_shortcuts finds, alignment.cu:60-91).  No path gains
-// more than m[t] at frame t, so a state that leaves the window with prefix
-// loss lambda = m[0] + ... + m[t] - alpha larger than the final path's loss
-// plus the fp32 rounding bound cannot lie on the conventional DP's path; when
-// every state that left is that far behind, the window DP made every
-// decision of the full DP along its path and returned its exact outputs
-// (certified).  Otherwise the record runs the full conventional DP
-// (ffa_window_fallback).
+// First the greedy pass: one warp per kGreedyChunk-frame chunk of a record
+// finds each frame's greedy bound m[t] -- the largest emission over the
+// record's transcript alphabet, the maximum the reference's greedy_shortcuts
+// finds (alignment.cu:60-91) -- and, as that kernel does, whether the chunk's
+// greedy labels have exactly one legal placement (the shortcut statistics).
+// Then one warp per record runs the conventional DP restricted to a window of
+// kWinStates consecutive states that slides up the trellis, 2 states per
+// lane.  No path gains more than m[t] at frame t, so a state that leaves the
+// window with prefix loss lambda = m[0] + ... + m[t] - alpha larger than the
+// final path's loss plus the fp32 rounding bound cannot lie on the
+// conventional DP's path; when every state that left is that far behind, the
+// window DP made every decision of the full DP along its path and returned
+// its exact outputs (certified).  Otherwise the record runs the full
+// conventional DP (ffa_window_fallback).
 constexpr int kWinWarps = 8;          // records (warps) per CTA at most
 constexpr int kWinStates = 64;        // window width: 32 lanes x 2 states
 constexpr int kWinSlide = 16;         // states a slide moves the window by
-constexpr int kWinHigh = 40;          // slide when the best state sits this far up
+constexpr int kWinHigh = 32;          // slide when the best state sits this far up (4 frames before)
 constexpr int kWinChunk = 32;         // frames per TMA row copy = traceback segment
 constexpr int kWinRing = 3;           // row copies in flight per record
 constexpr int kWinMaxFrames = 8192;   // longer records take the chunked route
-constexpr int kWinGreedyChunk = 128;  // the reference's greedy chunk (shortcut_stats)
+constexpr int kGreedyChunk = 128;     // the reference's greedy chunk (alignment.py:498: chunk_frames)
+constexpr int kGreedyWarps = 8;       // greedy chunks per CTA
+// Greedy chunk verdict byte: bits 0-1 the reference's outcome (0 rejected, 1
+// accepted, 2 several placements); bit 2 an alphabet column holds NaN or
+// +inf; bit 3 a frame's bound is positive.
+enum : uint8_t { kGreedyAccepted = 1, kGreedyMultiple = 2, kGreedyPoison = 4, kGreedyPositive = 8 };
+
+struct GreedyItem {
+  int32_t record;
+  int32_t chunk;  // frames [kGreedyChunk chunk, ...)
+};
+struct GreedyParams {
+  const RecordDev* recs;
+  const GreedyItem* items;
+  int64_t count;
+  const float* lse;          // as ForwardParams::lse
+  float* bound;              // m[t] of record r's frame t at recs[r].out_off + t
+  uint8_t* verdicts;         // one per item
+};
+cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream);
 
 // One record's slice of a window CTA's dynamic shared memory; offsets in
 // bytes from the slice start (the host sizes CTAs with the same function).
 struct WinLayout {
-  uint32_t ring, tok, lpos, lstart, bp, gb, map, anc, stash, path, greedy, bytes;
+  uint32_t ring, tok, bp, gb, map, anc, stash, path, bytes;
 };
 __host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize) {
   auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
@@ -304,16 +325,13 @@ __host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize) 
   WinLayout w{};
   uint32_t off = 0;
   w.ring = off;   off = up(off + static_cast<uint32_t>(kWinRing * kWinChunk * V * esize), 128);
-  w.tok = off;    off = up(off + static_cast<uint32_t>(U) + 1, 16);          // label column of each token
-  w.lpos = off;   off = up(off + static_cast<uint32_t>(U) * 2 + 2, 16);      // token positions grouped by label
-  w.lstart = off; off = up(off + static_cast<uint32_t>(V + 1) * 4, 16);      // each label's first entry, a cursor
+  w.tok = off;    off = up(off + static_cast<uint32_t>(U) + 1, 16);  // label column of each token
   w.bp = off;     off = up(off + groups * 32 * 4, 16);   // per 8 frames: a word per lane (4 bits a frame)
   w.gb = off;     off = up(off + groups * 2, 16);        // window base per 8 frames
   w.map = off;    off = up(off + segs * kWinStates * 2, 16);  // per segment: each window state's ancestor
   w.anc = off;    off = up(off + segs * 2, 16);          // path state at each segment end
   w.stash = off;  off = up(off + kWinChunk * 4, 16);     // the top window state's score per frame of a chunk
-  w.path = off;   off = up(off + static_cast<uint32_t>(T) * 2, 16);  // path state per frame
-  w.greedy = off; off = up(off + static_cast<uint32_t>(T), 128);     // greedy label per frame (0xff: none)
+  w.path = off;   off = up(off + static_cast<uint32_t>(T) * 2, 128);  // path state per frame
   w.bytes = off;
   return w;
 }
@@ -332,9 +350,12 @@ struct WindowParams {
   const uint8_t* mask;
   int32_t check_inputs;
   OutputsDev out;
-  const float* lse;          // as ForwardParams::lse
-  int32_t* fallback_list;    // records whose window was not certified
-  int32_t* fallback_count;   // zeroed with the descriptor upload
+  const float* lse;           // as ForwardParams::lse
+  const float* bound;         // the greedy pass's m[t] (GreedyParams::bound)
+  const uint8_t* verdicts;    // the greedy pass's chunk verdicts
+  const int32_t* greedy_first;  // per record: its first greedy item
+  int32_t* fallback_list;     // records whose window was not certified
+  int32_t* fallback_count;    // zeroed with the descriptor upload
 };
 cudaError_t launch_window(const WindowParams& params, int num_ctas, int row_vocab, int fmt, unsigned smem_bytes,
                           cudaStream_t stream);

@@ -54,7 +54,7 @@ using namespace dev;
 namespace {
 
 static_assert(kWinStates == 64 && kWinChunk == 32, "window geometry: 32 lanes x 2 states, 32-frame segments");
-static_assert(kWinGreedyChunk % kWinChunk == 0, "greedy chunks are whole segments");
+static_assert(kGreedyChunk == 4 * 32, "a greedy chunk is four frames per lane");
 constexpr unsigned kFull = 0xffffffffu;
 
 // An order-preserving key of a float for an unsigned max (NaN never occurs
@@ -71,31 +71,30 @@ __device__ __forceinline__ double warp_min(double v) {
 }
 
 // The reference's greedy chunk test (alignment.cu:93-153) on one chunk of
-// frames [a, b): every frame's greedy label g[t] (the unique finite maximum
-// over the alphabet; 0xff when there is none) must exist, and the label
-// sequence must match exactly one placement s .. s + r[b-1] among the
-// record's states (a legal CTC walk: the state advances by 0 on a repeated
-// label, by 1 into or out of a blank, by 2 between tokens).  Returns 1 for an
-// accepted chunk, 2 for a chunk with several placements, 0 otherwise.  By the
-// whole warp; g, tok and the label position lists (lpos[lstart[c] ..
-// lstart[c+1]): the token positions u with tok[u] == c) in shared memory.
-__device__ int greedy_chunk(const uint8_t* g, const uint8_t* tok, const uint16_t* lpos, const uint16_t* lstart,
-                            int a, int b, int T, int S, int blank, int lane) {
-  bool bad = false;
-  for (int t = a + lane; t < b; t += 32) bad |= g[t] == 0xff;
-  if (__any_sync(kFull, bad)) return 0;
-  // r[t] - r[a] by a warp scan: lane j takes frames a + 4j .. a + 4j + 3.
+// frames [a, b), by the whole warp: lane j holds the greedy labels lab[q] of
+// frames a + 4j + q (the unique finite maximum over the alphabet; every frame
+// of the chunk has one).  The label sequence must match exactly one placement
+// s .. s + r[b-1] among the record's states (a legal CTC walk: the state
+// advances by 0 on a repeated label, by 1 into or out of a blank, by 2
+// between tokens).  Returns kGreedyAccepted, kGreedyMultiple (several
+// placements) or 0.  label_of(s): the label column of state s.
+template <typename LabelOf>
+__device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, int U, int blank,
+                              const int64_t* targets, int V, LabelOf label_of, int lane) {
+  // r[t] - r[a] by a warp scan of the increments.
   int inc[4], own = 0;
-  bool change = false;
+  unsigned chg = 0;
+  int prev = __shfl_up_sync(kFull, lab[3], 1);
+  if (lane == 0) prev = lab[0];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int t = a + 4 * lane + q;
     int d = 0;
-    if (t > a && t < b) {
-      const int x = g[t], y = g[t - 1];
-      d = x == y ? 0 : ((x == blank || y == blank) ? 1 : 2);
+    if (t > a && t < b && lab[q] != prev) {
+      d = (lab[q] == blank || prev == blank) ? 1 : 2;
+      chg |= 1u << q;
     }
-    change |= d != 0;
+    prev = lab[q];
     own += d;
     inc[q] = own;
   }
@@ -105,56 +104,168 @@ __device__ int greedy_chunk(const uint8_t* g, const uint8_t* tok, const uint16_t
     const int v = __shfl_up_sync(kFull, scan, o);
     if (lane >= o) scan += v;
   }
-  const int before = scan - own;                 // increments of the frames before this lane's four
-  const int R = __shfl_sync(kFull, scan, 31);    // r[b-1]
-  auto label_of = [&](int s) { return (s & 1) ? static_cast<int>(tok[s >> 1]) : blank; };
-  const int ga = g[a];
+  const int before = scan - own;               // increments of the frames before this lane's four
+  const int R = __shfl_sync(kFull, scan, 31);  // r[b-1]
+#pragma unroll
+  for (int q = 0; q < 4; ++q) inc[q] += before;
+  const int ga = __shfl_sync(kFull, lab[0], 0);
   const int hi_start = a == 0 ? 1 : S - 1;  // the first chunk starts at state 0 or 1 (alignment.cu:119)
   auto in_range = [&](int s) {
     const int term = s + R;
     return s >= 0 && s <= hi_start && term < S && !(b == T && term < S - 2);
   };
+  auto token = [&](int u) { return clamp_label(__ldg(targets + u), V); };
+  const unsigned changers = __ballot_sync(kFull, chg != 0);
   int matches = 0;
-  if (!__any_sync(kFull, change)) {
+  if (changers == 0) {
     // One label throughout: every state holding it in range is a placement.
     if (ga == blank) {
       const int lo = b == T ? max(0, S - 2) : 0, hi = min(hi_start, S - 1);
       matches = hi < lo ? 0 : (hi / 2 - (lo + 1) / 2 + 1);  // even states in [lo, hi]
     } else {
-      for (int j = lstart[ga] + lane; j < lstart[ga + 1]; j += 32) matches += in_range(2 * lpos[j] + 1) ? 1 : 0;
+      for (int u = lane; u < U; u += 32) matches += (token(u) == ga && in_range(2 * u + 1)) ? 1 : 0;
       matches = __reduce_add_sync(kFull, matches);
     }
-    return matches == 1 ? 1 : (matches > 1 ? 2 : 0);
+    return matches == 1 ? kGreedyAccepted : (matches > 1 ? kGreedyMultiple : 0);
   }
-  // The start is a token state of label g[a] when g[a] is a token, else the
-  // blank just below a token state of the label of the first change.
-  int first = 1 << 30;
-  for (int k = lane; k < b - a; k += 32)
-    if (k > 0 && g[a + k] != g[a + k - 1]) first = min(first, k);
-  first = __reduce_min_sync(kFull, first);
-  const int lab = ga != blank ? ga : g[a + first];
-  const int shift = ga != blank ? 1 : 0;  // start = 2u + shift for token position u of `lab`
-  const int n1 = lstart[lab + 1];
-  for (int j0 = lstart[lab]; j0 < n1; j0 += 32) {
-    const int j = j0 + lane;
-    unsigned cands = __ballot_sync(kFull, j < n1 && in_range(2 * lpos[j] + shift));
+  // The first change (label gc at offset rc) fixes the placement once its
+  // state is chosen: the start is a token state of label g[a] when g[a] is a
+  // token, else the blank just below a token state of label gc.
+  const int lc = __ffs(changers) - 1;
+  int q0 = __ffs(chg) - 1;
+  q0 = __shfl_sync(kFull, q0, lc);
+  int gcv = 0, rcv = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (q == q0) { gcv = lab[q]; rcv = inc[q]; }
+  const int gc = __shfl_sync(kFull, gcv, lc), rc = __shfl_sync(kFull, rcv, lc);
+  const int lb = ga != blank ? ga : gc;
+  const int shift = ga != blank ? 1 : 0;  // start = 2u + shift for a token u of label lb
+  for (int u0 = 0; u0 < U; u0 += 32) {
+    const int u = u0 + lane;
+    const int s0 = 2 * u + shift;
+    const bool cand = u < U && token(u) == lb && in_range(s0) && s0 + rc < S && label_of(s0 + rc) == gc;
+    unsigned cands = __ballot_sync(kFull, cand);
     while (cands) {
       const int q = __ffs(cands) - 1;
       cands &= cands - 1;
-      const int s0 = 2 * lpos[j0 + q] + shift;
+      const int st0 = 2 * (u0 + q) + shift;
       bool ok = true;  // every label change lands on a state holding the new label
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int t = a + 4 * lane + k;
-        if (t > a && t < b && g[t] != g[t - 1]) {
-          const int st = s0 + before + inc[k];
-          ok &= st < S && label_of(st) == g[t];
-        }
-      }
+      for (int k = 0; k < 4; ++k)
+        if ((chg >> k) & 1u) ok &= st0 + inc[k] < S && label_of(st0 + inc[k]) == lab[k];
       if (__all_sync(kFull, ok)) ++matches;
     }
   }
-  return matches == 1 ? 1 : (matches > 1 ? 2 : 0);
+  return matches == 1 ? kGreedyAccepted : (matches > 1 ? kGreedyMultiple : 0);
+}
+
+// max with NaN propagated (PTX max.NaN): a NaN anywhere in a reduction shows.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// The greedy pass: one warp per kGreedyChunk-frame chunk of a record.  Lane
+// j scans the rows of frames a + 4j .. a + 4j + 3 over the record's alphabet
+// (16-byte loads of whole rows): each frame's greedy bound m[t] (written to
+// the bound arena), its greedy label (the unique finite maximum, as
+// alignment.cu:60-91 finds it; NaN columns never compare greater or equal
+// there), and whether an alphabet column holds NaN or +inf.  The chunk's
+// verdict (greedy_verdict) and flags go to one byte.
+template <int kFmt, int kV>
+__global__ void __launch_bounds__(32 * kGreedyWarps)
+ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
+  using In = Input<kFmt>;
+  using Elem = typename In::Elem;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const int64_t index = static_cast<int64_t>(blockIdx.x) * kGreedyWarps + warp;
+  if (index >= P.count) return;
+  const GreedyItem item = P.items[index];
+  const RecordDev rec = P.recs[item.record];
+  const int T = rec.T, U = rec.U, blank = rec.blank;
+  const int V = kV > 0 ? kV : rec.V;
+  const int S = 2 * U + 1;
+  const int64_t* targets = rec.targets;
+  // The transcript alphabet (V <= 64), blank included.
+  unsigned alo = 0, ahi = 0;
+  for (int k = lane; k < U; k += 32) {
+    const int c = clamp_label(__ldg(targets + k), V);
+    if (c < 32) alo |= 1u << c; else ahi |= 1u << (c - 32);
+  }
+  alo = __reduce_or_sync(kFull, alo);
+  ahi = __reduce_or_sync(kFull, ahi);
+  if (blank < 32) alo |= 1u << blank; else ahi |= 1u << (blank - 32);
+  const int a = item.chunk * kGreedyChunk, b = min(T, a + kGreedyChunk);
+  const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
+  int lab[4];
+  bool poison = false, positive = false, rejected = false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int t = a + 4 * lane + q;
+    lab[q] = -1;
+    if (t >= b) continue;
+    const Elem* row = e + static_cast<int64_t>(t) * V;
+    float best = -INFINITY, bn = -INFINITY;
+    int arg = 0, ties = 0;
+    if constexpr (kV == 32 && kFmt == 0) {
+      float xs[32];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 v4 = __ldcs(reinterpret_cast<const float4*>(row) + k);  // streamed: read once
+        xs[4 * k] = v4.x; xs[4 * k + 1] = v4.y; xs[4 * k + 2] = v4.z; xs[4 * k + 3] = v4.w;
+      }
+      float bf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, bq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float v = ((alo >> k) & 1u) ? xs[k] : -INFINITY;
+        bf[k & 3] = fmaxf(bf[k & 3], v);
+        bq[k & 3] = max_nan(bq[k & 3], v);
+      }
+      best = fmaxf(fmaxf(bf[0], bf[1]), fmaxf(bf[2], bf[3]));
+      bn = max_nan(max_nan(bq[0], bq[1]), max_nan(bq[2], bq[3]));
+      int tq[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const bool hit = ((alo >> k) & 1u) && xs[k] == best;
+        tq[k & 3] += hit ? 1 : 0;
+        arg = hit ? k : arg;
+      }
+      ties = tq[0] + tq[1] + tq[2] + tq[3];
+    } else {
+      for (int col = 0; col < V; ++col) {
+        const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
+        if (!in) continue;
+        const float v = elem_to_float(row[col]);
+        bn = max_nan(bn, v);
+        if (v > best) { best = v; arg = col; ties = 1; }
+        else if (v == best) ++ties;
+      }
+    }
+    bool nonfinite = !(bn < INFINITY);  // NaN or +inf in an alphabet column
+    float m = best;
+    if constexpr (In::kLogits) {
+      const float z = P.lse[rec.out_off + t];
+      m = __fsub_rn(best, z);
+      nonfinite |= !isfinite(z);
+    }
+    P.bound[rec.out_off + t] = m;
+    poison |= nonfinite;
+    positive |= m > 0.0f;
+    const bool ok = ties == 1 && isfinite(m);
+    rejected |= !ok;
+    lab[q] = ok ? arg : 0xff;
+  }
+  poison = __any_sync(kFull, poison);
+  positive = __any_sync(kFull, positive);
+  int verdict = 0;
+  if (!__any_sync(kFull, rejected)) {
+    auto label_of = [&](int s) { return (s & 1) ? clamp_label(__ldg(targets + (s >> 1)), V) : blank; };
+    verdict = greedy_verdict(lab, a, b, T, S, U, blank, targets, V, label_of, lane);
+  }
+  if (lane == 0)
+    P.verdicts[index] = static_cast<uint8_t>(verdict | (poison ? kGreedyPoison : 0) | (positive ? kGreedyPositive : 0));
 }
 
 // A lane's two states: base + 2 lane (a blank) and base + 2 lane + 1, their
@@ -205,24 +316,20 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)));
   Elem* ring = reinterpret_cast<Elem*>(sm + L.ring);
   uint8_t* tok = sm + L.tok;
-  uint16_t* lpos = reinterpret_cast<uint16_t*>(sm + L.lpos);
-  uint16_t* lstart = reinterpret_cast<uint16_t*>(sm + L.lstart);
   uint32_t* bp = reinterpret_cast<uint32_t*>(sm + L.bp);
   uint16_t* gb = reinterpret_cast<uint16_t*>(sm + L.gb);
   uint16_t* map = reinterpret_cast<uint16_t*>(sm + L.map);
   int16_t* anc = reinterpret_cast<int16_t*>(sm + L.anc);
   float* stash = reinterpret_cast<float*>(sm + L.stash);
   uint16_t* path = reinterpret_cast<uint16_t*>(sm + L.path);
-  uint8_t* greedy = sm + L.greedy;
   int64_t* labels = P.out.labels + rec.out_off;
   float* scores = P.out.scores + rec.out_off;
   const float kNegInf = -INFINITY;
 
   // ---- status: mask, then target validation (alignment.cu:836, 852-874);
-  //      the transcript's label columns into shared memory, its alphabet ----
+  //      the transcript's label columns into shared memory ----
   int status = (P.mask != nullptr && !P.mask[r]) ? 2 : 0;
   int bad = 0, rep = 0;
-  unsigned alo = 0, ahi = 0;  // the transcript alphabet as a bit mask (V <= 64)
   int64_t carry = 0;          // the token before this 32-token block
 #pragma unroll 4
   for (int base = 0; base < U; base += 32) {
@@ -234,9 +341,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     if (k < U) {
       bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
       if (k > 0) rep += token == prev ? 1 : 0;
-      const int c = clamp_label(token, V);
-      tok[k] = static_cast<uint8_t>(c);
-      if (c < 32) alo |= 1u << c; else ahi |= 1u << (c - 32);
+      tok[k] = static_cast<uint8_t>(clamp_label(token, V));
     }
   }
   if (P.check_inputs) {
@@ -245,9 +350,6 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     if (bad) status = 3;
     else if (static_cast<int64_t>(U) + rep > T) status = 4;
   }
-  alo = __reduce_or_sync(kFull, alo);
-  ahi = __reduce_or_sync(kFull, ahi);
-  if (blank < 32) alo |= 1u << blank; else ahi |= 1u << (blank - 32);
   if (lane == 0) {
     // Diagnostics start at zero (alignment.py:101-129).
     P.out.stitched[r] = 0;
@@ -278,75 +380,49 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     fence_mbar_init();
     for (int c = 0; c < kWinRing && c < nchunks; ++c) issue(c);
   }
-  {
-    // Token positions grouped by label (a counting sort by the warp) for the
-    // greedy chunks' placement search.  Lanes holding equal labels form a
-    // group (match_any); the group's first lane updates the label's count.
-    uint16_t* cursor = lstart + (V + 1);
-    for (int c = lane; c <= V; c += 32) cursor[c] = 0;
-    __syncwarp();
-    for (int base = 0; base < U; base += 32) {
-      const int k = base + lane;
-      const int c = k < U ? tok[k] : 0x100 + lane;
-      const unsigned grp = __match_any_sync(kFull, c);
-      if (k < U && lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
-      __syncwarp();
-    }
-    // Exclusive prefix over labels (V <= 64: two per lane).
-    const int c0 = 2 * lane, c1 = c0 + 1;
-    const int n0 = c0 < V ? cursor[c0] : 0, n1 = c1 < V ? cursor[c1] : 0;
-    int incl = n0 + n1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const int excl = incl - n0 - n1;
-    __syncwarp();
-    if (c0 <= V) { lstart[c0] = static_cast<uint16_t>(excl); cursor[c0] = static_cast<uint16_t>(excl); }
-    if (c1 <= V) { lstart[c1] = static_cast<uint16_t>(excl + n0); cursor[c1] = static_cast<uint16_t>(excl + n0); }
-    if (lane == 0) lstart[V] = static_cast<uint16_t>(U);  // (V = 64 lies past the lanes' pairs)
-    __syncwarp();
-    for (int base = 0; base < U; base += 32) {
-      const int k = base + lane;
-      const int c = k < U ? tok[k] : 0x100 + lane;
-      const unsigned grp = __match_any_sync(kFull, c);
-      const int at = k < U ? cursor[c] + __popc(grp & ((1u << lane) - 1u)) : 0;
-      __syncwarp();
-      if (k < U) {
-        lpos[at] = static_cast<uint16_t>(k);
-        if (lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
-      }
-      __syncwarp();
-    }
-  }
   LseStream lse{};
   if constexpr (In::kLogits) lse.start(P.lse + rec.out_off, T, 0, lane);
-  const int rot = lane % V;
-  const bool full_alphabet = V == 32 && alo == kFull;
 
   // ---- the window: lane l owns states base + 2l (a blank) and base + 2l + 1 ----
   int base = 0;
   WinState x{kNegInf, kNegInf, 0, 0};
-  int col1 = blank;  // label column of state base + 2l + 1
-  bool v0 = false, v1 = false, sk1 = false;
   auto label_of = [&](int s) { return (s & 1) ? static_cast<int>(tok[s >> 1]) : blank; };
-  auto lane_states = [&]() {
-    const int s1 = base + 2 * lane + 1;
-    v0 = s1 - 1 < S;
-    v1 = s1 < S;
-    col1 = v1 ? label_of(s1) : blank;
-    const int u = s1 >> 1;  // skip s1-2 -> s1: a token unlike the blank and its predecessor (alignment.cu:407)
-    sk1 = v1 && u >= 1 && tok[u] != blank && tok[u] != tok[u - 1];
+  // Label column and skip legality of token state s1 (skip s1-2 -> s1: a
+  // token unlike the blank and its predecessor, alignment.cu:407).
+  auto token_info = [&](int s1, int& col, bool& sk) {
+    const bool valid = s1 < S;
+    const int u = s1 >> 1;
+    col = valid ? static_cast<int>(tok[u]) : blank;
+    sk = valid && u >= 1 && tok[u] != blank && tok[u] != tok[u - 1];
   };
-  lane_states();
+  int col1;
+  bool sk1;
+  token_info(2 * lane + 1, col1, sk1);
+  sk1 = sk1 && lane > 0;  // lane 0's skip source lies below the window
+  // The top lanes' states after the next slide, loaded ahead of it.
+  constexpr int kShift = kWinSlide / 2;
+  int next_col = blank;
+  bool next_sk = false;
+  if (lane >= 32 - kShift) token_info(base + kWinSlide + 2 * lane + 1, next_col, next_sk);
   const bool first_lane = lane == 0, top_lane = lane == 31;
 
   double Mbase = 0.0;     // sum of the greedy bounds m of the frames before this chunk
   double esc = INFINITY;  // smallest recorded prefix loss of a state that left the window (this lane's)
-  bool poison = false, positive = false, fault = false;
+  bool fault = false;
   // A state s at frame t can still reach a terminal state (S-2 or S-1).
   auto reaches_end = [&](int s, int t) { return s + 2 * (T - 1 - t) >= S - 2; };
+  // Whether the window's best state that can still reach the end sits at or
+  // above base + kWinHigh, judged at frame t (a heuristic: any choice is
+  // safe): the best key among all lanes and among the lanes below
+  // kWinHigh / 2, reduced mid-group and compared after it.
+  auto slide_keys = [&](int t, unsigned& kall, unsigned& klow) {
+    const int s0 = base + 2 * lane;
+    unsigned key = 0;
+    if (s0 < S && reaches_end(s0, t)) key = order_key(x.a0);
+    if (s0 + 1 < S && reaches_end(s0 + 1, t)) key = max(key, order_key(x.a1));
+    kall = __reduce_max_sync(kFull, key);
+    klow = __reduce_max_sync(kFull, 2 * lane < kWinHigh ? key : 0u);
+  };
 
   for (int c = 0; c < nchunks; ++c) {
     const int t0 = c * kWinChunk;
@@ -357,62 +433,8 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     const Elem* chunk = ring + (c % kWinRing) * kWinChunk * V;
     if constexpr (In::kLogits)
       if (c > 0) lse.advance(t0, lane);
-    // Greedy bound of frame t0 + lane: the largest emission over the
-    // alphabet, whether it is the unique maximum (and its column), and
-    // whether an alphabet column holds NaN or +inf.  Columns are read in an
-    // order rotated by the lane, against bank conflicts.
-    float m = 0.0f;
-    if (lane < rows) {
-      const Elem* row = chunk + lane * V;
-      float best = -INFINITY;
-      bool nonfinite = false;
-      int arg = 0, ties = 0;
-      if constexpr (kV == 32 && kFmt == 0) {
-        float xs[32];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int quad = (q + lane) & 7;
-          const float4 v4 = reinterpret_cast<const float4*>(row)[quad];
-          xs[4 * q] = v4.x; xs[4 * q + 1] = v4.y; xs[4 * q + 2] = v4.z; xs[4 * q + 3] = v4.w;
-        }
-        const unsigned amask = (alo >> (4 * (lane & 7))) | (alo << ((32 - 4 * (lane & 7)) & 31));
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          // xs[k] is column (k + 4 lane) mod 32; amask bit k says whether it is in the alphabet.
-          const bool in = full_alphabet || ((amask >> k) & 1u);
-          nonfinite |= in && !(xs[k] < INFINITY);
-          best = fmaxf(best, in ? xs[k] : -INFINITY);
-        }
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const bool in = full_alphabet || ((amask >> k) & 1u);
-          const bool hit = in && xs[k] == best;
-          ties += hit ? 1 : 0;
-          arg = hit ? ((k + 4 * lane) & 31) : arg;
-        }
-      } else {
-        for (int k = 0; k < V; ++k) {
-          int col = k + rot;
-          if (col >= V) col -= V;
-          const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
-          if (!in) continue;
-          const float v = elem_to_float(row[col]);
-          nonfinite |= !(v < INFINITY);
-          if (v > best) { best = v; arg = col; ties = 1; }
-          else if (v == best) ++ties;
-        }
-      }
-      m = best;
-      if constexpr (In::kLogits) {
-        m = __fsub_rn(best, lse.cur);
-        nonfinite |= !isfinite(lse.cur);
-      }
-      poison |= nonfinite;
-      positive |= m > 0.0f;
-      // The greedy label (alignment.cu:60-91): the unique finite maximum (a
-      // NaN column never compares greater or equal, so it drops out there).
-      greedy[t0 + lane] = (ties == 1 && isfinite(m)) ? static_cast<uint8_t>(arg) : 0xff;
-    }
+    // The greedy bound of frame t0 + lane (the greedy pass wrote it).
+    const float m = lane < rows ? __ldg(P.bound + rec.out_off + t0 + lane) : 0.0f;
     // M of each frame of the chunk: lane f holds m[t0] + ... + m[t0 + f] (fp64).
     double Mpre = static_cast<double>(m);
 #pragma unroll
@@ -422,34 +444,6 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     }
     for (int g = 0; g < kWinChunk / 8 && 8 * g < rows; ++g) {
       const int tg = t0 + 8 * g;
-      if (tg > 0 && base + kWinStates < S) {
-        // Slide: while the best state that can still reach the end sits at or
-        // above base + kWinHigh, drop the bottom kWinSlide states (recording
-        // their prefix losses at frame tg-1) and take kWinSlide new ones.
-        const double Mprev = tg > t0 ? Mbase + __shfl_sync(kFull, Mpre, tg - 1 - t0) : Mbase;
-        for (int it = 0; it < 2 && base + kWinStates < S; ++it) {
-          const int s0 = base + 2 * lane;
-          unsigned key = 0;
-          if (v0 && reaches_end(s0, tg - 1)) key = max(key, order_key(x.a0));
-          if (v1 && reaches_end(s0 + 1, tg - 1)) key = max(key, order_key(x.a1));
-          const unsigned kmax = __reduce_max_sync(kFull, key);
-          if (kmax <= order_key(kNegInf)) break;
-          const int best_lane = __ffs(__ballot_sync(kFull, key == kmax)) - 1;
-          if (2 * best_lane < kWinHigh) break;
-          if (lane < kWinSlide / 2) {
-            if (v0 && reaches_end(s0, tg - 1)) esc = fmin(esc, Mprev - static_cast<double>(x.a0));
-            if (v1 && reaches_end(s0 + 1, tg - 1)) esc = fmin(esc, Mprev - static_cast<double>(x.a1));
-          }
-          constexpr int kShift = kWinSlide / 2;
-          x.a0 = __shfl_down_sync(kFull, x.a0, kShift);
-          x.a1 = __shfl_down_sync(kFull, x.a1, kShift);
-          x.anc0 = __shfl_down_sync(kFull, x.anc0, kShift);
-          x.anc1 = __shfl_down_sync(kFull, x.anc1, kShift);
-          if (lane >= 32 - kShift) { x.a0 = kNegInf; x.a1 = kNegInf; }
-          base += kWinSlide;
-          lane_states();
-        }
-      }
       if (lane == 0) gb[tg >> 3] = static_cast<uint16_t>(base);
       // While states lie above the window, the top state's score is kept at
       // every frame (an exit above the window at the next frame scores at
@@ -462,6 +456,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
       const bool seg0 = g == 0;  // the chunk's first frame starts a traceback segment
       const Elem* grow = chunk + 8 * g * V;
       uint32_t w = 0;  // this lane's jump codes of the group: 4 bits a frame
+      unsigned kall = 0, klow = 0;
       auto emissions_of = [&](int j, float& eb, float& et) {
         const Elem* row = grow + j * V;
         eb = elem_to_float(row[blank]);
@@ -479,6 +474,9 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
           emissions_of(j, eb, et);
           w |= win_frame(x, eb, et, sk1, first_lane, s0, seg0 && j == 0, j);
           if (keep_top) stash[8 * g + j] = x.a1;
+          // Reduce the slide keys mid-group, so that the reductions overlap
+          // the group's last frames; the slide is applied after them.
+          if (j == 3 && open) slide_keys(tg + 3, kall, klow);
         }
       } else {
         for (int j = 0; j < 8 && tg + j < T; ++j) {
@@ -504,6 +502,27 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
         uint16_t* mp = map + (tl / kWinChunk) * kWinStates + 2 * lane;
         mp[0] = static_cast<uint16_t>(x.anc0);
         mp[1] = static_cast<uint16_t>(x.anc1);
+      }
+      if (kall > order_key(kNegInf) && klow < kall) {
+        // Drop the bottom kWinSlide states (recording their prefix losses at
+        // frame tl) and take kWinSlide new ones at the top (-inf).
+        const double Mtl = Mbase + __shfl_sync(kFull, Mpre, tl - t0);
+        if (lane < kShift) {
+          if (reaches_end(s0, tl)) esc = fmin(esc, Mtl - static_cast<double>(x.a0));
+          if (reaches_end(s0 + 1, tl)) esc = fmin(esc, Mtl - static_cast<double>(x.a1));
+        }
+        x.a0 = __shfl_down_sync(kFull, x.a0, kShift);
+        x.a1 = __shfl_down_sync(kFull, x.a1, kShift);
+        x.anc0 = __shfl_down_sync(kFull, x.anc0, kShift);
+        x.anc1 = __shfl_down_sync(kFull, x.anc1, kShift);
+        const int ncol = __shfl_down_sync(kFull, col1, kShift);
+        const bool nsk = __shfl_down_sync(kFull, sk1 ? 1 : 0, kShift) != 0;
+        const bool top = lane >= 32 - kShift;
+        col1 = top ? next_col : ncol;
+        sk1 = top ? next_sk : nsk;
+        if (top) { x.a0 = kNegInf; x.a1 = kNegInf; }
+        base += kWinSlide;
+        if (top) token_info(base + kWinSlide + 2 * lane + 1, next_col, next_sk);
       }
     }
     __syncwarp();  // the top state's scores are in the stash; every lane has read the ring entry
@@ -538,8 +557,29 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   const bool take_prev = S > 1 && vprev >= vlast;
   const float opt = take_prev ? vprev : vlast;
   const int term = take_prev ? S - 2 : S - 1;
+  // The greedy pass's verdicts: NaN / +inf in an alphabet column, positive
+  // bounds, and the reference's greedy chunk statistics (alignment.cu:130-153).
+  const int nitems = (T + kGreedyChunk - 1) / kGreedyChunk;
+  const uint8_t* verdicts = P.verdicts + P.greedy_first[r];
+  int accepted = 0, frames = 0, multiple = 0;
+  bool poison = false, positive = false;
+  for (int k = lane; k < nitems; k += 32) {
+    const int v = verdicts[k];
+    poison |= (v & kGreedyPoison) != 0;
+    positive |= (v & kGreedyPositive) != 0;
+    if ((v & 3) == kGreedyAccepted) { ++accepted; frames += min(T, (k + 1) * kGreedyChunk) - k * kGreedyChunk; }
+    if ((v & 3) == kGreedyMultiple) ++multiple;
+  }
   poison = __any_sync(kFull, poison);
   positive = __any_sync(kFull, positive);
+  accepted = __reduce_add_sync(kFull, accepted);
+  frames = __reduce_add_sync(kFull, frames);
+  multiple = __reduce_add_sync(kFull, multiple);
+  if (lane == 0) {
+    P.out.shortcut_stats[3 * r + 0] = accepted;
+    P.out.shortcut_stats[3 * r + 1] = frames;
+    P.out.shortcut_stats[3 * r + 2] = multiple;
+  }
   const double exit_loss = warp_min(esc);
   const double loss = M - static_cast<double>(opt);
   // Rounding: T additions along the full DP's path, each within 2^-24 of
@@ -551,23 +591,6 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   const bool certified =
       covers && !poison && !positive && isfinite(opt) && isfinite(M) && exit_loss > loss + margin;
 
-  {
-    // Greedy chunk statistics (alignment.cu:130-153), whichever DP solves the
-    // record: accepted chunks, their frames, chunks with several placements.
-    __syncwarp();
-    int64_t accepted = 0, frames = 0, multiple = 0;
-    for (int a = 0; a < T; a += kWinGreedyChunk) {
-      const int b = min(T, a + kWinGreedyChunk);
-      const int verdict = greedy_chunk(greedy, tok, lpos, lstart, a, b, T, S, blank, lane);
-      if (verdict == 1) { ++accepted; frames += b - a; }
-      if (verdict == 2) ++multiple;
-    }
-    if (lane == 0) {
-      P.out.shortcut_stats[3 * r + 0] = accepted;
-      P.out.shortcut_stats[3 * r + 1] = frames;
-      P.out.shortcut_stats[3 * r + 2] = multiple;
-    }
-  }
   if (!certified) {
     // The full conventional DP takes the record (ffa_window_fallback); the
     // reference's routing state 2 is its completed early fallback.
@@ -625,7 +648,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
 }
 
 template <int kFmt, int kV>
-__global__ void __launch_bounds__(32 * kWinWarps)
+__global__ void __launch_bounds__(32 * kWinWarps, 1)
 ffa_window_viterbi(const __grid_constant__ WindowParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ unsigned long long bars[kWinWarps][kWinRing];
@@ -636,20 +659,37 @@ ffa_window_viterbi(const __grid_constant__ WindowParams P) {
   window_record<kFmt, kV>(P, slot.record, smem_raw + slot.smem_off, bars[warp], lane);
 }
 
+constexpr int kWindowVariantsDecl = 4;
+int window_variant(int row_vocab, int fmt) { return fmt == 0 ? (row_vocab == 32 ? 0 : 1) : 1 + fmt; }
+using GreedyKernel = void (*)(GreedyParams);
+const GreedyKernel kGreedyKernels[kWindowVariantsDecl] = {
+    ffa_greedy_pass<0, 32>, ffa_greedy_pass<0, 0>, ffa_greedy_pass<1, 0>, ffa_greedy_pass<2, 0>};
+
 using WindowKernel = void (*)(WindowParams);
 // Variants: log-probabilities with V = 32 specialised, any row vocabulary,
 // fp32 and bf16 logits.
 constexpr int kWindowVariants = 4;
+static_assert(kWindowVariants == kWindowVariantsDecl, "variant tables");
 const WindowKernel kWindowKernels[kWindowVariants] = {
     ffa_window_viterbi<0, 32>, ffa_window_viterbi<0, 0>, ffa_window_viterbi<1, 0>, ffa_window_viterbi<2, 0>};
 
 }  // namespace
 
+cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream) {
+  if (params.count <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  const int64_t blocks = (params.count + kGreedyWarps - 1) / kGreedyWarps;
+  count_launch();
+  kGreedyKernels[window_variant(row_vocab, fmt)]<<<static_cast<unsigned>(blocks), 32 * kGreedyWarps, 0, stream>>>(
+      params);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_window(const WindowParams& params, int num_ctas, int row_vocab, int fmt, unsigned smem_bytes,
                           cudaStream_t stream) {
   if (num_ctas <= 0) return cudaSuccess;
   if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
-  const int variant = fmt == 0 ? (row_vocab == 32 ? 0 : 1) : 1 + fmt;
+  const int variant = window_variant(row_vocab, fmt);
   static std::atomic<uint64_t> opted[kWindowVariants];
   const WindowKernel kernel = kWindowKernels[variant];
   // The CTA's static shared memory (its mbarriers) stays under 1 KiB.

@@ -218,9 +218,10 @@ FFA_API int ffa_align_noalloc(const ffa_record* records, int64_t count, int mode
 
 /* While set, ffa_align calls made on the calling thread record `before` and
  * `after` (two cudaEvent_t created by the caller) on their stream immediately
- * around the first forward pass -- the launch that streams every emission row
- * once (every piece of the optimized route, every record of the conventional
- * one) -- so the caller can read its device time with cudaEventElapsedTime.
+ * around the launch that streams every emission row once -- the greedy pass
+ * when the call has records of the window route, else the first forward pass
+ * (every piece of the chunked route, every record of the conventional mode)
+ * -- so the caller can read its device time with cudaEventElapsedTime.
  * Pass NULL, NULL to clear. */
 FFA_API int ffa_profile_forward_events(void* before, void* after);
 
