@@ -250,8 +250,8 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
   L->fill = off; off = align_up(off + sizeof(ffa::FillItem) * fill, 16);
   // Zeroed counters of round 0's plan in the first pass (per record, then
   // per finisher group), uploaded with the descriptors.
-  // (and the window fallback's list length).
-  L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups + 1), 16);
+  // (and the window tiers' list lengths).
+  L->counters = off; off = align_up(off + sizeof(int32_t) * (count + ffa::kFinishGroups + 2), 16);
   // Window route: one slot per record, at most one CTA per record.
   L->win_slots = off; off = align_up(off + sizeof(ffa::WinSlot) * count, 16);
   L->win_ctas = off; off = align_up(off + sizeof(ffa::WinCta) * count, 16);
@@ -273,7 +273,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, bool wi
   L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->fill_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
   L->finish_done = off; off = align_up(off + sizeof(int32_t) * count, 256);
-  L->fallback = off; off = align_up(off + sizeof(int32_t) * count, 256);
+  L->fallback = off; off = align_up(off + sizeof(int32_t) * 2 * count, 256);  // the two tiers' lists
   L->bound = off; off = align_up(off + (greedy ? sizeof(float) * frames : 0), 256);
   L->verdicts = off; off = align_up(off + greedy, 256);
   // Logits: each frame's row log-sum-exp.
@@ -615,7 +615,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     frontier_off += g.frontier_elems;
   }
 
-  std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups + 1));
+  std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups + 2));
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
       align_up(static_cast<size_t>(ffa::kRowRing) * ffa::kChunkFrames * max_row_vocab * esize, 128));
@@ -765,7 +765,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   auto* wslots = reinterpret_cast<ffa::WinSlot*>(host + L.win_slots);
   auto* wctas = reinterpret_cast<ffa::WinCta*>(host + L.win_ctas);
   int64_t n_wcta = 0;
-  uint32_t win_smem = 0;
+  uint32_t win_smem = 0, wide_smem = 0;
   int win_vocab = -1;
   if (!win_records.empty()) {
     const int64_t nwin = static_cast<int64_t>(win_records.size());
@@ -783,7 +783,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       const int32_t i = sorted_win[k];
       const ffa::RecordDev& d = recs[i];
       win_vocab = (win_vocab < 0 || win_vocab == d.V) ? d.V : 0;
-      const uint32_t need = ffa::win_layout(d.T, d.U, d.V, static_cast<int>(esize)).bytes;
+      const uint32_t need = ffa::win_layout(d.T, d.U, d.V, static_cast<int>(esize), 2).bytes;
+      wide_smem = std::max(wide_smem, ffa::win_layout(std::min(d.T, ffa::kWinWideMaxFrames), d.U, d.V,
+                                                      static_cast<int>(esize), 4).bytes);
       if (n_wcta == 0 || wctas[n_wcta - 1].count == per_cta || cur + need > budget) {
         wctas[n_wcta++] = ffa::WinCta{static_cast<int32_t>(k), 0};
         cur = 0;
@@ -885,12 +887,25 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     wp.bound = gp.bound;
     wp.verdicts = gp.verdicts;
     wp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
-    wp.fallback_list = reinterpret_cast<int32_t*>(dev + L.fallback);
-    wp.fallback_count = fp.slot_done + count + ffa::kFinishGroups;
+    // Tier lists: the 64-state window hands records to the 128-state one
+    // (list 1), which hands them to the full DP (list 2).
+    int32_t* list1 = reinterpret_cast<int32_t*>(dev + L.fallback);
+    int32_t* list2 = list1 + count;
+    int32_t* count1 = fp.slot_done + count + ffa::kFinishGroups;
+    int32_t* count2 = count1 + 1;
+    wp.fallback_list = list1;
+    wp.fallback_count = count1;
     err = ffa::launch_window(wp, static_cast<int>(n_wcta), wv, fmt, win_smem, s);
     if (err != cudaSuccess) return cuda_fail(err, "window launch");
-    err = ffa::launch_window_fallback(fp, wp.fallback_list, wp.fallback_count, static_cast<int>(win_records.size()),
-                                      wv, fmt, static_cast<unsigned>(header + row_slot_bytes), s);
+    ffa::WindowParams wide = wp;
+    wide.in_list = list1;
+    wide.in_count = count1;
+    wide.fallback_list = list2;
+    wide.fallback_count = count2;
+    err = ffa::launch_window_wide(wide, static_cast<int>(win_records.size()), wv, fmt, wide_smem, s);
+    if (err != cudaSuccess) return cuda_fail(err, "wide window launch");
+    err = ffa::launch_window_fallback(fp, list2, count2, static_cast<int>(win_records.size()), wv, fmt,
+                                      static_cast<unsigned>(header + row_slot_bytes), s);
     if (err != cudaSuccess) return cuda_fail(err, "window fallback launch");
   }
   // Long records: the conventional DP on one cluster each, one launch per

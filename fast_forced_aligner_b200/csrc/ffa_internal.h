@@ -293,6 +293,7 @@ constexpr int kWinHigh = 32;          // slide when the best state sits this far
 constexpr int kWinChunk = 32;         // frames per TMA row copy = traceback segment
 constexpr int kWinRing = 3;           // row copies in flight per record
 constexpr int kWinMaxFrames = 8192;   // longer records take the chunked route
+constexpr int kWinWideMaxFrames = 4096;  // the 128-state tier's limit (longer: the full DP)
 constexpr int kGreedyChunk = 128;     // the reference's greedy chunk (alignment.py:498: chunk_frames)
 constexpr int kGreedyWarps = 8;       // greedy chunks per CTA
 // Greedy chunk verdict byte: bits 0-1 the reference's outcome (0 rejected, 1
@@ -314,21 +315,22 @@ struct GreedyParams {
 };
 cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream);
 
-// One record's slice of a window CTA's dynamic shared memory; offsets in
-// bytes from the slice start (the host sizes CTAs with the same function).
+// One record's slice of a window CTA's dynamic shared memory for K states
+// per lane (a window of 32 K states); offsets in bytes from the slice start
+// (the host sizes CTAs with the same function).
 struct WinLayout {
   uint32_t ring, tok, bp, gb, map, anc, stash, path, bytes;
 };
-__host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize) {
+__host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, int K) {
   auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
   const uint32_t groups = static_cast<uint32_t>((T + 7) / 8), segs = static_cast<uint32_t>((T + 31) / 32);
   WinLayout w{};
   uint32_t off = 0;
   w.ring = off;   off = up(off + static_cast<uint32_t>(kWinRing * kWinChunk * V * esize), 128);
   w.tok = off;    off = up(off + static_cast<uint32_t>(U) + 1, 16);  // label column of each token
-  w.bp = off;     off = up(off + groups * 32 * 4, 16);   // per 8 frames: a word per lane (4 bits a frame)
+  w.bp = off;     off = up(off + groups * 32 * 4 * static_cast<uint32_t>(K / 2), 16);  // per 8 frames: K/2 words a lane
   w.gb = off;     off = up(off + groups * 2, 16);        // window base per 8 frames
-  w.map = off;    off = up(off + segs * kWinStates * 2, 16);  // per segment: each window state's ancestor
+  w.map = off;    off = up(off + segs * 32 * static_cast<uint32_t>(K) * 2, 16);  // per segment: each state's ancestor
   w.anc = off;    off = up(off + segs * 2, 16);          // path state at each segment end
   w.stash = off;  off = up(off + kWinChunk * 4, 16);     // the top window state's score per frame of a chunk
   w.path = off;   off = up(off + static_cast<uint32_t>(T) * 2, 128);  // path state per frame
@@ -354,11 +356,18 @@ struct WindowParams {
   const float* bound;         // the greedy pass's m[t] (GreedyParams::bound)
   const uint8_t* verdicts;    // the greedy pass's chunk verdicts
   const int32_t* greedy_first;  // per record: its first greedy item
-  int32_t* fallback_list;     // records whose window was not certified
+  int32_t* fallback_list;     // records handed to the next tier
   int32_t* fallback_count;    // zeroed with the descriptor upload
+  const int32_t* in_list;     // the 128-state tier: the records it takes
+  const int32_t* in_count;
 };
 cudaError_t launch_window(const WindowParams& params, int num_ctas, int row_vocab, int fmt, unsigned smem_bytes,
                           cudaStream_t stream);
+// The 128-state window over the device-written list of records the 64-state
+// window did not certify (in_list, in_count); one warp per CTA, smem_bytes
+// the largest record's slice.
+cudaError_t launch_window_wide(const WindowParams& params, int max_count, int row_vocab, int fmt,
+                               unsigned smem_bytes, cudaStream_t stream);
 // The full conventional DP, traceback and outputs of each listed record
 // (one CTA per record, grid-stride over the device-written list).
 cudaError_t launch_window_fallback(const ForwardParams& params, const int32_t* list, const int32_t* count,

@@ -268,52 +268,93 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
     P.verdicts[index] = static_cast<uint8_t>(verdict | (poison ? kGreedyPoison : 0) | (positive ? kGreedyPositive : 0));
 }
 
-// A lane's two states: base + 2 lane (a blank) and base + 2 lane + 1, their
+// A lane's K states: base + K lane + k (even k: blanks, odd k: tokens), their
 // scores and their ancestors (each state's path state at the frame before
 // the current traceback segment).
-struct WinState {
-  float a0, a1;
-  int anc0, anc1;
+template <int K>
+struct WinLane {
+  float a[K];
+  int anc[K];
 };
 
-// One frame of the recurrence (alignment.cu:414-429): stay, then step if
-// strictly greater, then skip if strictly greater and legal; one fp32
-// round-to-nearest add per cell.  seg: the frame starts a traceback segment
-// (ancestors restart from the predecessors).  s0: the lane's blank state.
-// Returns the frame's 4 code bits shifted to slot j of the group's word.
-__device__ __forceinline__ uint32_t win_frame(WinState& x, float eb, float et, bool sk1, bool first_lane, int s0,
-                                              bool seg, int j) {
-  float p1 = __shfl_up_sync(kFull, x.a1, 1);  // s-1 for the blank, s-2 for the token
-  int pa = __shfl_up_sync(kFull, x.anc1, 1);
-  if (seg) { x.anc0 = s0; x.anc1 = s0 + 1; pa = s0 - 1; }
-  p1 = first_lane ? -INFINITY : p1;           // below the window: -inf
-  const bool c0 = p1 > x.a0;
-  const bool c1 = x.a0 > x.a1;
-  float b1 = c1 ? x.a0 : x.a1;
-  int n1 = c1 ? x.anc0 : x.anc1;
-  const bool j2 = sk1 && p1 > b1;
-  b1 = j2 ? p1 : b1;
-  n1 = j2 ? pa : n1;
-  const float b0 = c0 ? p1 : x.a0;
-  x.anc0 = c0 ? pa : x.anc0;
-  x.anc1 = n1;
-  x.a0 = __fadd_rn(b0, eb);
-  x.a1 = __fadd_rn(b1, et);
-  return ((c0 ? 1u : 0u) | (j2 ? 8u : (c1 ? 4u : 0u))) << (4 * j);
+// One frame of the recurrence (alignment.cu:414-429) for a lane's K states:
+// stay, then step if strictly greater, then skip if strictly greater and
+// legal; one fp32 round-to-nearest add per cell.  seg: the frame starts a
+// traceback segment (ancestors restart from the predecessors).  s0: the
+// lane's first state.  Returns the frame's 2K code bits (state k at bits 2k).
+template <int K>
+__device__ __forceinline__ uint32_t win_step(WinLane<K>& x, float eb, const float (&et)[K / 2],
+                                             const bool (&sk)[K / 2], bool first_lane, int s0, bool seg) {
+  float p1 = __shfl_up_sync(kFull, x.a[K - 1], 1);  // state s0 - 1, the lane below's last
+  int pa = __shfl_up_sync(kFull, x.anc[K - 1], 1);
+  if (seg) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) x.anc[k] = s0 + k;
+    pa = s0 - 1;
+  }
+  p1 = first_lane ? -INFINITY : p1;  // below the window: -inf
+  float na[K];
+  int nn[K];
+  uint32_t bits = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float x1 = k >= 1 ? x.a[k - 1] : p1;
+    const int n1 = k >= 1 ? x.anc[k - 1] : pa;
+    const bool c = x1 > x.a[k];
+    float b = c ? x1 : x.a[k];
+    int n = c ? n1 : x.anc[k];
+    uint32_t code = c ? 1u : 0u;
+    if (k & 1) {
+      const float x2 = k >= 2 ? x.a[k - 2] : p1;
+      const int n2 = k >= 2 ? x.anc[k - 2] : pa;
+      const bool j2 = sk[k >> 1] && x2 > b;
+      b = j2 ? x2 : b;
+      n = j2 ? n2 : n;
+      code = j2 ? 2u : code;
+      na[k] = __fadd_rn(b, et[k >> 1]);
+    } else {
+      na[k] = __fadd_rn(b, eb);
+    }
+    nn[k] = n;
+    bits |= code << (2 * k);
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) { x.a[k] = na[k]; x.anc[k] = nn[k]; }
+  return bits;
 }
 
-// The window DP of one record by one warp.  sm: the record's slice of the
-// CTA's dynamic shared memory (WinLayout); full: its kWinRing mbarriers.
-template <int kFmt, int kV>
-__device__ __forceinline__ void window_record(const WindowParams& P, int r, unsigned char* sm,
+// a[idx] of a register array without a dynamic register index.
+template <int K>
+__device__ __forceinline__ float pick(const float (&a)[K], int idx) {
+  float v = a[0];
+#pragma unroll
+  for (int k = 1; k < K; ++k) v = idx == k ? a[k] : v;
+  return v;
+}
+
+// The window DP of one record by one warp, K states per lane (window of 32 K
+// states, sliding by 8 lanes).  sm: the record's slice of dynamic shared
+// memory (win_layout); full: its kWinRing mbarriers.  wide: the 128-state
+// second tier, for a record the 64-state window did not certify (its
+// diagnostics and shortcut statistics are already written).  Returns false
+// when a bounded wait gave up (status 5 written).
+template <int kFmt, int kV, int K>
+__device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsigned char* sm,
                                               unsigned long long* full, int lane) {
   using In = Input<kFmt>;
   using Elem = typename In::Elem;
+  constexpr bool kWide = K == 4;
+  constexpr int W = 32 * K;           // window states
+  constexpr int kWords = K / 2;       // code words per lane per 8-frame group
+  constexpr int kFramesPerWord = 8 / kWords;
+  constexpr int kShift = 8;           // a slide moves the window by 8 lanes
+  constexpr int kSlide = kShift * K;  // = 8 K states
+  constexpr int kHighLane = 16;       // slide when the best state lies in lane 16 or above
   const RecordDev rec = P.recs[r];
   const int T = rec.T, U = rec.U, blank = rec.blank;
   const int V = kV > 0 ? kV : rec.V;
   const int S = 2 * U + 1;
-  const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)));
+  const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)), K);
   Elem* ring = reinterpret_cast<Elem*>(sm + L.ring);
   uint8_t* tok = sm + L.tok;
   uint32_t* bp = reinterpret_cast<uint32_t*>(sm + L.bp);
@@ -330,7 +371,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   //      the transcript's label columns into shared memory ----
   int status = (P.mask != nullptr && !P.mask[r]) ? 2 : 0;
   int bad = 0, rep = 0;
-  int64_t carry = 0;          // the token before this 32-token block
+  int64_t carry = 0;  // the token before this 32-token block
 #pragma unroll 4
   for (int base = 0; base < U; base += 32) {
     const int k = base + lane;
@@ -350,7 +391,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     if (bad) status = 3;
     else if (static_cast<int64_t>(U) + rep > T) status = 4;
   }
-  if (lane == 0) {
+  if (!kWide && lane == 0) {
     // Diagnostics start at zero (alignment.py:101-129).
     P.out.stitched[r] = 0;
     P.out.repair_passes[r] = 0;
@@ -361,7 +402,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   if (status >= 2) {
     if (lane == 0) { P.out.status[r] = status; P.out.objective[r] = -INFINITY; }
     for (int t = lane; t < T; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
-    return;
+    return true;
   }
   __syncwarp();
 
@@ -378,14 +419,17 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   if (lane == 0) {
     for (int k = 0; k < kWinRing; ++k) mbar_init(&full[k], 1);
     fence_mbar_init();
+    fence_proxy_async();  // shared memory a previous record read is rewritten by the copies
     for (int c = 0; c < kWinRing && c < nchunks; ++c) issue(c);
   }
   LseStream lse{};
   if constexpr (In::kLogits) lse.start(P.lse + rec.out_off, T, 0, lane);
 
-  // ---- the window: lane l owns states base + 2l (a blank) and base + 2l + 1 ----
+  // ---- the window: lane l owns states base + K l + k ----
   int base = 0;
-  WinState x{kNegInf, kNegInf, 0, 0};
+  WinLane<K> x;
+#pragma unroll
+  for (int k = 0; k < K; ++k) { x.a[k] = kNegInf; x.anc[k] = 0; }
   auto label_of = [&](int s) { return (s & 1) ? static_cast<int>(tok[s >> 1]) : blank; };
   // Label column and skip legality of token state s1 (skip s1-2 -> s1: a
   // token unlike the blank and its predecessor, alignment.cu:407).
@@ -395,15 +439,16 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     col = valid ? static_cast<int>(tok[u]) : blank;
     sk = valid && u >= 1 && tok[u] != blank && tok[u] != tok[u - 1];
   };
-  int col1;
-  bool sk1;
-  token_info(2 * lane + 1, col1, sk1);
-  sk1 = sk1 && lane > 0;  // lane 0's skip source lies below the window
-  // The top lanes' states after the next slide, loaded ahead of it.
-  constexpr int kShift = kWinSlide / 2;
-  int next_col = blank;
-  bool next_sk = false;
-  if (lane >= 32 - kShift) token_info(base + kWinSlide + 2 * lane + 1, next_col, next_sk);
+  int col[K / 2], next_col[K / 2];
+  bool sk[K / 2], next_sk[K / 2];
+#pragma unroll
+  for (int q = 0; q < K / 2; ++q) {
+    token_info(K * lane + 2 * q + 1, col[q], sk[q]);
+    next_col[q] = blank;
+    next_sk[q] = false;
+    // The top lanes' states after the next slide, loaded ahead of it.
+    if (lane >= 32 - kShift) token_info(kSlide + K * lane + 2 * q + 1, next_col[q], next_sk[q]);
+  }
   const bool first_lane = lane == 0, top_lane = lane == 31;
 
   double Mbase = 0.0;     // sum of the greedy bounds m of the frames before this chunk
@@ -411,17 +456,18 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   bool fault = false;
   // A state s at frame t can still reach a terminal state (S-2 or S-1).
   auto reaches_end = [&](int s, int t) { return s + 2 * (T - 1 - t) >= S - 2; };
-  // Whether the window's best state that can still reach the end sits at or
-  // above base + kWinHigh, judged at frame t (a heuristic: any choice is
-  // safe): the best key among all lanes and among the lanes below
-  // kWinHigh / 2, reduced mid-group and compared after it.
+  // Whether the window's best state that can still reach the end lies in
+  // lane kHighLane or above, judged at frame t (a heuristic: any choice is
+  // safe): the best key among all lanes and among the lanes below, reduced
+  // mid-group and compared after it.
   auto slide_keys = [&](int t, unsigned& kall, unsigned& klow) {
-    const int s0 = base + 2 * lane;
+    const int s0 = base + K * lane;
     unsigned key = 0;
-    if (s0 < S && reaches_end(s0, t)) key = order_key(x.a0);
-    if (s0 + 1 < S && reaches_end(s0 + 1, t)) key = max(key, order_key(x.a1));
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+      if (s0 + k < S && reaches_end(s0 + k, t)) key = max(key, order_key(x.a[k]));
     kall = __reduce_max_sync(kFull, key);
-    klow = __reduce_max_sync(kFull, 2 * lane < kWinHigh ? key : 0u);
+    klow = __reduce_max_sync(kFull, lane < kHighLane ? key : 0u);
   };
 
   for (int c = 0; c < nchunks; ++c) {
@@ -448,81 +494,98 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
       // While states lie above the window, the top state's score is kept at
       // every frame (an exit above the window at the next frame scores at
       // most that plus the next frame's bound); otherwise -inf.
-      const bool open = base + kWinStates < S;
+      const bool open = base + W < S;
       const bool keep_top = top_lane && open;
       if (top_lane && !open)
         for (int j = 0; j < 8; ++j) stash[8 * g + j] = kNegInf;
-      const int s0 = base + 2 * lane;
+      const int s0 = base + K * lane;
       const bool seg0 = g == 0;  // the chunk's first frame starts a traceback segment
       const Elem* grow = chunk + 8 * g * V;
-      uint32_t w = 0;  // this lane's jump codes of the group: 4 bits a frame
+      uint32_t w[kWords];
+#pragma unroll
+      for (int q = 0; q < kWords; ++q) w[q] = 0;
       unsigned kall = 0, klow = 0;
-      auto emissions_of = [&](int j, float& eb, float& et) {
+      auto emissions_of = [&](int j, float& eb, float (&et)[K / 2]) {
         const Elem* row = grow + j * V;
         eb = elem_to_float(row[blank]);
-        et = elem_to_float(row[col1]);
+#pragma unroll
+        for (int q = 0; q < K / 2; ++q) et[q] = elem_to_float(row[col[q]]);
         if constexpr (In::kLogits) {
           const float z = lse.at(8 * g + j);
           eb = __fsub_rn(eb, z);
-          et = __fsub_rn(et, z);
+#pragma unroll
+          for (int q = 0; q < K / 2; ++q) et[q] = __fsub_rn(et[q], z);
         }
       };
       if (tg > 0 && tg + 8 <= T) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float eb, et;
+          float eb, et[K / 2];
           emissions_of(j, eb, et);
-          w |= win_frame(x, eb, et, sk1, first_lane, s0, seg0 && j == 0, j);
-          if (keep_top) stash[8 * g + j] = x.a1;
+          const uint32_t bits = win_step<K>(x, eb, et, sk, first_lane, s0, seg0 && j == 0);
+          w[j / kFramesPerWord] |= bits << (2 * K * (j % kFramesPerWord));
+          if (keep_top) stash[8 * g + j] = x.a[K - 1];
           // Reduce the slide keys mid-group, so that the reductions overlap
           // the group's last frames; the slide is applied after them.
           if (j == 3 && open) slide_keys(tg + 3, kall, klow);
         }
       } else {
         for (int j = 0; j < 8 && tg + j < T; ++j) {
-          float eb, et;
+          float eb, et[K / 2];
           emissions_of(j, eb, et);
           if (tg + j == 0) {
             // Frame 0: alpha[s] = e[0, l[s]] for s < 2 (alignment.cu:409).
-            x.a0 = first_lane ? eb : kNegInf;
-            x.a1 = (first_lane && S > 1) ? et : kNegInf;
-            x.anc0 = s0;
-            x.anc1 = s0 + 1;
+#pragma unroll
+            for (int k = 0; k < K; ++k) { x.a[k] = kNegInf; x.anc[k] = s0 + k; }
+            if (first_lane) {
+              x.a[0] = eb;
+              if (S > 1) x.a[1] = et[0];
+            }
           } else {
-            w |= win_frame(x, eb, et, sk1, first_lane, s0, seg0 && j == 0, j);
+            const uint32_t bits = win_step<K>(x, eb, et, sk, first_lane, s0, seg0 && j == 0);
+            w[j / kFramesPerWord] |= bits << (2 * K * (j % kFramesPerWord));
           }
-          if (keep_top) stash[8 * g + j] = x.a1;
+          if (keep_top) stash[8 * g + j] = x.a[K - 1];
         }
       }
-      bp[(tg >> 3) * 32 + lane] = w;
+#pragma unroll
+      for (int q = 0; q < kWords; ++q) bp[((tg >> 3) * kWords + q) * 32 + lane] = w[q];
       const int tl = min(tg + 8, T) - 1;
       if ((tl & (kWinChunk - 1)) == kWinChunk - 1 || tl == T - 1) {
         // Segment map: each window state's path state at the frame before
         // the segment.
-        uint16_t* mp = map + (tl / kWinChunk) * kWinStates + 2 * lane;
-        mp[0] = static_cast<uint16_t>(x.anc0);
-        mp[1] = static_cast<uint16_t>(x.anc1);
+        uint16_t* mp = map + (tl / kWinChunk) * W + K * lane;
+#pragma unroll
+        for (int k = 0; k < K; ++k) mp[k] = static_cast<uint16_t>(x.anc[k]);
       }
       if (kall > order_key(kNegInf) && klow < kall) {
-        // Drop the bottom kWinSlide states (recording their prefix losses at
-        // frame tl) and take kWinSlide new ones at the top (-inf).
+        // Drop the bottom kSlide states (recording their prefix losses at
+        // frame tl) and take kSlide new ones at the top (-inf).
         const double Mtl = Mbase + __shfl_sync(kFull, Mpre, tl - t0);
         if (lane < kShift) {
-          if (reaches_end(s0, tl)) esc = fmin(esc, Mtl - static_cast<double>(x.a0));
-          if (reaches_end(s0 + 1, tl)) esc = fmin(esc, Mtl - static_cast<double>(x.a1));
+#pragma unroll
+          for (int k = 0; k < K; ++k)
+            if (reaches_end(s0 + k, tl)) esc = fmin(esc, Mtl - static_cast<double>(x.a[k]));
         }
-        x.a0 = __shfl_down_sync(kFull, x.a0, kShift);
-        x.a1 = __shfl_down_sync(kFull, x.a1, kShift);
-        x.anc0 = __shfl_down_sync(kFull, x.anc0, kShift);
-        x.anc1 = __shfl_down_sync(kFull, x.anc1, kShift);
-        const int ncol = __shfl_down_sync(kFull, col1, kShift);
-        const bool nsk = __shfl_down_sync(kFull, sk1 ? 1 : 0, kShift) != 0;
         const bool top = lane >= 32 - kShift;
-        col1 = top ? next_col : ncol;
-        sk1 = top ? next_sk : nsk;
-        if (top) { x.a0 = kNegInf; x.a1 = kNegInf; }
-        base += kWinSlide;
-        if (top) token_info(base + kWinSlide + 2 * lane + 1, next_col, next_sk);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          x.a[k] = __shfl_down_sync(kFull, x.a[k], kShift);
+          x.anc[k] = __shfl_down_sync(kFull, x.anc[k], kShift);
+          if (top) x.a[k] = kNegInf;
+        }
+#pragma unroll
+        for (int q = 0; q < K / 2; ++q) {
+          const int ncol = __shfl_down_sync(kFull, col[q], kShift);
+          const bool nsk = __shfl_down_sync(kFull, sk[q] ? 1 : 0, kShift) != 0;
+          col[q] = top ? next_col[q] : ncol;
+          sk[q] = top ? next_sk[q] : nsk;
+        }
+        base += kSlide;
+        if (top) {
+#pragma unroll
+          for (int q = 0; q < K / 2; ++q) token_info(base + kSlide + K * lane + 2 * q + 1, next_col[q], next_sk[q]);
+        }
       }
     }
     __syncwarp();  // the top state's scores are in the stash; every lane has read the ring entry
@@ -544,16 +607,17 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
       P.out.objective[r] = -INFINITY;
     }
     for (int t = lane; t < T; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
-    return;
+    return false;
   }
+  if (lane == 0)
+    for (int k = 0; k < kWinRing; ++k) mbar_inval(&full[k]);  // every copy has landed and been read
 
   // ---- terminal rule (alignment.cu:496-510) and the certificate ----
   const double M = Mbase;
-  const bool covers = base + kWinStates >= S;  // S-1 and S-2 inside the window
-  const int l_last = min(max((S - 1 - base) >> 1, 0), 31);
-  const int l_prev = min(max((S - 3 - base) >> 1, 0), 31);
-  const float vlast = __shfl_sync(kFull, x.a0, l_last);
-  const float vprev = S > 1 ? __shfl_sync(kFull, x.a1, l_prev) : kNegInf;
+  const bool covers = base + W >= S;  // S-1 and S-2 inside the window
+  const int r_last = min(max(S - 1 - base, 0), W - 1), r_prev = min(max(S - 2 - base, 0), W - 1);
+  const float vlast = __shfl_sync(kFull, pick<K>(x.a, r_last % K), r_last / K);
+  const float vprev = S > 1 ? __shfl_sync(kFull, pick<K>(x.a, r_prev % K), r_prev / K) : kNegInf;
   const bool take_prev = S > 1 && vprev >= vlast;
   const float opt = take_prev ? vprev : vlast;
   const int term = take_prev ? S - 2 : S - 1;
@@ -575,7 +639,7 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   accepted = __reduce_add_sync(kFull, accepted);
   frames = __reduce_add_sync(kFull, frames);
   multiple = __reduce_add_sync(kFull, multiple);
-  if (lane == 0) {
+  if (!kWide && lane == 0) {
     P.out.shortcut_stats[3 * r + 0] = accepted;
     P.out.shortcut_stats[3 * r + 1] = frames;
     P.out.shortcut_stats[3 * r + 2] = multiple;
@@ -590,15 +654,15 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
       static_cast<double>(T) * (ldexp(aopt, -23) + ldexp(am, -50)) + ldexp(aopt + am, -21) + 1e-9;
   const bool certified =
       covers && !poison && !positive && isfinite(opt) && isfinite(M) && exit_loss > loss + margin;
-
   if (!certified) {
-    // The full conventional DP takes the record (ffa_window_fallback); the
-    // reference's routing state 2 is its completed early fallback.
+    // The next tier takes the record: the 128-state window, then the full
+    // conventional DP (the reference's routing state 2: its completed early
+    // fallback).
     if (lane == 0) {
-      P.out.routing_stats[3 * r] = 2;
+      if (kWide || poison || positive) P.out.routing_stats[3 * r] = 2;
       P.fallback_list[atomicAdd(P.fallback_count, 1)] = r;
     }
-    return;
+    return true;
   }
 
   // ---- traceback in shared memory ----
@@ -610,8 +674,8 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
       anc[g] = static_cast<int16_t>(s);
       if (g > 0) {
         const int tl = min(T, (g + 1) * kWinChunk) - 1;
-        const int k = min(max(s - static_cast<int>(gb[tl >> 3]), 0), kWinStates - 1);
-        s = map[g * kWinStates + k];
+        const int k = min(max(s - static_cast<int>(gb[tl >> 3]), 0), W - 1);
+        s = map[g * W + k];
       }
     }
   }
@@ -624,9 +688,10 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
     int s = anc[g];
     path[t_hi] = static_cast<uint16_t>(s);
     for (int t = t_hi; t > t_lo; --t) {
-      const int k = min(max(s - static_cast<int>(gb[t >> 3]), 0), kWinStates - 1);
-      const uint32_t word = bp[(t >> 3) * 32 + (k >> 1)];
-      s -= static_cast<int>((word >> (4 * (t & 7) + 2 * (k & 1))) & 3u);
+      const int k = min(max(s - static_cast<int>(gb[t >> 3]), 0), W - 1);
+      const int j = t & 7;
+      const uint32_t word = bp[((t >> 3) * kWords + j / kFramesPerWord) * 32 + k / K];
+      s -= static_cast<int>((word >> (2 * K * (j % kFramesPerWord) + 2 * (k % K))) & 3u);
       path[t - 1] = static_cast<uint16_t>(s);
     }
   }
@@ -644,9 +709,13 @@ __device__ __forceinline__ void window_record(const WindowParams& P, int r, unsi
   if (lane == 0) {
     P.out.objective[r] = opt;
     P.out.status[r] = 0;
+    if (kWide) P.out.routing_stats[3 * r] = 0;
   }
+  return true;
 }
 
+// The 64-state window: one warp per record of the call's window route, the
+// CTA's records listed by the host.
 template <int kFmt, int kV>
 __global__ void __launch_bounds__(32 * kWinWarps, 1)
 ffa_window_viterbi(const __grid_constant__ WindowParams P) {
@@ -656,7 +725,30 @@ ffa_window_viterbi(const __grid_constant__ WindowParams P) {
   const WinCta cta = P.ctas[blockIdx.x];
   if (warp >= cta.count) return;
   const WinSlot slot = P.slots[cta.first + warp];
-  window_record<kFmt, kV>(P, slot.record, smem_raw + slot.smem_off, bars[warp], lane);
+  window_record<kFmt, kV, 2>(P, slot.record, smem_raw + slot.smem_off, bars[warp], lane);
+}
+
+// The 128-state window for the records the 64-state window did not certify:
+// one warp per CTA, striding over the device-written list (records longer
+// than kWinWideMaxFrames go straight to the full DP's list).
+template <int kFmt, int kV>
+__global__ void __launch_bounds__(32, 1)
+ffa_window_wide(const __grid_constant__ WindowParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ unsigned long long bars[kWinRing];
+  const int lane = static_cast<int>(threadIdx.x);
+  const int n = *P.in_count;
+  for (int i = static_cast<int>(blockIdx.x); i < n; i += static_cast<int>(gridDim.x)) {
+    const int r = P.in_list[i];
+    if (P.recs[r].T > kWinWideMaxFrames) {
+      if (lane == 0) {
+        P.out.routing_stats[3 * r] = 2;
+        P.fallback_list[atomicAdd(P.fallback_count, 1)] = r;
+      }
+      continue;
+    }
+    if (!window_record<kFmt, kV, 4>(P, r, smem_raw, bars, lane)) break;  // copies may be in flight
+  }
 }
 
 constexpr int kWindowVariantsDecl = 4;
@@ -664,14 +756,28 @@ int window_variant(int row_vocab, int fmt) { return fmt == 0 ? (row_vocab == 32 
 using GreedyKernel = void (*)(GreedyParams);
 const GreedyKernel kGreedyKernels[kWindowVariantsDecl] = {
     ffa_greedy_pass<0, 32>, ffa_greedy_pass<0, 0>, ffa_greedy_pass<1, 0>, ffa_greedy_pass<2, 0>};
-
 using WindowKernel = void (*)(WindowParams);
-// Variants: log-probabilities with V = 32 specialised, any row vocabulary,
-// fp32 and bf16 logits.
-constexpr int kWindowVariants = 4;
-static_assert(kWindowVariants == kWindowVariantsDecl, "variant tables");
-const WindowKernel kWindowKernels[kWindowVariants] = {
+const WindowKernel kWindowKernels[kWindowVariantsDecl] = {
     ffa_window_viterbi<0, 32>, ffa_window_viterbi<0, 0>, ffa_window_viterbi<1, 0>, ffa_window_viterbi<2, 0>};
+const WindowKernel kWideKernels[kWindowVariantsDecl] = {
+    ffa_window_wide<0, 32>, ffa_window_wide<0, 0>, ffa_window_wide<1, 0>, ffa_window_wide<2, 0>};
+
+// Opt a window kernel in to the dynamic shared memory budget (once per
+// device); the CTA's static shared memory (its mbarriers) stays under 1 KiB.
+constexpr size_t kWinStatic = 1024;
+static_assert(sizeof(unsigned long long) * kWinWarps * kWinRing <= kWinStatic, "window static shared memory");
+cudaError_t window_opt_in(WindowKernel kernel, std::atomic<uint64_t>& opted) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
+  if (bit != 0 && (opted.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBudget - kWinStatic));
+  if (err != cudaSuccess) return err;
+  if (bit) opted.fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
 
 }  // namespace
 
@@ -689,25 +795,30 @@ cudaError_t launch_window(const WindowParams& params, int num_ctas, int row_voca
                           cudaStream_t stream) {
   if (num_ctas <= 0) return cudaSuccess;
   if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted[kWindowVariantsDecl];
   const int variant = window_variant(row_vocab, fmt);
-  static std::atomic<uint64_t> opted[kWindowVariants];
-  const WindowKernel kernel = kWindowKernels[variant];
-  // The CTA's static shared memory (its mbarriers) stays under 1 KiB.
-  constexpr size_t kStatic = 1024;
-  static_assert(sizeof(unsigned long long) * kWinWarps * kWinRing <= kStatic, "window static shared memory");
-  int device = 0;
-  cudaError_t err = cudaGetDevice(&device);
+  cudaError_t err = window_opt_in(kWindowKernels[variant], opted[variant]);
   if (err != cudaSuccess) return err;
-  const uint64_t bit = device < 64 ? uint64_t{1} << device : 0;
-  if (bit == 0 || !(opted[variant].load(std::memory_order_acquire) & bit)) {
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kSmemBudget - kStatic));
-    if (err != cudaSuccess) return err;
-    if (bit) opted[variant].fetch_or(bit, std::memory_order_acq_rel);
-  }
-  if (smem_bytes > kSmemBudget - kStatic) return cudaErrorInvalidValue;
+  if (smem_bytes > kSmemBudget - kWinStatic) return cudaErrorInvalidValue;
   count_launch();
-  kernel<<<num_ctas, 32 * kWinWarps, smem_bytes, stream>>>(params);
+  kWindowKernels[variant]<<<num_ctas, 32 * kWinWarps, smem_bytes, stream>>>(params);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_window_wide(const WindowParams& params, int max_count, int row_vocab, int fmt,
+                               unsigned smem_bytes, cudaStream_t stream) {
+  if (max_count <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> opted[kWindowVariantsDecl];
+  const int variant = window_variant(row_vocab, fmt);
+  cudaError_t err = window_opt_in(kWideKernels[variant], opted[variant]);
+  if (err != cudaSuccess) return err;
+  if (smem_bytes > kSmemBudget - kWinStatic) return cudaErrorInvalidValue;
+  int device = 0, sms = 0;
+  if ((err = cudaGetDevice(&device)) != cudaSuccess) return err;
+  if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return err;
+  count_launch();
+  kWideKernels[variant]<<<std::min(max_count, std::max(sms, 1)), 32, smem_bytes, stream>>>(params);
   return cudaGetLastError();
 }
 
