@@ -224,6 +224,75 @@ def unfused_logits_ms(ffa, e_dev, t_dev, wl, args, flush):
     return sum(a.elapsed_time(b) for a, b in evs) / args.steps
 
 
+def queued_device_ms(call, steps, warmup, flush):
+    """Device time of `call` per step, timed as the value loop: `warmup`
+    untimed calls, then `steps` calls queued back to back (no host sync),
+    the L2 flushed on the device before each, CUDA events around each call.
+    Returns the list of per-step milliseconds."""
+    import torch
+    for _ in range(warmup):
+        flush.zero_()
+        call()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        a.record(); b.record()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(20_000_000)
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        call()
+        b.record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def reference_cuda_lane(wl, e_dev, t_dev, steps, warmup, flush):
+    """The reference's own CUDA extension (compiled in place from its
+    alignment.cu into oracle/_ref) on the same device-resident batch, both
+    modes, timed exactly like `value`; None if it is not built."""
+    from oracle import oracle
+    if not oracle.load_reference_cuda():
+        return None
+    es = list(e_dev.split(wl.lengths.tolist()))
+    ts = list(t_dev.split(wl.target_lengths.tolist()))
+    blanks = [wl.blank] * wl.batch
+    frames = int(wl.lengths.sum())
+    out = {}
+    for mode in ("optimized", "conventional"):
+        ms = queued_device_ms(lambda: oracle.reference_cuda_align(es, ts, blanks, mode=mode, check_inputs=True),
+                              steps, warmup, flush)
+        out[mode] = {"value": frames * steps / (sum(ms) / 1e3), "ms_per_step": sum(ms) / steps}
+    return out
+
+
+def strong_cfg4_lane(ffa, rank, world, device, steps, warmup, flush, max_over_ranks, barrier):
+    """Strong scaling on the multi-GPU configuration (cfg4): every rank draws
+    the same 8,256-record batch and aligns its LPT share (shard_of_rank),
+    device-resident, timed as `value`; the whole box's frames/s over the
+    slowest rank's time."""
+    import torch
+    from fast_forced_aligner_b200 import workloads
+    from fast_forced_aligner_b200.sharding import shard_of_rank
+    pool = workloads.config(4)
+    shard = pool.subset(shard_of_rank(pool.lengths, pool.target_lengths, rank, world))
+    e = torch.from_numpy(shard.emissions).to(device)
+    t = torch.from_numpy(shard.targets).to(device)
+
+    def call():
+        return ffa.align_packed(e, shard.lengths, t, shard.target_lengths, blank_id=0, mode="optimized")
+    barrier()
+    ms = queued_device_ms(call, steps, warmup, flush)
+    total = max_over_ranks(sum(ms))
+    barrier()
+    frames = int(pool.lengths.sum())
+    return {"value": frames * steps / (total / 1e3), "unit": "frames/s", "ms_per_step": total / steps,
+            "n_gpus": world, "scaling": "strong", "records_total": pool.batch, "frames_total": frames,
+            "records_this_rank": shard.batch,
+            "how": "cfg4 (8,256 records) LPT-partitioned over the ranks by record cost (shard_of_rank), "
+                   "optimized mode, device-resident, L2 flushed before every step; max over ranks"}
+
+
 def cpu_reference_runner(wl):
     """The reference's corrected C++ comparator (oracle/_ref) over all host
     threads, one record per task with the GIL released, as in its benchmark
@@ -434,6 +503,11 @@ def run_ours(args):
         if e_dev.dtype == torch.float32 else None
     unfused = unfused_logits_ms(ffa, e_dev, t_dev, wl, args, flush) if from_logits else None
 
+    ref_cuda = reference_cuda_lane(wl, e_dev, t_dev, args.steps, args.warmup, flush) \
+        if world == 1 and not from_logits and args.scale == 1.0 else None
+    strong = strong_cfg4_lane(ffa, rank, world, device, args.steps, args.warmup, flush, max_over_ranks, barrier) \
+        if args.config == 1 and not args.split and not from_logits and args.scale == 1.0 else None
+
     all_frames = sum_over_ranks(frames)
     value = all_frames * args.steps / (total_ms / 1e3)
     e2e_value = all_frames * args.steps / (e2e_ms / 1e3)
@@ -488,6 +562,15 @@ def run_ours(args):
                              "ffa_launch_count), in the device-resident and the end-to-end timed loops",
         "status_ok": status_ok,
     }
+    if ref_cuda is not None:
+        line["reference_cuda"] = dict(
+            ref_cuda, ratio_value=value / ref_cuda[args.mode]["value"],
+            ratio_value_vs_optimized=value / ref_cuda["optimized"]["value"],
+            how="the reference's CUDA extension (its alignment.cu compiled in place for sm_100a with the flags "
+                "its loader passes) on the same device-resident batch, called with its public-API arguments "
+                "(alignment.py:496-501), timed exactly as value")
+    if strong is not None:
+        line["strong_cfg4"] = strong
     if unfused is not None:
         line["unfused"] = {"ms_per_step": unfused, "value": frames * world / (unfused / 1e3),
                            "pipeline": "torch.log_softmax(logits.float(), -1) then align_packed on the "

@@ -219,12 +219,13 @@ def emission_validity(emissions: Sequence[Tensor]) -> Tensor:
         return torch.ops.ffa_b200.emission_validity(list(emissions))
 
 
-_ROUTES = ("auto", "pieces")
+_ROUTES = {"auto": 1, "pieces": 2, "window": 3}
 
 
 def _mode(mode, check_inputs, from_logits=False, route="auto") -> int:
     """The torch op's mode code: 0 conventional, 1 optimized, 2 optimized on
-    the chunked route for every record (``route="pieces"``)."""
+    the chunked route for every record (``route="pieces"``), 3 on the window
+    route wherever it applies (``route="window"``)."""
     if mode not in _MODES:
         raise ValueError("mode must be 'optimized' or 'conventional'")
     if type(check_inputs) is not bool:
@@ -232,8 +233,8 @@ def _mode(mode, check_inputs, from_logits=False, route="auto") -> int:
     if type(from_logits) is not bool:
         raise TypeError("from_logits must be bool")
     if route not in _ROUTES:
-        raise ValueError("route must be 'auto' or 'pieces'")
-    return 2 if (_MODES[mode] == 1 and route == "pieces") else _MODES[mode]
+        raise ValueError("route must be 'auto', 'pieces' or 'window'")
+    return _ROUTES[route] if _MODES[mode] == 1 else _MODES[mode]
 
 
 def _input_format(first, from_logits: bool) -> int:
@@ -316,13 +317,14 @@ def align(
         blank_id: one Python int or ``B`` Python ints (bools rejected).
         mode: ``"optimized"`` (default) or ``"conventional"``.  Conventional
             runs the exact max-plus Viterbi DP (stay > step > skip tie rule).
-            Optimized runs, for records of at most 64 labels (16-byte aligned
-            rows), 4096 states and 8192 frames, the window route: the same DP
-            restricted to 64 states that slide up the trellis, certified on
-            the GPU against each frame's greedy bound (the best emission over
-            the transcript alphabet) -- its outputs are then the conventional
-            ones bit for bit, ties included -- with the full DP where the
-            certificate fails.  Other records take the chunked route:
+            Optimized has two routes (``route``).  The window route: a
+            greedy pass (each frame's best emission over the transcript
+            alphabet), then the same DP restricted to 64 states that slide up
+            the trellis, certified on the GPU against those bounds -- its
+            outputs are then the conventional ones bit for bit, ties included
+            -- with a 128-state window and then the full DP where the
+            certificate fails; for records of at most 64 labels (16-byte
+            aligned rows), 4096 states and 8192 frames.  The chunked route:
             32-frame pieces joined at legal seams (with repairs, and the
             conventional DP as fallback), which returns the conventional
             outputs bit for bit unless the conventional DP meets a tie on its
@@ -339,10 +341,12 @@ def align(
             subtracts the row's log-sum-exp (``log_softmax`` returns the same
             matrices, for inspection).  Not in the reference, whose examples
             call ``torch.log_softmax`` first.
-        route: ``"auto"`` (default) as described under ``mode``, or
-            ``"pieces"``: the chunked route for every record of the
-            optimized mode (the reference's optimized design).  Not in the
-            reference.
+        route: which optimized route a record takes.  ``"auto"`` (default):
+            the window route for records of at most 2048 frames in batches of
+            more than 4 such records per SM, the chunked route for the rest;
+            ``"pieces"``: the chunked route for every record (the reference's
+            optimized design); ``"window"``: the window route for every
+            record it can take.  Not in the reference.
 
     Returns:
         AlignmentBatch with packed CUDA outputs.  Failures are recorded in

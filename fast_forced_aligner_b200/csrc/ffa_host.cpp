@@ -48,6 +48,8 @@ int fail(int code, const std::string& message) {
 
 constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+constexpr int kKnownFlags = FFA_FLAG_CHECK_INPUTS | FFA_FLAG_PIECE_ROUTE | FFA_FLAG_WINDOW_ROUTE;
+
 struct Geometry {
   bool window;   // optimized mode: the window DP (ffa_window.cu), full DP as fallback
   bool chunked;  // optimized mode: solved in pieces
@@ -91,17 +93,39 @@ bool row_staged(const ffa_record& r) {
          (reinterpret_cast<uintptr_t>(r.emissions) & 15) == 0;
 }
 
-// Records the window DP takes (windows: optimized mode without
-// FFA_FLAG_PIECE_ROUTE): row-staged, at most kMaxStates states, and short
-// enough for their backpointers to stay in shared memory.
-bool window_record(const ffa_record& r, bool windows) {
-  return windows && 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates &&
-         r.frames <= ffa::kWinMaxFrames && row_staged(r);
+// Which records of the optimized mode the window DP takes: row-staged, at
+// most kMaxStates states, and at most max_frames frames (0: none).  By
+// default the window route runs only where it is faster: a batch with many
+// records (more than kWinAutoRecordsPerSm per SM: one warp per record is a
+// latency chain, so it pays where records keep every SM busy) and records of
+// at most kWinAutoMaxFrames frames; FFA_FLAG_WINDOW_ROUTE gives it every
+// record it can hold, FFA_FLAG_PIECE_ROUTE none.
+struct WindowPolicy {
+  int64_t max_frames;
+};
+constexpr int64_t kWinAutoRecordsPerSm = 4;
+constexpr int64_t kWinAutoMaxFrames = 2048;
+
+bool window_shape(const ffa_record& r, int64_t max_frames) {
+  return 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates && r.frames <= max_frames && row_staged(r);
+}
+
+int device_sms();
+WindowPolicy window_policy(const ffa_record* records, int64_t count, int mode, int flags) {
+  if (mode != FFA_MODE_OPTIMIZED || (flags & FFA_FLAG_PIECE_ROUTE)) return WindowPolicy{0};
+  if (flags & FFA_FLAG_WINDOW_ROUTE) return WindowPolicy{ffa::kWinMaxFrames};
+  int64_t n = 0;
+  for (int64_t i = 0; i < count; ++i) n += window_shape(records[i], kWinAutoMaxFrames) ? 1 : 0;
+  return WindowPolicy{n > kWinAutoRecordsPerSm * device_sms() ? kWinAutoMaxFrames : 0};
+}
+
+bool window_record(const ffa_record& r, const WindowPolicy& w) {
+  return w.max_frames > 0 && window_shape(r, w.max_frames);
 }
 
 // Records of the optimized mode solved in pieces: the rest, when long enough.
-bool chunked_record(const ffa_record& r, bool optimized, bool windows) {
-  return optimized && !window_record(r, windows) && r.frames >= ffa::kPieceMinFrames;
+bool chunked_record(const ffa_record& r, bool optimized, const WindowPolicy& w) {
+  return optimized && !window_record(r, w) && r.frames >= ffa::kPieceMinFrames;
 }
 
 // Pieces of kPieceFrames frames; the last one also takes a remainder shorter
@@ -112,7 +136,7 @@ int64_t piece_count(int64_t T) {
   return std::max<int64_t>(C, 1);
 }
 
-Geometry geometry(const ffa_record& r, bool optimized, bool windows, bool latency_bound) {
+Geometry geometry(const ffa_record& r, bool optimized, const WindowPolicy& windows, bool latency_bound) {
   Geometry g{};
   const int64_t S = 2 * static_cast<int64_t>(r.tokens) + 1;
   if (S > ffa::kMaxStates) {
@@ -214,7 +238,8 @@ bool latency_bound(int64_t slots) { return slots <= device_sms(); }
 
 // Sizes of one call.  Everything here is independent of the thread layout
 // (states per thread), so one pass over the records suffices.
-int plan_align(const ffa_record* records, int64_t count, bool optimized, bool windows, AlignLayout* L) {
+int plan_align(const ffa_record* records, int64_t count, bool optimized, const WindowPolicy& windows,
+               AlignLayout* L) {
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
@@ -502,10 +527,12 @@ int ffa_align_query(const ffa_record* records, int64_t count, int mode, int flag
   if (sizes == nullptr) return fail(FFA_ERR_INVALID_ARGUMENT, "sizes must not be NULL");
   if (mode != FFA_MODE_CONVENTIONAL && mode != FFA_MODE_OPTIMIZED)
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
-  if (flags & ~(FFA_FLAG_CHECK_INPUTS | FFA_FLAG_PIECE_ROUTE)) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  if (flags & ~kKnownFlags) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
   AlignLayout L{};
   const bool optimized = mode == FFA_MODE_OPTIMIZED;
-  const int rc = plan_align(records, count, optimized, optimized && !(flags & FFA_FLAG_PIECE_ROUTE), &L);
+  if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
+  const int rc = plan_align(records, count, optimized, window_policy(records, count, mode, flags), &L);
   if (rc) return rc;
   sizes->staging_bytes = L.staging_bytes;
   sizes->workspace_bytes = L.workspace_bytes;
@@ -524,9 +551,13 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return fail(FFA_ERR_INVALID_ARGUMENT, "every output buffer except reuse_stats is required");
   if (mode != FFA_MODE_CONVENTIONAL && mode != FFA_MODE_OPTIMIZED)
     return fail(FFA_ERR_INVALID_ARGUMENT, "mode must be conventional or optimized");
-  if (flags & ~(FFA_FLAG_CHECK_INPUTS | FFA_FLAG_PIECE_ROUTE)) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  if (flags & ~kKnownFlags) return fail(FFA_ERR_INVALID_ARGUMENT, "unknown flags");
+  if ((flags & FFA_FLAG_PIECE_ROUTE) && (flags & FFA_FLAG_WINDOW_ROUTE))
+    return fail(FFA_ERR_INVALID_ARGUMENT, "choose one of the piece and window routes");
   const bool optimized = mode == FFA_MODE_OPTIMIZED;
-  const bool windows = optimized && !(flags & FFA_FLAG_PIECE_ROUTE);
+  if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
+    return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
+  const WindowPolicy windows = window_policy(records, count, mode, flags);
   AlignLayout L{};
   int rc = plan_align(records, count, optimized, windows, &L);
   if (rc) return rc;

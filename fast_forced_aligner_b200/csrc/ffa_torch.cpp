@@ -179,9 +179,11 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> run_align(
     const uint8_t* mask, bool check_inputs, c10::cuda::CUDAStream stream,
     std::vector<int64_t> lengths) {
   const int64_t count = static_cast<int64_t>(recs.size());
-  // mode 0 conventional, 1 optimized, 2 optimized on the chunked route only.
+  // mode 0 conventional, 1 optimized, 2 optimized on the chunked route only,
+  // 3 optimized on the window route wherever it applies.
   const int cmode = mode == 0 ? FFA_MODE_CONVENTIONAL : FFA_MODE_OPTIMIZED;
-  const int flags = (check_inputs ? FFA_FLAG_CHECK_INPUTS : 0) | (mode == 2 ? FFA_FLAG_PIECE_ROUTE : 0);
+  const int flags = (check_inputs ? FFA_FLAG_CHECK_INPUTS : 0) | (mode == 2 ? FFA_FLAG_PIECE_ROUTE : 0) |
+                    (mode == 3 ? FFA_FLAG_WINDOW_ROUTE : 0);
   ffa_sizes sizes{};
   check_status(ffa_align_query(recs.data(), count, cmode, flags, &sizes));
 
@@ -216,7 +218,7 @@ std::tuple<std::vector<at::Tensor>, std::vector<int64_t>> run_align(
 }
 
 void check_mode(int64_t mode) {
-  TORCH_CHECK_VALUE(mode >= 0 && mode <= 2, "mode must be 'optimized' or 'conventional'");
+  TORCH_CHECK_VALUE(mode >= 0 && mode <= 3, "mode must be 'optimized' or 'conventional'");
 }
 
 // Input format (ffa_input_format) and the dtype it stores: fp32

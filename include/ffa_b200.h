@@ -63,21 +63,28 @@ typedef enum ffa_mode {
   FFA_MODE_OPTIMIZED = 1     /* greedy-bounded window DP / chunked route, exact DP fallback */
 } ffa_mode;
 
-/* Optimized mode solves a record whose rows can be TMA-staged (vocab <= 64,
- * 16-byte aligned rows), with at most 4096 states and 8192 frames, by the
- * window route: the conventional DP restricted to a 64-state window that
- * slides up the trellis, certified on the device against the greedy bound of
- * every frame (the largest emission over the transcript alphabet, the
- * maximum the reference's greedy_shortcuts finds, alignment.cu:29-153) --
- * its outputs are then the conventional DP's, bit for bit, ties included --
- * and the full conventional DP where the certificate fails.  Every other
- * record of the optimized mode (or every record, with FFA_FLAG_PIECE_ROUTE)
- * takes the chunked route of the reference's optimized mode
- * (alignment.cu:163-228, 525-592): relaxed 32-frame pieces joined at legal
- * seams, repairs of merged regions, the full DP as fallback. */
+/* Optimized mode has two routes.
+ *   Window route: a greedy pass over the emission rows (per frame, the
+ *     largest emission over the transcript alphabet -- the maximum the
+ *     reference's greedy_shortcuts finds, alignment.cu:29-153 -- and its
+ *     greedy chunk statistics), then the conventional DP restricted to a
+ *     64-state window that slides up the trellis, one warp per record,
+ *     certified on the device against those bounds: its outputs are then the
+ *     conventional DP's, bit for bit, ties included.  Where the certificate
+ *     fails, a 128-state window, then the full conventional DP.  For records
+ *     whose rows can be TMA-staged (vocab <= 64, 16-byte aligned rows), with
+ *     at most 4096 states and 8192 frames.
+ *   Chunked route (the reference's optimized design, alignment.cu:163-228,
+ *     525-592): relaxed 32-frame pieces joined at legal seams, repairs of
+ *     merged regions, the full DP as fallback.
+ * By default the window route takes the records of at most 2048 frames of a
+ * batch with more than 4 such records per SM (where one warp per record keeps
+ * the GPU busy), the chunked route the rest; the flags choose one route for
+ * every record it can take. */
 enum {
   FFA_FLAG_CHECK_INPUTS = 1, /* validate target IDs and frame feasibility on the device */
-  FFA_FLAG_PIECE_ROUTE = 2   /* optimized mode: the chunked route for every record */
+  FFA_FLAG_PIECE_ROUTE = 2,  /* optimized mode: the chunked route for every record */
+  FFA_FLAG_WINDOW_ROUTE = 4  /* optimized mode: the window route for every record it can take */
 };
 
 /* Limits (alignment.py:237, 249-250).  The reference stops at 2047 tokens
