@@ -467,6 +467,30 @@ cudaError_t upload_descriptors(void* dst, const void* staging, size_t bytes, cud
   return cudaMemcpyAsync(dst, staging, bytes, cudaMemcpyHostToDevice, s);
 }
 
+// A side stream and two events per host thread and device: a call whose
+// records take both optimized routes runs the window route there, forked
+// from and joined back into the caller's stream, so the two routes' kernels
+// share the GPU instead of queueing behind each other.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+cudaError_t side_stream(SideStream** out) {
+  thread_local SideStream sides[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  SideStream& side = sides[dev];
+  if (side.stream == nullptr) {
+    if ((err = cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking)) != cudaSuccess) return err;
+    if ((err = cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming)) != cudaSuccess) return err;
+    if ((err = cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming)) != cudaSuccess) return err;
+  }
+  *out = &side;
+  return cudaSuccess;
+}
+
 int cuda_fail(cudaError_t err, const char* what) {
   return fail(FFA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
 }
@@ -888,8 +912,19 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return e == cudaSuccess ? FFA_OK : cuda_fail(e, "profiling event");
   };
   if ((rc = mark(FFA_PROFILE_START))) return rc;
-  // Window route: the window DP of every such record, then the full DP of
-  // those whose window was not certified (a device-written list).
+  // Window route: the greedy pass, the window DP of every such record, then
+  // the wider window and the full DP of those a tier did not certify
+  // (device-written lists) -- on a side stream when the chunked route or the
+  // long records have work too.
+  cudaStream_t ws = s;
+  SideStream* side = nullptr;
+  const bool forked = n_wcta > 0 && (nb > 0 || !long_keys.empty());
+  if (forked) {
+    if ((err = side_stream(&side)) != cudaSuccess) return cuda_fail(err, "side stream");
+    if ((err = cudaEventRecord(side->fork, s)) != cudaSuccess) return cuda_fail(err, "stream fork");
+    if ((err = cudaStreamWaitEvent(side->stream, side->fork, 0)) != cudaSuccess) return cuda_fail(err, "stream fork");
+    ws = side->stream;
+  }
   if (n_wcta > 0) {
     const int wv = win_vocab > 0 ? win_vocab : 0;
     // The greedy pass streams every row of the window records once: it is
@@ -901,11 +936,11 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     gp.lse = fp.lse;
     gp.bound = reinterpret_cast<float*>(dev + L.bound);
     gp.verdicts = reinterpret_cast<uint8_t*>(dev + L.verdicts);
-    if (g_profile_before != nullptr && (err = cudaEventRecord(g_profile_before, s)) != cudaSuccess)
+    if (g_profile_before != nullptr && (err = cudaEventRecord(g_profile_before, ws)) != cudaSuccess)
       return cuda_fail(err, "profiling event");
-    err = ffa::launch_greedy(gp, wv, fmt, s);
+    err = ffa::launch_greedy(gp, wv, fmt, ws);
     if (err != cudaSuccess) return cuda_fail(err, "greedy pass launch");
-    if (g_profile_after != nullptr && (err = cudaEventRecord(g_profile_after, s)) != cudaSuccess)
+    if (g_profile_after != nullptr && (err = cudaEventRecord(g_profile_after, ws)) != cudaSuccess)
       return cuda_fail(err, "profiling event");
     ffa::WindowParams wp{};
     wp.recs = fp.recs;
@@ -926,17 +961,17 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     int32_t* count2 = count1 + 1;
     wp.fallback_list = list1;
     wp.fallback_count = count1;
-    err = ffa::launch_window(wp, static_cast<int>(n_wcta), wv, fmt, win_smem, s);
+    err = ffa::launch_window(wp, static_cast<int>(n_wcta), wv, fmt, win_smem, ws);
     if (err != cudaSuccess) return cuda_fail(err, "window launch");
     ffa::WindowParams wide = wp;
     wide.in_list = list1;
     wide.in_count = count1;
     wide.fallback_list = list2;
     wide.fallback_count = count2;
-    err = ffa::launch_window_wide(wide, static_cast<int>(win_records.size()), wv, fmt, wide_smem, s);
+    err = ffa::launch_window_wide(wide, static_cast<int>(win_records.size()), wv, fmt, wide_smem, ws);
     if (err != cudaSuccess) return cuda_fail(err, "wide window launch");
     err = ffa::launch_window_fallback(fp, list2, count2, static_cast<int>(win_records.size()), wv, fmt,
-                                      static_cast<unsigned>(header + row_slot_bytes), s);
+                                      static_cast<unsigned>(header + row_slot_bytes), ws);
     if (err != cudaSuccess) return cuda_fail(err, "window fallback launch");
   }
   // Long records: the conventional DP on one cluster each, one launch per
@@ -1013,6 +1048,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                          static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, fp.lse,
                          fmt, s);
   if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
+  if (forked) {
+    if ((err = cudaEventRecord(side->join, ws)) != cudaSuccess) return cuda_fail(err, "stream join");
+    if ((err = cudaStreamWaitEvent(s, side->join, 0)) != cudaSuccess) return cuda_fail(err, "stream join");
+  }
   if ((rc = mark(FFA_PROFILE_FILL))) return rc;
   return FFA_OK;
 }
