@@ -2,10 +2,11 @@
 own CPU comparator (golden fixtures) and the reference's own CUDA extension.
 
 Configs follow the benchmark configurations (fast_forced_aligner_b200.workloads); cfg4 runs
-at full size.  Both modes must return the conventional DP's exact outputs on
-every record without a constructed tie; on cfg4's 64 tie records the
-optimized route must return the same optimum (a path of equal score), and the
-count of tie records that also got the conventional path is printed.
+at full size.  Conventional mode returns the oracle's outputs bit for bit on
+every record.  Optimized mode does too on the window route; on the chunked
+route a record may get another path only where the conventional DP met an
+fp32 tie, and every such record is classified exactly
+(tests/helpers.classify_divergence) and counted against pinned numbers.
 """
 import ctypes
 
@@ -17,7 +18,7 @@ import fast_forced_aligner_b200 as ffa
 from fast_forced_aligner_b200 import workloads
 from oracle import oracle
 from tests.golden.make_golden import load as load_golden
-from tests.helpers import (assert_matches_oracle, assert_same_bits, assert_same_optimum, collapse,
+from tests.helpers import (assert_matches_oracle, assert_same_bits, classify_divergence, collapse,
                            cuda_records, sequential_sum)
 
 pytestmark = pytest.mark.gpu
@@ -45,31 +46,63 @@ def test_golden_reference_cpu_cases(cuda, mode):
     assert_same_bits(result.scores.cpu().numpy(), np.concatenate([c[4] for c in cases]), "scores")
 
 
-@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("index, scale", [(0, 1.0), (1, 1.0), (3, 1.0), (4, 1.0)])
-def test_configs_match_oracle(cuda, mode, index, scale):
+def test_conventional_configs_match_oracle(cuda, index, scale):
     wl, ref = config(index, scale)
     es, ts = cuda_records(*wl.records())
-    result = ffa.align(es, ts, blank_id=wl.blank, mode=mode)
+    result = ffa.align(es, ts, blank_id=wl.blank, mode="conventional")
     assert (ref.status == 0).all()
-    if mode == "conventional" or not wl.tie_frames:
-        assert_matches_oracle(result, ref, f"cfg{index}")
-        return
-    # Besides the constructed ties, records of this size hold a few fp32
-    # ties: paths whose scores differ by less than the rounding step of the
-    # conventional running sum, which the conventional DP cannot tell apart.
-    # Every record must reach the conventional optimum; all but a handful of
-    # the non-tie records must also get the conventional path itself.
-    same = assert_same_optimum(result, ref, *wl.records(), wl.blank, f"cfg{index}")
+    assert_matches_oracle(result, ref, f"cfg{index}")
+
+
+# Records on which the optimized mode's path differs from the conventional
+# DP's, by exact class (tests/helpers.classify_divergence), per route and
+# config: the window route is exact everywhere (its certificate proves the
+# conventional path); the chunked route may return another path only where
+# the conventional DP met an fp32 tie.  Any "worse" record fails; the counts
+# are pinned, so a new divergence of any class fails too.
+EXPECTED_DIVERGENCES = {
+    ("window", 0): {}, ("window", 1): {}, ("window", 4): {},
+    ("pieces", 0): {}, ("pieces", 1): {}, ("pieces", 3): {}, ("pieces", 4): {},
+    ("auto", 0): {}, ("auto", 1): {}, ("auto", 3): {}, ("auto", 4): {},
+}
+
+
+@pytest.mark.parametrize("route", ["auto", "window", "pieces"])
+@pytest.mark.parametrize("index", [0, 1, 3, 4])
+def test_optimized_divergences_are_proven_ties(cuda, route, index):
+    if route == "window" and index == 3:
+        pytest.skip("V = 1025 rows are not row-staged: the window route does not take them")
+    wl, ref = config(index)
+    es_h, ts_h = wl.records()
+    es, ts = cuda_records(es_h, ts_h)
+    result = ffa.align(es, ts, blank_id=wl.blank, mode="optimized", route=route)
+    assert_same_bits(result.status.cpu().numpy(), ref.status, "status")
     labels = result.labels.cpu().numpy()
+    scores = result.scores.cpu().numpy()
+    objective = result.objective.cpu().numpy()
     off = wl.frame_offsets
-    differ = [i for i in range(wl.batch)
-              if not np.array_equal(labels[off[i]:off[i + 1]], ref.labels[off[i]:off[i + 1]])]
-    non_tie_differ = [i for i in differ if i not in wl.tie_frames]
-    print(f"cfg{index} optimized: conventional path on {same}/{wl.batch} records; differing: "
-          f"{len(differ) - len(non_tie_differ)}/{len(wl.tie_frames)} tie records, "
-          f"{len(non_tie_differ)} others {non_tie_differ[:10]}")
-    assert len(non_tie_differ) <= max(3, wl.batch // 1000)
+    classes = {}
+    for i in range(wl.batch):
+        lo, hi = off[i], off[i + 1]
+        p, q = labels[lo:hi], ref.labels[lo:hi]
+        if np.array_equal(p, q):
+            assert_same_bits(scores[lo:hi], ref.scores[lo:hi], f"record {i} scores")
+            assert_same_bits(objective[i:i + 1], ref.objective[i:i + 1], f"record {i} objective")
+            continue
+        # A different path: legal, its own scores, and an exact class.
+        np.testing.assert_array_equal(collapse(p, wl.blank), ts_h[i], f"record {i} transcript")
+        selected = es_h[i][np.arange(hi - lo), p]
+        assert_same_bits(scores[lo:hi], selected, f"record {i} scores")
+        assert sequential_sum(selected) == objective[i], f"record {i} objective"
+        cls = classify_divergence(es_h[i], ts_h[i], wl.blank, p, q)
+        classes.setdefault(cls, []).append(i)
+    counts = {k: len(v) for k, v in sorted(classes.items())}
+    tie_records = set(wl.tie_frames)
+    print(f"cfg{index} {route}: differing records by class {counts}; constructed ties among them: "
+          f"{sorted(set(sum(classes.values(), [])) & tie_records)[:10]}; others {dict((k, v[:8]) for k, v in classes.items())}")
+    assert "worse" not in classes, f"genuine divergences: {classes['worse'][:10]}"
+    assert counts == EXPECTED_DIVERGENCES[(route, index)]
 
 
 @pytest.mark.parametrize("mode", MODES)
@@ -144,6 +177,32 @@ def test_matches_reference_cuda_conventional(cuda, index, scale):
             if mode == "optimized":
                 a, b = (a[frames], b[frames]) if name in ("labels", "scores") else (a[keep], b[keep])
             assert_same_bits(a, b, f"cfg{index} {mode} {name}")
+
+
+def test_optimized_audit_against_reference_cuda(cuda):
+    # The reference's own optimized mode and ours, each audited against the
+    # conventional DP with the classes of the reference's accuracy audit
+    # (benchmarks/accuracy.py:67-105): ours may not be worse anywhere, and
+    # must be identical on at least as many records as the reference.
+    reference_or_skip()
+    for index in (1, 3):
+        wl, ref = config(index)
+        es_h, ts_h = wl.records()
+        es, ts = cuda_records(es_h, ts_h)
+        tensors, _ = oracle.reference_cuda_align(es, ts, [wl.blank] * wl.batch, mode="optimized")
+        theirs = tensors[0].cpu().numpy()
+        mine = ffa.align(es, ts, blank_id=wl.blank, mode="optimized").labels.cpu().numpy()
+        off = wl.frame_offsets
+        audit = {"ours": {}, "reference": {}}
+        for name, labels in (("ours", mine), ("reference", theirs)):
+            for i in range(wl.batch):
+                lo, hi = off[i], off[i + 1]
+                cls = classify_divergence(es_h[i], ts_h[i], wl.blank, labels[lo:hi], ref.labels[lo:hi]) \
+                    if labels[lo] >= 0 else "failed"
+                audit[name][cls] = audit[name].get(cls, 0) + 1
+        print(f"cfg{index} optimized vs conventional: {audit}")
+        assert "worse" not in audit["ours"] and "failed" not in audit["ours"]
+        assert audit["ours"].get("identical", 0) >= audit["reference"].get("identical", 0)
 
 
 def test_matches_reference_cuda_on_reference_test_inputs(cuda):
