@@ -266,7 +266,7 @@ def reference_cuda_lane(wl, e_dev, t_dev, steps, warmup, flush):
     return out
 
 
-def strong_cfg4_lane(ffa, rank, world, device, steps, warmup, flush, max_over_ranks, barrier):
+def strong_cfg4_lane(ffa, lib, rank, world, device, steps, warmup, flush, max_over_ranks, barrier, peak):
     """Strong scaling on the multi-GPU configuration (cfg4): every rank draws
     the same 8,256-record batch and aligns its LPT share (shard_of_rank),
     device-resident, timed as `value`; the whole box's frames/s over the
@@ -285,12 +285,40 @@ def strong_cfg4_lane(ffa, rank, world, device, steps, warmup, flush, max_over_ra
     ms = queued_device_ms(call, steps, warmup, flush)
     total = max_over_ranks(sum(ms))
     barrier()
+    # The greedy pass of the window route (the launch that streams every row
+    # of the window records once): its device time from the forward
+    # profiling events, against the rows it reads and the bounds it writes.
+    import ctypes
+    greedy = None
+    window = (shard.lengths <= 2048) & (2 * shard.target_lengths + 1 <= 4096)
+    if window.sum() > 4 * torch.cuda.get_device_properties(device).multi_processor_count:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for x in ev:
+            x.record()
+        times = []
+        for _ in range(5):
+            flush.zero_()
+            lib.ffa_profile_forward_events(ctypes.c_void_p(ev[0].cuda_event), ctypes.c_void_p(ev[1].cuda_event))
+            call()
+            lib.ffa_profile_forward_events(None, None)
+            torch.cuda.synchronize()
+            times.append(ev[0].elapsed_time(ev[1]))
+        g_ms = statistics.median(times)
+        wf = int(shard.lengths[window].sum())
+        nbytes = wf * shard.vocab * 4 + wf * 4  # every row of a window record (its alphabet fills V = 32), and m[t]
+        greedy = {"kernel": "ffa_greedy_pass (window route: each frame's bound over the alphabet and the "
+                            "reference's greedy chunk verdicts)", "bound": "hbm", "bytes": nbytes, "ms": g_ms,
+                  "achieved": nbytes / (g_ms / 1e3) / 1e9, "unit": "GB/s", "peak": peak,
+                  "frac": nbytes / (g_ms / 1e3) / 1e9 / peak, "frames": wf}
     frames = int(pool.lengths.sum())
-    return {"value": frames * steps / (total / 1e3), "unit": "frames/s", "ms_per_step": total / steps,
+    out = {"value": frames * steps / (total / 1e3), "unit": "frames/s", "ms_per_step": total / steps,
             "n_gpus": world, "scaling": "strong", "records_total": pool.batch, "frames_total": frames,
             "records_this_rank": shard.batch,
             "how": "cfg4 (8,256 records) LPT-partitioned over the ranks by record cost (shard_of_rank), "
                    "optimized mode, device-resident, L2 flushed before every step; max over ranks"}
+    if greedy is not None:
+        out["greedy_pass_rank0" if world > 1 else "greedy_pass"] = greedy
+    return out
 
 
 def cpu_reference_runner(wl):
@@ -505,7 +533,8 @@ def run_ours(args):
 
     ref_cuda = reference_cuda_lane(wl, e_dev, t_dev, args.steps, args.warmup, flush) \
         if world == 1 and not from_logits and args.scale == 1.0 else None
-    strong = strong_cfg4_lane(ffa, rank, world, device, args.steps, args.warmup, flush, max_over_ranks, barrier) \
+    strong = strong_cfg4_lane(ffa, lib, rank, world, device, args.steps, args.warmup, flush, max_over_ranks, barrier,
+                              peaks()[0]) \
         if args.config == 1 and not args.split and not from_logits and args.scale == 1.0 else None
 
     all_frames = sum_over_ranks(frames)

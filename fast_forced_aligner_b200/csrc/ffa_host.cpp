@@ -216,10 +216,11 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, slots, keys, classes,
+  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, tok_off, slots, keys,
+      classes,
       staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, lse,
-      workspace_bytes;
+  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, alphabet,
+      lpos, lstart, lse, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy;
   int format;  // the call's input format
 };
@@ -243,7 +244,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0, longs = 0, greedy = 0;
+          pieces = 0, longs = 0, greedy = 0, tokens = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
@@ -258,6 +259,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
     longs += g.cluster > 0 ? 1 : 0;
     pieces += g.pieces;
     greedy += g.greedy_items;
+    tokens += records[i].tokens;
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
@@ -280,9 +282,10 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   // Window route: one slot per record, at most one CTA per record.
   L->win_slots = off; off = align_up(off + sizeof(ffa::WinSlot) * count, 16);
   L->win_ctas = off; off = align_up(off + sizeof(ffa::WinCta) * count, 16);
-  // Greedy pass: its items, and each record's first item.
+  // Greedy pass: its chunks, each record's first chunk verdict and first token.
   L->greedy_items = off; off = align_up(off + sizeof(ffa::GreedyItem) * greedy, 16);
   L->greedy_first = off; off = align_up(off + sizeof(int32_t) * count, 16);
+  L->tok_off = off; off = align_up(off + sizeof(int32_t) * count, 16);
   L->num_greedy = greedy;
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
@@ -301,6 +304,9 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   L->fallback = off; off = align_up(off + sizeof(int32_t) * 2 * count, 256);  // the two tiers' lists
   L->bound = off; off = align_up(off + (greedy ? sizeof(float) * frames : 0), 256);
   L->verdicts = off; off = align_up(off + greedy, 256);
+  L->alphabet = off; off = align_up(off + (greedy ? sizeof(uint64_t) * count : 0), 256);
+  L->lpos = off; off = align_up(off + (greedy ? sizeof(uint16_t) * tokens : 0), 256);
+  L->lstart = off; off = align_up(off + (greedy ? sizeof(uint16_t) * ffa::kGreedyLabels * count : 0), 256);
   // Logits: each frame's row log-sum-exp.
   L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
   L->workspace_bytes = off;
@@ -617,7 +623,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   win_records.clear();
   auto* gitems = reinterpret_cast<ffa::GreedyItem*>(host + L.greedy_items);
   auto* gfirst = reinterpret_cast<int32_t*>(host + L.greedy_first);
-  int64_t ngreedy = 0;
+  auto* tokoff = reinterpret_cast<int32_t*>(host + L.tok_off);
+  int64_t ngreedy = 0, ntok = 0;
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, windows, lat);
@@ -651,6 +658,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     } else if (g.window) {
       win_records.push_back(static_cast<int32_t>(i));
       gfirst[i] = static_cast<int32_t>(ngreedy);
+      tokoff[i] = static_cast<int32_t>(ntok);
+      ntok += r.tokens;
       for (int64_t k = 0; k < g.greedy_items; ++k)
         gitems[ngreedy++] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
     } else if (g.chunked) {
@@ -931,8 +940,15 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     // the launch the forward profiling events bracket.
     ffa::GreedyParams gp{};
     gp.recs = fp.recs;
+    gp.slots = reinterpret_cast<const ffa::WinSlot*>(dev + L.win_slots);  // the window records, longest first
+    gp.num_records = static_cast<int64_t>(win_records.size());
     gp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items);
     gp.count = ngreedy;
+    gp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
+    gp.tok_off = reinterpret_cast<const int32_t*>(dev + L.tok_off);
+    gp.alphabet = reinterpret_cast<uint64_t*>(dev + L.alphabet);
+    gp.lpos = reinterpret_cast<uint16_t*>(dev + L.lpos);
+    gp.lstart = reinterpret_cast<uint16_t*>(dev + L.lstart);
     gp.lse = fp.lse;
     gp.bound = reinterpret_cast<float*>(dev + L.bound);
     gp.verdicts = reinterpret_cast<uint8_t*>(dev + L.verdicts);

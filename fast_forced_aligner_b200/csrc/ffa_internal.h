@@ -305,14 +305,27 @@ struct GreedyItem {
   int32_t record;
   int32_t chunk;  // frames [kGreedyChunk chunk, ...)
 };
+// Per window record, from the greedy preparation: the transcript alphabet
+// (label columns, blank included) as a 64-bit mask, and its token positions
+// grouped by label: lpos[tok_off[r] + lstart[kGreedyLabels r + c] ..] are
+// the positions u with label c, for the placement search.
+constexpr int kGreedyLabels = 66;  // V + 1 <= 65 list starts, rounded up
 struct GreedyParams {
   const RecordDev* recs;
-  const GreedyItem* items;
+  const struct WinSlot* slots;  // preparation: the window route's records, a warp each
+  int64_t num_records;
+  const GreedyItem* items;      // the pass: a warp per chunk
   int64_t count;
-  const float* lse;          // as ForwardParams::lse
-  float* bound;              // m[t] of record r's frame t at recs[r].out_off + t
-  uint8_t* verdicts;         // one per item
+  const int32_t* greedy_first;  // per record: its first chunk's verdict
+  const int32_t* tok_off;       // per record: its first token in lpos
+  uint64_t* alphabet;           // per record
+  uint16_t* lpos;
+  uint16_t* lstart;             // kGreedyLabels per record
+  const float* lse;             // as ForwardParams::lse
+  float* bound;                 // m[t] of record r's frame t at recs[r].out_off + t
+  uint8_t* verdicts;            // one per chunk
 };
+// The preparation (a warp per record) and the pass (a warp per chunk).
 cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream);
 
 // One record's slice of a window CTA's dynamic shared memory for K states

@@ -79,8 +79,8 @@ __device__ __forceinline__ double warp_min(double v) {
 // between tokens).  Returns kGreedyAccepted, kGreedyMultiple (several
 // placements) or 0.  label_of(s): the label column of state s.
 template <typename LabelOf>
-__device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, int U, int blank,
-                              const int64_t* targets, int V, LabelOf label_of, int lane) {
+__device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, int blank, const uint16_t* lpos,
+                              const uint16_t* lstart, LabelOf label_of, int lane) {
   // r[t] - r[a] by a warp scan of the increments.
   int inc[4], own = 0;
   unsigned chg = 0;
@@ -114,7 +114,6 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
     const int term = s + R;
     return s >= 0 && s <= hi_start && term < S && !(b == T && term < S - 2);
   };
-  auto token = [&](int u) { return clamp_label(__ldg(targets + u), V); };
   const unsigned changers = __ballot_sync(kFull, chg != 0);
   int matches = 0;
   if (changers == 0) {
@@ -123,7 +122,7 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
       const int lo = b == T ? max(0, S - 2) : 0, hi = min(hi_start, S - 1);
       matches = hi < lo ? 0 : (hi / 2 - (lo + 1) / 2 + 1);  // even states in [lo, hi]
     } else {
-      for (int u = lane; u < U; u += 32) matches += (token(u) == ga && in_range(2 * u + 1)) ? 1 : 0;
+      for (int j = lstart[ga] + lane; j < lstart[ga + 1]; j += 32) matches += in_range(2 * lpos[j] + 1) ? 1 : 0;
       matches = __reduce_add_sync(kFull, matches);
     }
     return matches == 1 ? kGreedyAccepted : (matches > 1 ? kGreedyMultiple : 0);
@@ -141,15 +140,20 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
   const int gc = __shfl_sync(kFull, gcv, lc), rc = __shfl_sync(kFull, rcv, lc);
   const int lb = ga != blank ? ga : gc;
   const int shift = ga != blank ? 1 : 0;  // start = 2u + shift for a token u of label lb
-  for (int u0 = 0; u0 < U; u0 += 32) {
-    const int u = u0 + lane;
-    const int s0 = 2 * u + shift;
-    const bool cand = u < U && token(u) == lb && in_range(s0) && s0 + rc < S && label_of(s0 + rc) == gc;
+  const int n1 = lstart[lb + 1];
+  for (int j0 = lstart[lb]; j0 < n1; j0 += 32) {
+    const int j = j0 + lane;
+    int s0 = 0;
+    bool cand = false;
+    if (j < n1) {
+      s0 = 2 * lpos[j] + shift;
+      cand = in_range(s0) && s0 + rc < S && label_of(s0 + rc) == gc;  // passes the first change
+    }
     unsigned cands = __ballot_sync(kFull, cand);
     while (cands) {
       const int q = __ffs(cands) - 1;
       cands &= cands - 1;
-      const int st0 = 2 * (u0 + q) + shift;
+      const int st0 = __shfl_sync(kFull, s0, q);
       bool ok = true;  // every label change lands on a state holding the new label
 #pragma unroll
       for (int k = 0; k < 4; ++k)
@@ -167,15 +171,135 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   return r;
 }
 
-// The greedy pass: one warp per kGreedyChunk-frame chunk of a record.  Lane
-// j scans the rows of frames a + 4j .. a + 4j + 3 over the record's alphabet
-// (16-byte loads of whole rows): each frame's greedy bound m[t] (written to
-// the bound arena), its greedy label (the unique finite maximum, as
-// alignment.cu:60-91 finds it; NaN columns never compare greater or equal
-// there), and whether an alphabet column holds NaN or +inf.  The chunk's
-// verdict (greedy_verdict) and flags go to one byte.
-template <int kFmt, int kV>
+// Greedy bound and label of one frame from its row over the alphabet
+// (alo, ahi): the largest emission (NaN columns never compare greater or
+// equal), whether it is unique, its column, and whether an alphabet column is
+// NaN or +inf.
+struct GreedyFrame {
+  float best;
+  int arg, ties;
+  bool nonfinite;
+};
+// A 32-column fp32 row already in registers.
+__device__ __forceinline__ GreedyFrame greedy_row32(const float4 (&v4)[8], unsigned alo) {
+  GreedyFrame f{-INFINITY, 0, 0, false};
+  float bn = -INFINITY;
+  {
+    float xs[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      xs[4 * k] = v4[k].x; xs[4 * k + 1] = v4[k].y; xs[4 * k + 2] = v4[k].z; xs[4 * k + 3] = v4[k].w;
+    }
+    float bf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float bq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const float v = ((alo >> k) & 1u) ? xs[k] : -INFINITY;
+      bf[k & 3] = fmaxf(bf[k & 3], v);
+      bq[k & 3] = max_nan(bq[k & 3], v);
+    }
+    f.best = fmaxf(fmaxf(bf[0], bf[1]), fmaxf(bf[2], bf[3]));
+    bn = max_nan(max_nan(bq[0], bq[1]), max_nan(bq[2], bq[3]));
+    int tq[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const bool hit = ((alo >> k) & 1u) && xs[k] == f.best;
+      tq[k & 3] += hit ? 1 : 0;
+      f.arg = hit ? k : f.arg;
+    }
+    f.ties = tq[0] + tq[1] + tq[2] + tq[3];
+  }
+  f.nonfinite = !(bn < INFINITY);
+  return f;
+}
+
+// Any row of V <= 64 columns, read column by column.
+template <int kFmt>
+__device__ __forceinline__ GreedyFrame greedy_row(const typename Input<kFmt>::Elem* row, int V, unsigned alo,
+                                                  unsigned ahi) {
+  GreedyFrame f{-INFINITY, 0, 0, false};
+  float bn = -INFINITY;
+  {
+    for (int col = 0; col < V; ++col) {
+      const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
+      if (!in) continue;
+      const float v = elem_to_float(row[col]);
+      bn = max_nan(bn, v);
+      if (v > f.best) { f.best = v; f.arg = col; f.ties = 1; }
+      else if (v == f.best) ++f.ties;
+    }
+  }
+  f.nonfinite = !(bn < INFINITY);
+  return f;
+}
+
+// The greedy preparation: a warp per record of the window route.  The
+// transcript alphabet (label columns, blank included) as a 64-bit mask, and
+// the token positions grouped by label (a counting sort: lanes holding equal
+// labels form a group, whose first lane updates the label's count).
 __global__ void __launch_bounds__(32 * kGreedyWarps)
+ffa_greedy_prep(const __grid_constant__ GreedyParams P) {
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const int64_t index = static_cast<int64_t>(blockIdx.x) * kGreedyWarps + warp;
+  if (index >= P.num_records) return;
+  const int r = P.slots[index].record;
+  const RecordDev rec = P.recs[r];
+  const int U = rec.U, V = rec.V, blank = rec.blank;
+  uint16_t* lpos = P.lpos + P.tok_off[r];
+  uint16_t* lstart = P.lstart + static_cast<int64_t>(kGreedyLabels) * r;
+  __shared__ uint16_t cursor_s[kGreedyWarps][kGreedyLabels];
+  uint16_t* cursor = cursor_s[warp];
+  for (int c = lane; c < kGreedyLabels; c += 32) cursor[c] = 0;
+  __syncwarp();
+  uint64_t alpha = uint64_t{1} << blank;
+  for (int base = 0; base < U; base += 32) {
+    const int k = base + lane;
+    const int c = k < U ? clamp_label(__ldg(rec.targets + k), V) : 0x100 + lane;
+    if (k < U) alpha |= uint64_t{1} << c;
+    const unsigned grp = __match_any_sync(kFull, c);
+    if (k < U && lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
+    __syncwarp();
+  }
+  const unsigned lo = __reduce_or_sync(kFull, static_cast<unsigned>(alpha));
+  const unsigned hi = __reduce_or_sync(kFull, static_cast<unsigned>(alpha >> 32));
+  if (lane == 0) P.alphabet[r] = static_cast<uint64_t>(hi) << 32 | lo;
+  // Exclusive prefix over labels (V <= 64: two per lane).
+  const int c0 = 2 * lane, c1 = c0 + 1;
+  const int n0 = c0 < V ? cursor[c0] : 0, n1 = c1 < V ? cursor[c1] : 0;
+  int incl = n0 + n1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  const int excl = incl - n0 - n1;
+  __syncwarp();
+  if (c0 <= V) { lstart[c0] = static_cast<uint16_t>(excl); cursor[c0] = static_cast<uint16_t>(excl); }
+  if (c1 <= V) { lstart[c1] = static_cast<uint16_t>(excl + n0); cursor[c1] = static_cast<uint16_t>(excl + n0); }
+  if (lane == 0) lstart[V] = static_cast<uint16_t>(U);  // (V = 64 lies past the lanes' pairs)
+  __syncwarp();
+  for (int base = 0; base < U; base += 32) {
+    const int k = base + lane;
+    const int c = k < U ? clamp_label(__ldg(rec.targets + k), V) : 0x100 + lane;
+    const unsigned grp = __match_any_sync(kFull, c);
+    const int at = k < U ? cursor[c] + __popc(grp & ((1u << lane) - 1u)) : 0;
+    __syncwarp();
+    if (k < U) {
+      lpos[at] = static_cast<uint16_t>(k);
+      if (lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
+    }
+    __syncwarp();
+  }
+}
+
+// The greedy pass: a warp per kGreedyChunk-frame chunk of a record of the
+// window route.  Lane j scans the rows of frames a + 4j .. a + 4j + 3 over the
+// record's alphabet (16-byte loads of whole rows, streamed): each frame's
+// greedy bound m[t] (to the bound arena) and greedy label (the unique finite
+// maximum, as alignment.cu:60-91 finds it); then the chunk's verdict
+// (greedy_verdict) and flags go to one byte.
+template <int kFmt, int kV>
+__global__ void __launch_bounds__(32 * kGreedyWarps, 4)
 ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
   using In = Input<kFmt>;
   using Elem = typename In::Elem;
@@ -183,89 +307,67 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
   const int64_t index = static_cast<int64_t>(blockIdx.x) * kGreedyWarps + warp;
   if (index >= P.count) return;
   const GreedyItem item = P.items[index];
-  const RecordDev rec = P.recs[item.record];
+  const int r = item.record;
+  const RecordDev rec = P.recs[r];
   const int T = rec.T, U = rec.U, blank = rec.blank;
   const int V = kV > 0 ? kV : rec.V;
   const int S = 2 * U + 1;
-  const int64_t* targets = rec.targets;
-  // The transcript alphabet (V <= 64), blank included.
-  unsigned alo = 0, ahi = 0;
-  for (int k = lane; k < U; k += 32) {
-    const int c = clamp_label(__ldg(targets + k), V);
-    if (c < 32) alo |= 1u << c; else ahi |= 1u << (c - 32);
-  }
-  alo = __reduce_or_sync(kFull, alo);
-  ahi = __reduce_or_sync(kFull, ahi);
-  if (blank < 32) alo |= 1u << blank; else ahi |= 1u << (blank - 32);
-  const int a = item.chunk * kGreedyChunk, b = min(T, a + kGreedyChunk);
+  const uint64_t alpha = __ldg(P.alphabet + r);
+  const unsigned alo = static_cast<unsigned>(alpha), ahi = static_cast<unsigned>(alpha >> 32);
   const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
+  const int a = item.chunk * kGreedyChunk, b = min(T, a + kGreedyChunk);
   int lab[4];
   bool poison = false, positive = false, rejected = false;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  // Frame t's bound, flags and greedy label from its row's scan.
+  auto take = [&](int q, const GreedyFrame& f) {
     const int t = a + 4 * lane + q;
     lab[q] = -1;
-    if (t >= b) continue;
-    const Elem* row = e + static_cast<int64_t>(t) * V;
-    float best = -INFINITY, bn = -INFINITY;
-    int arg = 0, ties = 0;
-    if constexpr (kV == 32 && kFmt == 0) {
-      float xs[32];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 v4 = __ldcs(reinterpret_cast<const float4*>(row) + k);  // streamed: read once
-        xs[4 * k] = v4.x; xs[4 * k + 1] = v4.y; xs[4 * k + 2] = v4.z; xs[4 * k + 3] = v4.w;
-      }
-      float bf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, bq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float v = ((alo >> k) & 1u) ? xs[k] : -INFINITY;
-        bf[k & 3] = fmaxf(bf[k & 3], v);
-        bq[k & 3] = max_nan(bq[k & 3], v);
-      }
-      best = fmaxf(fmaxf(bf[0], bf[1]), fmaxf(bf[2], bf[3]));
-      bn = max_nan(max_nan(bq[0], bq[1]), max_nan(bq[2], bq[3]));
-      int tq[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const bool hit = ((alo >> k) & 1u) && xs[k] == best;
-        tq[k & 3] += hit ? 1 : 0;
-        arg = hit ? k : arg;
-      }
-      ties = tq[0] + tq[1] + tq[2] + tq[3];
-    } else {
-      for (int col = 0; col < V; ++col) {
-        const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
-        if (!in) continue;
-        const float v = elem_to_float(row[col]);
-        bn = max_nan(bn, v);
-        if (v > best) { best = v; arg = col; ties = 1; }
-        else if (v == best) ++ties;
-      }
-    }
-    bool nonfinite = !(bn < INFINITY);  // NaN or +inf in an alphabet column
-    float m = best;
+    if (t >= b) return;
+    bool nonfinite = f.nonfinite;
+    float m = f.best;
     if constexpr (In::kLogits) {
       const float z = P.lse[rec.out_off + t];
-      m = __fsub_rn(best, z);
+      m = __fsub_rn(f.best, z);
       nonfinite |= !isfinite(z);
     }
     P.bound[rec.out_off + t] = m;
     poison |= nonfinite;
     positive |= m > 0.0f;
-    const bool ok = ties == 1 && isfinite(m);
+    const bool ok = f.ties == 1 && isfinite(m);
     rejected |= !ok;
-    lab[q] = ok ? arg : 0xff;
+    lab[q] = ok ? f.arg : 0xff;
+  };
+  if constexpr (kV == 32 && kFmt == 0) {
+    // A row's eight 16-byte loads in flight at a time (streamed: read once);
+    // few registers keep many warps resident, which covers the latency.
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float4 v4[8];
+      const int t = min(a + 4 * lane + q, b - 1);
+      const float4* row = reinterpret_cast<const float4*>(e + static_cast<int64_t>(t) * 32);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v4[k] = __ldcs(row + k);
+      take(q, greedy_row32(v4, alo));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int t = min(a + 4 * lane + q, b - 1);
+      take(q, greedy_row<kFmt>(e + static_cast<int64_t>(t) * V, V, alo, ahi));
+    }
   }
   poison = __any_sync(kFull, poison);
   positive = __any_sync(kFull, positive);
   int verdict = 0;
   if (!__any_sync(kFull, rejected)) {
+    const int64_t* targets = rec.targets;
     auto label_of = [&](int s) { return (s & 1) ? clamp_label(__ldg(targets + (s >> 1)), V) : blank; };
-    verdict = greedy_verdict(lab, a, b, T, S, U, blank, targets, V, label_of, lane);
+    verdict = greedy_verdict(lab, a, b, T, S, blank, P.lpos + P.tok_off[r],
+                             P.lstart + static_cast<int64_t>(kGreedyLabels) * r, label_of, lane);
   }
   if (lane == 0)
-    P.verdicts[index] = static_cast<uint8_t>(verdict | (poison ? kGreedyPoison : 0) | (positive ? kGreedyPositive : 0));
+    P.verdicts[P.greedy_first[r] + item.chunk] =
+        static_cast<uint8_t>(verdict | (poison ? kGreedyPoison : 0) | (positive ? kGreedyPositive : 0));
 }
 
 // A lane's K states: base + K lane + k (even k: blanks, odd k: tokens), their
@@ -782,12 +884,17 @@ cudaError_t window_opt_in(WindowKernel kernel, std::atomic<uint64_t>& opted) {
 }  // namespace
 
 cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream) {
-  if (params.count <= 0) return cudaSuccess;
+  if (params.count <= 0 || params.num_records <= 0) return cudaSuccess;
   if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
-  const int64_t blocks = (params.count + kGreedyWarps - 1) / kGreedyWarps;
   count_launch();
-  kGreedyKernels[window_variant(row_vocab, fmt)]<<<static_cast<unsigned>(blocks), 32 * kGreedyWarps, 0, stream>>>(
-      params);
+  ffa_greedy_prep<<<static_cast<unsigned>((params.num_records + kGreedyWarps - 1) / kGreedyWarps),
+                    32 * kGreedyWarps, 0, stream>>>(params);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  count_launch();
+  kGreedyKernels[window_variant(row_vocab, fmt)]<<<static_cast<unsigned>((params.count + kGreedyWarps - 1) /
+                                                                         kGreedyWarps),
+                                                   32 * kGreedyWarps, 0, stream>>>(params);
   return cudaGetLastError();
 }
 
