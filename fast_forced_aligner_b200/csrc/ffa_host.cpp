@@ -58,7 +58,7 @@ struct Geometry {
   int nw;        // warps for the DP
   int seg_log2;  // traceback segment length
   int64_t segments;
-  int64_t greedy_items;  // window records: greedy pass chunks
+  int64_t greedy_items;  // greedy pass chunks (greedy_record)
   int64_t bp_words;
   int64_t map_elems;
   int64_t pieces;
@@ -123,6 +123,14 @@ bool window_record(const ffa_record& r, const WindowPolicy& w) {
   return w.max_frames > 0 && window_shape(r, w.max_frames);
 }
 
+// Records of the optimized mode the greedy pass covers: row-staged (at most
+// 64 columns: the alphabet is a 64-bit mask) with at most kMaxStates states
+// (the reference's own limit).  The window route needs its bounds; for the
+// other records it computes the reference's shortcut statistics.
+bool greedy_record(const ffa_record& r, bool optimized) {
+  return optimized && r.frames > 0 && 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates && row_staged(r);
+}
+
 // Records of the optimized mode solved in pieces: the rest, when long enough.
 bool chunked_record(const ffa_record& r, bool optimized, const WindowPolicy& w) {
   return optimized && !window_record(r, w) && r.frames >= ffa::kPieceMinFrames;
@@ -165,7 +173,7 @@ Geometry geometry(const ffa_record& r, bool optimized, const WindowPolicy& windo
       ++g.seg_log2;
   }
   g.segments = (r.frames + (int64_t{1} << g.seg_log2) - 1) >> g.seg_log2;
-  g.greedy_items = g.window ? (r.frames + ffa::kGreedyChunk - 1) / ffa::kGreedyChunk : 0;
+  g.greedy_items = greedy_record(r, optimized) ? (r.frames + ffa::kGreedyChunk - 1) / ffa::kGreedyChunk : 0;
   // Backpointer rows, frontiers and maps do not depend on the thread layout.
   const int S32 = static_cast<int>(S);
   g.bp_words = r.frames * ffa::bp_row_words(S32);
@@ -216,12 +224,13 @@ int device_sms() {
 // (it reserves room for one slot and one bundle per piece); the upload stops
 // at their end.
 struct AlignLayout {
-  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, tok_off, slots, keys,
+  size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, tok_off, greedy_recs,
+      slots, keys,
       classes,
       staging_bytes;
-  size_t bp, maps, anchors, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, alphabet,
+  size_t bp, maps, anchors, path_states, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, alphabet,
       lpos, lstart, lse, workspace_bytes;
-  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy;
+  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy, num_greedy_window;
   int format;  // the call's input format
 };
 
@@ -244,7 +253,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0, longs = 0, greedy = 0, tokens = 0;
+          pieces = 0, longs = 0, greedy = 0, greedy_window = 0, tokens = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
@@ -259,6 +268,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
     longs += g.cluster > 0 ? 1 : 0;
     pieces += g.pieces;
     greedy += g.greedy_items;
+    greedy_window += g.window ? g.greedy_items : 0;
     tokens += records[i].tokens;
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
@@ -282,11 +292,14 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   // Window route: one slot per record, at most one CTA per record.
   L->win_slots = off; off = align_up(off + sizeof(ffa::WinSlot) * count, 16);
   L->win_ctas = off; off = align_up(off + sizeof(ffa::WinCta) * count, 16);
-  // Greedy pass: its chunks, each record's first chunk verdict and first token.
+  // Greedy pass: its chunks (the window records' first), each record's first
+  // chunk verdict (-1: none) and first token, and its records (window first).
   L->greedy_items = off; off = align_up(off + sizeof(ffa::GreedyItem) * greedy, 16);
   L->greedy_first = off; off = align_up(off + sizeof(int32_t) * count, 16);
   L->tok_off = off; off = align_up(off + sizeof(int32_t) * count, 16);
+  L->greedy_recs = off; off = align_up(off + sizeof(int32_t) * count, 16);
   L->num_greedy = greedy;
+  L->num_greedy_window = greedy_window;
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
@@ -296,6 +309,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   L->bp = off; off = align_up(off + sizeof(uint32_t) * bp_words, 256);
   L->maps = off; off = align_up(off + sizeof(uint16_t) * map_elems, 256);
   L->anchors = off; off = align_up(off + sizeof(int32_t) * segments, 256);
+  L->path_states = off; off = align_up(off + (chunked ? sizeof(int16_t) * frames : 0), 256);
   L->frontiers = off; off = align_up(off + sizeof(float) * frontier, 256);
   L->pstates = off; off = align_up(off + sizeof(ffa::PieceState) * pieces, 256);
   L->route = off; off = align_up(off + sizeof(int32_t) * count, 256);
@@ -624,7 +638,13 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   auto* gitems = reinterpret_cast<ffa::GreedyItem*>(host + L.greedy_items);
   auto* gfirst = reinterpret_cast<int32_t*>(host + L.greedy_first);
   auto* tokoff = reinterpret_cast<int32_t*>(host + L.tok_off);
-  int64_t ngreedy = 0, ntok = 0;
+  auto* grecs = reinterpret_cast<int32_t*>(host + L.greedy_recs);
+  // Greedy chunks: the window records' from 0, the others' after them.
+  int64_t ngreedy = 0, nstats_items = 0, ntok = 0;
+  int64_t unchunked_fill = 0;  // records off both optimized routes (the fill launch's own)
+  thread_local std::vector<int32_t> stats_records;  // greedy records off the window route
+  stats_records.clear();
+  int stats_vocab = -1;  // their common vocabulary, 0 if mixed
   for (int64_t i = 0; i < count; ++i) {
     const ffa_record& r = records[i];
     const Geometry g = geometry(r, optimized, windows, lat);
@@ -657,18 +677,31 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       long_keys.push_back(static_cast<uint64_t>(i));  // keyed below, once the batch is known
     } else if (g.window) {
       win_records.push_back(static_cast<int32_t>(i));
-      gfirst[i] = static_cast<int32_t>(ngreedy);
-      tokoff[i] = static_cast<int32_t>(ntok);
-      ntok += r.tokens;
-      for (int64_t k = 0; k < g.greedy_items; ++k)
-        gitems[ngreedy++] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
     } else if (g.chunked) {
       ++nchunked;
       runs_model.add(cls, g.pieces);
     } else {
       runs_model.add_whole(cls);
     }
+    gfirst[i] = -1;
+    if (g.greedy_items > 0) {
+      int64_t first = ngreedy;
+      if (!g.window) {
+        first = L.num_greedy_window + nstats_items;
+        nstats_items += g.greedy_items;
+        stats_records.push_back(static_cast<int32_t>(i));
+        stats_vocab = (stats_vocab < 0 || stats_vocab == r.vocab) ? r.vocab : 0;
+      } else {
+        ngreedy += g.greedy_items;
+      }
+      gfirst[i] = static_cast<int32_t>(first);
+      tokoff[i] = static_cast<int32_t>(ntok);
+      ntok += r.tokens;
+      for (int64_t k = 0; k < g.greedy_items; ++k)
+        gitems[first + k] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
+    }
     np += g.pieces;
+    if (!g.window && !g.chunked) ++unchunked_fill;
     if (!g.window)
       for (int64_t s = 0; s < g.segments; s += ffa::kFillWarps)
         fill[nfill++] = ffa::FillItem{static_cast<int32_t>(i), static_cast<int32_t>(s)};
@@ -679,6 +712,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     frontier_off += g.frontier_elems;
   }
 
+  std::copy(win_records.begin(), win_records.end(), grecs);
+  std::copy(stats_records.begin(), stats_records.end(), grecs + win_records.size());
   std::memset(host + L.counters, 0, sizeof(int32_t) * (count + ffa::kFinishGroups + 2));
   const size_t header = ffa::forward_header_bytes();  // 128-byte aligned ring offset
   const unsigned row_slot_bytes = static_cast<unsigned>(
@@ -877,6 +912,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   fp.bp = reinterpret_cast<uint32_t*>(dev + L.bp);
   fp.maps = reinterpret_cast<uint16_t*>(dev + L.maps);
   fp.anchors = reinterpret_cast<int32_t*>(dev + L.anchors);
+  fp.path_states = reinterpret_cast<int16_t*>(dev + L.path_states);
   fp.frontiers = reinterpret_cast<float*>(dev + L.frontiers);
   fp.pstates = reinterpret_cast<ffa::PieceState*>(dev + L.pstates);
   fp.route = reinterpret_cast<int32_t*>(dev + L.route);
@@ -889,6 +925,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // 1747 vs 1842; 8256 records, on the finisher's small CTAs: 3274 vs 3240.)
   fp.plan_first = nchunked > sms && !many_chunked ? 1 : 0;
   fp.finish_narrow = many_chunked ? 1 : 0;
+  // Records that do not outnumber the SMs each have a finisher CTA to
+  // themselves, which then also fills and folds the record: one launch and
+  // its tail less on the latency-bound path.
+  fp.fill_in_finisher = nchunked > 0 && nchunked <= sms ? 1 : 0;
   fp.slot_done = reinterpret_cast<int32_t*>(dev + L.counters);
   fp.finish_count = fp.slot_done + count;
   fp.finish_list = reinterpret_cast<int32_t*>(dev + L.chunked);
@@ -900,6 +940,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   fp.row_slot_bytes = row_slot_bytes;
   fp.run_pieces = run_pieces;
   fp.lse = fmt != FFA_INPUT_LOG_PROBS ? reinterpret_cast<const float*>(dev + L.lse) : nullptr;
+  fp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
   const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + bundles_off);
   const int rv = row_vocab > 0 ? row_vocab : 0;
 
@@ -924,10 +965,26 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // Window route: the greedy pass, the window DP of every such record, then
   // the wider window and the full DP of those a tier did not certify
   // (device-written lists) -- on a side stream when the chunked route or the
-  // long records have work too.
+  // long records have work too.  The greedy pass of the other records
+  // (statistics only) follows on the side stream, once the first pass has
+  // taken its SMs.
   cudaStream_t ws = s;
   SideStream* side = nullptr;
-  const bool forked = n_wcta > 0 && (nb > 0 || !long_keys.empty());
+  const bool stats_greedy = !stats_records.empty();
+  const bool forked = (n_wcta > 0 && (nb > 0 || !long_keys.empty())) || stats_greedy;
+  ffa::GreedyParams gp{};
+  gp.recs = fp.recs;
+  gp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
+  gp.tok_off = reinterpret_cast<const int32_t*>(dev + L.tok_off);
+  gp.alphabet = reinterpret_cast<uint64_t*>(dev + L.alphabet);
+  gp.lpos = reinterpret_cast<uint16_t*>(dev + L.lpos);
+  gp.lstart = reinterpret_cast<uint16_t*>(dev + L.lstart);
+  gp.lse = fp.lse;
+  gp.bound = reinterpret_cast<float*>(dev + L.bound);
+  gp.verdicts = reinterpret_cast<uint8_t*>(dev + L.verdicts);
+  gp.mask = fp.mask;
+  gp.check_inputs = fp.check_inputs;
+  gp.shortcut_stats = outputs->shortcut_stats;
   if (forked) {
     if ((err = side_stream(&side)) != cudaSuccess) return cuda_fail(err, "side stream");
     if ((err = cudaEventRecord(side->fork, s)) != cudaSuccess) return cuda_fail(err, "stream fork");
@@ -938,20 +995,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     const int wv = win_vocab > 0 ? win_vocab : 0;
     // The greedy pass streams every row of the window records once: it is
     // the launch the forward profiling events bracket.
-    ffa::GreedyParams gp{};
-    gp.recs = fp.recs;
-    gp.slots = reinterpret_cast<const ffa::WinSlot*>(dev + L.win_slots);  // the window records, longest first
+    gp.records = reinterpret_cast<const int32_t*>(dev + L.greedy_recs);
     gp.num_records = static_cast<int64_t>(win_records.size());
     gp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items);
     gp.count = ngreedy;
-    gp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
-    gp.tok_off = reinterpret_cast<const int32_t*>(dev + L.tok_off);
-    gp.alphabet = reinterpret_cast<uint64_t*>(dev + L.alphabet);
-    gp.lpos = reinterpret_cast<uint16_t*>(dev + L.lpos);
-    gp.lstart = reinterpret_cast<uint16_t*>(dev + L.lstart);
-    gp.lse = fp.lse;
-    gp.bound = reinterpret_cast<float*>(dev + L.bound);
-    gp.verdicts = reinterpret_cast<uint8_t*>(dev + L.verdicts);
     if (g_profile_before != nullptr && (err = cudaEventRecord(g_profile_before, ws)) != cudaSuccess)
       return cuda_fail(err, "profiling event");
     err = ffa::launch_greedy(gp, wv, fmt, ws);
@@ -1032,6 +1079,15 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     err = cudaEventRecord(g_profile_after, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
+  if (stats_greedy) {
+    ffa::GreedyParams sp = gp;
+    sp.records = reinterpret_cast<const int32_t*>(dev + L.greedy_recs) + win_records.size();
+    sp.num_records = static_cast<int64_t>(stats_records.size());
+    sp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items) + L.num_greedy_window;
+    sp.count = nstats_items;
+    err = ffa::launch_greedy(sp, stats_vocab > 0 ? stats_vocab : 0, fmt, ws);
+    if (err != cudaSuccess) return cuda_fail(err, "greedy pass launch");
+  }
   if ((rc = mark(FFA_PROFILE_FIRST))) return rc;
   // The optimized route's seam plans, repairs and fallback: a CTA per record
   // (the first round spread over up to four while the records leave SMs
@@ -1060,10 +1116,12 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     if (err != cudaSuccess) return cuda_fail(err, "finish launch");
   }
   if ((rc = mark(FFA_PROFILE_FINISH))) return rc;
-  err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
-                         static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done, fp.lse,
-                         fmt, s);
-  if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
+  if (!fp.fill_in_finisher || unchunked_fill > 0) {
+    err = ffa::launch_fill(fp.recs, reinterpret_cast<const ffa::FillItem*>(dev + L.fill),
+                           static_cast<int>(nfill), fp.bp, fp.anchors, fp.out, fp.route, fp.fill_done,
+                           fp.path_states, fp.lse, fmt, s);
+    if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
+  }
   if (forked) {
     if ((err = cudaEventRecord(side->join, ws)) != cudaSuccess) return cuda_fail(err, "stream join");
     if ((err = cudaStreamWaitEvent(s, side->join, 0)) != cudaSuccess) return cuda_fail(err, "stream join");

@@ -189,6 +189,9 @@ struct ForwardParams {
   uint32_t* bp;
   uint16_t* maps;
   int32_t* anchors;
+  // The chunked route's path: the state at each frame, as the piece and
+  // repair traces found it (record r's frame t at path_states[recs[r].out_off + t]).
+  int16_t* path_states;
   float* frontiers;
   PieceState* pstates;
   int32_t* route;            // per record: kRoute* (the finisher writes it)
@@ -204,6 +207,11 @@ struct ForwardParams {
   // finish_count arrive zeroed with the descriptor upload.
   int32_t plan_first;
   int32_t finish_narrow;     // the finisher's 128/256-thread CTA groups are in use
+  // The finisher also fills the traceback and folds the objective of each of
+  // its records (set when every record of the route has its own 512-thread
+  // finisher CTA and nothing else queues behind it: the fill launch then
+  // skips them).
+  int32_t fill_in_finisher;
   int32_t* slot_done;        // per record: first-pass slots finished
   int32_t* finish_list;
   int32_t* finish_count;     // [kFinishGroups]
@@ -211,6 +219,10 @@ struct ForwardParams {
   // Logits input (formats 1, 2): row log-sum-exps, z of record r's frame t
   // at lse[recs[r].out_off + t]; null for log-probabilities.
   const float* lse;
+  // Per record: its first greedy verdict, or -1 for a record the greedy pass
+  // does not cover.  The greedy pass owns a covered record's shortcut
+  // statistics (it may run concurrently on another stream).
+  const int32_t* greedy_first;
 };
 
 // row_vocab: the vocabulary shared by every row-staged record of the
@@ -232,8 +244,8 @@ cudaError_t launch_finish(const ForwardParams& params, const int32_t* records, i
 // last fill CTA of the record also folds the objective of a joined path.
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        const int32_t* route, int32_t* fill_done, const float* lse, int fmt,
-                        cudaStream_t stream);
+                        const int32_t* route, int32_t* fill_done, const int16_t* path_states, const float* lse,
+                        int fmt, cudaStream_t stream);
 // Row log-sum-exps of a logits batch (fmt 1 or 2): z[i] for each of the
 // `rows` frames in packed record order (records' out_off, T, V, emissions);
 // max_vocab: the largest V among the records.
@@ -305,25 +317,32 @@ struct GreedyItem {
   int32_t record;
   int32_t chunk;  // frames [kGreedyChunk chunk, ...)
 };
-// Per window record, from the greedy preparation: the transcript alphabet
-// (label columns, blank included) as a 64-bit mask, and its token positions
-// grouped by label: lpos[tok_off[r] + lstart[kGreedyLabels r + c] ..] are
-// the positions u with label c, for the placement search.
+// Per record of a greedy launch, from the greedy preparation: the
+// transcript alphabet (label columns, blank included) as a 64-bit mask, and
+// its token positions grouped by label: lpos[tok_off[r] + lstart[kGreedyLabels
+// r + c] ..] are the positions u with label c, for the placement search.
+// The greedy pass covers every record of the optimized mode with at most 64
+// row-staged columns and kMaxStates states: the window route's records need
+// its bounds; for the others (chunked route, short records) it computes the
+// reference's shortcut statistics only, on a side stream.
 constexpr int kGreedyLabels = 66;  // V + 1 <= 65 list starts, rounded up
 struct GreedyParams {
   const RecordDev* recs;
-  const struct WinSlot* slots;  // preparation: the window route's records, a warp each
+  const int32_t* records;       // preparation: the launch's records, a warp each
   int64_t num_records;
   const GreedyItem* items;      // the pass: a warp per chunk
   int64_t count;
   const int32_t* greedy_first;  // per record: its first chunk's verdict
   const int32_t* tok_off;       // per record: its first token in lpos
-  uint64_t* alphabet;           // per record
+  uint64_t* alphabet;           // per record; 0 for a record of status >= 2
   uint16_t* lpos;
   uint16_t* lstart;             // kGreedyLabels per record
   const float* lse;             // as ForwardParams::lse
   float* bound;                 // m[t] of record r's frame t at recs[r].out_off + t
   uint8_t* verdicts;            // one per chunk
+  const uint8_t* mask;          // emission-validity mask or null (status 2)
+  int32_t check_inputs;         // statuses 3 and 4 are checked
+  int64_t* shortcut_stats;      // [count, 3]: zeroed by the preparation, counted by the pass
 };
 // The preparation (a warp per record) and the pass (a warp per chunk).
 cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream);

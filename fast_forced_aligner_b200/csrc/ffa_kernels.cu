@@ -498,9 +498,18 @@ __device__ __forceinline__ int piece_dp(const SlotCtx& x, const RecordDev& rec, 
       const int first = t0 + k * kPieceFrames;
       const int end = k + 1 < run.pieces ? first + kPieceFrames : t1;
       const int a0 = run.pieces > 1 ? first : run.a0;
-      if (lane == 0) anc[(end - 1) >> rec.seg_log2] = s_end;
+      // The path's state at every frame of the region as well (the fill of
+      // a joined record gathers its outputs from them without a walk).
+      int16_t* states = P.path_states + rec.out_off;
+      if (lane == 0) {
+        anc[(end - 1) >> rec.seg_log2] = s_end;
+        states[end - 1] = static_cast<int16_t>(s_end);
+      }
       const int s0 = warp_trace(bpr, row_words, s_end, end - 1, a0, lane, [&](int t, int s) {
-        if (lane == 0 && (t & hmask) == hmask) anc[t >> rec.seg_log2] = s;
+        if (lane == 0) {
+          if ((t & hmask) == hmask) anc[t >> rec.seg_log2] = s;
+          states[t] = static_cast<int16_t>(s);
+        }
       });
       if (lane == 0 && run.end_piece >= 0) {
         // Whether a skip into the region's first state is legal: it is a
@@ -765,7 +774,10 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
         P.out.stitched[r] = 0;
         P.out.repair_passes[r] = 0;
         P.out.repaired_frames[r] = 0;
-        for (int j = 0; j < 3; ++j) { P.out.shortcut_stats[3 * r + j] = 0; P.out.routing_stats[3 * r + j] = 0; }
+        for (int j = 0; j < 3; ++j) P.out.routing_stats[3 * r + j] = 0;
+        // A record the greedy pass covers gets its shortcut statistics there.
+        if (P.greedy_first == nullptr || P.greedy_first[r] < 0)
+          for (int j = 0; j < 3; ++j) P.out.shortcut_stats[3 * r + j] = 0;
         if (P.out.reuse_stats) for (int j = 0; j < 4; ++j) P.out.reuse_stats[4 * r + j] = 0;
         if (status >= 2) P.out.objective[r] = -INFINITY;
         if (status >= 2 || chunked) P.out.status[r] = status;
@@ -806,6 +818,119 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
     piece_dp<8, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
   if (chunked && P.plan_first) plan_round0(x, rec, sh, P);
 }
+
+// Traceback segment c of a record by one warp: the warp walks the
+// backpointers from the segment's anchor (path[t-1] = path[t] - bp[t, path[t]],
+// alignment.cu:656-659), then maps states to labels and gathers the selected
+// scores (alignment.cu:662-666); a logits input's score is the same x - z the
+// DPs used (fmt, lse: as in ForwardParams).  A failed record gets -1 / -inf
+// (alignment.cu:650-652).  p: this warp's path scratch (1 << kMaxSegLog2).
+__device__ __forceinline__ void fill_segment(const RecordDev& rec, int record, int c, const uint32_t* bp_arena,
+                                             const int32_t* anchors, const OutputsDev& out, const float* lse,
+                                             int fmt, int32_t* p, int lane) {
+  const int T = rec.T;
+  const int H = 1 << rec.seg_log2;
+  const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
+  if (c >= C) return;
+  int64_t* labels = out.labels + rec.out_off;
+  float* scores = out.scores + rec.out_off;
+  const int a = c * H;
+  const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
+  if (out.status[record] != 0) {
+    for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
+    return;
+  }
+  const int s_end = __ldcg(anchors + rec.seg_off + c);  // another CTA may have written it
+  if (lane == 0) p[b - 1 - a] = s_end;
+  warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
+                  [&](int t, int s) { if (lane == 0) p[t - a] = s; });
+  __syncwarp();
+  for (int t = a + lane; t < b; t += 32) {
+    const int s = p[t - a];
+    const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
+    const int64_t i = static_cast<int64_t>(t) * rec.V + label;
+    float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
+                           : rec.emissions[i];
+    if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
+    labels[t] = label;
+    scores[t] = score;
+  }
+  __syncwarp();
+}
+
+// Outputs of frames [a, b) of a joined record of the chunked route from the
+// path's state at each frame (the traces' path_states), by `nthreads`
+// threads: labels and the selected scores as fill_segment writes them, with
+// no backpointer walk.
+// stash (or null): shared memory that also takes frame t's score at t - a.
+__device__ __forceinline__ void gather_joined(const RecordDev& rec, int record, int a, int b,
+                                              const int16_t* path_states, const OutputsDev& out, const float* lse,
+                                              int fmt, int tid, int nthreads, float* stash = nullptr) {
+  int64_t* labels = out.labels + rec.out_off;
+  float* scores = out.scores + rec.out_off;
+  if (out.status[record] != 0) {
+    for (int t = a + tid; t < b; t += nthreads) { labels[t] = -1; scores[t] = -INFINITY; }
+    return;
+  }
+  const int16_t* states = path_states + rec.out_off;
+#pragma unroll 4
+  for (int t = a + tid; t < b; t += nthreads) {
+    const int s = __ldcg(states + t);  // written by other CTAs of the traces' launches
+    const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
+    const int64_t i = static_cast<int64_t>(t) * rec.V + label;
+    float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
+                           : rec.emissions[i];
+    if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
+    labels[t] = label;
+    scores[t] = score;
+    if (stash != nullptr) stash[t - a] = score;
+  }
+}
+
+// n values of shared memory added in order to obj with one fp32 add each
+// (by one thread): the next 8 load while the current 8 are added.
+__device__ __forceinline__ float fold_span(const float* window, int n, float obj) {
+  int k = 0;
+  float cur[8], nxt[8];
+  if (n >= 8) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cur[q] = window[q];
+    for (k = 8; k + 8 <= n; k += 8) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) nxt[q] = window[k + q];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
+  }
+  for (; k < n; ++k) obj = __fadd_rn(obj, window[k]);
+  return obj;
+}
+
+// Objective of a joined record: the path's selected emissions summed in
+// frame order with one fp32 add each -- the conventional DP's accumulation
+// along the same path (alignment.cu:423), so equal paths give equal
+// objectives.  By every thread of the CTA: the scores pass through `window`
+// (shared, room floats) and thread 0 adds them (its result; the others
+// return -0).
+__device__ float fold_path_scores(const float* scores, int T, float* window, int room, int tid, int nthreads) {
+  float obj = -0.0f;  // -0 + x == x exactly for every x
+  for (int base = 0; base < T; base += room) {
+    const int n = min(room, T - base);
+    __syncthreads();
+#pragma unroll 4
+    for (int k = tid; k < n; k += nthreads) window[k] = __ldcg(scores + base + k);
+    __syncthreads();
+    if (tid == 0) obj = fold_span(window, n, obj);
+  }
+  return obj;
+}
+
+// fill_done of a record the finisher filled and folded (ffa_trace_fill skips it).
+constexpr int32_t kFilledByFinisher = INT32_MIN;
 
 // The finisher's static shared memory (its job list) stays under 2 KiB; the
 // rest of the budget is dynamic.
@@ -942,73 +1067,90 @@ ffa_finish_route(const __grid_constant__ ForwardParams P, const int32_t* __restr
     if (x.tl == 0) sh.slot_fault[0] = 0;
     piece_dp<8, kRow, kV, true, kFmt>(x, rec, run, sh, smem_raw, P);
   }
-}
-
-// Traceback segment c of a record by one warp: the warp walks the
-// backpointers from the segment's anchor (path[t-1] = path[t] - bp[t, path[t]],
-// alignment.cu:656-659), then maps states to labels and gathers the selected
-// scores (alignment.cu:662-666); a logits input's score is the same x - z the
-// DPs used (fmt, lse: as in ForwardParams).  A failed record gets -1 / -inf
-// (alignment.cu:650-652).  p: this warp's path scratch (1 << kMaxSegLog2).
-__device__ __forceinline__ void fill_segment(const RecordDev& rec, int record, int c, const uint32_t* bp_arena,
-                                             const int32_t* anchors, const OutputsDev& out, const float* lse,
-                                             int fmt, int32_t* p, int lane) {
+  if (!P.fill_in_finisher) return;
+  // The record's traceback fill and, for a joined path, its objective
+  // (as ffa_trace_fill does, which then skips the record): every warp of the
+  // CTA takes segments, their path scratch and then the fold's window in the
+  // dynamic shared memory the DPs' rings are done with.
+  __syncthreads();  // route, status, anchors and backpointers are written
   const int T = rec.T;
-  const int H = 1 << rec.seg_log2;
-  const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
-  if (c >= C) return;
-  int64_t* labels = out.labels + rec.out_off;
-  float* scores = out.scores + rec.out_off;
-  const int a = c * H;
-  const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + H));
-  if (out.status[record] != 0) {
-    for (int t = a + lane; t < b; t += 32) { labels[t] = -1; scores[t] = -INFINITY; }
-    return;
+  const int C = static_cast<int>((static_cast<int64_t>(T) + (1 << rec.seg_log2) - 1) >> rec.seg_log2);
+  int32_t* scratch = reinterpret_cast<int32_t*>(smem_raw + kForwardHeader);
+  const int room = static_cast<int>((dynamic_smem - kForwardHeader) / sizeof(int32_t));
+  // A joined record that fits the scratch keeps its scores there for the fold.
+  float* window = reinterpret_cast<float*>(scratch);
+  const bool stashed = route_s == kRouteStitched && T <= room;
+  if (route_s == kRouteStitched) {
+    gather_joined(rec, r, 0, T, P.path_states, P.out, P.lse, kFmt, x.tid, static_cast<int>(blockDim.x),
+                  stashed ? window : nullptr);
+  } else {
+    // The conventional DP's path (segment maps and anchors), or -1 / -inf.
+    const int fill_warps = min(nwarps, room >> rec.seg_log2);
+    if (x.warp < fill_warps)
+      for (int c = x.warp; c < C; c += fill_warps)
+        fill_segment(rec, r, c, P.bp, P.anchors, P.out, P.lse, kFmt, scratch + (x.warp << rec.seg_log2), x.lane);
   }
-  const int s_end = anchors[rec.seg_off + c];
-  if (lane == 0) p[b - 1 - a] = s_end;
-  warp_trace_lean(bp_arena + rec.bp_off, bp_row_words(2 * rec.U + 1), s_end, b - 1, a, lane,
-                  [&](int t, int s) { if (lane == 0) p[t - a] = s; });
-  __syncwarp();
-  for (int t = a + lane; t < b; t += 32) {
-    const int s = p[t - a];
-    const int label = (s & 1) ? clamp_label(rec.targets[s >> 1], rec.V) : rec.blank;
-    const int64_t i = static_cast<int64_t>(t) * rec.V + label;
-    float score = fmt == 2 ? bf16_to_float(reinterpret_cast<const uint16_t*>(rec.emissions)[i])
-                           : rec.emissions[i];
-    if (fmt != 0) score = __fsub_rn(score, lse[rec.out_off + t]);
-    labels[t] = label;
-    scores[t] = score;
+  if (route_s == kRouteStitched) {
+    // (fold_path_scores begins with a barrier: the fill's scores are written.)
+    float obj;
+    if (stashed) {
+      __syncthreads();
+      obj = x.tid == 0 ? fold_span(window, T, -0.0f) : 0.0f;
+    } else {
+      obj = fold_path_scores(P.out.scores + rec.out_off, T, window, room, x.tid, static_cast<int>(blockDim.x));
+    }
+    if (x.tid == 0) {
+      P.out.objective[r] = obj;
+      last_s = isfinite(obj) ? 1 : 0;
+      if (!isfinite(obj)) P.out.status[r] = 1;
+    }
+    __syncthreads();
+    if (!last_s)
+      for (int t = x.tid; t < T; t += static_cast<int>(blockDim.x)) {
+        P.out.labels[rec.out_off + t] = -1;
+        P.out.scores[rec.out_off + t] = -INFINITY;
+      }
   }
-  __syncwarp();
+  if (x.tid == 0) P.fill_done[r] = kFilledByFinisher;
 }
 
-// One warp per traceback segment (fill_segment); for a record of the
-// chunked route, the record's last fill CTA to finish (a counter per
-// record) then folds the objective of a joined path.
+// One warp per traceback segment (fill_segment); a joined record of the
+// chunked route gathers its CTA's frames from the path states instead, and
+// the record's last fill CTA to finish (a counter per record) then folds its
+// objective.
 __global__ void __launch_bounds__(32 * kFillWarps)
 ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ items,
                const uint32_t* __restrict__ bp_arena, const int32_t* __restrict__ anchors,
                OutputsDev out, const int32_t* __restrict__ route, int32_t* __restrict__ fill_done,
-               const float* __restrict__ lse, int fmt) {
+               const int16_t* __restrict__ path_states, const float* __restrict__ lse, int fmt) {
   __shared__ int32_t path[kFillWarps][1 << kMaxSegLog2];
   __shared__ int fold_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const FillItem item = items[blockIdx.x];
   const RecordDev rec = recs[item.record];
+  // A record of the chunked route the finisher filled and folded (its
+  // counter is zeroed by the first pass; other records' is not used).
+  // Uniform over the CTA.
+  if (rec.num_pieces > 1 && fill_done[item.record] < 0) return;
   const int T = rec.T;
   const int H = 1 << rec.seg_log2;
   const int C = static_cast<int>((static_cast<int64_t>(T) + H - 1) >> rec.seg_log2);
   int64_t* labels = out.labels + rec.out_off;
   float* scores = out.scores + rec.out_off;
-  fill_segment(rec, item.record, item.first_seg + warp, bp_arena, anchors, out, lse, fmt, path[warp], lane);
-  if (rec.num_pieces <= 1) return;  // uniform over the CTA
+  if (rec.num_pieces <= 1) {
+    fill_segment(rec, item.record, item.first_seg + warp, bp_arena, anchors, out, lse, fmt, path[warp], lane);
+    return;  // uniform over the CTA
+  }
+  if (route[item.record] == kRouteStitched) {
+    const int a = item.first_seg << rec.seg_log2;
+    const int b = static_cast<int>(min(static_cast<int64_t>(T), static_cast<int64_t>(a) + (kFillWarps << rec.seg_log2)));
+    gather_joined(rec, item.record, a, b, path_states, out, lse, fmt, threadIdx.x, 32 * kFillWarps);
+  } else {
+    fill_segment(rec, item.record, item.first_seg + warp, bp_arena, anchors, out, lse, fmt, path[warp], lane);
+  }
 
-  // Objective of a joined record: the path's selected emissions summed in
-  // frame order with one fp32 add each -- the conventional DP's accumulation
-  // along the same path (alignment.cu:423), so equal paths give equal
-  // objectives.  A non-finite sum marks the record failed (alignment.cu:
-  // 507-510, 650-652).
+  // The objective of a joined path (fold_path_scores); a non-finite sum
+  // marks the record failed (alignment.cu:507-510, 650-652).
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -1019,36 +1161,8 @@ ffa_trace_fill(const RecordDev* __restrict__ recs, const FillItem* __restrict__ 
   __syncthreads();
   if (!fold_flag) return;
   __threadfence();
-  float* window = reinterpret_cast<float*>(&path[0][0]);
-  constexpr int kWindow = kFillWarps << kMaxSegLog2;
-  float obj = -0.0f;  // -0 + x == x exactly for every x
-  for (int base = 0; base < T; base += kWindow) {
-    const int n = min(kWindow, T - base);
-    __syncthreads();
-#pragma unroll 4
-    for (int k = threadIdx.x; k < n; k += 32 * kFillWarps) window[k] = scores[base + k];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      // The next 8 values load while the current 8 are added.
-      int k = 0;
-      float cur[8], nxt[8];
-      if (n >= 8) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) cur[q] = window[q];
-        for (k = 8; k + 8 <= n; k += 8) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) nxt[q] = window[k + q];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) obj = __fadd_rn(obj, cur[q]);
-      }
-      for (; k < n; ++k) obj = __fadd_rn(obj, window[k]);
-    }
-  }
+  const float obj = fold_path_scores(scores, T, reinterpret_cast<float*>(&path[0][0]), kFillWarps << kMaxSegLog2,
+                                     threadIdx.x, 32 * kFillWarps);
   if (threadIdx.x == 0) {
     out.objective[item.record] = obj;
     fold_flag = isfinite(obj) ? 1 : 0;
@@ -1523,12 +1637,12 @@ cudaError_t launch_lse(const RecordDev* recs, int count, int64_t rows, int max_v
 
 cudaError_t launch_fill(const RecordDev* recs, const FillItem* items, int num_items,
                         const uint32_t* bp, const int32_t* anchors, const OutputsDev& out,
-                        const int32_t* route, int32_t* fill_done, const float* lse, int fmt,
-                        cudaStream_t stream) {
+                        const int32_t* route, int32_t* fill_done, const int16_t* path_states, const float* lse,
+                        int fmt, cudaStream_t stream) {
   if (num_items <= 0) return cudaSuccess;
   ++g_launches;
   ffa_trace_fill<<<num_items, 32 * kFillWarps, 0, stream>>>(recs, items, bp, anchors, out, route,
-                                                             fill_done, lse, fmt);
+                                                             fill_done, path_states, lse, fmt);
   return cudaGetLastError();
 }
 

@@ -233,36 +233,76 @@ __device__ __forceinline__ GreedyFrame greedy_row(const typename Input<kFmt>::El
   return f;
 }
 
-// The greedy preparation: a warp per record of the window route.  The
-// transcript alphabet (label columns, blank included) as a 64-bit mask, and
-// the token positions grouped by label (a counting sort: lanes holding equal
-// labels form a group, whose first lane updates the label's count).
+// The greedy preparation: a warp per record of the launch.  The transcript
+// alphabet (label columns, blank included) as a 64-bit mask, and the token
+// positions grouped by label (a counting sort: lanes holding equal labels
+// form a group, whose first lane updates the label's count).  The reference
+// runs no greedy chunk of a record of status >= 2 (alignment.cu:35): the
+// same mask and target checks as the DP kernels' (alignment.cu:836,
+// 852-874) mark such a record with an empty alphabet, and its statistics stay
+// zero.
 __global__ void __launch_bounds__(32 * kGreedyWarps)
 ffa_greedy_prep(const __grid_constant__ GreedyParams P) {
   const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
   const int64_t index = static_cast<int64_t>(blockIdx.x) * kGreedyWarps + warp;
   if (index >= P.num_records) return;
-  const int r = P.slots[index].record;
+  const int r = P.records[index];
   const RecordDev rec = P.recs[r];
-  const int U = rec.U, V = rec.V, blank = rec.blank;
+  const int T = rec.T, U = rec.U, V = rec.V, blank = rec.blank;
   uint16_t* lpos = P.lpos + P.tok_off[r];
   uint16_t* lstart = P.lstart + static_cast<int64_t>(kGreedyLabels) * r;
   __shared__ uint16_t cursor_s[kGreedyWarps][kGreedyLabels];
+  __shared__ uint8_t label_s[kGreedyWarps][kMaxStates / 2];  // U < kMaxStates / 2 here
   uint16_t* cursor = cursor_s[warp];
+  uint8_t* labs = label_s[warp];
   for (int c = lane; c < kGreedyLabels; c += 32) cursor[c] = 0;
+  // The transcript's label columns (clamped into the row), four 32-token
+  // blocks of loads in flight at a time; invalid IDs (status 3).
+  int bad = 0;
+  for (int base = 0; base < U; base += 128) {
+    int64_t token[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = base + 32 * q + lane;
+      token[q] = k < U ? __ldg(rec.targets + k) : 0;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = base + 32 * q + lane;
+      if (k < U) {
+        bad |= (token[q] < 0 || token[q] >= V || token[q] == blank) ? 1 : 0;
+        labs[k] = static_cast<uint8_t>(clamp_label(token[q], V));
+      }
+    }
+  }
   __syncwarp();
+  // Alphabet, adjacent repeats (status 4; with every ID valid the labels are
+  // the IDs) and each label's token count.
   uint64_t alpha = uint64_t{1} << blank;
+  int rep = 0;
   for (int base = 0; base < U; base += 32) {
     const int k = base + lane;
-    const int c = k < U ? clamp_label(__ldg(rec.targets + k), V) : 0x100 + lane;
-    if (k < U) alpha |= uint64_t{1} << c;
+    const int c = k < U ? labs[k] : 0x100 + lane;
+    if (k < U) {
+      alpha |= uint64_t{1} << c;
+      if (k > 0 && labs[k - 1] == c) ++rep;
+    }
     const unsigned grp = __match_any_sync(kFull, c);
     if (k < U && lane == __ffs(grp) - 1) cursor[c] = static_cast<uint16_t>(cursor[c] + __popc(grp));
     __syncwarp();
   }
+  bool rejected = P.mask != nullptr && !P.mask[r];
+  if (P.check_inputs) {
+    bad = __reduce_or_sync(kFull, bad);
+    rep = __reduce_add_sync(kFull, rep);
+    rejected |= bad != 0 || static_cast<int64_t>(U) + rep > T;
+  }
   const unsigned lo = __reduce_or_sync(kFull, static_cast<unsigned>(alpha));
   const unsigned hi = __reduce_or_sync(kFull, static_cast<unsigned>(alpha >> 32));
-  if (lane == 0) P.alphabet[r] = static_cast<uint64_t>(hi) << 32 | lo;
+  if (lane == 0) {
+    P.alphabet[r] = rejected ? 0 : static_cast<uint64_t>(hi) << 32 | lo;
+    for (int j = 0; j < 3; ++j) P.shortcut_stats[3 * r + j] = 0;
+  }
   // Exclusive prefix over labels (V <= 64: two per lane).
   const int c0 = 2 * lane, c1 = c0 + 1;
   const int n0 = c0 < V ? cursor[c0] : 0, n1 = c1 < V ? cursor[c1] : 0;
@@ -280,7 +320,7 @@ ffa_greedy_prep(const __grid_constant__ GreedyParams P) {
   __syncwarp();
   for (int base = 0; base < U; base += 32) {
     const int k = base + lane;
-    const int c = k < U ? clamp_label(__ldg(rec.targets + k), V) : 0x100 + lane;
+    const int c = k < U ? labs[k] : 0x100 + lane;
     const unsigned grp = __match_any_sync(kFull, c);
     const int at = k < U ? cursor[c] + __popc(grp & ((1u << lane) - 1u)) : 0;
     __syncwarp();
@@ -365,9 +405,19 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
     verdict = greedy_verdict(lab, a, b, T, S, blank, P.lpos + P.tok_off[r],
                              P.lstart + static_cast<int64_t>(kGreedyLabels) * r, label_of, lane);
   }
-  if (lane == 0)
+  if (lane == 0) {
     P.verdicts[P.greedy_first[r] + item.chunk] =
         static_cast<uint8_t>(verdict | (poison ? kGreedyPoison : 0) | (positive ? kGreedyPositive : 0));
+    // The reference's statistics (alignment.cu:130-146): accepted chunks and
+    // their frames; chunks with several placements.
+    unsigned long long* stats = reinterpret_cast<unsigned long long*>(P.shortcut_stats + 3 * r);
+    if (alpha != 0 && verdict == kGreedyAccepted) {
+      atomicAdd(stats, 1ull);
+      atomicAdd(stats + 1, static_cast<unsigned long long>(b - a));
+    } else if (alpha != 0 && verdict == kGreedyMultiple) {
+      atomicAdd(stats + 2, 1ull);
+    }
+  }
 }
 
 // A lane's K states: base + K lane + k (even k: blanks, odd k: tokens), their
@@ -498,7 +548,8 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
     P.out.stitched[r] = 0;
     P.out.repair_passes[r] = 0;
     P.out.repaired_frames[r] = 0;
-    for (int j = 0; j < 3; ++j) { P.out.shortcut_stats[3 * r + j] = 0; P.out.routing_stats[3 * r + j] = 0; }
+    // (The greedy pass owns the shortcut statistics.)
+    for (int j = 0; j < 3; ++j) P.out.routing_stats[3 * r + j] = 0;
     if (P.out.reuse_stats) for (int j = 0; j < 4; ++j) P.out.reuse_stats[4 * r + j] = 0;
   }
   if (status >= 2) {
@@ -724,28 +775,17 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
   const float opt = take_prev ? vprev : vlast;
   const int term = take_prev ? S - 2 : S - 1;
   // The greedy pass's verdicts: NaN / +inf in an alphabet column, positive
-  // bounds, and the reference's greedy chunk statistics (alignment.cu:130-153).
+  // bounds.
   const int nitems = (T + kGreedyChunk - 1) / kGreedyChunk;
   const uint8_t* verdicts = P.verdicts + P.greedy_first[r];
-  int accepted = 0, frames = 0, multiple = 0;
   bool poison = false, positive = false;
   for (int k = lane; k < nitems; k += 32) {
     const int v = verdicts[k];
     poison |= (v & kGreedyPoison) != 0;
     positive |= (v & kGreedyPositive) != 0;
-    if ((v & 3) == kGreedyAccepted) { ++accepted; frames += min(T, (k + 1) * kGreedyChunk) - k * kGreedyChunk; }
-    if ((v & 3) == kGreedyMultiple) ++multiple;
   }
   poison = __any_sync(kFull, poison);
   positive = __any_sync(kFull, positive);
-  accepted = __reduce_add_sync(kFull, accepted);
-  frames = __reduce_add_sync(kFull, frames);
-  multiple = __reduce_add_sync(kFull, multiple);
-  if (!kWide && lane == 0) {
-    P.out.shortcut_stats[3 * r + 0] = accepted;
-    P.out.shortcut_stats[3 * r + 1] = frames;
-    P.out.shortcut_stats[3 * r + 2] = multiple;
-  }
   const double exit_loss = warp_min(esc);
   const double loss = M - static_cast<double>(opt);
   // Rounding: T additions along the full DP's path, each within 2^-24 of

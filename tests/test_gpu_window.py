@@ -182,15 +182,54 @@ def test_auto_route_policy(cuda):
     assert stitched[short].sum() == 0  # window records are never joined from pieces
 
 
-def test_matches_the_references_greedy_counts(cuda):
+@pytest.mark.parametrize("route", ["window", "pieces", "auto"])
+def test_matches_the_references_greedy_counts(cuda, route):
     # The reference's own extension counts greedy chunks (shortcut_stats,
-    # alignment.cu:130-153) in optimized mode: the window route's counts are
-    # the same numbers.
+    # alignment.cu:130-153) in optimized mode: every route reports the same
+    # numbers (the chunked route runs the greedy pass for them alone).
     if not oracle.load_reference_cuda():
         pytest.skip("reference CUDA extension not built under oracle/_ref")
     for index in (0, 1):
         wl = workloads.config(index)
         es, ts = cuda_records(*wl.records())
         tensors, _ = oracle.reference_cuda_align(es, ts, [wl.blank] * wl.batch, mode="optimized")
-        mine = ffa.align(es, ts, blank_id=wl.blank, mode="optimized", route="window")
+        mine = ffa.align(es, ts, blank_id=wl.blank, mode="optimized", route=route)
         np.testing.assert_array_equal(mine.shortcut_stats.cpu().numpy(), tensors[7].cpu().numpy())
+
+
+@pytest.mark.parametrize("route", ["pieces", "auto"])
+@pytest.mark.parametrize("index, scale", [(0, 1.0), (1, 1.0), (4, 0.12)])
+def test_chunked_route_counts_greedy_chunks(cuda, route, index, scale):
+    # Records off the window route (pieces, short records, mixed batches)
+    # carry the greedy statistics of the oracle's greedy_shortcuts
+    # restatement as well; the outputs stay the route's own.
+    wl = workloads.config(index, scale=scale)
+    es, ts = wl.records()
+    d_es, d_ts = cuda_records(es, ts)
+    result = ffa.align(d_es, d_ts, blank_id=wl.blank, mode="optimized", route=route)
+    np.testing.assert_array_equal(result.shortcut_stats.cpu().numpy(), greedy_counts(es, ts, wl.blank))
+    assert int(result.shortcut_stats[:, 0].sum()) > 0
+
+
+def test_greedy_counts_skip_rejected_records(cuda):
+    # A record of status >= 2 runs no greedy chunk (alignment.cu:35): masked,
+    # invalid IDs, too few frames -- on both routes, beside valid records
+    # whose counts are unchanged.
+    rng = np.random.default_rng(5)
+    T, V = 700, 32
+    good = torch.randn(T, V, device=cuda).log_softmax(-1)
+    path = torch.from_numpy(rng.integers(1, V, 120)).to(cuda)
+    strong = good.clone()
+    strong[torch.arange(T, device=cuda), path.repeat_interleave(T // 120 + 1)[:T]] += 8
+    strong = strong.log_softmax(-1)
+    short = strong[:100].contiguous()
+    ems = [strong, strong, strong, short]
+    tgts = [path, torch.tensor([1, 40, 2], device=cuda), path, path]
+    mask = torch.tensor([True, True, False, True], device=cuda)
+    for route in ("pieces", "window"):
+        result = ffa.align(ems, tgts, mode="optimized", route=route, emission_validity=mask)
+        assert result.status.tolist()[1:] == [3, 2, 4]
+        assert result.shortcut_stats[1:].count_nonzero() == 0
+        expected = oracle.greedy_chunk_stats(strong.cpu().numpy(), path.cpu().numpy(), 0)
+        np.testing.assert_array_equal(result.shortcut_stats[0].cpu().numpy(), expected)
+        assert expected[0] > 0
