@@ -64,6 +64,8 @@ def parse_args():
                    help="partition one batch over the ranks (strong scaling) instead of one batch per rank")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="CPU work in the cpu_baseline sample")
+    p.add_argument("--route", default="auto", choices=["auto", "pieces", "window"],
+                   help="optimized mode's route for the device-resident timing (align's route=)")
     p.add_argument("--input", default="log-probs", choices=["log-probs", "logits-f32", "logits-bf16"],
                    help="what the batch holds: fp32 log-probabilities (the reference's input), or a "
                         "model's logits aligned as their log_softmax inside the kernels (from_logits)")
@@ -107,12 +109,14 @@ def algorithmic_bytes(wl, element_bytes=4):
     return read, read + out
 
 
-def traffic_from_profile(config_name):
-    """dram bytes per forward launch from the committed ncu summary, if any."""
+def from_profile(config_name, key):
+    """A per-launch figure of the first pass (`key: value`) from the committed
+    ncu summary of that workload, if any: traffic_bytes_per_launch (dram
+    bytes read + written) or warp_instructions_per_launch."""
     path = ROOT / "profiles" / f"ffa_viterbi_forward_{config_name}.md"
     if not path.exists():
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    m = re.search(key + r":\s*([0-9.eE+]+)", path.read_text())
     return float(m.group(1)) if m else None
 
 
@@ -414,7 +418,7 @@ def run_ours(args):
 
     def step(e, t):
         return ffa.align_packed(e, wl.lengths, t, wl.target_lengths, blank_id=wl.blank, mode=args.mode,
-                                from_logits=from_logits)
+                                from_logits=from_logits, route=args.route)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     import ctypes
@@ -552,7 +556,8 @@ def run_ours(args):
     read_bytes, alg_bytes = algorithmic_bytes(wl, e_dev.element_size())
     peak, peak_kind = peaks()
     achieved = read_bytes / (fwd_avg_ms / 1e3) / 1e9
-    traffic = traffic_from_profile(wl.name)
+    traffic = from_profile(wl.name, "traffic_bytes_per_launch")
+    instructions = from_profile(wl.name, "warp_instructions_per_launch")
     cells = wl.cells()
     line = {
         "metric": "aligned frames/sec", "value": value, "unit": "frames/s",
@@ -566,7 +571,7 @@ def run_ours(args):
         "config": {"workload": wl.name if args.scale == 1.0 else f"{wl.name} at scale {args.scale}",
                    "records_per_gpu": wl.batch, "frames_per_gpu": frames,
                    "records_total": records_total, "frames_total": int(all_frames),
-                   "vocab": wl.vocab, "mode": args.mode, "check_inputs": True,
+                   "vocab": wl.vocab, "mode": args.mode, "route": args.route, "check_inputs": True,
                    "inputs": ("packed device-resident fp32 [sum T, V] log-probabilities" if not from_logits
                               else f"packed device-resident {args.input[7:]} [sum T, V] logits, aligned as their "
                                    "log_softmax inside the kernels (from_logits)") + " + int64 targets",
@@ -615,6 +620,18 @@ def run_ours(args):
                                        "resident, timed as value"}
     clock = clocks.summary()
     line["clocks"] = clock
+    if instructions is not None and args.route == "auto":
+        # The first pass's issue roofline: its warp instructions per launch (the
+        # committed ncu summary) over its live duration, against every SMSP
+        # issuing one warp instruction per cycle at the sampled clock.
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        issue_peak = sms * 4 * clock["sm_mhz"] * 1e6 / 1e9 if clock.get("sm_mhz") else None
+        issue = instructions / (fwd_avg_ms / 1e3) / 1e9
+        line["roofline"]["issue"] = {
+            "bound": "issue", "achieved": issue, "peak": issue_peak, "unit": "G warp-instructions/s",
+            "frac": issue / issue_peak if issue_peak else None, "instructions_per_launch": instructions,
+            "peak_source": f"{sms} SMs x 4 SMSPs x 1 warp-instruction per cycle at the sampled SM clock",
+            "source": f"profiles/ffa_viterbi_forward_{wl.name}.md"}
     if rank == 0 and world == 1:
         run, kind, threads, pool = cpu_reference_runner(wl)
         cpu_value, passes, seconds = time_cpu(run, frames, args.cpu_seconds)
