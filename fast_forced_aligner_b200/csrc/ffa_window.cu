@@ -592,16 +592,10 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
     col = valid ? static_cast<int>(tok[u]) : blank;
     sk = valid && u >= 1 && tok[u] != blank && tok[u] != tok[u - 1];
   };
-  int col[K / 2], next_col[K / 2];
-  bool sk[K / 2], next_sk[K / 2];
+  int col[K / 2];
+  bool sk[K / 2];
 #pragma unroll
-  for (int q = 0; q < K / 2; ++q) {
-    token_info(K * lane + 2 * q + 1, col[q], sk[q]);
-    next_col[q] = blank;
-    next_sk[q] = false;
-    // The top lanes' states after the next slide, loaded ahead of it.
-    if (lane >= 32 - kShift) token_info(kSlide + K * lane + 2 * q + 1, next_col[q], next_sk[q]);
-  }
+  for (int q = 0; q < K / 2; ++q) token_info(K * lane + 2 * q + 1, col[q], sk[q]);
   const bool first_lane = lane == 0, top_lane = lane == 31;
 
   double Mbase = 0.0;     // sum of the greedy bounds m of the frames before this chunk
@@ -727,18 +721,10 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
           x.anc[k] = __shfl_down_sync(kFull, x.anc[k], kShift);
           if (top) x.a[k] = kNegInf;
         }
-#pragma unroll
-        for (int q = 0; q < K / 2; ++q) {
-          const int ncol = __shfl_down_sync(kFull, col[q], kShift);
-          const bool nsk = __shfl_down_sync(kFull, sk[q] ? 1 : 0, kShift) != 0;
-          col[q] = top ? next_col[q] : ncol;
-          sk[q] = top ? next_sk[q] : nsk;
-        }
+        // Every lane reads its new states' label columns from shared memory.
         base += kSlide;
-        if (top) {
 #pragma unroll
-          for (int q = 0; q < K / 2; ++q) token_info(base + kSlide + K * lane + 2 * q + 1, next_col[q], next_sk[q]);
-        }
+        for (int q = 0; q < K / 2; ++q) token_info(base + K * lane + 2 * q + 1, col[q], sk[q]);
       }
     }
     __syncwarp();  // the top state's scores are in the stash; every lane has read the ring entry
