@@ -876,7 +876,10 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     auto* sorted_win = reinterpret_cast<int32_t*>(host + L.keys);  // the first pass is done with the keys
     for (int32_t i : win_records) sorted_win[bucket_start[bucket(i)]++] = i;
     const int64_t per_cta = std::clamp<int64_t>((nwin + sms - 1) / sms, 1, ffa::kWinWarps);
-    const uint32_t budget = static_cast<uint32_t>(ffa::kSmemBudget - 1024);
+    // Two CTAs share an SM when each stays under half the budget: twice the
+    // warps to cover each warp's per-frame dependency chain.  A record larger
+    // than that gets a CTA of its own.
+    const uint32_t budget = static_cast<uint32_t>((ffa::kSmemBudget - 2048) / 2);
     uint32_t cur = 0;
     for (int64_t k = 0; k < nwin; ++k) {
       const int32_t i = sorted_win[k];

@@ -303,7 +303,7 @@ constexpr int kWinStates = 64;        // window width: 32 lanes x 2 states
 constexpr int kWinSlide = 16;         // states a slide moves the window by
 constexpr int kWinHigh = 32;          // slide when the best state sits this far up (4 frames before)
 constexpr int kWinChunk = 32;         // frames per TMA row copy = traceback segment
-constexpr int kWinRing = 3;           // row copies in flight per record
+constexpr int kWinRing = 2;           // row copies in flight per record (a chunk takes microseconds)
 constexpr int kWinMaxFrames = 8192;   // longer records take the chunked route
 constexpr int kWinWideMaxFrames = 4096;  // the 128-state tier's limit (longer: the full DP)
 constexpr int kGreedyChunk = 128;     // the reference's greedy chunk (alignment.py:498: chunk_frames)
