@@ -1082,15 +1082,20 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     err = cudaEventRecord(g_profile_after, s);
     if (err != cudaSuccess) return cuda_fail(err, "profiling event");
   }
-  if (stats_greedy) {
+  // The greedy pass of the records off the window route (their statistics
+  // only): beside the first pass on the side stream when the window route has
+  // nothing there, else after the fill on this stream, which then ends before
+  // the window route's chain.
+  auto stats_pass = [&](cudaStream_t stream) {
     ffa::GreedyParams sp = gp;
     sp.records = reinterpret_cast<const int32_t*>(dev + L.greedy_recs) + win_records.size();
     sp.num_records = static_cast<int64_t>(stats_records.size());
     sp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items) + L.num_greedy_window;
     sp.count = nstats_items;
-    err = ffa::launch_greedy(sp, stats_vocab > 0 ? stats_vocab : 0, fmt, ws);
-    if (err != cudaSuccess) return cuda_fail(err, "greedy pass launch");
-  }
+    const cudaError_t e = ffa::launch_greedy(sp, stats_vocab > 0 ? stats_vocab : 0, fmt, stream);
+    return e == cudaSuccess ? FFA_OK : cuda_fail(e, "greedy pass launch");
+  };
+  if (stats_greedy && n_wcta == 0 && (rc = stats_pass(ws))) return rc;
   if ((rc = mark(FFA_PROFILE_FIRST))) return rc;
   // The optimized route's seam plans, repairs and fallback: a CTA per record
   // (the first round spread over up to four while the records leave SMs
@@ -1125,6 +1130,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                            fp.path_states, fp.lse, fmt, s);
     if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
   }
+  if (stats_greedy && n_wcta > 0 && (rc = stats_pass(s))) return rc;
   if (forked) {
     if ((err = cudaEventRecord(side->join, ws)) != cudaSuccess) return cuda_fail(err, "stream join");
     if ((err = cudaStreamWaitEvent(s, side->join, 0)) != cudaSuccess) return cuda_fail(err, "stream join");

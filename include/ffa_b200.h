@@ -123,12 +123,17 @@ typedef struct ffa_record {
 } ffa_record;
 
 /* Caller-allocated device outputs, packed in record order without padding
- * (reference AlignmentBatch fields, alignment.py:138-148).  Diagnostics of
- * the window route: stitched, repair_passes, repaired_frames and reuse_stats
- * are 0; shortcut_stats holds the reference's greedy chunk counts (accepted
- * 128-frame chunks, their frames, chunks with several placements); the
- * routing state routing_stats[i, 0] is 2 when the record ran the full DP as
- * fallback (the reference's completed early fallback), else 0. */
+ * (reference AlignmentBatch fields, alignment.py:138-148).  Diagnostics in
+ * optimized mode: shortcut_stats holds the reference's greedy chunk counts
+ * (accepted 128-frame chunks, their frames, chunks with several placements)
+ * for every record whose rows can be TMA-staged (vocab <= 64) with at most
+ * 4096 states, on either route, and 0 for the others and for records of
+ * status >= 2; stitched, repair_passes, repaired_frames and reuse_stats count
+ * the chunked route's joins and repairs (0 on the window route); the routing
+ * state routing_stats[i, 0] is 2 when a window-route record ran the full DP as
+ * fallback (the reference's completed early fallback), else 0.  When a call
+ * has work for both routes, one of them runs on a per-thread side stream
+ * forked from `stream` and joined back into it before ffa_align returns. */
 typedef struct ffa_outputs {
   int64_t* labels;          /* [sum T] vocabulary id per frame; -1 for failed records */
   float* scores;            /* [sum T] selected emission per frame; -inf for failed */
