@@ -273,6 +273,19 @@ def reference_cuda_lane(wl, e_dev, t_dev, steps, warmup, flush):
     return out
 
 
+def window_records(wl, sms, route="auto"):
+    """Which records the library's route policy gives the window route
+    (window_policy, ffa_host.cpp): row-staged (V <= 64, 16-byte rows), at most
+    4096 states and 2048 frames, when more than 4 per SM of them are in the
+    call; route="window" raises the frame limit to 8192."""
+    row = wl.vocab <= 64 and (wl.vocab * 4) % 16 == 0
+    limit = 8192 if route == "window" else 2048
+    ok = (wl.lengths <= limit) & (2 * wl.target_lengths + 1 <= 4096) & row
+    if route == "auto" and ok.sum() <= 4 * sms:
+        ok[:] = False
+    return ok
+
+
 def strong_cfg4_lane(ffa, lib, rank, world, device, steps, warmup, flush, max_over_ranks, barrier, peak):
     """Strong scaling on the multi-GPU configuration (cfg4): every rank draws
     the same 8,256-record batch and aligns its LPT share (shard_of_rank),
@@ -297,8 +310,8 @@ def strong_cfg4_lane(ffa, lib, rank, world, device, steps, warmup, flush, max_ov
     # profiling events, against the rows it reads and the bounds it writes.
     import ctypes
     greedy = None
-    window = (shard.lengths <= 2048) & (2 * shard.target_lengths + 1 <= 4096)
-    if window.sum() > 4 * torch.cuda.get_device_properties(device).multi_processor_count:
+    window = window_records(shard, torch.cuda.get_device_properties(device).multi_processor_count)
+    if window.any():
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for x in ev:
             x.record()
@@ -555,6 +568,17 @@ def run_ours(args):
     fwd_avg_ms = max_over_ranks(statistics.fmean(fwd_ms))
     read_bytes, alg_bytes = algorithmic_bytes(wl, e_dev.element_size())
     peak, peak_kind = peaks()
+    # With records on the window route, the profiled launch is the greedy pass
+    # (every row of those records once, and each frame's bound written).
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    win = window_records(wl, sms, args.route) if args.mode == "optimized" and args.route != "pieces" else None
+    if win is not None and win.any():
+        wf = int(wl.lengths[win].sum())
+        read_bytes = wf * wl.vocab * e_dev.element_size() + wf * 4
+        roofline_kernel = ("ffa_greedy_pass (window route: each frame's bound over the alphabet and the "
+                           "reference's greedy chunk verdicts; its span overlaps the chunked route's kernels)")
+    else:
+        roofline_kernel = "ffa_viterbi_forward (first pass: streams every emission row)"
     achieved = read_bytes / (fwd_avg_ms / 1e3) / 1e9
     traffic = from_profile(wl.name, "traffic_bytes_per_launch")
     instructions = from_profile(wl.name, "warp_instructions_per_launch")
@@ -585,7 +609,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": int(frames * 12 + wl.batch * 8),
                 "api": "fast_forced_aligner_b200.AlignStream.submit (align_packed, the torch op over the "
                        "C ABI, with host copies overlapped on separate streams)"},
-        "roofline": {"kernel": "ffa_viterbi_forward (first pass: streams every emission row)",
+        "roofline": {"kernel": roofline_kernel,
                      "bound": "hbm", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic,
@@ -620,11 +644,10 @@ def run_ours(args):
                                        "resident, timed as value"}
     clock = clocks.summary()
     line["clocks"] = clock
-    if instructions is not None and args.route == "auto":
+    if instructions is not None and args.route == "auto" and not (win is not None and win.any()):
         # The first pass's issue roofline: its warp instructions per launch (the
         # committed ncu summary) over its live duration, against every SMSP
         # issuing one warp instruction per cycle at the sampled clock.
-        sms = torch.cuda.get_device_properties(device).multi_processor_count
         issue_peak = sms * 4 * clock["sm_mhz"] * 1e6 / 1e9 if clock.get("sm_mhz") else None
         issue = instructions / (fwd_avg_ms / 1e3) / 1e9
         line["roofline"]["issue"] = {

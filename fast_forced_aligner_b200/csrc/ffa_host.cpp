@@ -997,14 +997,12 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   if (n_wcta > 0) {
     const int wv = win_vocab > 0 ? win_vocab : 0;
     // The greedy pass streams every row of the window records once: it is
-    // the launch the forward profiling events bracket.
+    // the launch the forward profiling events bracket (after the preparation).
     gp.records = reinterpret_cast<const int32_t*>(dev + L.greedy_recs);
     gp.num_records = static_cast<int64_t>(win_records.size());
     gp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.greedy_items);
     gp.count = ngreedy;
-    if (g_profile_before != nullptr && (err = cudaEventRecord(g_profile_before, ws)) != cudaSuccess)
-      return cuda_fail(err, "profiling event");
-    err = ffa::launch_greedy(gp, wv, fmt, ws);
+    err = ffa::launch_greedy(gp, wv, fmt, ws, g_profile_before);
     if (err != cudaSuccess) return cuda_fail(err, "greedy pass launch");
     if (g_profile_after != nullptr && (err = cudaEventRecord(g_profile_after, ws)) != cudaSuccess)
       return cuda_fail(err, "profiling event");

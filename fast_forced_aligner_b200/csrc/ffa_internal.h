@@ -344,8 +344,10 @@ struct GreedyParams {
   int32_t check_inputs;         // statuses 3 and 4 are checked
   int64_t* shortcut_stats;      // [count, 3]: zeroed by the preparation, counted by the pass
 };
-// The preparation (a warp per record) and the pass (a warp per chunk).
-cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream);
+// The preparation (a warp per record) and the pass (a warp per chunk);
+// `between` (or null) is recorded on the stream between the two.
+cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream,
+                          cudaEvent_t between = nullptr);
 
 // One record's slice of a window CTA's dynamic shared memory for K states
 // per lane (a window of 32 K states); offsets in bytes from the slice start

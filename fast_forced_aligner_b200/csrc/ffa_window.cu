@@ -909,7 +909,8 @@ cudaError_t window_opt_in(WindowKernel kernel, std::atomic<uint64_t>& opted) {
 
 }  // namespace
 
-cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream) {
+cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream,
+                          cudaEvent_t between) {
   if (params.count <= 0 || params.num_records <= 0) return cudaSuccess;
   if (fmt < 0 || fmt > 2) return cudaErrorInvalidValue;
   count_launch();
@@ -917,6 +918,7 @@ cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cu
                     32 * kGreedyWarps, 0, stream>>>(params);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
+  if (between != nullptr && (err = cudaEventRecord(between, stream)) != cudaSuccess) return err;
   count_launch();
   kGreedyKernels[window_variant(row_vocab, fmt)]<<<static_cast<unsigned>((params.count + kGreedyWarps - 1) /
                                                                          kGreedyWarps),

@@ -229,12 +229,12 @@ FFA_API int ffa_align_noalloc(const ffa_record* records, int64_t count, int mode
  *      per-kernel timing) --------------------------------------------------- */
 
 /* While set, ffa_align calls made on the calling thread record `before` and
- * `after` (two cudaEvent_t created by the caller) on their stream immediately
- * around the launch that streams every emission row once -- the greedy pass
- * when the call has records of the window route, else the first forward pass
- * (every piece of the chunked route, every record of the conventional mode)
- * -- so the caller can read its device time with cudaEventElapsedTime.
- * Pass NULL, NULL to clear. */
+ * `after` (two cudaEvent_t created by the caller) immediately around the
+ * launch that streams every emission row once, on the stream it runs on --
+ * the greedy pass (after its preparation) when the call has records of the
+ * window route, else the first forward pass (every piece of the chunked
+ * route, every record of the conventional mode) -- so the caller can read its
+ * device time with cudaEventElapsedTime.  Pass NULL, NULL to clear. */
 FFA_API int ffa_profile_forward_events(void* before, void* after);
 
 /* Number of CUDA kernels the ffa_* calls of the calling thread have launched
