@@ -27,7 +27,11 @@
  *   - Thread safety: every function except ffa_align_noalloc is reentrant;
  *     concurrent calls on different streams or devices share no mutable
  *     state.  ffa_align_noalloc uses one process-wide device scratch array
- *     and one host staging array: see its own comment.
+ *     and one host staging array: see its own comment.  A call of optimized
+ *     mode with work for both of its routes runs one route on a side stream
+ *     of the calling thread and device (see ffa_outputs), so two such calls
+ *     from one thread on different streams order their side-stream work one
+ *     after the other; their results are unaffected.
  */
 #ifndef FFA_B200_H
 #define FFA_B200_H
