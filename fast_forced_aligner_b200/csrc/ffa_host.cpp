@@ -784,42 +784,66 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
         chunked[nc++] = static_cast<int32_t>(i);
     finish_end[grp] = nc;
   }
-  // Warps per CTA: the launch's warps spread evenly over the SMs (one CTA
-  // runs per SM): the smallest per-CTA target whose packing still fits one
-  // wave, so that every SM gets a share and none gets more than it must.
-  int64_t first_warps = 0;
-  for (const ClassRun& run : runs) first_warps += run.slots * class_warps(run.cls);
-  auto capacity = [&](const ClassRun& run, int64_t target) {
+  // CTAs of the first pass: each class run cut into consecutive slots whose
+  // work stays within one budget, the smallest that still fits one wave (one
+  // CTA per SM), so that the SMs finish together.  A slot's work per frame,
+  // fitted to per-CTA times measured on a B200 (cfg1, CTAs of 4 to 16 slots
+  // sharing an SM): about 22.6 + 1.06 K ns per warp at K states per thread,
+  // plus 10.6 ns per slot (its barrier and boundary exchange) -- in units of
+  // about 1.06 ns, nw (21 + K) + 10 -- times its frames.
+  auto slot_cost = [&](int64_t s) -> int64_t {
+    const ffa::RecordDev& d = recs[order[s].record];
+    const int64_t first = static_cast<int64_t>(order[s].piece) * ffa::kPieceFrames;
+    const int64_t frames = d.num_pieces > 1 && order[s].piece + run_pieces < d.num_pieces
+                               ? static_cast<int64_t>(run_pieces) * ffa::kPieceFrames
+                               : d.T - first;
+    return (static_cast<int64_t>(d.nw) * (21 + static_cast<int64_t>(d.kst)) + 10) * frames;
+  };
+  // Cuts one class run at `budget` (and at kMaxWarps warps and, row-staged,
+  // row_slots rings per CTA); emit(first slot, slots) for each CTA.
+  auto cut = [&](const ClassRun& run, int64_t budget, auto&& emit) {
     const int nw = class_warps(run.cls);
-    int64_t cap = std::min<int64_t>(ffa::kMaxWarps / nw, std::max<int64_t>(1, target / nw));
+    int64_t cap = ffa::kMaxWarps / nw;
     if (class_row(run.cls)) cap = std::min(cap, row_slots);
-    return cap;
-  };
-  auto ctas_for = [&](int64_t target) {
-    int64_t ctas = 0;
-    for (const ClassRun& run : runs) {
-      const int64_t cap = capacity(run, target);
-      ctas += (run.slots + cap - 1) / cap;
+    int64_t first = run.first, m = 0, work = 0;
+    for (int64_t k = run.first; k < run.first + run.slots; ++k) {
+      const int64_t c = slot_cost(k);
+      if (m > 0 && (m == cap || work + c > budget)) {
+        emit(first, m);
+        first = k;
+        m = 0;
+        work = 0;
+      }
+      ++m;
+      work += c;
     }
-    return ctas;
+    if (m > 0) emit(first, m);
   };
-  int64_t target = std::min<int64_t>(ffa::kMaxWarps, (first_warps + sms - 1) / sms);
-  while (target < ffa::kMaxWarps && ctas_for(target) > sms) ++target;
-  // Bundles: each class run cut into CTAs of at most `capacity` slots; the
-  // row-staged runs come first (one launch each kind).
+  auto ctas_for = [&](int64_t budget) {
+    int64_t n = 0;
+    for (const ClassRun& run : runs) cut(run, budget, [&](int64_t, int64_t) { ++n; });
+    return n;
+  };
+  int64_t budget = INT64_MAX;  // (when even full CTAs take more than one wave)
+  if (ctas_for(budget) <= sms) {
+    int64_t total = 0;
+    for (const ClassRun& run : runs)
+      for (int64_t k = run.first; k < run.first + run.slots; ++k) total += slot_cost(k);
+    budget = std::max<int64_t>(1, (total + sms - 1) / sms);
+    while (ctas_for(budget) > sms) budget += std::max<int64_t>(1, budget / 32);
+  }
+  // Bundles; the row-staged runs come first (one launch each kind).
   const size_t bundles_off = align_up(L.slots + sizeof(ffa::SlotRef) * n_first, 16);
   auto* bundles = reinterpret_cast<ffa::Bundle*>(host + bundles_off);
   int64_t nb = 0, nb_row = 0, max_row_slots = 1;
   int max_gather_k = 8;
   for (const ClassRun& run : runs) {
-    const int64_t cap = capacity(run, target);
     const int nw = class_warps(run.cls);
-    for (int64_t off = 0; off < run.slots; off += cap) {
-      const int64_t m = std::min(cap, run.slots - off);
-      bundles[nb++] = ffa::Bundle{static_cast<int32_t>(run.first + off), static_cast<uint8_t>(nw),
-                                  static_cast<uint8_t>(m), run.kst, 0};
+    cut(run, budget, [&](int64_t first, int64_t m) {
+      bundles[nb++] = ffa::Bundle{static_cast<int32_t>(first), static_cast<uint8_t>(nw), static_cast<uint8_t>(m),
+                                  run.kst, 0};
       if (class_row(run.cls)) max_row_slots = std::max(max_row_slots, m);
-    }
+    });
     if (class_row(run.cls)) nb_row = nb;
   }
   for (int64_t i = 0; i < count; ++i)

@@ -746,11 +746,25 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
       int status = masked ? 2 : 0;
       if (tl == 0) sh.slot_fault[x.slot] = 0;
       if (P.check_inputs) {
+        // Four strides of loads in flight at a time: a one-warp slot walks a
+        // long transcript in few round trips.
         int bad = 0, rep = 0;
-        for (int k = tl; k < U; k += x.NT) {
-          const int64_t token = tgt[k];
-          bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
-          if (k > 0) rep += token == tgt[k - 1] ? 1 : 0;
+        for (int k0 = tl; k0 < U; k0 += 4 * x.NT) {
+          int64_t cur[4], prv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int k = k0 + q * x.NT;
+            cur[q] = k < U ? tgt[k] : 0;
+            prv[q] = k < U && k > 0 ? tgt[k - 1] : 0;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int k = k0 + q * x.NT;
+            if (k < U) {
+              bad |= (cur[q] < 0 || cur[q] >= V || cur[q] == blank) ? 1 : 0;
+              if (k > 0) rep += cur[q] == prv[q] ? 1 : 0;
+            }
+          }
         }
         bad = __reduce_or_sync(0xffffffffu, bad);
         rep = __reduce_add_sync(0xffffffffu, rep);
