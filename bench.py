@@ -388,6 +388,10 @@ def run_ours(args):
     rank, world, local = rank_info()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    # One process per GPU: its host batches and submitting thread on the
+    # GPU's NUMA node (before any pinned buffer is touched).
+    from fast_forced_aligner_b200.pipeline import bind_host_to_device
+    host_cpus = bind_host_to_device(device) if world > 1 else None
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
@@ -608,7 +612,8 @@ def run_ours(args):
                 "h2d_bytes_per_step": int(e_host.numel() * e_host.element_size() + t_host.numel() * 8),
                 "d2h_bytes_per_step": int(frames * 12 + wl.batch * 8),
                 "api": "fast_forced_aligner_b200.AlignStream.submit (align_packed, the torch op over the "
-                       "C ABI, with host copies overlapped on separate streams)"},
+                       "C ABI, with host copies overlapped on separate streams)",
+                "host_cpus": len(host_cpus) if host_cpus else None},
         "roofline": {"kernel": roofline_kernel,
                      "bound": "hbm", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -13,6 +13,7 @@ host results are pinned tensors from PyTorch's caching host allocator.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -98,3 +99,39 @@ class AlignStream:
         done = torch.cuda.Event()
         done.record(self.copy_out)
         return PendingAlignment(done, HostAlignment(tuple(frames_t.tolist()), labels, scores, status, objective))
+
+
+def parse_cpulist(text: str) -> list[int]:
+    """CPUs of a Linux cpulist string ("0-3,8,10-11")."""
+    cpus: list[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.extend(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def bind_host_to_device(device: torch.device | str | int) -> list[int] | None:
+    """Restrict the calling process to the CPUs of the NUMA node that holds
+    `device`'s PCIe link (Linux sysfs), so that pinned host batches -- placed
+    by the first thread to touch them -- and the thread that submits them sit
+    next to the GPU.  With one process per GPU, host-to-device copies then do
+    not cross the socket link.  Returns the CPUs, or None (and changes
+    nothing) where the node is unknown."""
+    try:
+        props = torch.cuda.get_device_properties(torch.device(device))
+        bdf = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bdf}/numa_node") as f:
+            node = int(f.read())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            allowed = os.sched_getaffinity(0)
+            cpus = [c for c in parse_cpulist(f.read()) if c in allowed]
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return cpus
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None
