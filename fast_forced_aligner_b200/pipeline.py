@@ -133,5 +133,5 @@ def bind_host_to_device(device: torch.device | str | int) -> list[int] | None:
             return None
         os.sched_setaffinity(0, cpus)
         return cpus
-    except (OSError, ValueError, AttributeError, RuntimeError):
+    except (OSError, ValueError, AttributeError, RuntimeError, AssertionError):
         return None
