@@ -731,9 +731,44 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     if (class_row(cls)) c = std::min(c, row_slots);
     return c;
   };
-  int run_pieces = 1;
-  if (nchunked > 0)
-    while (run_pieces < ffa::kMaxRunPieces && runs_model.ctas(run_pieces, slots_per_cta) > sms) ++run_pieces;
+  (void)slots_per_cta;
+  (void)runs_model;
+  // A slot's work per frame, fitted to per-CTA times measured on a B200
+  // (cfg1, CTAs of 4 to 16 slots sharing an SM): about 22.6 + 1.06 K ns per
+  // warp at K states per thread, plus 10.6 ns per slot (its barrier and
+  // boundary exchange) -- in units of about 1.06 ns, nw (21 + K) + 10.
+  auto frame_cost = [](const ffa::RecordDev& d) {
+    return static_cast<int64_t>(d.nw) * (21 + static_cast<int64_t>(d.kst)) + 10;
+  };
+  // Pieces per slot of the chunked route, per (staging, states per thread,
+  // warps) class: as many as make a CTA full of the class's slots (kMaxWarps
+  // warps, or row_slots rings) about one SM's share of the pass's work, so
+  // that the classes' CTAs take about the same time; each piece of a slot
+  // still restarts its relaxed DP.
+  uint8_t run_by[2][2][ffa::kMaxWarps + 1];
+  std::fill_n(&run_by[0][0][0], sizeof(run_by), static_cast<uint8_t>(1));
+  auto run_of = [&](const ffa::RecordDev& d) -> int32_t {
+    return d.num_pieces > 1 ? run_by[d.row_mode ? 1 : 0][d.kst == 16 ? 1 : 0][d.nw] : 1;
+  };
+  auto first_pass = [&](int32_t i) {
+    return 2 * recs[i].U + 1 <= ffa::kMaxStates && !window_record(records[i], windows);
+  };
+  if (nchunked > 0) {
+    int64_t total = 0;
+    for (int64_t i = 0; i < count; ++i)
+      if (first_pass(static_cast<int32_t>(i))) total += recs[i].T * frame_cost(recs[i]);
+    const double share = static_cast<double>(total) / static_cast<double>(sms);
+    for (int row = 0; row < 2; ++row)
+      for (int k16 = 0; k16 < 2; ++k16)
+        for (int nw = 1; nw <= ffa::kMaxWarps; ++nw) {
+          int64_t cap = ffa::kMaxWarps / nw;
+          if (row) cap = std::min(cap, row_slots);
+          const double per_piece = static_cast<double>(cap) * ffa::kPieceFrames *
+                                   static_cast<double>(nw * (21 + (k16 ? 16 : 8)) + 10);
+          run_by[row][k16][nw] = static_cast<uint8_t>(
+              std::clamp<int64_t>(std::llround(share / per_piece), 1, ffa::kMaxRunPieces));
+        }
+  }
 
   // Packing order: records by slot class, longest first; a record's pieces
   // stay together.  Slots of one class form one contiguous run.
@@ -744,21 +779,24 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     uint8_t cls, kst;
   };
   thread_local std::vector<ClassRun> runs;
-  runs.clear();
   auto* order = reinterpret_cast<ffa::SlotRef*>(host + L.slots);
   int64_t n_first = 0;
-  for (int64_t k = 0; k < count; ++k) {
-    const int32_t i = sorted[k];
-    const ffa::RecordDev& d = recs[i];
-    if (2 * d.U + 1 > ffa::kMaxStates) continue;  // long records run on clusters
-    if (window_record(records[i], windows)) continue;  // the window route
-    const int64_t before = n_first;
-    const int32_t step = d.num_pieces > 1 ? run_pieces : 1;
-    for (int32_t j = 0; j < d.num_pieces; j += step) order[n_first++] = ffa::SlotRef{i, j};
-    if (runs.empty() || runs.back().cls != classes[i])
-      runs.push_back(ClassRun{before, 0, classes[i], d.kst});
-    runs.back().slots += n_first - before;
-  }
+  auto build_order = [&]() {
+    runs.clear();
+    n_first = 0;
+    for (int64_t k = 0; k < count; ++k) {
+      const int32_t i = sorted[k];
+      const ffa::RecordDev& d = recs[i];
+      if (!first_pass(i)) continue;  // long records run on clusters; window records on their route
+      const int64_t before = n_first;
+      const int32_t step = run_of(d);
+      for (int32_t j = 0; j < d.num_pieces; j += step) order[n_first++] = ffa::SlotRef{i, j};
+      if (runs.empty() || runs.back().cls != classes[i])
+        runs.push_back(ClassRun{before, 0, classes[i], d.kst});
+      runs.back().slots += n_first - before;
+    }
+  };
+  build_order();
   // Records of the optimized route for the finisher, one launch per group:
   // row-staged before gathered, then by CTA size.  A record's CTA runs its
   // repair jobs in slots side by side, so every record gets a 512-thread CTA
@@ -793,11 +831,12 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // about 1.06 ns, nw (21 + K) + 10 -- times its frames.
   auto slot_cost = [&](int64_t s) -> int64_t {
     const ffa::RecordDev& d = recs[order[s].record];
+    const int32_t m = run_of(d);
     const int64_t first = static_cast<int64_t>(order[s].piece) * ffa::kPieceFrames;
-    const int64_t frames = d.num_pieces > 1 && order[s].piece + run_pieces < d.num_pieces
-                               ? static_cast<int64_t>(run_pieces) * ffa::kPieceFrames
+    const int64_t frames = d.num_pieces > 1 && order[s].piece + m < d.num_pieces
+                               ? static_cast<int64_t>(m) * ffa::kPieceFrames
                                : d.T - first;
-    return (static_cast<int64_t>(d.nw) * (21 + static_cast<int64_t>(d.kst)) + 10) * frames;
+    return frame_cost(d) * frames;
   };
   // Cuts one class run at `budget` (and at kMaxWarps warps and, row-staged,
   // row_slots rings per CTA); emit(first slot, slots) for each CTA.
@@ -824,6 +863,12 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     for (const ClassRun& run : runs) cut(run, budget, [&](int64_t, int64_t) { ++n; });
     return n;
   };
+  // Longer runs while even full CTAs would take more than one wave.
+  for (int grow = 0; grow < ffa::kMaxRunPieces && ctas_for(INT64_MAX) > sms; ++grow) {
+    uint8_t* m = &run_by[0][0][0];
+    for (size_t k = 0; k < sizeof(run_by); ++k) m[k] = static_cast<uint8_t>(std::min<int>(m[k] + 1, ffa::kMaxRunPieces));
+    build_order();
+  }
   int64_t budget = INT64_MAX;  // (when even full CTAs take more than one wave)
   if (ctas_for(budget) <= sms) {
     int64_t total = 0;
@@ -965,7 +1010,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
                            outputs->stitched, outputs->repair_passes, outputs->repaired_frames,
                            outputs->shortcut_stats, outputs->routing_stats, outputs->reuse_stats};
   fp.row_slot_bytes = row_slot_bytes;
-  fp.run_pieces = run_pieces;
+  std::memcpy(fp.run_by, run_by, sizeof(run_by));
   fp.lse = fmt != FFA_INPUT_LOG_PROBS ? reinterpret_cast<const float*>(dev + L.lse) : nullptr;
   fp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
   const auto* dbundles = reinterpret_cast<const ffa::Bundle*>(dev + bundles_off);

@@ -197,7 +197,9 @@ struct ForwardParams {
   int32_t* route;            // per record: kRoute* (the finisher writes it)
   OutputsDev out;
   uint32_t row_slot_bytes;
-  int32_t run_pieces;        // first pass: consecutive pieces per slot of the optimized route
+  // First pass: consecutive pieces per slot of the chunked route, by
+  // [row-staged][16 states per thread][warps] (run_pieces_of).
+  uint8_t run_by[2][2][kMaxWarps + 1];
   int32_t* fill_done;        // per record: fill CTAs finished (zeroed by the first pass)
   int32_t* finish_done;      // per record: finisher CTAs through round 0 (zeroed by the first pass)
   // Round 0's plan in the first pass (set when the optimized route's records

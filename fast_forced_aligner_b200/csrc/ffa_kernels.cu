@@ -667,6 +667,11 @@ __device__ __forceinline__ int finish_group(const RecordDev& rec, bool narrow) {
   return (rec.row_mode ? 0 : 3) + size;
 }
 
+// Pieces per first-pass slot of a record of the chunked route.
+__device__ __forceinline__ int run_pieces_of(const ForwardParams& P, const RecordDev& rec) {
+  return P.run_by[rec.row_mode ? 1 : 0][rec.kst == 16 ? 1 : 0][rec.nw];
+}
+
 // Round 0's plan in the first pass: every slot of a record counts itself out
 // once its pieces' states are written; the last one plans round 0 with its
 // first warp.  A joined record is done here (route and diagnostics; the fill
@@ -677,7 +682,8 @@ __device__ void plan_round0(const SlotCtx& x, const RecordDev& rec, ForwardShare
   x.sync();  // the slot's traces have written its pieces' states
   if (x.tl == 0) {
     __threadfence();
-    const int slots = (rec.num_pieces + P.run_pieces - 1) / P.run_pieces;
+    const int rp = run_pieces_of(P, rec);
+    const int slots = (rec.num_pieces + rp - 1) / rp;
     sh.slot_status[x.slot] = atomicAdd(&P.slot_done[x.r], 1) == slots - 1 ? 1 : 0;
     __threadfence();
   }
@@ -809,7 +815,7 @@ ffa_viterbi_forward(const __grid_constant__ ForwardParams P) {
     }
     if (chunked) {
       // Pieces index .. index+m-1 of the record, back to back.
-      const int m = min(P.run_pieces, rec.num_pieces - pidx);
+      const int m = min(run_pieces_of(P, rec), rec.num_pieces - pidx);
       run.a0 = run.t0 = pfirst;
       run.t1 = pidx + m == rec.num_pieces ? T : pfirst + m * kPieceFrames;
       run.pieces = m;
