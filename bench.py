@@ -261,6 +261,9 @@ def reference_cuda_lane(wl, e_dev, t_dev, steps, warmup, flush):
     from oracle import oracle
     if not oracle.load_reference_cuda():
         return None
+    if (2 * wl.target_lengths + 1 > 4096).any():
+        return {"unavailable": "the reference's align rejects transcripts above 2047 tokens "
+                               "(alignment.cu:684, max_states <= 4096)"}
     es = list(e_dev.split(wl.lengths.tolist()))
     ts = list(t_dev.split(wl.target_lengths.tolist()))
     blanks = [wl.blank] * wl.batch
@@ -633,7 +636,9 @@ def run_ours(args):
                              "ffa_launch_count), in the device-resident and the end-to-end timed loops",
         "status_ok": status_ok,
     }
-    if ref_cuda is not None:
+    if ref_cuda is not None and "unavailable" in ref_cuda:
+        line["reference_cuda"] = ref_cuda
+    elif ref_cuda is not None:
         line["reference_cuda"] = dict(
             ref_cuda, ratio_value=value / ref_cuda[args.mode]["value"],
             ratio_value_vs_optimized=value / ref_cuda["optimized"]["value"],
