@@ -59,6 +59,7 @@ struct Geometry {
   int seg_log2;  // traceback segment length
   int64_t segments;
   int64_t greedy_items;  // greedy pass chunks (greedy_record)
+  int64_t wide_items;    // chunks of the statistics-only pass of the other records (wide_greedy_record)
   int64_t bp_words;
   int64_t map_elems;
   int64_t pieces;
@@ -131,6 +132,13 @@ bool greedy_record(const ffa_record& r, bool optimized) {
   return optimized && r.frames > 0 && 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates && row_staged(r);
 }
 
+// The other records of the optimized mode within the reference's limit (more
+// than 64 columns, or rows that are not staged): the reference counts their
+// greedy chunks too, so a statistics-only pass takes them.
+bool wide_greedy_record(const ffa_record& r, bool optimized) {
+  return optimized && r.frames > 0 && 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates && !row_staged(r);
+}
+
 // Records of the optimized mode solved in pieces: the rest, when long enough.
 bool chunked_record(const ffa_record& r, bool optimized, const WindowPolicy& w) {
   return optimized && !window_record(r, w) && r.frames >= ffa::kPieceMinFrames;
@@ -174,6 +182,7 @@ Geometry geometry(const ffa_record& r, bool optimized, const WindowPolicy& windo
   }
   g.segments = (r.frames + (int64_t{1} << g.seg_log2) - 1) >> g.seg_log2;
   g.greedy_items = greedy_record(r, optimized) ? (r.frames + ffa::kGreedyChunk - 1) / ffa::kGreedyChunk : 0;
+  g.wide_items = wide_greedy_record(r, optimized) ? (r.frames + ffa::kGreedyChunk - 1) / ffa::kGreedyChunk : 0;
   // Backpointer rows, frontiers and maps do not depend on the thread layout.
   const int S32 = static_cast<int>(S);
   g.bp_words = r.frames * ffa::bp_row_words(S32);
@@ -225,12 +234,13 @@ int device_sms() {
 // at their end.
 struct AlignLayout {
   size_t recs, chunked, longs, fill, counters, win_slots, win_ctas, greedy_items, greedy_first, tok_off, greedy_recs,
-      slots, keys,
+      wide_items, slots, keys,
       classes,
       staging_bytes;
   size_t bp, maps, anchors, path_states, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, alphabet,
       lpos, lstart, lse, workspace_bytes;
-  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy, num_greedy_window;
+  int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy, num_greedy_window, num_wide;
+  int wide_max_tokens, wide_max_vocab;  // the largest transcript and row among the wide_greedy_record records
   int format;  // the call's input format
 };
 
@@ -253,7 +263,8 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0, longs = 0, greedy = 0, greedy_window = 0, tokens = 0;
+          pieces = 0, longs = 0, greedy = 0, greedy_window = 0, tokens = 0, wide = 0;
+  int wide_tokens = 0, wide_vocab = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
     if (rc) return rc;
@@ -270,6 +281,11 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
     greedy += g.greedy_items;
     greedy_window += g.window ? g.greedy_items : 0;
     tokens += records[i].tokens;
+    wide += g.wide_items;
+    if (g.wide_items > 0) {
+      wide_tokens = std::max(wide_tokens, records[i].tokens);
+      wide_vocab = std::max(wide_vocab, records[i].vocab);
+    }
   }
   if (segments > INT32_MAX || fill > INT32_MAX || pieces > INT32_MAX)
     return fail(FFA_ERR_UNSUPPORTED, "batch exceeds the traceback segment index range");
@@ -300,6 +316,11 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   L->greedy_recs = off; off = align_up(off + sizeof(int32_t) * count, 16);
   L->num_greedy = greedy;
   L->num_greedy_window = greedy_window;
+  // The statistics-only pass of the other records: its chunks.
+  L->wide_items = off; off = align_up(off + sizeof(ffa::GreedyItem) * wide, 16);
+  L->num_wide = wide;
+  L->wide_max_tokens = wide_tokens;
+  L->wide_max_vocab = wide_vocab;
   L->slots = off; off = align_up(off + (sizeof(ffa::SlotRef) + sizeof(ffa::Bundle)) * pieces + 32, 256);
   const size_t device_part = off;  // the most that is uploaded
   L->keys = off; off = align_up(off + sizeof(int32_t) * count, 16);
@@ -494,6 +515,7 @@ cudaError_t upload_descriptors(void* dst, const void* staging, size_t bytes, cud
 struct SideStream {
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  cudaEvent_t first_pass = nullptr;  // the first pass is done (the statistics-only wide pass waits for it)
 };
 cudaError_t side_stream(SideStream** out) {
   thread_local SideStream sides[64];
@@ -506,6 +528,7 @@ cudaError_t side_stream(SideStream** out) {
     if ((err = cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking)) != cudaSuccess) return err;
     if ((err = cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming)) != cudaSuccess) return err;
     if ((err = cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming)) != cudaSuccess) return err;
+    if ((err = cudaEventCreateWithFlags(&side.first_pass, cudaEventDisableTiming)) != cudaSuccess) return err;
   }
   *out = &side;
   return cudaSuccess;
@@ -639,6 +662,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   auto* gfirst = reinterpret_cast<int32_t*>(host + L.greedy_first);
   auto* tokoff = reinterpret_cast<int32_t*>(host + L.tok_off);
   auto* grecs = reinterpret_cast<int32_t*>(host + L.greedy_recs);
+  auto* witems = reinterpret_cast<ffa::GreedyItem*>(host + L.wide_items);
+  int64_t nwide = 0;
   // Greedy chunks: the window records' from 0, the others' after them.
   int64_t ngreedy = 0, nstats_items = 0, ntok = 0;
   int64_t unchunked_fill = 0;  // records off both optimized routes (the fill launch's own)
@@ -700,6 +725,8 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       for (int64_t k = 0; k < g.greedy_items; ++k)
         gitems[first + k] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
     }
+    for (int64_t k = 0; k < g.wide_items; ++k)
+      witems[nwide++] = ffa::GreedyItem{static_cast<int32_t>(i), static_cast<int32_t>(k)};
     np += g.pieces;
     if (!g.window && !g.chunked) ++unchunked_fill;
     if (!g.window)
@@ -1039,11 +1066,13 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   // (device-written lists) -- on a side stream when the chunked route or the
   // long records have work too.  The greedy pass of the other records
   // (statistics only) follows on the side stream, once the first pass has
-  // taken its SMs.
+  // taken its SMs; that of the records with wider rows runs there after the
+  // first pass, beside the finisher.
   cudaStream_t ws = s;
   SideStream* side = nullptr;
   const bool stats_greedy = !stats_records.empty();
-  const bool forked = (n_wcta > 0 && (nb > 0 || !long_keys.empty())) || stats_greedy;
+  const bool wide_greedy = L.num_wide > 0;
+  const bool forked = (n_wcta > 0 && (nb > 0 || !long_keys.empty())) || stats_greedy || (wide_greedy && n_wcta == 0);
   ffa::GreedyParams gp{};
   gp.recs = fp.recs;
   gp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
@@ -1163,6 +1192,21 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     return e == cudaSuccess ? FFA_OK : cuda_fail(e, "greedy pass launch");
   };
   if (stats_greedy && n_wcta == 0 && (rc = stats_pass(ws))) return rc;
+  // The statistics of the records with wider rows: after the first pass,
+  // which zeroes them (on the side stream beside the finisher when the window
+  // route leaves it free, else after the fill).
+  auto wide_pass = [&](cudaStream_t stream) -> int {
+    ffa::GreedyParams wp = gp;
+    wp.items = reinterpret_cast<const ffa::GreedyItem*>(dev + L.wide_items);
+    wp.count = L.num_wide;
+    const cudaError_t e = ffa::launch_greedy_wide(wp, L.wide_max_tokens, L.wide_max_vocab, fmt, stream);
+    return e == cudaSuccess ? FFA_OK : cuda_fail(e, "greedy statistics launch");
+  };
+  if (wide_greedy && n_wcta == 0) {
+    if ((err = cudaEventRecord(side->first_pass, s)) != cudaSuccess) return cuda_fail(err, "stream fork");
+    if ((err = cudaStreamWaitEvent(ws, side->first_pass, 0)) != cudaSuccess) return cuda_fail(err, "stream fork");
+    if ((rc = wide_pass(ws))) return rc;
+  }
   if ((rc = mark(FFA_PROFILE_FIRST))) return rc;
   // The optimized route's seam plans, repairs and fallback: a CTA per record
   // (the first round spread over up to four while the records leave SMs
@@ -1198,6 +1242,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     if (err != cudaSuccess) return cuda_fail(err, "traceback launch");
   }
   if (stats_greedy && n_wcta > 0 && (rc = stats_pass(s))) return rc;
+  if (wide_greedy && n_wcta > 0 && (rc = wide_pass(s))) return rc;
   if (forked) {
     if ((err = cudaEventRecord(side->join, ws)) != cudaSuccess) return cuda_fail(err, "stream join");
     if ((err = cudaStreamWaitEvent(s, side->join, 0)) != cudaSuccess) return cuda_fail(err, "stream join");

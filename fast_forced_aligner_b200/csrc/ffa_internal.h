@@ -350,6 +350,13 @@ struct GreedyParams {
 // `between` (or null) is recorded on the stream between the two.
 cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cudaStream_t stream,
                           cudaEvent_t between = nullptr);
+// The statistics-only greedy pass of the other records of the optimized mode
+// (more than 64 columns, or gathered rows): a CTA per chunk of `items`
+// (count of them); it reads recs, mask, check_inputs, lse and
+// shortcut_stats, which the first pass has zeroed before it runs.
+// max_tokens, max_vocab: the largest transcript and row among them.
+cudaError_t launch_greedy_wide(const GreedyParams& params, int max_tokens, int max_vocab, int fmt,
+                               cudaStream_t stream);
 
 // One record's slice of a window CTA's dynamic shared memory for K states
 // per lane (a window of 32 K states); offsets in bytes from the slice start

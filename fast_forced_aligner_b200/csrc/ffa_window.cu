@@ -42,7 +42,9 @@
 // conventional DP (ffa_window_fallback in ffa_kernels.cu).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <climits>
 #include <cmath>
 #include <cstdint>
 
@@ -77,10 +79,12 @@ __device__ __forceinline__ double warp_min(double v) {
 // s .. s + r[b-1] among the record's states (a legal CTC walk: the state
 // advances by 0 on a repeated label, by 1 into or out of a blank, by 2
 // between tokens).  Returns kGreedyAccepted, kGreedyMultiple (several
-// placements) or 0.  label_of(s): the label column of state s.
-template <typename LabelOf>
-__device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, int blank, const uint16_t* lpos,
-                              const uint16_t* lstart, LabelOf label_of, int lane) {
+// placements) or 0.  label_of(s): the label column of state s.  Tokens of a
+// label L: tokens.at(j, L) for j in [tokens.begin(L), tokens.end(L)) is a
+// token position u holding L, or -1.
+template <typename LabelOf, typename Tokens>
+__device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, int blank, const Tokens& tokens,
+                              LabelOf label_of, int lane) {
   // r[t] - r[a] by a warp scan of the increments.
   int inc[4], own = 0;
   unsigned chg = 0;
@@ -122,7 +126,10 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
       const int lo = b == T ? max(0, S - 2) : 0, hi = min(hi_start, S - 1);
       matches = hi < lo ? 0 : (hi / 2 - (lo + 1) / 2 + 1);  // even states in [lo, hi]
     } else {
-      for (int j = lstart[ga] + lane; j < lstart[ga + 1]; j += 32) matches += in_range(2 * lpos[j] + 1) ? 1 : 0;
+      for (int j = tokens.begin(ga) + lane; j < tokens.end(ga); j += 32) {
+        const int u = tokens.at(j, ga);
+        matches += u >= 0 && in_range(2 * u + 1) ? 1 : 0;
+      }
       matches = __reduce_add_sync(kFull, matches);
     }
     return matches == 1 ? kGreedyAccepted : (matches > 1 ? kGreedyMultiple : 0);
@@ -140,13 +147,14 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
   const int gc = __shfl_sync(kFull, gcv, lc), rc = __shfl_sync(kFull, rcv, lc);
   const int lb = ga != blank ? ga : gc;
   const int shift = ga != blank ? 1 : 0;  // start = 2u + shift for a token u of label lb
-  const int n1 = lstart[lb + 1];
-  for (int j0 = lstart[lb]; j0 < n1; j0 += 32) {
+  const int n1 = tokens.end(lb);
+  for (int j0 = tokens.begin(lb); j0 < n1; j0 += 32) {
     const int j = j0 + lane;
     int s0 = 0;
     bool cand = false;
-    if (j < n1) {
-      s0 = 2 * lpos[j] + shift;
+    const int u = j < n1 ? tokens.at(j, lb) : -1;
+    if (u >= 0) {
+      s0 = 2 * u + shift;
       cand = in_range(s0) && s0 + rc < S && label_of(s0 + rc) == gc;  // passes the first change
     }
     unsigned cands = __ballot_sync(kFull, cand);
@@ -163,6 +171,29 @@ __device__ int greedy_verdict(const int (&lab)[4], int a, int b, int T, int S, i
   }
   return matches == 1 ? kGreedyAccepted : (matches > 1 ? kGreedyMultiple : 0);
 }
+
+// A record's tokens grouped by label (ffa_greedy_prep's lists).
+struct LabelLists {
+  const uint16_t* lpos;
+  const uint16_t* lstart;
+  __device__ __forceinline__ int begin(int L) const { return lstart[L]; }
+  __device__ __forceinline__ int end(int L) const { return lstart[L + 1]; }
+  __device__ __forceinline__ int at(int j, int) const { return lpos[j]; }
+};
+// A record's tokens as its label columns (cols[u]), scanned for a label.
+struct LabelScan {
+  const int* cols;
+  int U;
+  __device__ __forceinline__ int begin(int) const { return 0; }
+  __device__ __forceinline__ int end(int) const { return U; }
+  __device__ __forceinline__ int at(int j, int L) const { return cols[j] == L ? j : -1; }
+};
+
+// The reference accepts a chunk only if the fp32 sum of its frames' maxima,
+// added in frame order, is finite (alignment.cu:135-138).  With every
+// |maximum| at most kSumSafe the sum of at most kGreedyChunk of them cannot
+// overflow; otherwise it is formed exactly.
+constexpr float kSumSafe = 1.0e36f;
 
 // max with NaN propagated (PTX max.NaN): a NaN anywhere in a reduction shows.
 __device__ __forceinline__ float max_nan(float a, float b) {
@@ -213,18 +244,21 @@ __device__ __forceinline__ GreedyFrame greedy_row32(const float4 (&v4)[8], unsig
   return f;
 }
 
-// Any row of V <= 64 columns, read column by column.
+// Any row of V <= 64 columns, read column by column.  Logits are compared as
+// the emissions they stand for, x - z (rounding may tie two of them), and
+// `best` is then that emission.
 template <int kFmt>
 __device__ __forceinline__ GreedyFrame greedy_row(const typename Input<kFmt>::Elem* row, int V, unsigned alo,
-                                                  unsigned ahi) {
+                                                  unsigned ahi, float z) {
   GreedyFrame f{-INFINITY, 0, 0, false};
   float bn = -INFINITY;
   {
     for (int col = 0; col < V; ++col) {
       const bool in = col < 32 ? ((alo >> col) & 1u) : ((ahi >> (col - 32)) & 1u);
       if (!in) continue;
-      const float v = elem_to_float(row[col]);
+      float v = elem_to_float(row[col]);
       bn = max_nan(bn, v);
+      if constexpr (Input<kFmt>::kLogits) v = __fsub_rn(v, z);
       if (v > f.best) { f.best = v; f.arg = col; f.ties = 1; }
       else if (v == f.best) ++f.ties;
     }
@@ -357,22 +391,22 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
   const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
   const int a = item.chunk * kGreedyChunk, b = min(T, a + kGreedyChunk);
   int lab[4];
-  bool poison = false, positive = false, rejected = false;
-  // Frame t's bound, flags and greedy label from its row's scan.
+  bool poison = false, positive = false, rejected = false, large = false;
+  // z of frame t (logits).
+  auto lse_of = [&](int t) { return In::kLogits ? __ldg(P.lse + rec.out_off + t) : 0.0f; };
+  // Frame t's bound, flags and greedy label from its row's scan (for logits,
+  // greedy_row's maximum is already x - z).
   auto take = [&](int q, const GreedyFrame& f) {
     const int t = a + 4 * lane + q;
     lab[q] = -1;
     if (t >= b) return;
     bool nonfinite = f.nonfinite;
-    float m = f.best;
-    if constexpr (In::kLogits) {
-      const float z = P.lse[rec.out_off + t];
-      m = __fsub_rn(f.best, z);
-      nonfinite |= !isfinite(z);
-    }
+    const float m = f.best;
+    if constexpr (In::kLogits) nonfinite |= !isfinite(lse_of(t));
     P.bound[rec.out_off + t] = m;
     poison |= nonfinite;
     positive |= m > 0.0f;
+    large |= !(fabsf(m) <= kSumSafe);
     const bool ok = f.ties == 1 && isfinite(m);
     rejected |= !ok;
     lab[q] = ok ? f.arg : 0xff;
@@ -393,7 +427,7 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int t = min(a + 4 * lane + q, b - 1);
-      take(q, greedy_row<kFmt>(e + static_cast<int64_t>(t) * V, V, alo, ahi));
+      take(q, greedy_row<kFmt>(e + static_cast<int64_t>(t) * V, V, alo, ahi, lse_of(t)));
     }
   }
   poison = __any_sync(kFull, poison);
@@ -402,8 +436,16 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
   if (!__any_sync(kFull, rejected)) {
     const int64_t* targets = rec.targets;
     auto label_of = [&](int s) { return (s & 1) ? clamp_label(__ldg(targets + (s >> 1)), V) : blank; };
-    verdict = greedy_verdict(lab, a, b, T, S, blank, P.lpos + P.tok_off[r],
-                             P.lstart + static_cast<int64_t>(kGreedyLabels) * r, label_of, lane);
+    const LabelLists lists{P.lpos + P.tok_off[r], P.lstart + static_cast<int64_t>(kGreedyLabels) * r};
+    verdict = greedy_verdict(lab, a, b, T, S, blank, lists, label_of, lane);
+    if (verdict == kGreedyAccepted && __any_sync(kFull, large)) {
+      // The chunk's sum of maxima in frame order (the lanes' bounds above).
+      __syncwarp();
+      float total = 0.0f;
+      if (lane == 0)
+        for (int t = a; t < b; ++t) total = __fadd_rn(total, P.bound[rec.out_off + t]);
+      if (!__shfl_sync(kFull, isfinite(total) ? 1 : 0, 0)) verdict = 0;
+    }
   }
   if (lane == 0) {
     P.verdicts[P.greedy_first[r] + item.chunk] =
@@ -415,6 +457,195 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
       atomicAdd(stats, 1ull);
       atomicAdd(stats + 1, static_cast<unsigned long long>(b - a));
     } else if (alpha != 0 && verdict == kGreedyMultiple) {
+      atomicAdd(stats + 2, 1ull);
+    }
+  }
+}
+
+// The greedy pass of the records whose alphabet a 64-bit mask cannot hold
+// (more than 64 columns, or rows that are not staged): their shortcut
+// statistics only (the window route never takes them).  A CTA per
+// kGreedyChunk-frame chunk, kWideGreedyWarps warps.  Shared memory holds the
+// record's token columns (for the placement search) and its alphabet: the
+// distinct label columns in increasing order, from a bitmap of the row's
+// columns (or, past kWideBitmapWords words, every label column as it comes:
+// a repeated column is the same column, never a tie).  A frame's greedy
+// label is found by 8 lanes, each reading every 8th alphabet column of the
+// frame's row and keeping the largest emission, its column and whether a
+// different column reached it too -- the reference's unique finite maximum
+// over the alphabet (alignment.cu:60-91), NaN never compared greater or
+// equal.  Four frames share a warp's loads, two such groups are in flight
+// (16 loads per lane), and each warp takes 32 frames of the chunk.  Warp 0
+// then applies the verdict (greedy_verdict, finding a label's tokens by
+// scanning the token columns) and the finite-sum rule.  A record of status
+// >= 2 (mask, target checks: alignment.cu:35) runs no chunk.  Its
+// statistics were zeroed by the first pass, which this launch follows.
+constexpr int kWideGreedyWarps = 4;
+constexpr int kWideThreads = 32 * kWideGreedyWarps;
+template <int kFmt>
+__global__ void __launch_bounds__(kWideThreads)
+ffa_greedy_wide(const __grid_constant__ GreedyParams P, int max_tokens, int bitmap_words) {
+  using In = Input<kFmt>;
+  using Elem = typename In::Elem;
+  static_assert(kGreedyChunk == 32 * kWideGreedyWarps, "a warp takes 32 frames of a chunk");
+  extern __shared__ int wide_smem[];
+  int* cols = wide_smem;                  // the U token columns, then the blank
+  int* alph = cols + (max_tokens + 1);    // the alphabet (increasing columns)
+  unsigned* bits = reinterpret_cast<unsigned*>(alph + (max_tokens + 1));  // bitmap_words
+  __shared__ int lab_s[kGreedyChunk];
+  __shared__ float best_s[kGreedyChunk];
+  __shared__ int ok_s[kGreedyChunk];
+  __shared__ int rep_s, scan_s[kWideGreedyWarps];
+  const int tid = static_cast<int>(threadIdx.x), warp = tid >> 5, lane = tid & 31;
+  const GreedyItem item = P.items[blockIdx.x];
+  const int r = item.record;
+  const RecordDev rec = P.recs[r];
+  const int T = rec.T, U = rec.U, V = rec.V, blank = rec.blank;
+  const int S = 2 * U + 1;
+  if (P.mask != nullptr && !P.mask[r]) return;
+  const int words = (V + 31) >> 5;
+  const bool dedup = words <= bitmap_words;
+  if (tid == 0) rep_s = 0;
+  if (dedup)
+    for (int w = tid; w < words; w += kWideThreads) bits[w] = 0;
+  __syncthreads();
+  // Token columns, invalid IDs (status 3), adjacent repeats (status 4).
+  int bad = 0, rep = 0;
+  for (int j = tid; j <= U; j += kWideThreads) {
+    int c = blank;
+    if (j < U) {
+      const int64_t token = __ldg(rec.targets + j);
+      bad |= (token < 0 || token >= V || token == blank) ? 1 : 0;
+      if (j > 0) rep += __ldg(rec.targets + j - 1) == token ? 1 : 0;
+      c = clamp_label(token, V);
+    }
+    cols[j] = c;
+    if (dedup) atomicOr(&bits[c >> 5], 1u << (c & 31));
+  }
+  rep = __reduce_add_sync(kFull, rep);
+  if (lane == 0 && rep != 0) atomicAdd(&rep_s, rep);
+  bad = __syncthreads_or(bad);
+  if (P.check_inputs && (bad != 0 || static_cast<int64_t>(U) + rep_s > T)) return;
+  // The alphabet: thread i compacts bitmap words [i per, (i + 1) per) after
+  // the columns of the words before them (a block scan of their counts).
+  int A = U + 1;
+  const int* cols_in = cols;
+  if (dedup) {
+    const int per = (words + kWideThreads - 1) / kWideThreads;
+    const int w0 = min(words, tid * per), w1 = min(words, w0 + per);
+    int n = 0;
+    for (int w = w0; w < w1; ++w) n += __popc(bits[w]);
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) scan_s[warp] = incl;
+    __syncthreads();
+    int at = incl - n;
+    for (int k = 0; k < warp; ++k) at += scan_s[k];
+    A = 0;
+    for (int k = 0; k < kWideGreedyWarps; ++k) A += scan_s[k];
+    for (int w = w0; w < w1; ++w)
+      for (unsigned m = bits[w]; m != 0; m &= m - 1) alph[at++] = 32 * w + __ffs(m) - 1;
+    __syncthreads();
+    cols_in = alph;
+  }
+
+  const Elem* e = reinterpret_cast<const Elem*>(rec.emissions);
+  const int a = item.chunk * kGreedyChunk, b = min(T, a + kGreedyChunk);
+  const int g = lane >> 3, sub = lane & 7;
+  // Two frames per lane group at a time (offsets f and f + 4 in the chunk);
+  // each batch loads up to 8 alphabet columns of both rows before folding
+  // them in.
+#pragma unroll 1
+  for (int i = 0; i < 8; i += 2) {
+    const int f0 = 32 * warp + 4 * i + g;
+    int fr[2];
+    const Elem* row[2];
+    float z[2], best[2];
+    int arg[2];
+    bool tie[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      fr[h] = f0 + 4 * h;
+      const int t = min(a + fr[h], b - 1);
+      row[h] = e + static_cast<int64_t>(t) * V;
+      z[h] = In::kLogits ? __ldg(P.lse + rec.out_off + t) : 0.0f;
+      best[h] = -INFINITY;
+      arg[h] = INT_MAX;
+      tie[h] = false;
+    }
+    for (int j0 = sub; j0 < A; j0 += 64) {
+      int c[8];
+      float v[2][8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = j0 + 8 * k < A ? cols_in[j0 + 8 * k] : -1;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[h][k] = c[k] >= 0 ? elem_to_float(__ldg(row[h] + c[k])) : -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float x = v[h][k];
+          if constexpr (In::kLogits) x = __fsub_rn(x, z[h]);
+          const bool gt = c[k] >= 0 && x > best[h];
+          const bool eq = c[k] >= 0 && x == best[h] && c[k] != arg[h];
+          tie[h] = gt ? false : (tie[h] || eq);
+          arg[h] = gt ? c[k] : arg[h];
+          best[h] = gt ? x : best[h];
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      // The 8 lanes of the frame combine (a -inf maximum is rejected anyway).
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(kFull, best[h], o);
+        const int oa = __shfl_xor_sync(kFull, arg[h], o);
+        const bool ot = __shfl_xor_sync(kFull, tie[h] ? 1 : 0, o) != 0;
+        const bool gt = ob > best[h], eq = ob == best[h];
+        tie[h] = gt ? ot : (eq ? (tie[h] || ot || oa != arg[h]) : tie[h]);
+        arg[h] = gt ? oa : (eq ? min(arg[h], oa) : arg[h]);
+        best[h] = gt ? ob : best[h];
+      }
+      if (sub == 0 && a + fr[h] < b) {
+        lab_s[fr[h]] = arg[h];
+        best_s[fr[h]] = best[h];
+        ok_s[fr[h]] = !tie[h] && isfinite(best[h]) ? 1 : 0;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  int lab[4];
+  bool ok = true;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int f = 4 * lane + q;
+    lab[q] = a + f < b ? lab_s[f] : -1;
+    ok &= a + f >= b || ok_s[f] != 0;
+  }
+  if (!__all_sync(kFull, ok)) return;
+  auto label_of = [&](int s) { return (s & 1) ? cols[s >> 1] : blank; };
+  int verdict = greedy_verdict(lab, a, b, T, S, blank, LabelScan{cols, U}, label_of, lane);
+  if (verdict == kGreedyAccepted) {
+    // The fp32 sum of the chunk's maxima in frame order must be finite
+    // (alignment.cu:135-138).
+    float total = 0.0f;
+    if (lane == 0)
+      for (int f = 0; f < b - a; ++f) total = __fadd_rn(total, best_s[f]);
+    if (!__shfl_sync(kFull, isfinite(total) ? 1 : 0, 0)) verdict = 0;
+  }
+  if (lane == 0) {
+    unsigned long long* stats = reinterpret_cast<unsigned long long*>(P.shortcut_stats + 3 * r);
+    if (verdict == kGreedyAccepted) {
+      atomicAdd(stats, 1ull);
+      atomicAdd(stats + 1, static_cast<unsigned long long>(b - a));
+    } else if (verdict == kGreedyMultiple) {
       atomicAdd(stats + 2, 1ull);
     }
   }
@@ -884,6 +1115,10 @@ int window_variant(int row_vocab, int fmt) { return fmt == 0 ? (row_vocab == 32 
 using GreedyKernel = void (*)(GreedyParams);
 const GreedyKernel kGreedyKernels[kWindowVariantsDecl] = {
     ffa_greedy_pass<0, 32>, ffa_greedy_pass<0, 0>, ffa_greedy_pass<1, 0>, ffa_greedy_pass<2, 0>};
+using WideGreedyKernel = void (*)(GreedyParams, int, int);
+const WideGreedyKernel kWideGreedyKernels[3] = {ffa_greedy_wide<0>, ffa_greedy_wide<1>, ffa_greedy_wide<2>};
+// Alphabet bitmaps of rows up to 65,536 columns (8 KiB of shared memory).
+constexpr int kWideBitmapWords = 2048;
 using WindowKernel = void (*)(WindowParams);
 const WindowKernel kWindowKernels[kWindowVariantsDecl] = {
     ffa_window_viterbi<0, 32>, ffa_window_viterbi<0, 0>, ffa_window_viterbi<1, 0>, ffa_window_viterbi<2, 0>};
@@ -923,6 +1158,19 @@ cudaError_t launch_greedy(const GreedyParams& params, int row_vocab, int fmt, cu
   kGreedyKernels[window_variant(row_vocab, fmt)]<<<static_cast<unsigned>((params.count + kGreedyWarps - 1) /
                                                                          kGreedyWarps),
                                                    32 * kGreedyWarps, 0, stream>>>(params);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_greedy_wide(const GreedyParams& params, int max_tokens, int max_vocab, int fmt,
+                               cudaStream_t stream) {
+  if (params.count <= 0) return cudaSuccess;
+  if (fmt < 0 || fmt > 2 || max_tokens < 0 || 2 * max_tokens + 1 > kMaxStates || max_vocab < 1)
+    return cudaErrorInvalidValue;
+  const int words = std::min((max_vocab + 31) / 32, kWideBitmapWords);
+  const size_t smem = sizeof(int) * 2 * (static_cast<size_t>(max_tokens) + 1) + sizeof(unsigned) * words;
+  count_launch();
+  kWideGreedyKernels[fmt]<<<static_cast<unsigned>(params.count), kWideThreads, smem, stream>>>(params, max_tokens,
+                                                                                                words);
   return cudaGetLastError();
 }
 

@@ -72,7 +72,7 @@ def batch_fields(b):
     return {
         "labels": b.labels, "scores": b.scores, "status": b.status, "objective": b.objective,
         "stitched": b.stitched, "repair_passes": b.repair_passes, "repaired_frames": b.repaired_frames,
-        "routing_stats": b.routing_stats, "reuse_stats": b.reuse_stats,
+        "routing_stats": b.routing_stats, "reuse_stats": b.reuse_stats, "shortcut_stats": b.shortcut_stats,
     }
 
 

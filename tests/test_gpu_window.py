@@ -189,7 +189,7 @@ def test_matches_the_references_greedy_counts(cuda, route):
     # numbers (the chunked route runs the greedy pass for them alone).
     if not oracle.load_reference_cuda():
         pytest.skip("reference CUDA extension not built under oracle/_ref")
-    for index in (0, 1):
+    for index in (0, 1, 3):  # cfg3: 1,025 columns (the statistics-only wide pass)
         wl = workloads.config(index)
         es, ts = cuda_records(*wl.records())
         tensors, _ = oracle.reference_cuda_align(es, ts, [wl.blank] * wl.batch, mode="optimized")
@@ -198,7 +198,7 @@ def test_matches_the_references_greedy_counts(cuda, route):
 
 
 @pytest.mark.parametrize("route", ["pieces", "auto"])
-@pytest.mark.parametrize("index, scale", [(0, 1.0), (1, 1.0), (4, 0.12)])
+@pytest.mark.parametrize("index, scale", [(0, 1.0), (1, 1.0), (4, 0.12), (3, 0.25)])
 def test_chunked_route_counts_greedy_chunks(cuda, route, index, scale):
     # Records off the window route (pieces, short records, mixed batches)
     # carry the greedy statistics of the oracle's greedy_shortcuts
@@ -211,12 +211,15 @@ def test_chunked_route_counts_greedy_chunks(cuda, route, index, scale):
     assert int(result.shortcut_stats[:, 0].sum()) > 0
 
 
-def test_greedy_counts_skip_rejected_records(cuda):
+@pytest.mark.parametrize("V", [32, 30, 1025])
+def test_greedy_counts_skip_rejected_records(cuda, V):
     # A record of status >= 2 runs no greedy chunk (alignment.cu:35): masked,
     # invalid IDs, too few frames -- on both routes, beside valid records
-    # whose counts are unchanged.
+    # whose counts are unchanged.  V = 30 rows are gathered (not 16-byte
+    # multiples) and V = 1025 exceeds the 64-bit alphabet mask: the
+    # statistics-only wide pass counts those.
     rng = np.random.default_rng(5)
-    T, V = 700, 32
+    T = 700
     good = torch.randn(T, V, device=cuda).log_softmax(-1)
     path = torch.from_numpy(rng.integers(1, V, 120)).to(cuda)
     strong = good.clone()
@@ -224,7 +227,7 @@ def test_greedy_counts_skip_rejected_records(cuda):
     strong = strong.log_softmax(-1)
     short = strong[:100].contiguous()
     ems = [strong, strong, strong, short]
-    tgts = [path, torch.tensor([1, 40, 2], device=cuda), path, path]
+    tgts = [path, torch.tensor([1, V + 8, 2], device=cuda), path, path]  # an ID past the row
     mask = torch.tensor([True, True, False, True], device=cuda)
     for route in ("pieces", "window"):
         result = ffa.align(ems, tgts, mode="optimized", route=route, emission_validity=mask)
@@ -233,3 +236,68 @@ def test_greedy_counts_skip_rejected_records(cuda):
         expected = oracle.greedy_chunk_stats(strong.cpu().numpy(), path.cpu().numpy(), 0)
         np.testing.assert_array_equal(result.shortcut_stats[0].cpu().numpy(), expected)
         assert expected[0] > 0
+
+
+@pytest.mark.parametrize("V", [30, 33, 129])
+def test_gathered_vocabularies_count_greedy_chunks(cuda, V):
+    # Records whose rows are gathered (V * 4 not a multiple of 16, or more
+    # than 64 columns), with repeated tokens, random blanks and lengths at
+    # the chunk boundaries: the oracle's counts, every route.
+    rng = np.random.default_rng(V)
+    es, ts, blanks = [], [], []
+    for T in [1, 2, 127, 128, 129, 255, 256, 257, 700, 1500]:
+        blank = int(rng.integers(0, V))
+        choices = np.array([c for c in range(V) if c != blank])
+        U = int(rng.integers(0, T // 3 + 1))
+        tokens = rng.choice(choices[:6], U) if rng.random() < 0.3 else rng.choice(choices, U)
+        x = rng.standard_normal((T, V)).astype(np.float32)
+        if U:
+            idx = np.sort(rng.choice(T, min(T, U), replace=False))
+            x[idx, tokens[:idx.size]] += 8.0
+        x[:, blank] += 3.0
+        es.append(torch.from_numpy(x).log_softmax(-1).numpy())
+        ts.append(tokens.astype(np.int64))
+        blanks.append(blank)
+    d_es, d_ts = cuda_records(es, ts)
+    expected = greedy_counts(es, ts, blanks)
+    assert expected[:, 0].sum() > 0
+    for route in ("pieces", "window", "auto"):
+        result = ffa.align(d_es, d_ts, blank_id=blanks, mode="optimized", route=route)
+        np.testing.assert_array_equal(result.shortcut_stats.cpu().numpy(), expected, err_msg=route)
+    conventional = ffa.align(d_es, d_ts, blank_id=blanks, mode="conventional")
+    assert conventional.shortcut_stats.count_nonzero() == 0  # the reference counts none there
+
+
+@pytest.mark.parametrize("V", [32, 1025])
+def test_greedy_ties_of_normalised_logits(cuda, V):
+    # Logits are aligned as x - z.  Two columns that differ by one ulp as
+    # logits, where z is large, round to the same emission: a tie, which
+    # rejects the chunk as it does on the materialised log_softmax.  At one
+    # label change per 128-frame chunk, the next label's column is set one ulp
+    # above the current one's (raw, the greedy label would just change a frame
+    # early).
+    rng = np.random.default_rng(V + 1)
+    T, U, blank = 1024, 160, 0
+    far = V - 1  # a column no label uses; it makes z about 1000
+    tokens = rng.integers(1, far, U)
+    tokens[1:][tokens[1:] == tokens[:-1]] = far - 1
+    path = np.repeat(np.arange(U), T // U + 1)[:T]
+    x = rng.standard_normal((T, V)).astype(np.float32)
+    x[np.arange(T), tokens[path]] += 8.0
+    x[:, far] = 1000.0
+    changes = [t for t in range(T - 1) if path[t] != path[t + 1]]
+    planted = [next(t for t in changes if t >= c) for c in range(0, T - 128, 128)]
+    for t in planted:
+        cur, nxt = tokens[path[t]], tokens[path[t + 1]]
+        x[t, nxt] = np.nextafter(x[t, cur], np.float32(np.inf))
+    logits = torch.from_numpy(x).to(cuda)
+    target = torch.from_numpy(tokens.astype(np.int64)).to(cuda)
+    fused = ffa.align([logits], [target], blank_id=blank, mode="optimized", from_logits=True)
+    emissions = ffa.log_softmax([logits])
+    plain = ffa.align(emissions, [target], blank_id=blank, mode="optimized")
+    e = emissions[0].cpu().numpy()
+    ties = sum(int(e[t, tokens[path[t]]] == e[t, tokens[path[t + 1]]]) for t in planted)
+    assert ties > 0  # the planted pairs collide after the subtraction
+    expected = oracle.greedy_chunk_stats(e, tokens, blank)
+    np.testing.assert_array_equal(plain.shortcut_stats[0].cpu().numpy(), expected)
+    np.testing.assert_array_equal(fused.shortcut_stats[0].cpu().numpy(), expected)
