@@ -130,9 +130,8 @@ typedef struct ffa_record {
  * (reference AlignmentBatch fields, alignment.py:138-148).  Diagnostics in
  * optimized mode: shortcut_stats holds the reference's greedy chunk counts
  * (accepted 128-frame chunks, their frames, chunks with several placements)
- * for every record whose rows can be TMA-staged (vocab <= 64) with at most
- * 4096 states, on either route, and 0 for the others and for records of
- * status >= 2; stitched, repair_passes, repaired_frames and reuse_stats count
+ * for every record with at most 4096 states, on either route, and 0 for the
+ * others and for records of status >= 2; stitched, repair_passes, repaired_frames and reuse_stats count
  * the chunked route's joins and repairs (0 on the window route); the routing
  * state routing_stats[i, 0] is 2 when a window-route record ran the full DP as
  * fallback (the reference's completed early fallback), else 0.  When a call
