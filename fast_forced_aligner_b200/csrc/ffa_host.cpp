@@ -238,7 +238,7 @@ struct AlignLayout {
       classes,
       staging_bytes;
   size_t bp, maps, anchors, path_states, frontiers, pstates, route, fill_done, finish_done, fallback, bound, verdicts, alphabet,
-      lpos, lstart, lse, workspace_bytes;
+      lpos, lstart, lse, win_codes, workspace_bytes;
   int64_t total_frames, num_pieces, num_chunked, num_long, fill_items, num_greedy, num_greedy_window, num_wide;
   int wide_max_tokens, wide_max_vocab;  // the largest transcript and row among the wide_greedy_record records
   int format;  // the call's input format
@@ -344,6 +344,10 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   L->lstart = off; off = align_up(off + (greedy ? sizeof(uint16_t) * ffa::kGreedyLabels * count : 0), 256);
   // Logits: each frame's row log-sum-exp.
   L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
+  // The window route's backpointer codes (ffa::win_codes_offset): 32 B per
+  // frame plus 256 B per record, when the call has window records.
+  L->win_codes = off;
+  off = align_up(off + (greedy_window > 0 ? sizeof(uint32_t) * static_cast<size_t>(8 * (frames + 8 * count)) : 0), 256);
   L->workspace_bytes = off;
   return FFA_OK;
 }
@@ -1113,6 +1117,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     wp.out = fp.out;
     wp.lse = fp.lse;
     wp.bound = gp.bound;
+    wp.codes = reinterpret_cast<uint32_t*>(dev + L.win_codes);
     wp.verdicts = gp.verdicts;
     wp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
     // Tier lists: the 64-state window hands records to the 128-state one

@@ -360,9 +360,11 @@ cudaError_t launch_greedy_wide(const GreedyParams& params, int max_tokens, int m
 
 // One record's slice of a window CTA's dynamic shared memory for K states
 // per lane (a window of 32 K states); offsets in bytes from the slice start
-// (the host sizes CTAs with the same function).
+// (the host sizes CTAs with the same function).  The window's backpointer
+// codes are not in the slice: they go to global memory (win_codes_offset),
+// which keeps the slice small enough for more records per SM.
 struct WinLayout {
-  uint32_t ring, tok, bp, gb, map, anc, stash, path, bytes;
+  uint32_t ring, tok, gb, map, anc, stash, path, bytes;
 };
 __host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, int K) {
   auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
@@ -371,7 +373,6 @@ __host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, 
   uint32_t off = 0;
   w.ring = off;   off = up(off + static_cast<uint32_t>(kWinRing * kWinChunk * V * esize), 128);
   w.tok = off;    off = up(off + static_cast<uint32_t>(U) + 1, 16);  // label column of each token
-  w.bp = off;     off = up(off + groups * 32 * 4 * static_cast<uint32_t>(K / 2), 16);  // per 8 frames: K/2 words a lane
   w.gb = off;     off = up(off + groups * 2, 16);        // window base per 8 frames
   w.map = off;    off = up(off + segs * 32 * static_cast<uint32_t>(K) * 2, 16);  // per segment: each state's ancestor
   w.anc = off;    off = up(off + segs * 2, 16);          // path state at each segment end
@@ -379,6 +380,14 @@ __host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, 
   w.path = off;   off = up(off + static_cast<uint32_t>(T) * 2, 128);  // path state per frame
   w.bytes = off;
   return w;
+}
+// First word of record r's window codes in WindowParams::codes: each
+// 8-frame group of the window holds K/2 words a lane (32 lanes), at most 64
+// words (K = 4, the 128-state tier), so a record takes at most
+// 8 (T + 7) words; 8 words per frame of the call plus 64 per record cover
+// every record (out_off: the record's first frame).
+__host__ __device__ inline int64_t win_codes_offset(int64_t out_off, int r) {
+  return 8 * (out_off + 8 * static_cast<int64_t>(r));
 }
 struct WinSlot {
   int32_t record;
@@ -397,6 +406,7 @@ struct WindowParams {
   OutputsDev out;
   const float* lse;           // as ForwardParams::lse
   const float* bound;         // the greedy pass's m[t] (GreedyParams::bound)
+  uint32_t* codes;            // the windows' backpointer codes (win_codes_offset)
   const uint8_t* verdicts;    // the greedy pass's chunk verdicts
   const int32_t* greedy_first;  // per record: its first greedy item
   int32_t* fallback_list;     // records handed to the next tier

@@ -211,39 +211,6 @@ struct GreedyFrame {
   int arg, ties;
   bool nonfinite;
 };
-// A 32-column fp32 row already in registers.
-__device__ __forceinline__ GreedyFrame greedy_row32(const float4 (&v4)[8], unsigned alo) {
-  GreedyFrame f{-INFINITY, 0, 0, false};
-  float bn = -INFINITY;
-  {
-    float xs[32];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      xs[4 * k] = v4[k].x; xs[4 * k + 1] = v4[k].y; xs[4 * k + 2] = v4[k].z; xs[4 * k + 3] = v4[k].w;
-    }
-    float bf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    float bq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const float v = ((alo >> k) & 1u) ? xs[k] : -INFINITY;
-      bf[k & 3] = fmaxf(bf[k & 3], v);
-      bq[k & 3] = max_nan(bq[k & 3], v);
-    }
-    f.best = fmaxf(fmaxf(bf[0], bf[1]), fmaxf(bf[2], bf[3]));
-    bn = max_nan(max_nan(bq[0], bq[1]), max_nan(bq[2], bq[3]));
-    int tq[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const bool hit = ((alo >> k) & 1u) && xs[k] == f.best;
-      tq[k & 3] += hit ? 1 : 0;
-      f.arg = hit ? k : f.arg;
-    }
-    f.ties = tq[0] + tq[1] + tq[2] + tq[3];
-  }
-  f.nonfinite = !(bn < INFINITY);
-  return f;
-}
-
 // Any row of V <= 64 columns, read column by column.  Logits are compared as
 // the emissions they stand for, x - z (rounding may tie two of them), and
 // `best` is then that emission.
@@ -412,16 +379,65 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
     lab[q] = ok ? f.arg : 0xff;
   };
   if constexpr (kV == 32 && kFmt == 0) {
-    // A row's eight 16-byte loads in flight at a time (streamed: read once);
-    // few registers keep many warps resident, which covers the latency.
+    // The chunk's rows are contiguous (128 B each), so one load instruction
+    // of the warp reads four whole rows, 512 bytes: load k of batch n gives
+    // lane l the columns 4 (l & 7) .. 4 (l & 7) + 3 of frame
+    // a + 4 (8 n + k) + (l >> 3).  Each group of 8 lanes reduces its frame:
+    // the largest alphabet emission by shuffles, the alphabet columns that
+    // equal it and any NaN or +inf column by ballots.  The group's first
+    // lane leaves the frame's result in shared memory for the lane that owns
+    // the frame (lane j: frames a + 4 j .. a + 4 j + 3).  Eight loads (4 KB)
+    // are in flight per warp; streamed, the rows are read once.
+    __shared__ float best_s[kGreedyWarps][kGreedyChunk];
+    __shared__ uint16_t info_s[kGreedyWarps][kGreedyChunk];  // column | ties << 5 | nonfinite << 8
+    const int g = lane >> 3, c4 = lane & 7;
+    const unsigned m4 = (alo >> (4 * c4)) & 0xfu;
+    const float4* rows = reinterpret_cast<const float4*>(e);
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
-      float4 v4[8];
-      const int t = min(a + 4 * lane + q, b - 1);
-      const float4* row = reinterpret_cast<const float4*>(e + static_cast<int64_t>(t) * 32);
+    for (int n = 0; n < kGreedyChunk / 32; ++n) {
+      float4 v[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v4[k] = __ldcs(row + k);
-      take(q, greedy_row32(v4, alo));
+      for (int k = 0; k < 8; ++k) {
+        const int t = min(a + 4 * (8 * n + k) + g, b - 1);
+        v[k] = __ldcs(rows + static_cast<int64_t>(t) * 8 + c4);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float x[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        float best = -INFINITY, bn = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float y = ((m4 >> j) & 1u) ? x[j] : -INFINITY;
+          best = fmaxf(best, y);
+          bn = max_nan(bn, y);
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(kFull, best, o));
+        const unsigned nf = __ballot_sync(kFull, !(bn < INFINITY));
+        unsigned hits[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hits[j] = __ballot_sync(kFull, ((m4 >> j) & 1u) && x[j] == best);
+        if (c4 == 0) {
+          int ties = 0, arg = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const unsigned h = (hits[j] >> (8 * g)) & 0xffu;
+            ties += __popc(h);
+            if (h != 0) arg = 4 * (__ffs(h) - 1) + j;  // the column when it is the only one
+          }
+          const int f = 4 * (8 * n + k) + g;
+          best_s[warp][f] = best;
+          info_s[warp][f] = static_cast<uint16_t>(arg | min(ties, 7) << 5 | (((nf >> (8 * g)) & 0xffu) != 0 ? 256 : 0));
+        }
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int f = 4 * lane + q;
+      const unsigned info = info_s[warp][f];
+      take(q, GreedyFrame{best_s[warp][f], static_cast<int>(info & 31u), static_cast<int>((info >> 5) & 7u),
+                          (info & 256u) != 0});
     }
   } else {
 #pragma unroll
@@ -740,7 +756,9 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
   const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)), K);
   Elem* ring = reinterpret_cast<Elem*>(sm + L.ring);
   uint8_t* tok = sm + L.tok;
-  uint32_t* bp = reinterpret_cast<uint32_t*>(sm + L.bp);
+  // Backpointer codes of the window: global memory, written once per 8-frame
+  // group (128 B a word per lane, coalesced), read back by the traceback.
+  uint32_t* bp = P.codes + win_codes_offset(rec.out_off, r);
   uint16_t* gb = reinterpret_cast<uint16_t*>(sm + L.gb);
   uint16_t* map = reinterpret_cast<uint16_t*>(sm + L.map);
   int16_t* anc = reinterpret_cast<int16_t*>(sm + L.anc);
@@ -927,7 +945,7 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
         }
       }
 #pragma unroll
-      for (int q = 0; q < kWords; ++q) bp[((tg >> 3) * kWords + q) * 32 + lane] = w[q];
+      for (int q = 0; q < kWords; ++q) __stcg(bp + ((tg >> 3) * kWords + q) * 32 + lane, w[q]);
       const int tl = min(tg + 8, T) - 1;
       if ((tl & (kWinChunk - 1)) == kWinChunk - 1 || tl == T - 1) {
         // Segment map: each window state's path state at the frame before
@@ -1039,9 +1057,18 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
     }
   }
   __syncwarp();
-  // Lane j walks segments j, j + 32, ... back from their anchors
-  // (path[t-1] = path[t] - jump(t, path[t]), alignment.cu:656-659).
-  for (int g = lane; g < nseg; g += 32) {
+  // Segment g walks back from its anchor (path[t-1] = path[t] - jump(t,
+  // path[t]), alignment.cu:656-659).  Its codes are first brought from
+  // global memory into the emission ring, free now, a batch of segments at a
+  // time (independent 16-byte loads), so that each step of the walks is a
+  // shared-memory read; with a ring too small for one segment's codes (a
+  // vocabulary of a few columns) the walks read global memory.
+  constexpr int kSegWords = (kWinChunk / 8) * kWords * 32;  // one segment's codes
+  const int total_words = ((T + 7) >> 3) * kWords * 32;
+  const int ring_words = kWinRing * kWinChunk * V * static_cast<int>(sizeof(Elem)) / 4;
+  const int per_batch = min(32, ring_words / kSegWords);
+  uint32_t* stage = reinterpret_cast<uint32_t*>(ring);
+  auto walk = [&](int g, const uint32_t* codes, int first_word) {
     const int t_lo = g * kWinChunk;
     const int t_hi = min(T, t_lo + kWinChunk) - 1;
     int s = anc[g];
@@ -1049,10 +1076,24 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
     for (int t = t_hi; t > t_lo; --t) {
       const int k = min(max(s - static_cast<int>(gb[t >> 3]), 0), W - 1);
       const int j = t & 7;
-      const uint32_t word = bp[((t >> 3) * kWords + j / kFramesPerWord) * 32 + k / K];
+      const int at = ((t >> 3) * kWords + j / kFramesPerWord) * 32 + k / K - first_word;
+      const uint32_t word = codes == bp ? __ldcg(codes + at) : codes[at];
       s -= static_cast<int>((word >> (2 * K * (j % kFramesPerWord) + 2 * (k % K))) & 3u);
       path[t - 1] = static_cast<uint16_t>(s);
     }
+  };
+  if (per_batch >= 1) {
+    for (int g0 = 0; g0 < nseg; g0 += per_batch) {
+      const int w0 = g0 * kSegWords;
+      const int w1 = min(total_words, (g0 + per_batch) * kSegWords);
+      for (int i = 4 * lane; i < w1 - w0; i += 128)
+        *reinterpret_cast<uint4*>(stage + i) = __ldcg(reinterpret_cast<const uint4*>(bp + w0 + i));
+      __syncwarp();
+      if (lane < per_batch && g0 + lane < nseg) walk(g0 + lane, stage, w0);
+      __syncwarp();
+    }
+  } else {
+    for (int g = lane; g < nseg; g += 32) walk(g, bp, 0);
   }
   __syncwarp();
   // Labels and the selected scores (alignment.cu:662-666), frame-coalesced.
