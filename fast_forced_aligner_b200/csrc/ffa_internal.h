@@ -300,7 +300,7 @@ cudaError_t launch_upload(const void* mapped_src, void* dst, size_t bytes, cudaS
 // window DP made every decision of the full DP along its path and returned
 // its exact outputs (certified).  Otherwise the record runs the full
 // conventional DP (ffa_window_fallback).
-constexpr int kWinWarps = 8;          // records (warps) per CTA at most
+constexpr int kWinWarps = 12;         // records (warps) per CTA at most (two CTAs share an SM)
 constexpr int kWinStates = 64;        // window width: 32 lanes x 2 states
 constexpr int kWinSlide = 16;         // states a slide moves the window by
 constexpr int kWinHigh = 32;          // slide when the best state sits this far up (4 frames before)

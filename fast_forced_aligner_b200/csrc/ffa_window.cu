@@ -1117,7 +1117,7 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
 // The 64-state window: one warp per record of the call's window route, the
 // CTA's records listed by the host.
 template <int kFmt, int kV>
-__global__ void __launch_bounds__(32 * kWinWarps, 1)
+__global__ void __launch_bounds__(32 * kWinWarps, 2)
 ffa_window_viterbi(const __grid_constant__ WindowParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ unsigned long long bars[kWinWarps][kWinRing];
