@@ -106,6 +106,8 @@ struct WindowPolicy {
 };
 constexpr int64_t kWinAutoRecordsPerSm = 4;
 constexpr int64_t kWinAutoMaxFrames = 2048;
+// Window records per SM up to which their codes stay in shared memory.
+constexpr int64_t kWinSmemCodesSpread = 8;
 
 bool window_shape(const ffa_record& r, int64_t max_frames) {
   return 2 * static_cast<int64_t>(r.tokens) + 1 <= ffa::kMaxStates && r.frames <= max_frames && row_staged(r);
@@ -966,6 +968,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
   int64_t n_wcta = 0;
   uint32_t win_smem = 0, wide_smem = 0;
   int win_vocab = -1;
+  bool win_smem_codes = false;
   if (!win_records.empty()) {
     const int64_t nwin = static_cast<int64_t>(win_records.size());
     thread_local std::vector<int32_t> bucket_start;
@@ -975,7 +978,14 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     for (int b = 0; b < kLengthBuckets; ++b) bucket_start[b + 1] += bucket_start[b];
     auto* sorted_win = reinterpret_cast<int32_t*>(host + L.keys);  // the first pass is done with the keys
     for (int32_t i : win_records) sorted_win[bucket_start[bucket(i)]++] = i;
-    const int64_t per_cta = std::clamp<int64_t>((nwin + sms - 1) / sms, 1, ffa::kWinWarps);
+    // Spread over the SMs, at most kWinSmemCodesSpread records each: the
+    // batch is latency-bound and fits the SMs at once with the codes in the
+    // slices, where the traceback walks them fastest.  More records per SM:
+    // the codes go to global memory and the smaller slices let up to
+    // kWinWarps records share a CTA.
+    const int64_t spread = (nwin + sms - 1) / sms;
+    win_smem_codes = spread <= kWinSmemCodesSpread;
+    const int64_t per_cta = std::clamp<int64_t>(spread, 1, win_smem_codes ? kWinSmemCodesSpread : ffa::kWinWarps);
     // Two CTAs share an SM when each stays under half the budget: twice the
     // warps to cover each warp's per-frame dependency chain.  A record larger
     // than that gets a CTA of its own.
@@ -985,9 +995,9 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
       const int32_t i = sorted_win[k];
       const ffa::RecordDev& d = recs[i];
       win_vocab = (win_vocab < 0 || win_vocab == d.V) ? d.V : 0;
-      const uint32_t need = ffa::win_layout(d.T, d.U, d.V, static_cast<int>(esize), 2).bytes;
+      const uint32_t need = ffa::win_layout(d.T, d.U, d.V, static_cast<int>(esize), 2, win_smem_codes).bytes;
       wide_smem = std::max(wide_smem, ffa::win_layout(std::min(d.T, ffa::kWinWideMaxFrames), d.U, d.V,
-                                                      static_cast<int>(esize), 4).bytes);
+                                                      static_cast<int>(esize), 4, win_smem_codes).bytes);
       if (n_wcta == 0 || wctas[n_wcta - 1].count == per_cta || cur + need > budget) {
         wctas[n_wcta++] = ffa::WinCta{static_cast<int32_t>(k), 0};
         cur = 0;
@@ -1118,6 +1128,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     wp.lse = fp.lse;
     wp.bound = gp.bound;
     wp.codes = reinterpret_cast<uint32_t*>(dev + L.win_codes);
+    wp.smem_codes = win_smem_codes ? 1 : 0;
     wp.verdicts = gp.verdicts;
     wp.greedy_first = reinterpret_cast<const int32_t*>(dev + L.greedy_first);
     // Tier lists: the 64-state window hands records to the 128-state one

@@ -361,18 +361,21 @@ cudaError_t launch_greedy_wide(const GreedyParams& params, int max_tokens, int m
 // One record's slice of a window CTA's dynamic shared memory for K states
 // per lane (a window of 32 K states); offsets in bytes from the slice start
 // (the host sizes CTAs with the same function).  The window's backpointer
-// codes are not in the slice: they go to global memory (win_codes_offset),
-// which keeps the slice small enough for more records per SM.
+// codes are in the slice when smem_codes is set (a batch whose window
+// records all fit the SMs at once: the traceback then walks shared memory),
+// else in global memory (win_codes_offset), which keeps the slice small
+// enough for more records per SM.
 struct WinLayout {
-  uint32_t ring, tok, gb, map, anc, stash, path, bytes;
+  uint32_t ring, tok, bp, gb, map, anc, stash, path, bytes;
 };
-__host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, int K) {
+__host__ __device__ inline WinLayout win_layout(int T, int U, int V, int esize, int K, bool smem_codes) {
   auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
   const uint32_t groups = static_cast<uint32_t>((T + 7) / 8), segs = static_cast<uint32_t>((T + 31) / 32);
   WinLayout w{};
   uint32_t off = 0;
   w.ring = off;   off = up(off + static_cast<uint32_t>(kWinRing * kWinChunk * V * esize), 128);
   w.tok = off;    off = up(off + static_cast<uint32_t>(U) + 1, 16);  // label column of each token
+  w.bp = off;     off = up(off + (smem_codes ? groups * 32 * 4 * static_cast<uint32_t>(K / 2) : 0), 16);  // per 8 frames: K/2 words a lane
   w.gb = off;     off = up(off + groups * 2, 16);        // window base per 8 frames
   w.map = off;    off = up(off + segs * 32 * static_cast<uint32_t>(K) * 2, 16);  // per segment: each state's ancestor
   w.anc = off;    off = up(off + segs * 2, 16);          // path state at each segment end
@@ -406,7 +409,8 @@ struct WindowParams {
   OutputsDev out;
   const float* lse;           // as ForwardParams::lse
   const float* bound;         // the greedy pass's m[t] (GreedyParams::bound)
-  uint32_t* codes;            // the windows' backpointer codes (win_codes_offset)
+  uint32_t* codes;            // the windows' backpointer codes (win_codes_offset), unless smem_codes
+  int32_t smem_codes;         // codes in each record's shared-memory slice (win_layout)
   const uint8_t* verdicts;    // the greedy pass's chunk verdicts
   const int32_t* greedy_first;  // per record: its first greedy item
   int32_t* fallback_list;     // records handed to the next tier

@@ -753,12 +753,14 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
   const int T = rec.T, U = rec.U, blank = rec.blank;
   const int V = kV > 0 ? kV : rec.V;
   const int S = 2 * U + 1;
-  const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)), K);
+  const bool smem_codes = P.smem_codes != 0;
+  const WinLayout L = win_layout(T, U, V, static_cast<int>(sizeof(Elem)), K, smem_codes);
   Elem* ring = reinterpret_cast<Elem*>(sm + L.ring);
   uint8_t* tok = sm + L.tok;
-  // Backpointer codes of the window: global memory, written once per 8-frame
-  // group (128 B a word per lane, coalesced), read back by the traceback.
-  uint32_t* bp = P.codes + win_codes_offset(rec.out_off, r);
+  // Backpointer codes of the window, written once per 8-frame group (a word
+  // per lane), read back by the traceback: in the slice, or in global memory
+  // (coalesced 128-byte stores).
+  uint32_t* bp = smem_codes ? reinterpret_cast<uint32_t*>(sm + L.bp) : P.codes + win_codes_offset(rec.out_off, r);
   uint16_t* gb = reinterpret_cast<uint16_t*>(sm + L.gb);
   uint16_t* map = reinterpret_cast<uint16_t*>(sm + L.map);
   int16_t* anc = reinterpret_cast<int16_t*>(sm + L.anc);
@@ -945,7 +947,11 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
         }
       }
 #pragma unroll
-      for (int q = 0; q < kWords; ++q) __stcg(bp + ((tg >> 3) * kWords + q) * 32 + lane, w[q]);
+      for (int q = 0; q < kWords; ++q) {
+        uint32_t* dst = bp + ((tg >> 3) * kWords + q) * 32 + lane;
+        if (smem_codes) *dst = w[q];
+        else __stcg(dst, w[q]);
+      }
       const int tl = min(tg + 8, T) - 1;
       if ((tl & (kWinChunk - 1)) == kWinChunk - 1 || tl == T - 1) {
         // Segment map: each window state's path state at the frame before
@@ -1058,9 +1064,9 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
   }
   __syncwarp();
   // Segment g walks back from its anchor (path[t-1] = path[t] - jump(t,
-  // path[t]), alignment.cu:656-659).  Its codes are first brought from
-  // global memory into the emission ring, free now, a batch of segments at a
-  // time (independent 16-byte loads), so that each step of the walks is a
+  // path[t]), alignment.cu:656-659).  Codes in global memory are first
+  // brought into the emission ring, free now, a batch of segments at a time
+  // (independent 16-byte loads), so that each step of the walks is a
   // shared-memory read; with a ring too small for one segment's codes (a
   // vocabulary of a few columns) the walks read global memory.
   constexpr int kSegWords = (kWinChunk / 8) * kWords * 32;  // one segment's codes
@@ -1068,7 +1074,7 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
   const int ring_words = kWinRing * kWinChunk * V * static_cast<int>(sizeof(Elem)) / 4;
   const int per_batch = min(32, ring_words / kSegWords);
   uint32_t* stage = reinterpret_cast<uint32_t*>(ring);
-  auto walk = [&](int g, const uint32_t* codes, int first_word) {
+  auto walk = [&](int g, const uint32_t* codes, int first_word, bool global) {
     const int t_lo = g * kWinChunk;
     const int t_hi = min(T, t_lo + kWinChunk) - 1;
     int s = anc[g];
@@ -1077,23 +1083,25 @@ __device__ __forceinline__ bool window_record(const WindowParams& P, int r, unsi
       const int k = min(max(s - static_cast<int>(gb[t >> 3]), 0), W - 1);
       const int j = t & 7;
       const int at = ((t >> 3) * kWords + j / kFramesPerWord) * 32 + k / K - first_word;
-      const uint32_t word = codes == bp ? __ldcg(codes + at) : codes[at];
+      const uint32_t word = global ? __ldcg(codes + at) : codes[at];
       s -= static_cast<int>((word >> (2 * K * (j % kFramesPerWord) + 2 * (k % K))) & 3u);
       path[t - 1] = static_cast<uint16_t>(s);
     }
   };
-  if (per_batch >= 1) {
+  if (smem_codes) {
+    for (int g = lane; g < nseg; g += 32) walk(g, bp, 0, false);
+  } else if (per_batch >= 1) {
     for (int g0 = 0; g0 < nseg; g0 += per_batch) {
       const int w0 = g0 * kSegWords;
       const int w1 = min(total_words, (g0 + per_batch) * kSegWords);
       for (int i = 4 * lane; i < w1 - w0; i += 128)
         *reinterpret_cast<uint4*>(stage + i) = __ldcg(reinterpret_cast<const uint4*>(bp + w0 + i));
       __syncwarp();
-      if (lane < per_batch && g0 + lane < nseg) walk(g0 + lane, stage, w0);
+      if (lane < per_batch && g0 + lane < nseg) walk(g0 + lane, stage, w0, false);
       __syncwarp();
     }
   } else {
-    for (int g = lane; g < nseg; g += 32) walk(g, bp, 0);
+    for (int g = lane; g < nseg; g += 32) walk(g, bp, 0, true);
   }
   __syncwarp();
   // Labels and the selected scores (alignment.cu:662-666), frame-coalesced.
