@@ -211,6 +211,39 @@ struct GreedyFrame {
   int arg, ties;
   bool nonfinite;
 };
+// A 32-column fp32 row already in registers.
+__device__ __forceinline__ GreedyFrame greedy_row32(const float4 (&v4)[8], unsigned alo) {
+  GreedyFrame f{-INFINITY, 0, 0, false};
+  float bn = -INFINITY;
+  {
+    float xs[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      xs[4 * k] = v4[k].x; xs[4 * k + 1] = v4[k].y; xs[4 * k + 2] = v4[k].z; xs[4 * k + 3] = v4[k].w;
+    }
+    float bf[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float bq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const float v = ((alo >> k) & 1u) ? xs[k] : -INFINITY;
+      bf[k & 3] = fmaxf(bf[k & 3], v);
+      bq[k & 3] = max_nan(bq[k & 3], v);
+    }
+    f.best = fmaxf(fmaxf(bf[0], bf[1]), fmaxf(bf[2], bf[3]));
+    bn = max_nan(max_nan(bq[0], bq[1]), max_nan(bq[2], bq[3]));
+    int tq[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const bool hit = ((alo >> k) & 1u) && xs[k] == f.best;
+      tq[k & 3] += hit ? 1 : 0;
+      f.arg = hit ? k : f.arg;
+    }
+    f.ties = tq[0] + tq[1] + tq[2] + tq[3];
+  }
+  f.nonfinite = !(bn < INFINITY);
+  return f;
+}
+
 // Any row of V <= 64 columns, read column by column.  Logits are compared as
 // the emissions they stand for, x - z (rounding may tie two of them), and
 // `best` is then that emission.
@@ -379,65 +412,16 @@ ffa_greedy_pass(const __grid_constant__ GreedyParams P) {
     lab[q] = ok ? f.arg : 0xff;
   };
   if constexpr (kV == 32 && kFmt == 0) {
-    // The chunk's rows are contiguous (128 B each), so one load instruction
-    // of the warp reads four whole rows, 512 bytes: load k of batch n gives
-    // lane l the columns 4 (l & 7) .. 4 (l & 7) + 3 of frame
-    // a + 4 (8 n + k) + (l >> 3).  Each group of 8 lanes reduces its frame:
-    // the largest alphabet emission by shuffles, the alphabet columns that
-    // equal it and any NaN or +inf column by ballots.  The group's first
-    // lane leaves the frame's result in shared memory for the lane that owns
-    // the frame (lane j: frames a + 4 j .. a + 4 j + 3).  Eight loads (4 KB)
-    // are in flight per warp; streamed, the rows are read once.
-    __shared__ float best_s[kGreedyWarps][kGreedyChunk];
-    __shared__ uint16_t info_s[kGreedyWarps][kGreedyChunk];  // column | ties << 5 | nonfinite << 8
-    const int g = lane >> 3, c4 = lane & 7;
-    const unsigned m4 = (alo >> (4 * c4)) & 0xfu;
-    const float4* rows = reinterpret_cast<const float4*>(e);
+    // A row's eight 16-byte loads in flight at a time (streamed: read once);
+    // few registers keep many warps resident, which covers the latency.
 #pragma unroll 1
-    for (int n = 0; n < kGreedyChunk / 32; ++n) {
-      float4 v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int t = min(a + 4 * (8 * n + k) + g, b - 1);
-        v[k] = __ldcs(rows + static_cast<int64_t>(t) * 8 + c4);
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float x[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-        float best = -INFINITY, bn = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float y = ((m4 >> j) & 1u) ? x[j] : -INFINITY;
-          best = fmaxf(best, y);
-          bn = max_nan(bn, y);
-        }
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(kFull, best, o));
-        const unsigned nf = __ballot_sync(kFull, !(bn < INFINITY));
-        unsigned hits[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) hits[j] = __ballot_sync(kFull, ((m4 >> j) & 1u) && x[j] == best);
-        if (c4 == 0) {
-          int ties = 0, arg = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const unsigned h = (hits[j] >> (8 * g)) & 0xffu;
-            ties += __popc(h);
-            if (h != 0) arg = 4 * (__ffs(h) - 1) + j;  // the column when it is the only one
-          }
-          const int f = 4 * (8 * n + k) + g;
-          best_s[warp][f] = best;
-          info_s[warp][f] = static_cast<uint16_t>(arg | min(ties, 7) << 5 | (((nf >> (8 * g)) & 0xffu) != 0 ? 256 : 0));
-        }
-      }
-    }
-    __syncwarp();
-#pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int f = 4 * lane + q;
-      const unsigned info = info_s[warp][f];
-      take(q, GreedyFrame{best_s[warp][f], static_cast<int>(info & 31u), static_cast<int>((info >> 5) & 7u),
-                          (info & 256u) != 0});
+      float4 v4[8];
+      const int t = min(a + 4 * lane + q, b - 1);
+      const float4* row = reinterpret_cast<const float4*>(e + static_cast<int64_t>(t) * 32);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v4[k] = __ldcs(row + k);
+      take(q, greedy_row32(v4, alo));
     }
   } else {
 #pragma unroll
