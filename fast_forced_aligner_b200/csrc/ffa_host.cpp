@@ -114,6 +114,13 @@ bool window_shape(const ffa_record& r, int64_t max_frames) {
 }
 
 int device_sms();
+// Whether a call's window records keep their codes in global memory: they
+// spread more than kWinSmemCodesSpread to an SM (the workspace planner and
+// the CTA packing decide it with this one function).
+bool window_codes_global(int64_t window_records) {
+  const int64_t sms = device_sms();
+  return window_records > 0 && (window_records + sms - 1) / sms > kWinSmemCodesSpread;
+}
 WindowPolicy window_policy(const ffa_record* records, int64_t count, int mode, int flags) {
   if (mode != FFA_MODE_OPTIMIZED || (flags & FFA_FLAG_PIECE_ROUTE)) return WindowPolicy{0};
   if (flags & FFA_FLAG_WINDOW_ROUTE) return WindowPolicy{ffa::kWinMaxFrames};
@@ -265,7 +272,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   if (records == nullptr || count < 1 || count > FFA_MAX_RECORDS)
     return fail(FFA_ERR_INVALID_ARGUMENT, "provide 1..65535 records");
   int64_t frames = 0, bp_words = 0, map_elems = 0, segments = 0, fill = 0, frontier = 0, chunked = 0,
-          pieces = 0, longs = 0, greedy = 0, greedy_window = 0, tokens = 0, wide = 0;
+          pieces = 0, longs = 0, greedy = 0, greedy_window = 0, tokens = 0, wide = 0, windows_n = 0;
   int wide_tokens = 0, wide_vocab = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int rc = check_record(records[i], i, true);
@@ -282,6 +289,7 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
     pieces += g.pieces;
     greedy += g.greedy_items;
     greedy_window += g.window ? g.greedy_items : 0;
+    windows_n += g.window ? 1 : 0;
     tokens += records[i].tokens;
     wide += g.wide_items;
     if (g.wide_items > 0) {
@@ -347,9 +355,11 @@ int plan_align(const ffa_record* records, int64_t count, bool optimized, const W
   // Logits: each frame's row log-sum-exp.
   L->lse = off; off = align_up(off + (L->format != FFA_INPUT_LOG_PROBS ? sizeof(float) * frames : 0), 256);
   // The window route's backpointer codes (ffa::win_codes_offset): 32 B per
-  // frame plus 256 B per record, when the call has window records.
+  // frame plus 256 B per record, when they go to global memory.
   L->win_codes = off;
-  off = align_up(off + (greedy_window > 0 ? sizeof(uint32_t) * static_cast<size_t>(8 * (frames + 8 * count)) : 0), 256);
+  off = align_up(off + (window_codes_global(windows_n) ? sizeof(uint32_t) * static_cast<size_t>(8 * (frames + 8 * count))
+                                                      : 0),
+                 256);
   L->workspace_bytes = off;
   return FFA_OK;
 }
@@ -984,7 +994,7 @@ int ffa_align(const ffa_record* records, int64_t count, int mode, int flags,
     // the codes go to global memory and the smaller slices let up to
     // kWinWarps records share a CTA.
     const int64_t spread = (nwin + sms - 1) / sms;
-    win_smem_codes = spread <= kWinSmemCodesSpread;
+    win_smem_codes = !window_codes_global(nwin);
     const int64_t per_cta = std::clamp<int64_t>(spread, 1, win_smem_codes ? kWinSmemCodesSpread : ffa::kWinWarps);
     // Two CTAs share an SM when each stays under half the budget: twice the
     // warps to cover each warp's per-frame dependency chain.  A record larger
