@@ -81,6 +81,24 @@ def test_align_query_sizes_long_records(lib):
     assert sizes.workspace_bytes >= (34000 * 65535 + 90000 * 54001) // 4
 
 
+def test_window_codes_arena_only_for_throughput_bound_batches(lib):
+    # Optimized mode gives records of at most 2048 frames to the window route
+    # when there are more than 4 per SM.  Up to 8 per SM their codes stay in
+    # shared memory; beyond that the workspace carries a global codes arena
+    # of 32 B per frame plus 256 B per record.  (Planning without a GPU
+    # assumes a B200's 148 SMs.)
+    def extra(n):
+        recs = records(*[(600, 32, 100, 0)] * n)
+        opt, conv = Sizes(), Sizes()
+        assert lib.ffa_align_query(recs, n, 1, 1, ctypes.byref(opt)) == 0
+        assert lib.ffa_align_query(recs, n, 0, 1, ctypes.byref(conv)) == 0
+        return opt.workspace_bytes - conv.workspace_bytes, 600 * n
+    latency_bound, frames = extra(600)      # 5 window records per SM
+    assert latency_bound < 32 * frames
+    throughput_bound, frames = extra(1200)  # 9 per SM
+    assert throughput_bound >= 32 * frames + 256 * 1200
+
+
 @pytest.mark.parametrize("spec, code", [
     ((0, 32, 1, 0), -2), ((10, 0, 1, 0), -2), ((10, 8193, 1, 0), -2),
     ((10, 32, 32768, 0), -2), ((10, 32, 1, 32), -2), ((10, 32, 1, -1), -2),
